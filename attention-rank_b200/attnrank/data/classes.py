@@ -1,0 +1,41 @@
+"""Frozen settings of the Python API (reference: attnrank/data/classes.py:9-80, profiling fields)."""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+DEFAULT_MAX_SEQUENCE = 4096
+DEFAULT_PREFILL_CHUNK = 512
+DEFAULT_MIN_EDGE_RATIO = 1.3
+DEFAULT_PROBE_SAMPLES = 400
+DEFAULT_SEED = 1234
+DEFAULT_MAX_BATCH_TOKENS = 16384
+DEFAULT_MAX_BATCH_PROMPTS = 256
+
+
+@dataclass(frozen=True, slots=True)
+class EngineSettings:
+    device: int = -1
+    max_sequence: int = DEFAULT_MAX_SEQUENCE
+    chunk: int = DEFAULT_PREFILL_CHUNK
+    chat_format: str = ""
+    system_prompt: str = ""
+    max_batch_tokens: int = DEFAULT_MAX_BATCH_TOKENS      # additive: packed tokens per forward
+    max_batch_prompts: int = DEFAULT_MAX_BATCH_PROMPTS    # additive
+
+
+@dataclass(frozen=True, slots=True)
+class LayerScanSettings:
+    layer_begin: int = 0
+    layer_end: int | None = None
+    min_edge_ratio: float = DEFAULT_MIN_EDGE_RATIO
+    normalize_by_length: bool = False
+    model_id: str | None = None
+
+
+@dataclass(frozen=True, slots=True)
+class ProfileSettings:
+    layer_index: int
+    layer_span: tuple[int, int] | None = None
+    average_all_layers: bool = False
+    normalize_by_length: bool = False
+    model_id: str | None = None

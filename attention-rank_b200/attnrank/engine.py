@@ -1,0 +1,236 @@
+"""Keyword-only Python API of the profiling path (reference: attnrank/engine.py).
+
+Same function names, arguments and return types as the reference for:
+  from_pretrained (:168-182), load_model (:148-165), basin_statistics (:258-259),
+  scan_attention_layers (:262-275), select_shallowest_basin_layer (:278-283), LayerScan (:286-334),
+  find_shallowest_attention_layer (:337-355), extract_attention_profile (:358-375),
+  save/load_attention_profile (:378-384), profile_to_dict (:387-388),
+  measure_attention_by_layer (:417-433), attention_slot_order (:436-437),
+  rerank_documents (:440-445), rerank_with_profile (:448-449), make_reranker (:452-471),
+  rerank_baseline (:474-490).
+Probe samples are token-id prompts (core.StructuredPrompt); the reference's text samples need its
+tokenizer and prompt builder, which are outside this build.
+"""
+from __future__ import annotations
+
+import json
+from dataclasses import dataclass, field
+from pathlib import Path
+from typing import Any, Callable, Sequence
+
+from attnrank import core
+from attnrank.core import (AttentionProfile, AttnRankError, Engine, LlamaConfig, RuntimeOptions, StructuredPrompt,
+                           TokenSpan)
+from attnrank.data.classes import DEFAULT_MIN_EDGE_RATIO, DEFAULT_SEED, EngineSettings, LayerScanSettings, ProfileSettings
+
+MODEL_CONFIG_FILE = "config.json"
+WEIGHT_FILE_PATTERNS = ("*.safetensors",)
+MINIMUM_BASIN_SLOTS = 3
+
+ProgressCallback = Callable[[int, int], None]
+
+
+def is_model_directory(*, path: Path) -> bool:
+    if not (path / MODEL_CONFIG_FILE).is_file():
+        return False
+    return any(any(path.glob(pattern)) for pattern in WEIGHT_FILE_PATTERNS)
+
+
+def runtime_options(settings: EngineSettings) -> RuntimeOptions:
+    return RuntimeOptions(device_index=settings.device, max_sequence_length=settings.max_sequence,
+                          prefill_chunk_tokens=settings.chunk, max_batch_tokens=settings.max_batch_tokens,
+                          max_batch_prompts=settings.max_batch_prompts)
+
+
+def load_model(*, model_dir: Path, settings: EngineSettings = EngineSettings()) -> Engine:
+    return Engine(str(model_dir), runtime_options(settings), settings.chat_format, settings.system_prompt)
+
+
+def from_pretrained(*, model: str | Path, settings: EngineSettings = EngineSettings(), cache_dir: Path | None = None,
+                    revision: str | None = None, token: str | None = None) -> Engine:
+    candidate = Path(model)
+    if is_model_directory(path=candidate):
+        return load_model(model_dir=candidate.resolve(), settings=settings)
+    if candidate.exists():
+        raise FileNotFoundError(f"{model} exists but holds no {MODEL_CONFIG_FILE} and weight shards")
+    raise FileNotFoundError(f"{model} is not a local checkpoint directory (hub downloads are outside this build)")
+
+
+def synthetic_engine(*, config: LlamaConfig, seed: int = 0, std: float = 0.02,
+                     settings: EngineSettings = EngineSettings()) -> Engine:
+    """Additive: an engine on the seeded synthetic checkpoint of ``config``'s architecture."""
+    return Engine.synthetic(config, seed=seed, std=std, options=runtime_options(settings))
+
+
+def make_prompt(*, tokens: Sequence[int], document_spans: Sequence[tuple[int, int]],
+                query_span: tuple[int, int]) -> StructuredPrompt:
+    """Additive: a token-id probe prompt."""
+    return StructuredPrompt(tokens=tokens, document_spans=[TokenSpan(*s) for s in document_spans],
+                            query_span=TokenSpan(*query_span))
+
+
+def basin_statistics(*, attention: Sequence[float], min_edge_ratio: float = DEFAULT_MIN_EDGE_RATIO) -> Any:
+    return core.basin_statistics(list(attention), core.BasinCriterion(min_edge_ratio))
+
+
+def scan_attention_layers(*, engine: Engine, samples: Sequence[StructuredPrompt],
+                          settings: LayerScanSettings = LayerScanSettings(),
+                          progress: ProgressCallback | None = None) -> list[AttentionProfile]:
+    config = core.LayerScanConfig()
+    config.model_id = settings.model_id or engine.model_directory
+    config.layer_begin = settings.layer_begin
+    config.layer_end = -1 if settings.layer_end is None else settings.layer_end
+    config.normalize_by_document_length = settings.normalize_by_length
+    config.progress_interval = 0
+    return core.scan_attention_layers(engine, list(samples), config, progress)
+
+
+def select_shallowest_basin_layer(*, profiles: Sequence[AttentionProfile],
+                                  min_edge_ratio: float = DEFAULT_MIN_EDGE_RATIO) -> int:
+    return core.select_shallowest_basin_layer(list(profiles), core.BasinCriterion(min_edge_ratio))
+
+
+@dataclass
+class LayerScan:
+    selected_layer: int
+    min_edge_ratio: float
+    profiles: list[AttentionProfile] = field(default_factory=list)
+
+    def statistics(self) -> list[Any]:
+        return [basin_statistics(attention=profile.attention, min_edge_ratio=self.min_edge_ratio)
+                for profile in self.profiles]
+
+    def profile_for(self, *, layer_index: int) -> AttentionProfile:
+        for profile in self.profiles:
+            if profile.layer_index == layer_index:
+                return profile
+        raise KeyError(f"layer {layer_index} is not part of this scan")
+
+    def highest_ratio_layer(self) -> int:
+        ratios = [statistics.edge_ratio for statistics in self.statistics()]
+        return self.profiles[max(range(len(ratios)), key=lambda index: ratios[index])].layer_index
+
+    def table(self) -> str:
+        lines = [f"{'layer':>5} {'first':>8} {'interior':>9} {'last':>8} {'ratio':>7}  basin"]
+        for profile, stats in zip(self.profiles, self.statistics()):
+            mark = "yes" if stats.is_basin else "-"
+            if profile.layer_index == self.selected_layer:
+                mark += "  <- selected"
+            lines.append(f"{profile.layer_index:>5} {stats.first:>8.4f} {stats.interior_mean:>9.4f} "
+                         f"{stats.last:>8.4f} {stats.edge_ratio:>7.2f}  {mark}")
+        return "\n".join(lines)
+
+    def to_dict(self) -> dict[str, Any]:
+        return {
+            "selected_layer": self.selected_layer,
+            "min_edge_ratio": self.min_edge_ratio,
+            "profiles": [
+                {"layer_index": profile.layer_index, "attention": list(profile.attention),
+                 "position_order": list(profile.position_order), "edge_ratio": stats.edge_ratio,
+                 "is_basin": stats.is_basin}
+                for profile, stats in zip(self.profiles, self.statistics())
+            ],
+        }
+
+
+def find_shallowest_attention_layer(*, engine: Engine, samples: Sequence[StructuredPrompt],
+                                    settings: LayerScanSettings = LayerScanSettings(),
+                                    progress: ProgressCallback | None = None) -> LayerScan:
+    if len(samples) == 0:
+        raise ValueError("at least one probe sample is required")
+    if len(samples[0].document_spans) < MINIMUM_BASIN_SLOTS:
+        raise ValueError(f"attention-basin detection needs at least {MINIMUM_BASIN_SLOTS} documents per sample")
+    profiles = scan_attention_layers(engine=engine, samples=samples, settings=settings, progress=progress)
+    selected = select_shallowest_basin_layer(profiles=profiles, min_edge_ratio=settings.min_edge_ratio)
+    return LayerScan(selected_layer=selected, min_edge_ratio=settings.min_edge_ratio, profiles=profiles)
+
+
+def extract_attention_profile(*, engine: Engine, samples: Sequence[StructuredPrompt], settings: ProfileSettings,
+                              progress: ProgressCallback | None = None) -> AttentionProfile:
+    if len(samples) == 0:
+        raise ValueError("at least one probe sample is required")
+    config = core.ProfilerConfig()
+    config.model_id = settings.model_id or engine.model_directory
+    config.layer_index = settings.layer_index
+    config.average_all_layers = settings.average_all_layers
+    if settings.layer_span is not None:
+        config.layer_span_begin, config.layer_span_end = settings.layer_span[0], settings.layer_span[1] + 1
+    config.normalize_by_document_length = settings.normalize_by_length
+    config.progress_interval = 0
+    return core.build_attention_profile(engine, list(samples), config, progress)
+
+
+def save_attention_profile(*, profile: AttentionProfile, path: Path) -> None:
+    path.parent.mkdir(parents=True, exist_ok=True)
+    profile.save(str(path))
+
+
+def load_attention_profile(*, path: Path) -> AttentionProfile:
+    return AttentionProfile.load(str(path))
+
+
+def profile_to_dict(*, profile: AttentionProfile) -> dict[str, Any]:
+    return json.loads(profile.to_json_string())
+
+
+def measure_attention_by_layer(*, engine: Engine, prompt: StructuredPrompt, layer_begin: int = 0,
+                               layer_end: int | None = None, normalize_by_length: bool = False) -> list[list[float]]:
+    result = engine.measure_attention_by_layer(prompt, layer_begin=layer_begin,
+                                               layer_end=-1 if layer_end is None else layer_end,
+                                               normalize_by_length=normalize_by_length)
+    return [list(row) for row in result.attention_by_layer]
+
+
+def measure_document_attention(*, engine: Engine, prompt: StructuredPrompt, layer_index: int = 0,
+                               layer_span: tuple[int, int] | None = None, average_all_layers: bool = False,
+                               normalize_by_length: bool = False) -> list[float]:
+    span_begin, span_end = (-1, -1) if layer_span is None else (layer_span[0], layer_span[1] + 1)
+    return engine.measure_attention(prompt, layer_index=layer_index, layer_span_begin=span_begin,
+                                    layer_span_end=span_end, average_all_layers=average_all_layers,
+                                    normalize_by_length=normalize_by_length)
+
+
+def attention_slot_order(*, position_order: Sequence[int], count: int) -> list[int]:
+    return list(core.resolve_position_order(list(position_order), count))
+
+
+def rerank_documents(*, documents_by_relevance: Sequence[Any], position_order: Sequence[int]) -> list[Any]:
+    slots = attention_slot_order(position_order=position_order, count=len(documents_by_relevance))
+    placed: list[Any] = [None] * len(documents_by_relevance)
+    for rank, document in enumerate(documents_by_relevance):
+        placed[slots[rank]] = document
+    return placed
+
+
+def rerank_with_profile(*, documents_by_relevance: Sequence[Any], profile: AttentionProfile) -> list[Any]:
+    return rerank_documents(documents_by_relevance=documents_by_relevance, position_order=profile.position_order)
+
+
+def make_reranker(*, strategy: str, position_order: Sequence[int] | None = None, seed: int = DEFAULT_SEED,
+                  lim_start_first: bool = False) -> Any:
+    if strategy == "attnrank":
+        if not position_order:
+            raise ValueError("strategy 'attnrank' needs a position_order")
+        return core.AttentionReranker(list(position_order))
+    if strategy == "descending":
+        return core.DescendingReranker()
+    if strategy == "ascending":
+        return core.AscendingReranker()
+    if strategy == "random":
+        return core.RandomReranker(seed)
+    if strategy == "lim":
+        return core.LostInTheMiddleReranker(lim_start_first)
+    raise ValueError(f"unknown strategy '{strategy}'")
+
+
+def rerank_baseline(*, documents_by_relevance: Sequence[Any], strategy: str, position_order: Sequence[int] | None = None,
+                    seed: int = DEFAULT_SEED, lim_start_first: bool = False) -> list[Any]:
+    reranker = make_reranker(strategy=strategy, position_order=position_order, seed=seed,
+                             lim_start_first=lim_start_first)
+    count = len(documents_by_relevance)
+    ranked = [core.ScoredDocument(index, float(count - index)) for index in range(count)]
+    return [documents_by_relevance[scored.index] for scored in reranker.rerank(ranked)]
+
+
+def reranker_names() -> list[str]:
+    return core.reranker_names()

@@ -1,0 +1,102 @@
+"""Multi-GPU probe scheduler: shard prompts across ranks, one all-reduce of the mass accumulator.
+
+The reference profiles on one GPU (README.md:17); multi-GPU use means separate processes on
+dataset shards run by hand (README.md:149). Here one process per GPU holds a full weight replica,
+prompts are sharded by length (longest-processing-time first, so ranks finish together), every
+rank adds the unit-sum rows of its prompts into an fp32 [layers x slots] accumulator on its GPU,
+and a single all-reduce (NCCL over NVLink on GPUs; gloo in the CPU tests) joins them. The sum of
+per-prompt rows is order independent, so the profile equals the single-GPU scan up to fp32
+rounding; profiles, the basin pick and the slot order are then computed identically on every rank.
+
+Failure handling: the process group is created with a timeout by the caller; a rank that raises
+before the all-reduce makes the others' all-reduce fail with an error instead of hanging (NCCL
+async error handling / gloo timeout), and the exception propagates to every caller.
+"""
+from __future__ import annotations
+
+import heapq
+from typing import Sequence
+
+import numpy as np
+
+from attnrank import core
+from attnrank.data.classes import LayerScanSettings
+
+
+def shard_by_length(lengths: Sequence[int], world_size: int) -> list[list[int]]:
+    """Longest-processing-time assignment: prompts by descending length to the least-loaded rank
+    (ties to the lowest rank). Each shard keeps ascending prompt order."""
+    if world_size <= 0:
+        raise ValueError("world_size must be positive")
+    heap = [(0, rank) for rank in range(world_size)]
+    shards: list[list[int]] = [[] for _ in range(world_size)]
+    for index in sorted(range(len(lengths)), key=lambda i: (-lengths[i], i)):
+        load, rank = heapq.heappop(heap)
+        shards[rank].append(index)
+        heapq.heappush(heap, (load + int(lengths[index]), rank))
+    return [sorted(shard) for shard in shards]
+
+
+def _dist():
+    import torch.distributed as dist
+    return dist if dist.is_available() and dist.is_initialized() else None
+
+
+class ProbeScheduler:
+    """Runs one layer scan over all ranks of the default (or given) process group."""
+
+    def __init__(self, engine, group=None):
+        self.engine = engine
+        self.group = group
+        dist = _dist()
+        self.rank = dist.get_rank(group) if dist else 0
+        self.world_size = dist.get_world_size(group) if dist else 1
+
+    def accumulator_device(self) -> str:
+        device = getattr(self.engine, "accumulator_device", None)
+        return device if device is not None else f"cuda:{self.engine.device}"
+
+    def shard(self, samples: Sequence[core.StructuredPrompt]) -> list[int]:
+        return shard_by_length([len(s.tokens) for s in samples], self.world_size)[self.rank]
+
+    def accumulate(self, samples: Sequence[core.StructuredPrompt], settings: LayerScanSettings = LayerScanSettings()):
+        """Sum over all prompts of their unit-sum rows, reduced over ranks: fp64 [layers, slots]."""
+        import torch
+
+        if len(samples) == 0:
+            raise core.AttnRankError("probe needs at least one sample")
+        begin = settings.layer_begin
+        end = self.engine.num_layers if settings.layer_end is None else settings.layer_end
+        slots = len(samples[0].document_spans)
+        accumulator = torch.zeros((end - begin) * slots, dtype=torch.float32, device=self.accumulator_device())
+        if accumulator.is_cuda:
+            torch.cuda.synchronize(accumulator.device)
+        mine = [samples[i] for i in self.shard(samples)]
+        if mine:
+            self.engine.scan(mine, begin, -1 if settings.layer_end is None else settings.layer_end,
+                             settings.normalize_by_length, accumulator=accumulator)
+        dist = _dist()
+        if dist is not None and self.world_size > 1:
+            dist.all_reduce(accumulator, op=dist.ReduceOp.SUM, group=self.group)
+        return accumulator.double().cpu().numpy().reshape(end - begin, slots)
+
+    def find_shallowest_attention_layer(self, samples: Sequence[core.StructuredPrompt],
+                                        settings: LayerScanSettings = LayerScanSettings()):
+        from attnrank.engine import LayerScan, MINIMUM_BASIN_SLOTS
+        if len(samples) == 0:
+            raise ValueError("at least one probe sample is required")
+        if len(samples[0].document_spans) < MINIMUM_BASIN_SLOTS:
+            raise ValueError(f"attention-basin detection needs at least {MINIMUM_BASIN_SLOTS} documents per sample")
+        accumulated = self.accumulate(samples, settings)
+        model_id = settings.model_id or getattr(self.engine, "model_directory", "")
+        profiles = [core.AttentionProfile.from_accumulated(model_id, settings.layer_begin + layer, len(samples),
+                                                           accumulated[layer])
+                    for layer in range(accumulated.shape[0])]
+        selected = core.select_shallowest_basin_layer(profiles, core.BasinCriterion(settings.min_edge_ratio))
+        return LayerScan(selected_layer=selected, min_edge_ratio=settings.min_edge_ratio, profiles=profiles)
+
+
+def find_shallowest_attention_layer_sharded(*, engine, samples: Sequence[core.StructuredPrompt],
+                                            settings: LayerScanSettings = LayerScanSettings(), group=None):
+    """find_shallowest_attention_layer over every rank of the process group (same result on all)."""
+    return ProbeScheduler(engine, group).find_shallowest_attention_layer(samples, settings)

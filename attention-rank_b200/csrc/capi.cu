@@ -1,0 +1,488 @@
+// extern "C" boundary of libattnrank_b200.so (declarations and reference citations in
+// include/attnrank_b200.h). Every entry point converts C++ exceptions into an error code and a
+// thread-local message, the way the reference's pybind layer maps attnrank::Error to
+// AttnRankError (attnrank/src/bindings.cpp:134).
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <limits>
+#include <numeric>
+#include <string>
+#include <vector>
+
+#include "../../include/attnrank_b200.h"
+#include "engine.h"
+#include "layer_kernels.h"
+#include "mass_plan.h"
+#include "profile.h"
+#include "synthetic.h"
+
+struct ar_engine {
+  std::unique_ptr<arb::Engine> engine;
+};
+
+struct ar_prepared_scan {
+  std::unique_ptr<arb::PreparedScan> scan;
+};
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& message) {
+  g_last_error = message;
+  return code;
+}
+
+template <typename F>
+int guarded(F&& body) {
+  try {
+    g_last_error.clear();
+    return body();
+  } catch (const arb::Error& error) {
+    const std::string what = error.what();
+    const bool device = what.find("device reported") != std::string::npos;
+    const bool cuda = what.find("CUDA error") != std::string::npos || what.find("cuBLASLt") != std::string::npos;
+    return fail(device ? AR_ERR_DEVICE : cuda ? AR_ERR_CUDA : AR_ERR_INVALID, what);
+  } catch (const std::bad_alloc&) {
+    return fail(AR_ERR_INTERNAL, "host allocation failed");
+  } catch (const std::exception& error) {
+    return fail(AR_ERR_INTERNAL, error.what());
+  }
+}
+
+int cuda_result(cudaError_t status, const char* what) {
+  if (status == cudaSuccess) return AR_OK;
+  return fail(status == cudaErrorInvalidValue ? AR_ERR_INVALID : AR_ERR_CUDA,
+              std::string(what) + ": " + cudaGetErrorString(status));
+}
+
+cudaStream_t as_stream(void* stream) { return static_cast<cudaStream_t>(stream); }
+
+std::vector<arb::PromptView> prompt_views(const ar_prompt* prompts, int count) {
+  if (prompts == nullptr || count <= 0) throw arb::Error("at least one probe prompt is required");
+  std::vector<arb::PromptView> views(count);
+  for (int i = 0; i < count; ++i) {
+    if (prompts[i].tokens == nullptr || prompts[i].spans == nullptr) throw arb::Error("probe prompt has null arrays");
+    views[i].tokens = prompts[i].tokens;
+    views[i].token_count = prompts[i].token_count;
+    views[i].query_begin = prompts[i].query_begin;
+    views[i].query_end = prompts[i].query_end;
+    views[i].spans = prompts[i].spans;
+  }
+  return views;
+}
+
+// Device scratch owned by one kernel-level call (released on the call's stream).
+struct StreamScratch {
+  cudaStream_t stream;
+  std::vector<void*> blocks;
+  explicit StreamScratch(cudaStream_t s) : stream(s) {}
+  void* get(size_t bytes) {
+    void* pointer = nullptr;
+    arb::check_cuda(cudaMallocAsync(&pointer, std::max<size_t>(bytes, 16), stream), "scratch allocation");
+    blocks.push_back(pointer);
+    return pointer;
+  }
+  ~StreamScratch() {
+    for (void* pointer : blocks) cudaFreeAsync(pointer, stream);
+  }
+};
+
+}  // namespace
+
+extern "C" {
+
+const char* ar_last_error(void) { return g_last_error.c_str(); }
+
+const char* ar_version(void) { return "attnrank-b200 0.1.0 (sm_100a)"; }
+
+int ar_embedding_rms_norm(const int32_t* token_ids, int token_count, const void* table_bf16, int vocab_size,
+                          int hidden_size, const float* gamma, float eps, float* residual, void* normed_bf16,
+                          int* device_status, void* stream) {
+  if (token_count < 0 || hidden_size <= 0 || hidden_size % 8 != 0 || vocab_size <= 0) {
+    return fail(AR_ERR_INVALID, "embedding: invalid sizes (hidden_size must be a positive multiple of 8)");
+  }
+  return cuda_result(arb::launch_embed_rms_norm(token_ids, token_count, table_bf16, vocab_size, hidden_size, gamma, eps,
+                                                residual, normed_bf16, device_status, as_stream(stream)),
+                     "embedding_rms_norm");
+}
+
+int ar_rms_norm_residual(float* residual, const void* delta_bf16, const float* gamma, int token_count, int hidden_size,
+                         float eps, void* normed_bf16, void* stream) {
+  if (token_count < 0 || hidden_size <= 0 || hidden_size % 8 != 0) {
+    return fail(AR_ERR_INVALID, "rms_norm_residual: hidden_size must be a positive multiple of 8");
+  }
+  return cuda_result(arb::launch_rms_norm_residual(residual, delta_bf16, gamma, token_count, hidden_size, eps,
+                                                   normed_bf16, as_stream(stream)),
+                     "rms_norm_residual");
+}
+
+int ar_rotary_embedding(void* qkv_bf16, const float* bias, const int32_t* positions, int token_count, int query_heads,
+                        int kv_heads, int head_dim, const float* cos_table, const float* sin_table,
+                        int table_positions, int* device_status, void* stream) {
+  if (token_count < 0 || query_heads <= 0 || kv_heads <= 0 || head_dim <= 0 || head_dim % 16 != 0) {
+    return fail(AR_ERR_INVALID, "rotary_embedding: head_dim must be a positive multiple of 16");
+  }
+  return cuda_result(arb::launch_rotary_bias(qkv_bf16, bias, positions, token_count, query_heads, kv_heads, head_dim,
+                                             cos_table, sin_table, table_positions, device_status, as_stream(stream)),
+                     "rotary_embedding");
+}
+
+int ar_rope_table(float* cos_table, float* sin_table, int positions, int head_dim, float theta, void* stream) {
+  if (positions < 0 || head_dim <= 0 || head_dim % 2 != 0) return fail(AR_ERR_INVALID, "rope_table: invalid sizes");
+  return cuda_result(arb::launch_rope_table(cos_table, sin_table, positions, head_dim, theta, as_stream(stream)),
+                     "rope_table");
+}
+
+int ar_silu_multiply(const void* gate_bf16, const void* up_bf16, int64_t in_row_stride, void* out_bf16,
+                     int64_t out_row_stride, int token_count, int width, void* stream) {
+  if (token_count < 0 || width <= 0 || width % 8 != 0 || in_row_stride % 8 != 0 || out_row_stride % 8 != 0) {
+    return fail(AR_ERR_INVALID, "silu_multiply: width and strides must be multiples of 8");
+  }
+  return cuda_result(arb::launch_silu_multiply(gate_bf16, up_bf16, in_row_stride, out_bf16, out_row_stride,
+                                               token_count, width, as_stream(stream)),
+                     "silu_multiply");
+}
+
+int ar_causal_attention(const void* qkv_bf16, void* out_bf16, float* lse, const int32_t* prompt_offsets_host,
+                        const int32_t* prompt_offsets_device, int prompt_count, int query_heads, int kv_heads,
+                        int head_dim, int sliding_window, void* stream) {
+  return guarded([&] {
+    if (prompt_count <= 0 || head_dim != 128 || kv_heads <= 0 || query_heads % kv_heads != 0) {
+      throw arb::Error("causal_attention: head_dim must be 128 and query_heads a multiple of kv_heads");
+    }
+    std::vector<int32_t> tiles;
+    int max_tiles = 0;
+    for (int p = 0; p < prompt_count; ++p) {
+      const int length = prompt_offsets_host[p + 1] - prompt_offsets_host[p];
+      if (length < 0) throw arb::Error("causal_attention: prompt offsets must be non-decreasing");
+      max_tiles = std::max(max_tiles, (length + arb::kAttentionQueryTile - 1) / arb::kAttentionQueryTile);
+    }
+    for (int t = max_tiles - 1; t >= 0; --t) {
+      for (int p = 0; p < prompt_count; ++p) {
+        if (t * arb::kAttentionQueryTile < prompt_offsets_host[p + 1] - prompt_offsets_host[p]) {
+          tiles.push_back(p);
+          tiles.push_back(t);
+        }
+      }
+    }
+    if (tiles.empty()) return AR_OK;
+    StreamScratch scratch(as_stream(stream));
+    auto* tiles_device = static_cast<int32_t*>(scratch.get(tiles.size() * sizeof(int32_t)));
+    arb::check_cuda(cudaMemcpyAsync(tiles_device, tiles.data(), tiles.size() * sizeof(int32_t), cudaMemcpyHostToDevice,
+                                    as_stream(stream)),
+                    "tile upload");
+    arb::AttentionArgs args;
+    args.qkv = qkv_bf16;
+    args.out = out_bf16;
+    args.lse = lse;
+    args.prompt_offsets = prompt_offsets_device;
+    args.tiles = tiles_device;
+    args.tile_count = static_cast<int>(tiles.size() / 2);
+    args.query_heads = query_heads;
+    args.kv_heads = kv_heads;
+    args.head_dim = head_dim;
+    args.sliding_window = sliding_window;
+    arb::check_cuda(arb::launch_causal_attention(args, as_stream(stream)), "causal_attention");
+    arb::check_cuda(cudaStreamSynchronize(as_stream(stream)), "causal_attention");  // host tile list lifetime
+    return AR_OK;
+  });
+}
+
+int ar_document_attention_mass(const void* qkv_bf16, int qkv_rows, const float* lse, const int32_t* prompt_offsets_host,
+                               int prompt_count, const int32_t* query_spans_host, const int32_t* spans_host,
+                               int span_count, int query_heads, int kv_heads, int head_dim, int sliding_window,
+                               int prefill_chunk_tokens, int normalize_by_length, double* mass_out, void* stream) {
+  return guarded([&] {
+    if (prompt_count <= 0 || span_count <= 0 || span_count > arb::kMassMaxSpans) {
+      throw arb::Error("document_attention_mass: 1..32 spans and at least one prompt are required");
+    }
+    if (head_dim != 128 || kv_heads <= 0 || query_heads % kv_heads != 0) {
+      throw arb::Error("document_attention_mass: head_dim must be 128 and query_heads a multiple of kv_heads");
+    }
+    if (prompt_offsets_host[prompt_count] > qkv_rows) throw arb::Error("document_attention_mass: prompts exceed qkv rows");
+    const int group = query_heads / kv_heads;
+    // metadata: offsets | query spans | spans | item offsets
+    std::vector<int32_t> meta;
+    meta.insert(meta.end(), prompt_offsets_host, prompt_offsets_host + prompt_count + 1);
+    const size_t queries_at = meta.size();
+    meta.insert(meta.end(), query_spans_host, query_spans_host + 2 * prompt_count);
+    const size_t spans_at = meta.size();
+    meta.insert(meta.end(), spans_host, spans_host + 2 * static_cast<size_t>(prompt_count) * span_count);
+    const size_t items_at = meta.size();
+    meta.push_back(0);
+    for (int p = 0; p < prompt_count; ++p) {
+      const int length = prompt_offsets_host[p + 1] - prompt_offsets_host[p];
+      if (query_spans_host[2 * p] < 0 || query_spans_host[2 * p + 1] < query_spans_host[2 * p]) {
+        throw arb::Error("document_attention_mass: invalid query span");
+      }
+      for (int s = 0; s < span_count; ++s) {
+        const int32_t* span = spans_host + 2 * (static_cast<size_t>(p) * span_count + s);
+        if (span[0] < 0 || span[1] < span[0]) throw arb::Error("document_attention_mass: invalid document span");
+      }
+      const arb::MassItemShape shape = arb::mass_item_shape(query_spans_host + 2 * p,
+                                                            spans_host + 2 * static_cast<size_t>(p) * span_count,
+                                                            span_count, length, group);
+      meta.push_back(meta.back() + arb::mass_items_for_prompt(shape, kv_heads));
+    }
+    const int item_count = meta.back();
+    cudaStream_t s = as_stream(stream);
+    StreamScratch scratch(s);
+    auto* meta_device = static_cast<int32_t*>(scratch.get(meta.size() * sizeof(int32_t)));
+    auto* partials = static_cast<float*>(scratch.get(static_cast<size_t>(item_count) * span_count * sizeof(float)));
+    auto* rows = static_cast<double*>(scratch.get(static_cast<size_t>(prompt_count) * span_count * sizeof(double)));
+    auto* status = static_cast<int*>(scratch.get(sizeof(int)));
+    arb::check_cuda(cudaMemsetAsync(status, 0, sizeof(int), s), "status reset");
+    arb::check_cuda(cudaMemcpyAsync(meta_device, meta.data(), meta.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s),
+                    "metadata upload");
+    arb::MassArgs args;
+    args.qkv = qkv_bf16;
+    args.qkv_rows_capacity = qkv_rows;
+    args.lse = lse;
+    args.prompt_offsets = meta_device;
+    args.query_spans = meta_device + queries_at;
+    args.spans = meta_device + spans_at;
+    args.item_offsets = meta_device + items_at;
+    args.prompt_count = prompt_count;
+    args.span_count = span_count;
+    args.item_count = item_count;
+    args.query_heads = query_heads;
+    args.kv_heads = kv_heads;
+    args.head_dim = head_dim;
+    args.sliding_window = sliding_window;
+    args.reference_chunk = prefill_chunk_tokens;
+    args.normalize_by_length = normalize_by_length;
+    args.partials = partials;
+    args.status = status;
+    arb::check_cuda(arb::launch_document_mass(args, s), "document_attention_mass");
+    arb::FinalizeArgs finalize;
+    finalize.partials = partials;
+    finalize.item_offsets = args.item_offsets;
+    finalize.query_spans = args.query_spans;
+    finalize.prompt_offsets = meta_device;
+    finalize.prompt_count = prompt_count;
+    finalize.span_count = span_count;
+    finalize.item_count = item_count;
+    finalize.layers = 1;
+    finalize.query_heads = query_heads;
+    finalize.raw_rows = rows;
+    arb::check_cuda(arb::launch_finalize_mass(finalize, s), "finalize");
+    int status_host = 0;
+    arb::check_cuda(cudaMemcpyAsync(mass_out, rows, static_cast<size_t>(prompt_count) * span_count * sizeof(double),
+                                    cudaMemcpyDeviceToHost, s),
+                    "mass download");
+    arb::check_cuda(cudaMemcpyAsync(&status_host, status, sizeof(int), cudaMemcpyDeviceToHost, s), "status download");
+    arb::check_cuda(cudaStreamSynchronize(s), "document_attention_mass");
+    if (status_host != 0) throw arb::Error("device reported an error in document_attention_mass (code " + std::to_string(status_host) + ")");
+    return AR_OK;
+  });
+}
+
+int ar_synthetic_fill(void* dst_bf16, int64_t count, uint64_t seed, int layer, int kind, float standard_deviation,
+                      void* stream) {
+  if (count < 0) return fail(AR_ERR_INVALID, "synthetic_fill: negative count");
+  return cuda_result(arb::launch_synthetic_fill(dst_bf16, count, arb::synthetic_tensor_key(seed, layer, kind),
+                                                arb::synthetic_scale(standard_deviation), as_stream(stream)),
+                     "synthetic_fill");
+}
+
+int ar_engine_create(const ar_llama_config* config, const ar_runtime_options* options, ar_engine** engine) {
+  return guarded([&] {
+    if (config == nullptr || engine == nullptr) throw arb::Error("engine_create: null argument");
+    arb::ModelConfig c;
+    c.hidden_size = config->hidden_size;
+    c.intermediate_size = config->intermediate_size;
+    c.num_hidden_layers = config->num_hidden_layers;
+    c.num_attention_heads = config->num_attention_heads;
+    c.num_key_value_heads = config->num_key_value_heads;
+    c.vocab_size = config->vocab_size;
+    c.max_position_embeddings = config->max_position_embeddings;
+    c.rms_norm_eps = config->rms_norm_eps;
+    c.rope_theta = config->rope_theta;
+    c.sliding_window = config->sliding_window;
+    c.attention_bias = config->attention_bias != 0;
+    arb::RuntimeOptions o;
+    if (options != nullptr) {
+      o.device_index = options->device_index;
+      if (options->max_sequence_length > 0) o.max_sequence_length = options->max_sequence_length;
+      if (options->prefill_chunk_tokens > 0) o.prefill_chunk_tokens = options->prefill_chunk_tokens;
+      if (options->max_batch_tokens > 0) o.max_batch_tokens = options->max_batch_tokens;
+      if (options->max_batch_prompts > 0) o.max_batch_prompts = options->max_batch_prompts;
+    }
+    auto holder = std::make_unique<ar_engine>();
+    holder->engine = std::make_unique<arb::Engine>(c, o);
+    *engine = holder.release();
+    return AR_OK;
+  });
+}
+
+void ar_engine_destroy(ar_engine* engine) { delete engine; }
+
+int ar_engine_load_tensor(ar_engine* engine, const char* name, int dtype, const int64_t* shape, int rank,
+                          const void* host_data) {
+  return guarded([&] {
+    if (engine == nullptr || name == nullptr || host_data == nullptr || rank < 0) throw arb::Error("load_tensor: null argument");
+    engine->engine->load_tensor(name, dtype, std::vector<int64_t>(shape, shape + rank), host_data);
+    return AR_OK;
+  });
+}
+
+int ar_engine_init_synthetic(ar_engine* engine, uint64_t seed, float standard_deviation) {
+  return guarded([&] {
+    if (engine == nullptr) throw arb::Error("init_synthetic: null engine");
+    engine->engine->init_synthetic(seed, standard_deviation);
+    return AR_OK;
+  });
+}
+
+int ar_engine_measure_attention_by_layer(ar_engine* engine, const ar_prompt* prompts, int prompt_count, int span_count,
+                                         int layer_begin, int layer_end, int normalize_by_length, double* rows_out,
+                                         int* layer_begin_out, int* layer_count_out) {
+  return guarded([&] {
+    if (engine == nullptr || rows_out == nullptr) throw arb::Error("measure_attention_by_layer: null argument");
+    const arb::LayerRange range = engine->engine->resolve_layers(layer_begin, layer_end);
+    engine->engine->probe(prompt_views(prompts, prompt_count), span_count, range, normalize_by_length != 0, rows_out,
+                          nullptr, nullptr);
+    if (layer_begin_out) *layer_begin_out = range.begin;
+    if (layer_count_out) *layer_count_out = range.count();
+    return AR_OK;
+  });
+}
+
+int ar_engine_measure_attention(ar_engine* engine, const ar_prompt* prompt, int span_count, int layer_begin,
+                                int layer_end, int normalize_by_length, double* attention_out) {
+  return guarded([&] {
+    if (engine == nullptr || attention_out == nullptr) throw arb::Error("measure_attention: null argument");
+    if (layer_begin < 0 || layer_end <= layer_begin) throw arb::Error("measure_attention: invalid layer range");
+    const arb::LayerRange range = engine->engine->resolve_layers(layer_begin, layer_end);
+    std::vector<double> raw(static_cast<size_t>(range.count()) * span_count);
+    engine->engine->probe(prompt_views(prompt, 1), span_count, range, normalize_by_length != 0, nullptr, raw.data(),
+                          nullptr);
+    // model.cu:576-589: totals / (query_rows * Hq * layers), summed over layers, unit-sum.
+    for (int s = 0; s < span_count; ++s) attention_out[s] = 0.0;
+    for (int l = 0; l < range.count(); ++l) {
+      for (int s = 0; s < span_count; ++s) attention_out[s] += raw[static_cast<size_t>(l) * span_count + s] / range.count();
+    }
+    arb::normalize_to_unit_sum(attention_out, span_count);
+    return AR_OK;
+  });
+}
+
+int ar_engine_scan(ar_engine* engine, const ar_prompt* prompts, int prompt_count, int span_count, int layer_begin,
+                   int layer_end, int normalize_by_length, float* device_accumulator, double* host_accumulator) {
+  return guarded([&] {
+    if (engine == nullptr || device_accumulator == nullptr) throw arb::Error("scan: null argument");
+    const arb::LayerRange range = engine->engine->resolve_layers(layer_begin, layer_end);
+    engine->engine->probe(prompt_views(prompts, prompt_count), span_count, range, normalize_by_length != 0, nullptr,
+                          nullptr, device_accumulator);
+    if (host_accumulator != nullptr) {
+      const size_t n = static_cast<size_t>(range.count()) * span_count;
+      std::vector<float> values(n);
+      arb::check_cuda(cudaMemcpyAsync(values.data(), device_accumulator, n * sizeof(float), cudaMemcpyDeviceToHost,
+                                      engine->engine->stream()),
+                      "accumulator download");
+      engine->engine->synchronize();
+      for (size_t i = 0; i < n; ++i) host_accumulator[i] = values[i];
+    }
+    return AR_OK;
+  });
+}
+
+int ar_engine_prepare_scan(ar_engine* engine, const ar_prompt* prompts, int prompt_count, int span_count,
+                           int layer_begin, int layer_end, int normalize_by_length, ar_prepared_scan** prepared) {
+  return guarded([&] {
+    if (engine == nullptr || prepared == nullptr) throw arb::Error("prepare_scan: null argument");
+    const arb::LayerRange range = engine->engine->resolve_layers(layer_begin, layer_end);
+    auto holder = std::make_unique<ar_prepared_scan>();
+    holder->scan = engine->engine->prepare_scan(prompt_views(prompts, prompt_count), span_count, range,
+                                                normalize_by_length != 0);
+    *prepared = holder.release();
+    return AR_OK;
+  });
+}
+
+int ar_engine_run_prepared_scan(ar_engine* engine, const ar_prepared_scan* prepared, float* device_accumulator,
+                                int synchronize) {
+  return guarded([&] {
+    if (engine == nullptr || prepared == nullptr || device_accumulator == nullptr) {
+      throw arb::Error("run_prepared_scan: null argument");
+    }
+    engine->engine->run_prepared(*prepared->scan, device_accumulator);
+    if (synchronize) arb::Engine::raise_on_status(engine->engine->read_status());
+    return AR_OK;
+  });
+}
+
+void ar_prepared_scan_destroy(ar_prepared_scan* prepared) { delete prepared; }
+
+int64_t ar_prepared_scan_bytes(const ar_prepared_scan* prepared) {
+  return prepared ? static_cast<int64_t>(prepared->scan->device_bytes) : 0;
+}
+
+int ar_engine_synchronize(ar_engine* engine) {
+  return guarded([&] {
+    if (engine == nullptr) throw arb::Error("synchronize: null engine");
+    const int status = engine->engine->read_status();
+    engine->engine->reset_status();
+    arb::Engine::raise_on_status(status);
+    return AR_OK;
+  });
+}
+
+void* ar_engine_stream(ar_engine* engine) { return engine ? static_cast<void*>(engine->engine->stream()) : nullptr; }
+
+int ar_engine_device(ar_engine* engine) { return engine ? engine->engine->options().device_index : -1; }
+
+int ar_profile_from_accumulated(const double* accumulated, int slots, int64_t sample_count, double* attention_out,
+                                int* position_order_out) {
+  return guarded([&] {
+    if (slots < 0 || (slots > 0 && (accumulated == nullptr || attention_out == nullptr))) {
+      throw arb::Error("profile_from_accumulated: invalid arguments");
+    }
+    arb::profile_from_accumulated(accumulated, slots, sample_count, attention_out, position_order_out);
+    return AR_OK;
+  });
+}
+
+int ar_position_order(const double* attention, int slots, int* position_order_out) {
+  return guarded([&] {
+    if (slots < 0) throw arb::Error("position_order: negative slot count");
+    arb::stable_descending_order(attention, slots, position_order_out);
+    return AR_OK;
+  });
+}
+
+int ar_basin_statistics(const double* attention, int slots, double min_edge_ratio, ar_basin_stats* out) {
+  return guarded([&] {
+    if (out == nullptr || slots < 0) throw arb::Error("basin_statistics: invalid arguments");
+    const arb::BasinStatistics stats = arb::basin_statistics(attention, slots, min_edge_ratio);
+    out->first = stats.first;
+    out->last = stats.last;
+    out->interior_mean = stats.interior_mean;
+    out->edge_ratio = stats.edge_ratio;
+    out->is_basin = stats.is_basin ? 1 : 0;
+    return AR_OK;
+  });
+}
+
+int ar_select_shallowest_basin_layer(const double* attention, const int* layer_indices, int profile_count, int slots,
+                                     double min_edge_ratio, int* selected_out) {
+  return guarded([&] {
+    if (selected_out == nullptr || profile_count < 0 || slots < 0) throw arb::Error("select_shallowest_basin_layer: invalid arguments");
+    *selected_out = arb::select_shallowest_basin_layer(attention, layer_indices, profile_count, slots, min_edge_ratio);
+    return AR_OK;
+  });
+}
+
+int ar_resolve_position_order(const int* preferred, int preferred_count, int count, int* order_out) {
+  return guarded([&] {
+    if (count < 0 || preferred_count < 0 || (count > 0 && order_out == nullptr)) {
+      throw arb::Error("resolve_position_order: invalid arguments");
+    }
+    arb::resolve_position_order(preferred, preferred_count, count, order_out);
+    return AR_OK;
+  });
+}
+
+}  // extern "C"

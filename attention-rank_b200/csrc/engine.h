@@ -1,0 +1,219 @@
+// B200 attention-profiling engine: a Llama-family prefill that captures per-layer
+// query->document attention mass for batches of packed prompts.
+//
+// It is the B200 counterpart of the reference's CudaLlamaModel in its IAttentionProvider role
+// (include/attnrank/model.hpp:79-86, :144-165; attnrank/src/model.cu:512-679). Differences that
+// are design, not semantics:
+//   * many prompts run in one forward (packed, variable length), so the projection GEMMs see
+//     thousands of rows instead of one prompt's chunk;
+//   * weights stay bf16 in HBM (q|k|v and gate|up fused into one matrix each), activations are
+//     bf16 except the fp32 residual stream;
+//   * attention never materialises scores; mass is captured by a tcgen05 kernel per layer and
+//     reduced on the device, with no host synchronisation until the caller asks for results.
+#pragma once
+
+#include <cublasLt.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <map>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <tuple>
+#include <vector>
+
+namespace arb {
+
+class Error : public std::runtime_error {
+ public:
+  explicit Error(const std::string& message) : std::runtime_error(message) {}
+};
+
+void check_cuda(cudaError_t status, const char* what);
+
+struct ModelConfig {
+  int hidden_size = 0;
+  int intermediate_size = 0;
+  int num_hidden_layers = 0;
+  int num_attention_heads = 0;
+  int num_key_value_heads = 0;
+  int vocab_size = 0;
+  int max_position_embeddings = 0;
+  float rms_norm_eps = 1e-6f;
+  float rope_theta = 10000.0f;
+  int sliding_window = 0;
+  bool attention_bias = false;
+
+  int head_dim() const { return hidden_size / num_attention_heads; }
+  int kv_width() const { return num_key_value_heads * head_dim(); }
+  int qkv_width() const { return (num_attention_heads + 2 * num_key_value_heads) * head_dim(); }
+};
+
+struct RuntimeOptions {
+  int device_index = 0;
+  int max_sequence_length = 32768;   // longest prompt (size of the RoPE table)
+  int prefill_chunk_tokens = 512;    // the reference's chunk length (normalize_by_length divisors)
+  int max_batch_tokens = 16384;      // packed tokens per forward
+  int max_batch_prompts = 256;
+};
+
+// One probe prompt as the host hands it over: token ids plus prompt-relative spans.
+struct PromptView {
+  const int32_t* tokens = nullptr;
+  int token_count = 0;
+  int query_begin = 0;
+  int query_end = 0;
+  const int32_t* spans = nullptr;  // [span_count][2] half-open [begin, end)
+};
+
+struct LayerRange {
+  int begin = 0;
+  int end = 0;
+  int count() const { return end - begin; }
+};
+
+// Offsets (int32 elements) of one batch's metadata inside a metadata buffer.
+struct BatchLayout {
+  size_t tokens_at = 0, offsets_at = 0, queries_at = 0, spans_at = 0, tiles_at = 0, items_at = 0, size = 0;
+  int first = 0;       // index of the batch's first prompt
+  int prompts = 0;
+  int tokens = 0;
+  int tile_count = 0;  // attention query tiles
+  int item_count = 0;  // mass CTAs
+};
+
+// A scan whose batch metadata is resident in HBM: running it launches kernels only.
+struct PreparedScan {
+  std::vector<BatchLayout> batches;
+  int32_t* device = nullptr;
+  size_t device_bytes = 0;
+  int span_count = 0;
+  int prompt_count = 0;
+  LayerRange range;
+  bool normalize_by_length = false;
+  ~PreparedScan();
+};
+
+class Engine {
+ public:
+  Engine(const ModelConfig& config, const RuntimeOptions& options);
+  ~Engine();
+  Engine(const Engine&) = delete;
+  Engine& operator=(const Engine&) = delete;
+
+  const ModelConfig& config() const { return config_; }
+  const RuntimeOptions& options() const { return options_; }
+  cudaStream_t stream() const { return stream_; }
+
+  // Weights. Names are the Hugging Face Llama/Qwen2 tensor names (reference model.cu:120-166).
+  // dtype: 0 = fp32, 1 = fp16, 2 = bf16. Host data is converted to the resident layout.
+  void load_tensor(const std::string& name, int dtype, const std::vector<int64_t>& shape, const void* host);
+  void init_synthetic(uint64_t seed, float standard_deviation);
+  bool weights_complete(std::string* missing) const;
+
+  LayerRange resolve_layers(int layer_begin, int layer_end) const;
+
+  // Probe prompts through layers [0, range.end), capturing mass for layers in `range`.
+  //   rows_host:      optional [prompts][range.count()][span_count] unit-sum rows (fp64)
+  //   raw_rows_host:  optional [prompts][range.count()][span_count] mass / observations before
+  //                   the unit-sum step (the input of the reference's measure_attention)
+  //   device_accumulator: optional fp32 [range.count()][span_count], += sum of the rows
+  // Prompts are packed into batches of at most max_batch_tokens tokens. The call returns after
+  // every requested host output is written (one stream synchronisation at the end).
+  void probe(const std::vector<PromptView>& prompts, int span_count, LayerRange range, bool normalize_by_length,
+             double* rows_host, double* raw_rows_host, float* device_accumulator);
+
+  // Scan with HBM-resident inputs: prepare once (validates, plans batches, uploads all metadata),
+  // then run_prepared enqueues the whole scan on stream() without any host synchronisation.
+  std::unique_ptr<PreparedScan> prepare_scan(const std::vector<PromptView>& prompts, int span_count, LayerRange range,
+                                             bool normalize_by_length);
+  void run_prepared(const PreparedScan& prepared, float* device_accumulator);
+
+  // Device-side status word (0 = ok): reset, read (synchronises the stream), raise on error.
+  void reset_status();
+  int read_status();
+  static void raise_on_status(int status);
+  int last_device_status() const { return last_status_; }
+
+  // Raw access for the kernel-level tests: the device buffers of the last batch.
+  const void* qkv_buffer() const { return qkv_; }
+  int qkv_capacity_rows() const { return capacity_tokens_; }
+
+  void synchronize();
+
+ private:
+  struct LayerWeights {
+    void* qkv = nullptr;     // bf16 [(Hq + 2 Hkv) D, H]
+    float* qkv_bias = nullptr;  // fp32 [(Hq + 2 Hkv) D] or null
+    void* out = nullptr;     // bf16 [H, Hq D]
+    void* gate_up = nullptr;  // bf16 [2 I, H]
+    void* down = nullptr;    // bf16 [H, I]
+    float* input_norm = nullptr;  // fp32 [H]
+    float* post_norm = nullptr;   // fp32 [H]
+  };
+
+  struct Batch {
+    int first = 0;
+    int count = 0;
+    int tokens = 0;
+  };
+
+  void allocate();
+  void ensure_partials(size_t items, int span_count, int layers);
+  void gemm(const void* x, const void* w, void* y, int m, int n, int k);
+  void run_batch(const std::vector<PromptView>& prompts, const Batch& batch, int span_count, LayerRange range,
+                 bool normalize_by_length, double* rows_device, double* raw_rows_device, float* device_accumulator,
+                 int slot);
+  BatchLayout build_metadata(const std::vector<PromptView>& prompts, const Batch& batch, int span_count, int32_t* host,
+                             size_t capacity) const;
+  void execute_batch(const BatchLayout& layout, const int32_t* device_metadata, int span_count, LayerRange range,
+                     bool normalize_by_length, double* rows_device, double* raw_rows_device,
+                     float* device_accumulator);
+  void validate(const std::vector<PromptView>& prompts, int span_count, LayerRange range) const;
+  std::vector<Batch> plan_batches(const std::vector<PromptView>& prompts) const;
+  void* device_alloc(size_t bytes);
+
+  ModelConfig config_;
+  RuntimeOptions options_;
+  int capacity_tokens_ = 0;
+  cudaStream_t stream_ = nullptr;
+  cublasLtHandle_t lt_ = nullptr;
+  void* lt_workspace_ = nullptr;
+  size_t lt_workspace_bytes_ = 0;
+  struct GemmPlans;
+  std::unique_ptr<GemmPlans> plans_;  // cuBLASLt descriptors + algorithm per (m, n, k)
+
+  std::vector<void*> allocations_;
+  void* embedding_ = nullptr;  // bf16 [V, H]
+  std::vector<LayerWeights> layers_;
+  float* final_norm_ = nullptr;
+  std::vector<std::vector<bool>> loaded_;  // per layer, per tensor kind
+  bool embedding_loaded_ = false;
+
+  // workspace
+  float* residual_ = nullptr;
+  void* normed_ = nullptr;
+  void* qkv_ = nullptr;
+  void* attn_ = nullptr;
+  void* delta_ = nullptr;
+  void* gate_up_ = nullptr;
+  void* act_ = nullptr;
+  float* lse_ = nullptr;
+  int32_t* positions_ = nullptr;
+  float* cos_table_ = nullptr;
+  float* sin_table_ = nullptr;
+  int* status_ = nullptr;
+  int32_t* meta_device_[2] = {nullptr, nullptr};
+  int32_t* meta_host_[2] = {nullptr, nullptr};
+  size_t meta_capacity_ = 0;  // int32 elements per metadata buffer
+  cudaEvent_t meta_free_[2] = {nullptr, nullptr};
+  float* partials_ = nullptr;
+  size_t partials_capacity_ = 0;  // floats
+  double* rows_device_ = nullptr;
+  size_t rows_capacity_ = 0;      // doubles per rows buffer (two buffers: rows, raw rows)
+  int* status_host_ = nullptr;
+  int last_status_ = 0;
+};
+
+}  // namespace arb

@@ -1,0 +1,359 @@
+// Fused per-layer kernels of the attention-profiling prefill, hand-written for sm_100a.
+//
+// All four are HBM-bound: each moves its operands through HBM exactly once with 128-bit
+// coalesced accesses, and grids are sized from the SM count. They replace these reference
+// kernels (attnrank/src/kernels.cu):
+//   embedding_lookup_kernel  (:50-58)   -> embed_rms_norm_kernel (gather + the first pre-norm)
+//   rms_norm_kernel (:60-83) + add_in_place_kernel (:172-175) -> rms_norm_residual_kernel
+//   rotary_embedding_kernel (:85-115) + add_row_bias_kernel (:177-184) -> rotary_bias_kernel
+//   silu_multiply_kernel (:164-170)     -> silu_multiply_kernel
+// The arithmetic of each op follows the reference formula line for line (fp32 math, the same
+// order of multiplies), only the storage type of activations changes from fp32 to bf16.
+#include "common.cuh"
+#include "layer_kernels.h"
+
+namespace arb {
+namespace {
+
+constexpr int kRowThreadsCap = 512;
+
+// ---------------------------------------------------------------------------------------------
+// Row kernels: one CTA per token row, each thread holds VPT vectors of 8 channels in registers,
+// so the row is read once, reduced, and written once.
+// ---------------------------------------------------------------------------------------------
+template <int VPT>
+__global__ void __launch_bounds__(kRowThreadsCap) embed_rms_norm_kernel(
+    const int32_t* __restrict__ token_ids, const __nv_bfloat16* __restrict__ table, int vocab,
+    int hidden, const float* __restrict__ gamma, float eps, float* __restrict__ residual,
+    __nv_bfloat16* __restrict__ normed, int* status) {
+  __shared__ float scratch[32];
+  const int row = blockIdx.x;
+  int token = token_ids[row];
+  if (token < 0 || token >= vocab) {
+    if (threadIdx.x == 0) report_status(status, kStatusTokenOutOfRange);
+    token = -1;
+  }
+  const int chunks = hidden >> 3;
+  float values[VPT][8];
+  float squares = 0.0f;
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int chunk = threadIdx.x + k * blockDim.x;
+    if (chunk < chunks && token >= 0) {
+      unpack8(load_nc(table + static_cast<size_t>(token) * hidden + chunk * 8), values[k]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) values[k][i] = 0.0f;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) squares += values[k][i] * values[k][i];
+  }
+  const float total = block_sum(squares, scratch);
+  const float scale = rsqrtf(total / static_cast<float>(hidden) + eps);
+  float* residual_row = residual + static_cast<size_t>(row) * hidden;
+  __nv_bfloat16* normed_row = normed + static_cast<size_t>(row) * hidden;
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int chunk = threadIdx.x + k * blockDim.x;
+    if (chunk >= chunks) continue;
+    const float4 g0 = __ldg(reinterpret_cast<const float4*>(gamma + chunk * 8));
+    const float4 g1 = __ldg(reinterpret_cast<const float4*>(gamma + chunk * 8 + 4));
+    const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+    float4* out = reinterpret_cast<float4*>(residual_row + chunk * 8);
+    __stcs(out, make_float4(values[k][0], values[k][1], values[k][2], values[k][3]));
+    __stcs(out + 1, make_float4(values[k][4], values[k][5], values[k][6], values[k][7]));
+    float y[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) y[i] = values[k][i] * scale * g[i];
+    *reinterpret_cast<uint4*>(normed_row + chunk * 8) = pack8(y);
+  }
+}
+
+template <int VPT>
+__global__ void __launch_bounds__(kRowThreadsCap) rms_norm_residual_kernel(
+    float* __restrict__ residual, const __nv_bfloat16* __restrict__ delta,
+    const float* __restrict__ gamma, int hidden, float eps, __nv_bfloat16* __restrict__ normed) {
+  __shared__ float scratch[32];
+  const int row = blockIdx.x;
+  const int chunks = hidden >> 3;
+  float* residual_row = residual + static_cast<size_t>(row) * hidden;
+  const __nv_bfloat16* delta_row = delta + static_cast<size_t>(row) * hidden;
+  float values[VPT][8];
+  float squares = 0.0f;
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int chunk = threadIdx.x + k * blockDim.x;
+    if (chunk < chunks) {
+      const float4 r0 = load_stream_f4(residual_row + chunk * 8);
+      const float4 r1 = load_stream_f4(residual_row + chunk * 8 + 4);
+      float d[8];
+      unpack8(load_stream(delta_row + chunk * 8), d);
+      values[k][0] = r0.x + d[0];
+      values[k][1] = r0.y + d[1];
+      values[k][2] = r0.z + d[2];
+      values[k][3] = r0.w + d[3];
+      values[k][4] = r1.x + d[4];
+      values[k][5] = r1.y + d[5];
+      values[k][6] = r1.z + d[6];
+      values[k][7] = r1.w + d[7];
+      float4* out = reinterpret_cast<float4*>(residual_row + chunk * 8);
+      __stcs(out, make_float4(values[k][0], values[k][1], values[k][2], values[k][3]));
+      __stcs(out + 1, make_float4(values[k][4], values[k][5], values[k][6], values[k][7]));
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) values[k][i] = 0.0f;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) squares += values[k][i] * values[k][i];
+  }
+  const float total = block_sum(squares, scratch);
+  const float scale = rsqrtf(total / static_cast<float>(hidden) + eps);
+  __nv_bfloat16* normed_row = normed + static_cast<size_t>(row) * hidden;
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int chunk = threadIdx.x + k * blockDim.x;
+    if (chunk >= chunks) continue;
+    const float4 g0 = __ldg(reinterpret_cast<const float4*>(gamma + chunk * 8));
+    const float4 g1 = __ldg(reinterpret_cast<const float4*>(gamma + chunk * 8 + 4));
+    const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+    float y[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) y[i] = values[k][i] * scale * g[i];
+    *reinterpret_cast<uint4*>(normed_row + chunk * 8) = pack8(y);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Bias + rotary embedding, in place on the fused [tokens, (Hq + 2 Hkv) * D] projection output.
+// One thread owns 8 rotation pairs (x_i, x_{i + D/2}) of one head of one token.
+// Query and key heads get bias + rotation; value heads get the bias only (skipped without bias).
+// ---------------------------------------------------------------------------------------------
+__global__ void rotary_bias_kernel(__nv_bfloat16* __restrict__ qkv, const float* __restrict__ bias,
+                                   const int32_t* __restrict__ positions, int tokens, int query_heads,
+                                   int kv_heads, int head_dim, const float* __restrict__ cos_table,
+                                   const float* __restrict__ sin_table, int table_positions,
+                                   int* status) {
+  const int half = head_dim >> 1;
+  const int chunks_per_head = half >> 3;
+  const int rotated_heads = query_heads + kv_heads;
+  const int heads = bias != nullptr ? rotated_heads + kv_heads : rotated_heads;
+  const int row_width = (query_heads + 2 * kv_heads) * head_dim;
+  const long long per_token = static_cast<long long>(heads) * chunks_per_head;
+  const long long total = per_token * tokens;
+  for (long long item = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; item < total;
+       item += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int token = static_cast<int>(item / per_token);
+    const int rest = static_cast<int>(item - static_cast<long long>(token) * per_token);
+    const int head = rest / chunks_per_head;
+    const int chunk = rest - head * chunks_per_head;
+    const int column = head * head_dim + chunk * 8;
+    __nv_bfloat16* low_ptr = qkv + static_cast<size_t>(token) * row_width + column;
+    __nv_bfloat16* high_ptr = low_ptr + half;
+    float low[8];
+    float high[8];
+    unpack8(*reinterpret_cast<const uint4*>(low_ptr), low);
+    unpack8(*reinterpret_cast<const uint4*>(high_ptr), high);
+    if (bias != nullptr) {
+      const float4 b0 = __ldg(reinterpret_cast<const float4*>(bias + column));
+      const float4 b1 = __ldg(reinterpret_cast<const float4*>(bias + column + 4));
+      const float4 b2 = __ldg(reinterpret_cast<const float4*>(bias + column + half));
+      const float4 b3 = __ldg(reinterpret_cast<const float4*>(bias + column + half + 4));
+      const float bl[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+      const float bh[8] = {b2.x, b2.y, b2.z, b2.w, b3.x, b3.y, b3.z, b3.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        low[i] += bl[i];
+        high[i] += bh[i];
+      }
+    }
+    if (head < rotated_heads) {
+      const int position = positions[token];
+      if (position < 0 || position >= table_positions) {
+        report_status(status, kStatusPositionOutOfRange);
+        continue;
+      }
+      const float* cos_row = cos_table + static_cast<size_t>(position) * half + chunk * 8;
+      const float* sin_row = sin_table + static_cast<size_t>(position) * half + chunk * 8;
+      const float4 c0 = __ldg(reinterpret_cast<const float4*>(cos_row));
+      const float4 c1 = __ldg(reinterpret_cast<const float4*>(cos_row + 4));
+      const float4 s0 = __ldg(reinterpret_cast<const float4*>(sin_row));
+      const float4 s1 = __ldg(reinterpret_cast<const float4*>(sin_row + 4));
+      const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+      const float s[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float l = low[i];
+        const float h = high[i];
+        low[i] = l * c[i] - h * s[i];
+        high[i] = h * c[i] + l * s[i];
+      }
+    }
+    *reinterpret_cast<uint4*>(low_ptr) = pack8(low);
+    *reinterpret_cast<uint4*>(high_ptr) = pack8(high);
+  }
+}
+
+// cos/sin of pos * theta^(-2i/D), written with the same fp32 expression as the reference's
+// per-element computation (kernels.cu:95-98), so the table holds identical values.
+__global__ void rope_table_kernel(float* __restrict__ cos_out, float* __restrict__ sin_out,
+                                  int positions, int head_dim, float theta) {
+  const int half = head_dim >> 1;
+  const long long total = static_cast<long long>(positions) * half;
+  for (long long item = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; item < total;
+       item += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int position = static_cast<int>(item / half);
+    const int index = static_cast<int>(item - static_cast<long long>(position) * half);
+    const float inverse_frequency = powf(theta, -2.0f * index / static_cast<float>(head_dim));
+    const float angle = position * inverse_frequency;
+    cos_out[item] = cosf(angle);
+    sin_out[item] = sinf(angle);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// SwiGLU: a = silu(g) * u with g, u read through arbitrary row strides (the fused gate|up GEMM
+// output has g in columns [0, I) and u in [I, 2I) of each row).
+// ---------------------------------------------------------------------------------------------
+__global__ void silu_multiply_kernel(const __nv_bfloat16* __restrict__ gate,
+                                     const __nv_bfloat16* __restrict__ up, long long in_stride,
+                                     __nv_bfloat16* __restrict__ out, long long out_stride, int tokens,
+                                     int width) {
+  const int chunks = width >> 3;
+  const long long total = static_cast<long long>(tokens) * chunks;
+  for (long long item = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; item < total;
+       item += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long token = item / chunks;
+    const int chunk = static_cast<int>(item - token * chunks);
+    float g[8];
+    float u[8];
+    unpack8(load_stream(gate + token * in_stride + chunk * 8), g);
+    unpack8(load_stream(up + token * in_stride + chunk * 8), u);
+    float a[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a[i] = (g[i] / (1.0f + __expf(-g[i]))) * u[i];
+    __stcs(reinterpret_cast<uint4*>(out + token * out_stride + chunk * 8), pack8(a));
+  }
+}
+
+// position of every packed token inside its own prompt: t - prompt_offsets[p].
+__global__ void positions_kernel(const int32_t* __restrict__ prompt_offsets, int prompt_count,
+                                 int tokens, int32_t* __restrict__ positions) {
+  for (int token = blockIdx.x * blockDim.x + threadIdx.x; token < tokens;
+       token += gridDim.x * blockDim.x) {
+    int lo = 0;
+    int hi = prompt_count - 1;
+    while (lo < hi) {  // last prompt whose offset <= token
+      const int mid = (lo + hi + 1) >> 1;
+      if (prompt_offsets[mid] <= token) lo = mid; else hi = mid - 1;
+    }
+    positions[token] = token - prompt_offsets[lo];
+  }
+}
+
+int row_threads(int hidden, int* vpt) {
+  const int chunks = hidden >> 3;
+  int per_thread = (chunks + kRowThreadsCap - 1) / kRowThreadsCap;
+  if (per_thread < 1) per_thread = 1;
+  *vpt = per_thread;
+  int threads = (chunks + per_thread - 1) / per_thread;
+  threads = (threads + 31) & ~31;
+  return threads;
+}
+
+}  // namespace
+
+int sm_count() {
+  static int cached = 0;
+  if (cached == 0) {
+    int device = 0;
+    cudaGetDevice(&device);
+    cudaDeviceGetAttribute(&cached, cudaDevAttrMultiProcessorCount, device);
+    if (cached <= 0) cached = 148;
+  }
+  return cached;
+}
+
+static int stride_grid(long long items, int threads, int ctas_per_sm) {
+  const long long needed = (items + threads - 1) / threads;
+  const long long cap = static_cast<long long>(sm_count()) * ctas_per_sm;
+  return static_cast<int>(needed < cap ? (needed > 0 ? needed : 1) : cap);
+}
+
+cudaError_t launch_embed_rms_norm(const int32_t* token_ids, int tokens, const void* table, int vocab,
+                                  int hidden, const float* gamma, float eps, float* residual,
+                                  void* normed, int* status, cudaStream_t stream) {
+  if (tokens <= 0) return cudaSuccess;
+  int vpt = 1;
+  const int threads = row_threads(hidden, &vpt);
+  const auto* t = static_cast<const __nv_bfloat16*>(table);
+  auto* n = static_cast<__nv_bfloat16*>(normed);
+  switch (vpt) {
+    case 1: embed_rms_norm_kernel<1><<<tokens, threads, 0, stream>>>(token_ids, t, vocab, hidden, gamma, eps, residual, n, status); break;
+    case 2: embed_rms_norm_kernel<2><<<tokens, threads, 0, stream>>>(token_ids, t, vocab, hidden, gamma, eps, residual, n, status); break;
+    case 3: embed_rms_norm_kernel<3><<<tokens, threads, 0, stream>>>(token_ids, t, vocab, hidden, gamma, eps, residual, n, status); break;
+    case 4: embed_rms_norm_kernel<4><<<tokens, threads, 0, stream>>>(token_ids, t, vocab, hidden, gamma, eps, residual, n, status); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rms_norm_residual(float* residual, const void* delta, const float* gamma, int tokens,
+                                     int hidden, float eps, void* normed, cudaStream_t stream) {
+  if (tokens <= 0) return cudaSuccess;
+  int vpt = 1;
+  const int threads = row_threads(hidden, &vpt);
+  const auto* d = static_cast<const __nv_bfloat16*>(delta);
+  auto* n = static_cast<__nv_bfloat16*>(normed);
+  switch (vpt) {
+    case 1: rms_norm_residual_kernel<1><<<tokens, threads, 0, stream>>>(residual, d, gamma, hidden, eps, n); break;
+    case 2: rms_norm_residual_kernel<2><<<tokens, threads, 0, stream>>>(residual, d, gamma, hidden, eps, n); break;
+    case 3: rms_norm_residual_kernel<3><<<tokens, threads, 0, stream>>>(residual, d, gamma, hidden, eps, n); break;
+    case 4: rms_norm_residual_kernel<4><<<tokens, threads, 0, stream>>>(residual, d, gamma, hidden, eps, n); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rotary_bias(void* qkv, const float* bias, const int32_t* positions, int tokens,
+                               int query_heads, int kv_heads, int head_dim, const float* cos_table,
+                               const float* sin_table, int table_positions, int* status,
+                               cudaStream_t stream) {
+  if (tokens <= 0) return cudaSuccess;
+  const int heads = query_heads + kv_heads + (bias != nullptr ? kv_heads : 0);
+  const long long items = static_cast<long long>(tokens) * heads * (head_dim / 16);
+  const int threads = 256;
+  rotary_bias_kernel<<<stride_grid(items, threads, 8), threads, 0, stream>>>(
+      static_cast<__nv_bfloat16*>(qkv), bias, positions, tokens, query_heads, kv_heads, head_dim,
+      cos_table, sin_table, table_positions, status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rope_table(float* cos_out, float* sin_out, int positions, int head_dim, float theta,
+                              cudaStream_t stream) {
+  const long long items = static_cast<long long>(positions) * (head_dim / 2);
+  if (items <= 0) return cudaSuccess;
+  rope_table_kernel<<<stride_grid(items, 256, 8), 256, 0, stream>>>(cos_out, sin_out, positions,
+                                                                     head_dim, theta);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_silu_multiply(const void* gate, const void* up, long long in_stride, void* out,
+                                 long long out_stride, int tokens, int width, cudaStream_t stream) {
+  const long long items = static_cast<long long>(tokens) * (width / 8);
+  if (items <= 0) return cudaSuccess;
+  const int threads = 256;
+  silu_multiply_kernel<<<stride_grid(items, threads, 8), threads, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(gate), static_cast<const __nv_bfloat16*>(up), in_stride,
+      static_cast<__nv_bfloat16*>(out), out_stride, tokens, width);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_positions(const int32_t* prompt_offsets, int prompt_count, int tokens,
+                             int32_t* positions, cudaStream_t stream) {
+  if (tokens <= 0) return cudaSuccess;
+  positions_kernel<<<stride_grid(tokens, 256, 4), 256, 0, stream>>>(prompt_offsets, prompt_count,
+                                                                    tokens, positions);
+  return cudaGetLastError();
+}
+
+}  // namespace arb

@@ -1,0 +1,108 @@
+// Host-side launchers of the fused per-layer kernels (layer_kernels.cu, attention.cu, mass.cu,
+// synthetic.cu). All pointers are device pointers; all launches are asynchronous on `stream`.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace arb {
+
+int sm_count();
+
+cudaError_t launch_embed_rms_norm(const int32_t* token_ids, int tokens, const void* table, int vocab,
+                                  int hidden, const float* gamma, float eps, float* residual,
+                                  void* normed, int* status, cudaStream_t stream);
+
+cudaError_t launch_rms_norm_residual(float* residual, const void* delta, const float* gamma, int tokens,
+                                     int hidden, float eps, void* normed, cudaStream_t stream);
+
+cudaError_t launch_rotary_bias(void* qkv, const float* bias, const int32_t* positions, int tokens,
+                               int query_heads, int kv_heads, int head_dim, const float* cos_table,
+                               const float* sin_table, int table_positions, int* status,
+                               cudaStream_t stream);
+
+cudaError_t launch_rope_table(float* cos_out, float* sin_out, int positions, int head_dim, float theta,
+                              cudaStream_t stream);
+
+cudaError_t launch_silu_multiply(const void* gate, const void* up, long long in_stride, void* out,
+                                 long long out_stride, int tokens, int width, cudaStream_t stream);
+
+cudaError_t launch_positions(const int32_t* prompt_offsets, int prompt_count, int tokens,
+                             int32_t* positions, cudaStream_t stream);
+
+// Causal prefill attention over packed prompts (attention.cu).
+struct AttentionArgs {
+  const void* qkv = nullptr;        // bf16 [tokens, (Hq + 2 Hkv) * D], Q | K | V column blocks
+  void* out = nullptr;              // bf16 [tokens, Hq * D]
+  float* lse = nullptr;             // fp32 [tokens, Hq], log2-domain log-sum-exp of scaled scores
+  const int32_t* prompt_offsets = nullptr;  // [prompts + 1]
+  const int32_t* tiles = nullptr;   // [tile_count * 2] (prompt, query tile) pairs, heaviest first
+  int tile_count = 0;
+  int query_heads = 0;
+  int kv_heads = 0;
+  int head_dim = 0;
+  int sliding_window = 0;           // 0 = unlimited
+};
+cudaError_t launch_causal_attention(const AttentionArgs& args, cudaStream_t stream);
+constexpr int kAttentionQueryTile = 128;
+
+// Query->document attention mass (mass.cu).
+struct MassArgs {
+  const void* qkv = nullptr;        // same packed projection buffer as AttentionArgs::qkv
+  int qkv_rows_capacity = 0;        // rows addressable through the TMA descriptors
+  const float* lse = nullptr;       // fp32 [tokens, Hq] from the attention kernel
+  const int32_t* prompt_offsets = nullptr;  // [prompts + 1]
+  const int32_t* query_spans = nullptr;     // [prompts * 2], prompt-relative [begin, end)
+  const int32_t* spans = nullptr;           // [prompts * span_count * 2], prompt-relative
+  const int32_t* item_offsets = nullptr;    // [prompts + 1] work items per prompt (prefix sums)
+  int prompt_count = 0;
+  int span_count = 0;
+  int item_count = 0;
+  int query_heads = 0;
+  int kv_heads = 0;
+  int head_dim = 0;
+  int sliding_window = 0;
+  int reference_chunk = 0;          // chunk length that bounds normalize_by_length divisors
+  int normalize_by_length = 0;
+  float* partials = nullptr;        // fp32 [item_count, span_count]
+  int* status = nullptr;
+};
+cudaError_t launch_document_mass(const MassArgs& args, cudaStream_t stream);
+constexpr int kMassRowTile = 128;   // GQA-stacked query rows per CTA
+constexpr int kMassKeyTile = 128;   // keys per tcgen05.mma N tile
+constexpr int kMassKeyTilesPerItem = 4;  // key tiles walked by one CTA
+constexpr int kMassMaxSpans = 32;
+
+// Work decomposition shared by the host planner, the mass kernel and the finalizer.
+struct MassItemShape {
+  int row_tiles;   // ceil(group * padded_query_rows / kMassRowTile)
+  int key_splits;  // ceil(key_tiles / kMassKeyTilesPerItem)
+  int key_begin;   // first key (multiple of kMassKeyTile) touched by any span
+  int key_tiles;   // 128-key tiles in [key_begin, key_end)
+};
+
+// Deterministic per-prompt normalisation + cross-prompt accumulation (mass.cu).
+struct FinalizeArgs {
+  const float* partials = nullptr;  // [layers][item_count][span_count]
+  const int32_t* item_offsets = nullptr;
+  const int32_t* query_spans = nullptr;
+  const int32_t* prompt_offsets = nullptr;
+  int prompt_count = 0;
+  int span_count = 0;
+  int item_count = 0;
+  int layers = 0;
+  int query_heads = 0;
+  double* rows = nullptr;           // optional [prompts][layers][span_count], unit-sum rows
+  double* raw_rows = nullptr;       // optional [prompts][layers][span_count], mass / observations
+  float* accumulator = nullptr;     // optional [layers][span_count], += sum over prompts of rows
+};
+cudaError_t launch_finalize_mass(const FinalizeArgs& args, cudaStream_t stream);
+
+// Seeded synthetic weights (synthetic.cu).
+cudaError_t launch_synthetic_fill(void* dst_bf16, long long count, uint64_t key, float scale,
+                                  cudaStream_t stream);
+cudaError_t launch_synthetic_fill_f32(float* dst, long long count, uint64_t key, float scale,
+                                      float offset, cudaStream_t stream);
+
+}  // namespace arb

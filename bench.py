@@ -1,0 +1,478 @@
+#!/usr/bin/env python
+"""Layer-scan throughput of the attention-profiling path on B200 (prompts/s).
+
+Workload: the Qwen2.5-7B architecture with seeded random-init bf16
+weights, 400 seeded synthetic prompts (5 documents of U[120, 240] random token ids + a 40-token
+question), a full layer scan (prefill with per-layer query->document mass capture, cross-prompt
+accumulation, all-reduce, basin pick with min_edge_ratio 1.3). One step = the whole 400-prompt
+scan, sharded across N GPUs (strong scaling).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+`value` is device-timed (CUDA events on the engine stream, max over ranks) with every input
+resident in HBM; `e2e` is the same scan through the public Python API with host prompts (H2D of
+tokens and batch metadata and D2H of the accumulator inside the timed region, wall clock, max over
+ranks). Inputs are larger than L2 (15 GB of weights stream through every batch), so no L2 flush
+is needed between steps.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "attention-rank_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "profiled prompts/s (7B arch, 1/2/4/8 B200); fused-kernel HBM GB/s vs peak"
+PROMPT_COUNT = 400
+MIN_EDGE_RATIO = 1.3
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse_args():
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=3)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    parser.add_argument("--prompts", type=int, default=PROMPT_COUNT)
+    parser.add_argument("--reference-sample", type=int, default=128,
+                        help="prompts per reference step (a bounded sample of the 400-prompt scan)")
+    parser.add_argument("--batch-tokens", type=int, default=16384)
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-kernels", action="store_true", help="skip the per-kernel roofline timing")
+    return parser.parse_args()
+
+
+def peaks() -> tuple[dict, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return json.loads(path.read_text()), "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.process = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.process = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.process = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.process.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.process is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.process.terminate()
+        try:
+            self.process.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.process.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+        sm, sm_max, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                sm_max.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(sm_max) if sm_max else None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def scan_flops(config, prompts) -> float:
+    """Algorithmic FLOPs of one full scan (projection GEMMs + causal attention + mass scoring)."""
+    H, I, L = config.hidden_size, config.intermediate_size, config.num_hidden_layers
+    Hq, Hkv, D = config.num_attention_heads, config.num_key_value_heads, config.head_dim
+    per_token = 2 * (H * (Hq + 2 * Hkv) * D + Hq * D * H + 3 * H * I)
+    total = 0.0
+    for p in prompts:
+        T = len(p.tokens)
+        Tq = p.query_span.end - p.query_span.begin
+        attention = 2 * Hq * D * T * (T + 1)          # QK^T and PV over the causal half
+        mass = 2 * Hq * Tq * T * D                    # mass scoring recomputes Q K^T for the query rows
+        total += L * (per_token * T + attention + mass)
+    return total
+
+
+def init_distributed(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    import torch
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device(f"cuda:{local_rank}"))
+    return rank, world, local_rank
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ---------------------------------------------------------------------------------------------
+# per-kernel roofline timing (live, CUDA events, on the engine's kernels through the C ABI)
+# ---------------------------------------------------------------------------------------------
+def kernel_rooflines(config, hbm_peak, tensor_peak, tokens: int = 16384, repeats: int = 20) -> dict:
+    import ctypes
+
+    import torch
+    from attnrank import _native
+
+    lib = _native.lib
+    dev = torch.device("cuda")
+    stream = torch.cuda.current_stream()
+    s = ctypes.c_void_p(stream.cuda_stream)
+    H, I, Hq, Hkv, D, V = (config.hidden_size, config.intermediate_size, config.num_attention_heads,
+                           config.num_key_value_heads, config.head_dim, config.vocab_size)
+    W = (Hq + 2 * Hkv) * D
+    gen = torch.Generator(device=dev).manual_seed(0)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    results = {}
+
+    def timed(name, launch, bytes_moved=None, flops=None):
+        for _ in range(3):
+            launch()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(repeats):
+            launch()
+        stop.record(stream)
+        stop.synchronize()
+        seconds = start.elapsed_time(stop) / 1000 / repeats
+        entry = {"us_per_launch": round(seconds * 1e6, 2)}
+        if bytes_moved is not None:
+            achieved = bytes_moved / seconds / 1e9
+            entry.update({"bound": "hbm", "algorithmic_bytes": int(bytes_moved), "achieved": round(achieved, 1),
+                          "unit": "GB/s", "frac": round(achieved / hbm_peak, 4)})
+        if flops is not None:
+            achieved = flops / seconds / 1e12
+            entry.update({"bound": "tensor", "algorithmic_flops": int(flops), "achieved": round(achieved, 1),
+                          "unit": "TFLOP/s", "frac": round(achieved / tensor_peak, 4)})
+        results[name] = entry
+
+    residual = torch.randn(tokens, H, device=dev, generator=gen)
+    delta = torch.randn(tokens, H, device=dev, generator=gen).to(torch.bfloat16)
+    gamma = torch.ones(H, device=dev)
+    normed = torch.empty(tokens, H, device=dev, dtype=torch.bfloat16)
+    timed("rms_norm_residual", lambda: _native.check(lib.ar_rms_norm_residual(
+        P(residual), P(delta), P(gamma), tokens, H, 1e-6, P(normed), s)), bytes_moved=12 * tokens * H + 4 * H)
+
+    table = (torch.randn(V, H, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+    ids = torch.randint(0, V, (tokens,), device=dev, dtype=torch.int32, generator=gen)
+    timed("embedding_rms_norm", lambda: _native.check(lib.ar_embedding_rms_norm(
+        P(ids), tokens, P(table), V, H, P(gamma), 1e-6, P(residual), P(normed), None, s)),
+        bytes_moved=tokens * (2 * H + 4 * H + 2 * H + 4))
+    del table
+
+    qkv = torch.randn(tokens, W, device=dev, generator=gen).to(torch.bfloat16)
+    bias = torch.zeros(W, device=dev)
+    cos = torch.empty(8192, D // 2, device=dev)
+    sin = torch.empty_like(cos)
+    _native.check(lib.ar_rope_table(P(cos), P(sin), 8192, D, config.rope_theta, s))
+    positions = (torch.arange(tokens, device=dev, dtype=torch.int32) % 940).contiguous()
+    timed("rotary_bias", lambda: _native.check(lib.ar_rotary_embedding(
+        P(qkv), P(bias), P(positions), tokens, Hq, Hkv, D, P(cos), P(sin), 8192, None, s)),
+        bytes_moved=4 * tokens * W)
+
+    gate_up = torch.randn(tokens, 2 * I, device=dev, generator=gen).to(torch.bfloat16)
+    act = torch.empty(tokens, I, device=dev, dtype=torch.bfloat16)
+    timed("silu_multiply", lambda: _native.check(lib.ar_silu_multiply(
+        P(gate_up), ctypes.c_void_p(gate_up.data_ptr() + 2 * I), 2 * I, P(act), I, tokens, I, s)),
+        bytes_moved=6 * tokens * I)
+    del gate_up, act
+
+    # attention + mass on 17 prompts of 940 tokens (a 16K-token batch of the scan)
+    from attnrank import synthetic
+    prompts = synthetic.prompts(17, V)
+    lengths = [len(p.tokens) for p in prompts]
+    import numpy as np
+    offsets = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
+    total = int(offsets[-1])
+    qkv2 = (torch.randn(total, W, device=dev, generator=gen)).to(torch.bfloat16)
+    out = torch.empty(total, Hq * D, device=dev, dtype=torch.bfloat16)
+    lse = torch.empty(total, Hq, device=dev)
+    offsets_d = torch.from_numpy(offsets).to(dev)
+    attention_flops = sum(2 * Hq * D * T * (T + 1) for T in lengths)
+    timed("causal_attention", lambda: _native.check(lib.ar_causal_attention(
+        P(qkv2), P(out), P(lse), offsets.ctypes.data, P(offsets_d), len(lengths), Hq, Hkv, D, 0, s)),
+        flops=attention_flops)
+    qs = np.ascontiguousarray(np.array([(p.query_span.begin, p.query_span.end) for p in prompts], np.int32).reshape(-1))
+    sp = np.ascontiguousarray(np.array([[(d.begin, d.end) for d in p.document_spans] for p in prompts],
+                                       np.int32).reshape(-1))
+    mass = np.zeros((len(prompts), 5))
+    mass_flops = sum(2 * Hq * (p.query_span.end - p.query_span.begin) * p.document_spans[-1].end * D for p in prompts)
+    timed("document_mass (incl. host planning + sync)", lambda: _native.check(lib.ar_document_attention_mass(
+        P(qkv2), total, P(lse), offsets.ctypes.data, len(prompts), qs.ctypes.data, sp.ctypes.data, 5, Hq, Hkv, D, 0,
+        512, 0, mass.ctypes.data, s)), flops=mass_flops)
+    torch.cuda.synchronize()
+    return results
+
+
+def cpu_baseline(config, prompt, layers: int = 4) -> dict:
+    """The oracle port (fp32 torch on the host cores) on a bounded sample: one prompt through the
+    first `layers` layers, scaled to the full depth."""
+    import torch
+    from oracle import forward as F
+    from oracle import weights as W
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    W.set_threads(cores)
+    shape = F.Shape(hidden=config.hidden_size, intermediate=config.intermediate_size, layers=layers,
+                    heads=config.num_attention_heads, kv_heads=config.num_key_value_heads, vocab=config.vocab_size,
+                    eps=config.rms_norm_eps, theta=config.rope_theta, bias=config.attention_bias)
+    model = F.OracleModel(shape, seed=0)
+    sample = F.Prompt(tokens=prompt.tokens, query_span=(prompt.query_span.begin, prompt.query_span.end),
+                      spans=[(s.begin, s.end) for s in prompt.document_spans])
+    start = time.perf_counter()
+    model.probe([sample])
+    seconds = (time.perf_counter() - start) * config.num_hidden_layers / layers
+    return {"value": round(1.0 / seconds, 5), "unit": "prompts/s", "cores": cores, "kind": "port",
+            "sample": f"1 prompt ({len(prompt.tokens)} tokens) x {layers} of {config.num_hidden_layers} layers, "
+                      f"fp32 torch-CPU oracle incl. weight generation, scaled to all layers"}
+
+
+# ---------------------------------------------------------------------------------------------
+def run_b200(args, rank, world, local_rank):
+    import numpy as np
+    import torch
+
+    import attnrank as ar
+    from attnrank import synthetic
+    from attnrank.scheduler import ProbeScheduler, shard_by_length
+
+    config = synthetic.qwen2_7b()
+    prompts = synthetic.prompts(args.prompts, config.vocab_size)
+    options = ar.RuntimeOptions(device_index=local_rank, max_sequence_length=4096, max_batch_tokens=args.batch_tokens)
+    engine = ar.Engine.synthetic(config, seed=0, options=options)
+    shard = shard_by_length([len(p.tokens) for p in prompts], world)[rank]
+    mine = [prompts[i] for i in shard]
+    slots = 5
+    L = config.num_hidden_layers
+    prepared = engine.prepare_scan(mine)
+    accumulator = torch.zeros(L * slots, dtype=torch.float32, device=f"cuda:{local_rank}")
+    torch.cuda.synchronize()
+    engine_stream = torch.cuda.ExternalStream(engine.stream, device=f"cuda:{local_rank}")
+
+    def step():
+        with torch.cuda.stream(engine_stream):
+            accumulator.zero_()
+            prepared.run(accumulator, synchronize=False)
+            if world > 1:
+                import torch.distributed as dist
+                dist.all_reduce(accumulator)
+
+    for _ in range(args.warmup):
+        step()
+    engine.synchronize()
+    barrier(world)
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.3)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(engine_stream)
+    for _ in range(args.steps):
+        step()
+    stop.record(engine_stream)
+    stop.synchronize()
+    clocks = sampler.stop()
+    engine.synchronize()  # raises on any device-reported error
+    elapsed_ms = max_over_ranks(start.elapsed_time(stop), world)
+    ms_per_step = elapsed_ms / args.steps
+    value = args.prompts / (ms_per_step / 1000.0)
+
+    # the scan result of the timed steps: accumulator of the last step -> profiles, basin pick
+    accumulated = accumulator.double().cpu().numpy().reshape(L, slots)
+    profiles = [ar.AttentionProfile.from_accumulated("synthetic", l, args.prompts, accumulated[l]) for l in range(L)]
+    selected = ar.select_shallowest_basin_layer(profiles=profiles, min_edge_ratio=MIN_EDGE_RATIO)
+
+    # end to end through the public API (host prompts in, H2D + D2H inside the timed region)
+    scheduler = ProbeScheduler(engine)
+    settings = ar.LayerScanSettings(min_edge_ratio=MIN_EDGE_RATIO)
+    scheduler.find_shallowest_attention_layer(prompts, settings)  # warm-up
+    e2e_seconds = []
+    for _ in range(max(1, args.steps)):
+        barrier(world)
+        t0 = time.perf_counter()
+        scan = scheduler.find_shallowest_attention_layer(prompts, settings)
+        e2e_seconds.append(time.perf_counter() - t0)
+    e2e_step = max_over_ranks(statistics.median(e2e_seconds), world)
+    tokens_mine = sum(len(p.tokens) for p in mine)
+    h2d = 4 * (tokens_mine + 6 * len(mine) + 2 * slots * len(mine)) + 8 * sum(
+        (len(p.tokens) + 127) // 128 for p in mine)
+    d2h = 4 * L * slots + 4
+
+    peak, peak_kind = peaks()
+    flops = scan_flops(config, prompts)
+    achieved_tflops = flops / (ms_per_step / 1000.0) / 1e12
+    tensor_peak = peak.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
+    launches_per_batch = 2 + L * 6 + 1
+    gpu_launches = args.steps * launches_per_batch * len(prepared_batches(prepared, args.batch_tokens, mine))
+    result = {
+        "metric": METRIC,
+        "value": round(value, 3),
+        "unit": "prompts/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 3),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded random-init bf16 weights, seeded random token-id prompts)",
+        "config": {"workload": "layer scan, Qwen2.5-7B architecture, 400 prompts x (5 docs U[120,240] + 40-token "
+                               "question), min_edge_ratio 1.3", "global_batch": args.prompts,
+                   "seq_len": round(sum(len(p.tokens) for p in prompts) / len(prompts), 1),
+                   "parallelism": f"dp{world} (prompt shards, one NCCL all-reduce)",
+                   "batch_tokens": args.batch_tokens,
+                   "l2": "inputs larger than L2 (15.2 GB of weights streamed per batch); no flush"},
+        "selected_layer": selected,
+        "slot_order_selected": profiles[selected].position_order if selected >= 0 else None,
+        "e2e": {"value": round(args.prompts / e2e_step, 3), "unit": "prompts/s", "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h), "selected_layer": scan.selected_layer,
+                "api": "attnrank.scheduler.ProbeScheduler.find_shallowest_attention_layer"},
+        "roofline": {"bound": "tensor", "kernel": "whole scan step (cuBLASLt GEMMs + attention + mass)",
+                     "achieved": round(achieved_tflops, 1), "peak": tensor_peak, "unit": "TFLOP/s",
+                     "frac": round(achieved_tflops / tensor_peak, 4), "traffic": None,
+                     "peak_source": f"{peak_kind} bf16_tflops_sustained",
+                     "algorithmic_flops_per_step": flops},
+        "clocks": clocks,
+        "gpu_launches": gpu_launches,
+    }
+    if rank == 0 and not args.no_kernels:
+        result["kernels"] = kernel_rooflines(config, peak.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]),
+                                             peak.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+        result["kernels_peak_source"] = f"{peak_kind} hbm_gbs / bf16_tflops (burst)"
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(config, prompts[0])
+    del prepared
+    engine.close()
+    return result
+
+
+def prepared_batches(prepared, batch_tokens, prompts):
+    batches, tokens, count = [], 0, 0
+    for p in prompts:
+        t = len(p.tokens)
+        if count and (tokens + t > batch_tokens or count + 1 > 256):
+            batches.append(count)
+            tokens, count = 0, 0
+        tokens += t
+        count += 1
+    if count:
+        batches.append(count)
+    return batches
+
+
+def run_reference(args, rank, world, local_rank):
+    from attnrank import synthetic
+    from attnrank.scheduler import shard_by_length
+    from oracle import reference
+
+    if reference.load_or_none() is None:
+        return {"impl": "reference", "unavailable": "oracle/_ref/libattnrank_ref.so was not built (make -C oracle reference)"}
+    config = synthetic.qwen2_7b()
+    prompts = synthetic.prompts(args.reference_sample, config.vocab_size)
+    shard = shard_by_length([len(p.tokens) for p in prompts], world)[rank]
+    mine = [prompts[i] for i in shard]
+    model = reference.ReferenceModel(config, seed=0, max_sequence_length=2048, device=local_rank)
+    for _ in range(args.warmup):
+        model.scan(mine[: max(1, len(mine) // 8)], min_edge_ratio=MIN_EDGE_RATIO)
+    barrier(world)
+    seconds = []
+    result = None
+    for _ in range(args.steps):
+        result = model.scan(mine, min_edge_ratio=MIN_EDGE_RATIO)
+        seconds.append(result.seconds)
+    step_seconds = max_over_ranks(sum(seconds) / len(seconds), world)
+    value = args.reference_sample / step_seconds
+    cores = os.cpu_count() or 1
+    model.close()
+    return {
+        "metric": METRIC, "impl": "reference", "value": round(value, 3), "unit": "prompts/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_seconds * 1000, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16/fp32",
+        "data": "synthetic (seeded random-init weights, seeded random token-id prompts)",
+        "config": {"workload": "layer scan, Qwen2.5-7B architecture, reference CudaLlamaModel + "
+                               "AttentionLayerScanner (stock path), min_edge_ratio 1.3",
+                   "global_batch": args.reference_sample, "parallelism": f"{world} independent processes on "
+                   "prompt shards (the reference's multi-GPU practice)"},
+        "selected_layer": result.selected_layer if result else None,
+        "cpu_baseline": {"value": round(value, 3), "unit": "prompts/s", "cores": cores, "kind": "reference",
+                         "sample": f"first {args.reference_sample} of the 400 prompts per step; the reference's "
+                                   "path is CUDA, so it runs on the GPU (wall clock around its synchronous scan)"},
+        "e2e": {"value": round(value, 3), "unit": "prompts/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    args = parse_args()
+    rank, world, local_rank = init_distributed(args)
+    if args.impl == "reference":
+        result = run_reference(args, rank, world, local_rank)
+    else:
+        result = run_b200(args, rank, world, local_rank)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

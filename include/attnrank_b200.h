@@ -1,0 +1,233 @@
+/*
+ * attnrank_b200.h -- C ABI of the B200 attention-profiling library (libattnrank_b200.so).
+ *
+ * Drop-in boundary for the hot path of AttnRank (Syun1208/attention-rank): the layer-kernel
+ * library, the attention-capture forward pass, the profile accumulator and the basin pick.
+ * Plain pointers and sizes only. Every function returns AR_OK (0) or an AR_ERR_* code; the
+ * message of the last failure on the calling thread is available from ar_last_error().
+ *
+ * Citations are to files of the reference project (path:line).
+ */
+#ifndef ATTNRANK_B200_H
+#define ATTNRANK_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AR_OK 0
+#define AR_ERR_INVALID 1   /* bad argument (the reference throws attnrank::Error)              */
+#define AR_ERR_CUDA 2      /* CUDA runtime / cuBLASLt failure (kernels.cu:244-254)               */
+#define AR_ERR_DEVICE 3    /* a kernel reported a bad input (token id, position) or a wait timeout */
+#define AR_ERR_INTERNAL 4
+
+#define AR_DTYPE_F32 0
+#define AR_DTYPE_F16 1
+#define AR_DTYPE_BF16 2
+
+/* Message of the last error raised on this thread ("" if none). */
+const char* ar_last_error(void);
+/* Library version string. */
+const char* ar_version(void);
+
+/* ------------------------------------------------------------------------------------------
+ * Layer kernels. Device pointers, asynchronous on `stream` (a cudaStream_t, NULL = default).
+ * They replace the reference's kernels:: launchers (attnrank/src/cuda_runtime.hpp:115-144).
+ * Activations are bf16, residual stream fp32, norm weights and biases fp32.
+ * ------------------------------------------------------------------------------------------ */
+
+/* Replaces kernels::embedding_lookup (cuda_runtime.hpp:123-124, kernels.cu:424-430) fused with
+ * the first kernels::rms_norm (kernels.cu:432-439): residual[t] = table[ids[t]] (fp32),
+ * normed[t] = bf16(residual[t] * rsqrt(mean(residual[t]^2) + eps) * gamma).
+ * Out-of-range ids set *device_status (nullable) to 1 and produce a zero row. */
+int ar_embedding_rms_norm(const int32_t* token_ids, int token_count, const void* table_bf16, int vocab_size,
+                          int hidden_size, const float* gamma, float eps, float* residual, void* normed_bf16,
+                          int* device_status, void* stream);
+
+/* Replaces kernels::add_in_place + kernels::rms_norm (cuda_runtime.hpp:126-127, :135;
+ * model.cu:398 then :408-409): residual += delta; normed = bf16(rms(residual) * gamma). */
+int ar_rms_norm_residual(float* residual, const void* delta_bf16, const float* gamma, int token_count,
+                         int hidden_size, float eps, void* normed_bf16, void* stream);
+
+/* Replaces kernels::add_row_bias (cuda_runtime.hpp:137) + kernels::rotary_embedding
+ * (cuda_runtime.hpp:129, kernels.cu:85-115), in place on the fused q|k|v projection output
+ * [token_count, (Hq + 2 Hkv) * head_dim] bf16. bias (nullable) is fp32 [(Hq + 2 Hkv) * head_dim];
+ * positions are int32 per token; cos/sin tables come from ar_rope_table. */
+int ar_rotary_embedding(void* qkv_bf16, const float* bias, const int32_t* positions, int token_count,
+                        int query_heads, int kv_heads, int head_dim, const float* cos_table,
+                        const float* sin_table, int table_positions, int* device_status, void* stream);
+
+/* cos/sin of position * theta^(-2i/head_dim), fp32 [positions, head_dim / 2] each; the values of
+ * the reference's per-element computation (kernels.cu:95-98). */
+int ar_rope_table(float* cos_table, float* sin_table, int positions, int head_dim, float theta, void* stream);
+
+/* Replaces kernels::silu_multiply (cuda_runtime.hpp:131, kernels.cu:164-170):
+ * out[t, i] = silu(gate[t, i]) * up[t, i], bf16, rows addressed with the given strides (elements). */
+int ar_silu_multiply(const void* gate_bf16, const void* up_bf16, int64_t in_row_stride, void* out_bf16,
+                     int64_t out_row_stride, int token_count, int width, void* stream);
+
+/* Replaces the materialised attention of LlamaForwardPass::attend (model.cu:426-480:
+ * scatter_kv_cache, SGEMM Q K^T, softmax_causal_kernel, SGEMM P V) for packed prompts.
+ * qkv: bf16 [tokens, (Hq + 2 Hkv) * 128]; out: bf16 [tokens, Hq * 128];
+ * lse: fp32 [tokens, Hq], log2-domain log-sum-exp of the scaled scores of each row.
+ * prompt_offsets: int32 [prompt_count + 1] (device). head_dim must be 128. */
+int ar_causal_attention(const void* qkv_bf16, void* out_bf16, float* lse, const int32_t* prompt_offsets_host,
+                        const int32_t* prompt_offsets_device, int prompt_count, int query_heads, int kv_heads,
+                        int head_dim, int sliding_window, void* stream);
+
+/* Replaces kernels::reduce_document_attention (cuda_runtime.hpp:139, kernels.cu:202-236) over
+ * the output of softmax_causal_kernel, without any score matrix. For each prompt p and span s,
+ *   mass[p][s] = sum over heads h and query rows q of sum_{k in span s} softmax(q.k / sqrt(D))
+ * (each (h, q) term divided by the span length when normalize_by_length), i.e. the value the
+ * reference accumulates for one layer. mass_out[p][s] = mass[p][s] / (query_rows * Hq), the row
+ * of model.cu:613 before its unit-sum step (fp64 host, [prompt_count][span_count]).
+ * Host arrays (prompt-relative): query_spans [prompt_count][2], spans [prompt_count][span_count][2].
+ * lse is the output of ar_causal_attention on the same qkv. Allocates its scratch (metadata and
+ * per-CTA partial sums) with cudaMallocAsync on `stream` and synchronises the stream. */
+int ar_document_attention_mass(const void* qkv_bf16, int qkv_rows, const float* lse, const int32_t* prompt_offsets_host,
+                               int prompt_count, const int32_t* query_spans_host, const int32_t* spans_host,
+                               int span_count, int query_heads, int kv_heads, int head_dim, int sliding_window,
+                               int prefill_chunk_tokens, int normalize_by_length, double* mass_out, void* stream);
+
+/* Seeded synthetic weights: fills count bf16 values of tensor (layer, kind) with the generator
+ * documented in csrc/synthetic.h (Irwin-Hall, bf16 round-to-nearest-even). */
+int ar_synthetic_fill(void* dst_bf16, int64_t count, uint64_t seed, int layer, int kind, float standard_deviation,
+                      void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Engine: the IAttentionProvider role of CudaLlamaModel (include/attnrank/model.hpp:79-86,
+ * :144-165) plus the layer-scan loop of AttentionLayerScanner (attnrank/src/attnrank.cpp:350-375).
+ * ------------------------------------------------------------------------------------------ */
+
+typedef struct ar_engine ar_engine;
+
+/* LlamaConfig (include/attnrank/model.hpp:16-38) fields the path uses. */
+typedef struct {
+  int hidden_size;
+  int intermediate_size;
+  int num_hidden_layers;
+  int num_attention_heads;
+  int num_key_value_heads;
+  int vocab_size;
+  int max_position_embeddings;
+  float rms_norm_eps;
+  float rope_theta;
+  int sliding_window;    /* 0 = none (kernels.cu:125-126) */
+  int attention_bias;    /* 1 when q/k/v projections have biases (Qwen2) */
+} ar_llama_config;
+
+/* LlamaRuntimeOptions (model.hpp:138-142) plus the batching limits of this build. */
+typedef struct {
+  int device_index;          /* -1 = device 0 */
+  int max_sequence_length;   /* longest prompt */
+  int prefill_chunk_tokens;  /* the reference's chunk length; only bounds normalize_by_length divisors */
+  int max_batch_tokens;      /* packed tokens per forward (>= max_sequence_length) */
+  int max_batch_prompts;
+} ar_runtime_options;
+
+/* One probe prompt: StructuredPrompt (include/attnrank/prompt.hpp:12-17) as token ids + spans. */
+typedef struct {
+  const int32_t* tokens;
+  int token_count;
+  int query_begin;       /* TokenSpan query_span (core.hpp:54-60), half-open */
+  int query_end;
+  const int32_t* spans;  /* document_spans: [span_count][2] half-open */
+} ar_prompt;
+
+/* Creates the model on a device (CudaLlamaModel::CudaLlamaModel, model.hpp:146-149). */
+int ar_engine_create(const ar_llama_config* config, const ar_runtime_options* options, ar_engine** engine);
+void ar_engine_destroy(ar_engine* engine);
+
+/* Uploads one checkpoint tensor by its Hugging Face name (DeviceWeights, model.cu:113-174).
+ * Unknown names (lm_head, rotary buffers) are accepted and ignored. */
+int ar_engine_load_tensor(ar_engine* engine, const char* name, int dtype, const int64_t* shape, int rank,
+                          const void* host_data);
+
+/* Fills every weight with the seeded synthetic checkpoint (norm weights 1.0). */
+int ar_engine_init_synthetic(ar_engine* engine, uint64_t seed, float standard_deviation);
+
+/* CudaLlamaModel::measure_attention_by_layer (model.hpp:159-160, model.cu:593-617) for a batch
+ * of prompts with the same span count: rows_out (host, fp64) [prompt_count][layers][span_count],
+ * each row divided by query_rows * Hq and normalised to unit sum. layer_begin/layer_end follow
+ * AttentionLayerProbeRequest::resolve_layers (model.cpp:66-68). *layer_begin_out (nullable)
+ * receives the resolved first layer and *layer_count_out (nullable) the layer count. */
+int ar_engine_measure_attention_by_layer(ar_engine* engine, const ar_prompt* prompts, int prompt_count, int span_count,
+                                         int layer_begin, int layer_end, int normalize_by_length, double* rows_out,
+                                         int* layer_begin_out, int* layer_count_out);
+
+/* CudaLlamaModel::measure_attention (model.hpp:157-158, model.cu:567-591) for one prompt:
+ * the per-layer totals over [layer_begin, layer_end) divided by query_rows * Hq * layers,
+ * summed, and normalised to unit sum. attention_out: host fp64 [span_count]. */
+int ar_engine_measure_attention(ar_engine* engine, const ar_prompt* prompt, int span_count, int layer_begin,
+                                int layer_end, int normalize_by_length, double* attention_out);
+
+/* The device half of AttentionLayerScanner::scan (attnrank.cpp:350-375): probes all prompts in
+ * packed batches and adds, for every resolved layer, the sum of the prompts' unit-sum rows into
+ * device_accumulator (fp32, device, [layers][span_count]; NOT cleared). host_accumulator (nullable,
+ * fp64 [layers][span_count]) receives the accumulator's value after the scan. Returns after the
+ * device work is complete. */
+int ar_engine_scan(ar_engine* engine, const ar_prompt* prompts, int prompt_count, int span_count, int layer_begin,
+                   int layer_end, int normalize_by_length, float* device_accumulator, double* host_accumulator);
+
+/* Scan with HBM-resident inputs (no counterpart in the reference, whose scan re-uploads every
+ * prompt): prepare once -- validates, packs the prompts into batches and uploads all batch
+ * metadata -- then run as often as needed. Running enqueues the whole scan on the engine's stream
+ * and returns without waiting unless `synchronize` is set (then it waits and reports device
+ * errors). The accumulator is as in ar_engine_scan (not cleared). */
+typedef struct ar_prepared_scan ar_prepared_scan;
+int ar_engine_prepare_scan(ar_engine* engine, const ar_prompt* prompts, int prompt_count, int span_count,
+                           int layer_begin, int layer_end, int normalize_by_length, ar_prepared_scan** prepared);
+int ar_engine_run_prepared_scan(ar_engine* engine, const ar_prepared_scan* prepared, float* device_accumulator,
+                                int synchronize);
+void ar_prepared_scan_destroy(ar_prepared_scan* prepared);
+/* Bytes of batch metadata the prepared scan keeps on the device (tokens + spans + work lists). */
+int64_t ar_prepared_scan_bytes(const ar_prepared_scan* prepared);
+
+/* Waits for the engine's stream and reports any device-side error since the last probe. */
+int ar_engine_synchronize(ar_engine* engine);
+
+/* The engine's CUDA stream (cudaStream_t) and device index. */
+void* ar_engine_stream(ar_engine* engine);
+int ar_engine_device(ar_engine* engine);
+
+/* ------------------------------------------------------------------------------------------
+ * Profile accumulator and basin pick (host functions of attnrank/src/attnrank.cpp).
+ * ------------------------------------------------------------------------------------------ */
+
+typedef struct {
+  double first;
+  double last;
+  double interior_mean;
+  double edge_ratio;
+  int is_basin;
+} ar_basin_stats;
+
+/* AttentionProfile::from_accumulated (attnrank.cpp:151-169) + recompute_position_order (:171-177):
+ * attention_out[s] = accumulated[s] / sample_count, renormalised to unit sum; position_order_out
+ * is the stable descending argsort of attention_out. */
+int ar_profile_from_accumulated(const double* accumulated, int slots, int64_t sample_count, double* attention_out,
+                                int* position_order_out);
+
+/* AttentionProfile::recompute_position_order (attnrank.cpp:171-177). */
+int ar_position_order(const double* attention, int slots, int* position_order_out);
+
+/* basin_statistics (attnrank.cpp:236-255). */
+int ar_basin_statistics(const double* attention, int slots, double min_edge_ratio, ar_basin_stats* out);
+
+/* select_shallowest_basin_layer (attnrank.cpp:257-265) over profiles given as a
+ * [profile_count][slots] attention matrix and their layer indices. Writes the layer or -1. */
+int ar_select_shallowest_basin_layer(const double* attention, const int* layer_indices, int profile_count, int slots,
+                                     double min_edge_ratio, int* selected_out);
+
+/* resolve_position_order (attnrank.cpp:377-392): preferred slots first (deduplicated, in range),
+ * then the remaining slots ascending. order_out has `count` entries. */
+int ar_resolve_position_order(const int* preferred, int preferred_count, int count, int* order_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ATTNRANK_B200_H */

@@ -1,0 +1,155 @@
+"""End-to-end parity of the B200 engine (C ABI, via the Python mirror of the reference API).
+
+  * a small Llama/Qwen-shaped model against the fp32 CPU oracle (oracle/forward.py);
+  * the Qwen2.5-7B architecture against the reference's own CUDA build (oracle/_ref) and the oracle;
+  * the full layer scan against the reference's stock AttentionLayerScanner path.
+Tolerances: per-prompt / per-layer mass rows rel 1e-3 (fp32 attention mass); selected layer and
+slot order bit-exact.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+MASS_REL = 1e-3
+
+
+def small_config(bias=True, layers=3):
+    import attnrank as ar
+    return ar.LlamaConfig(hidden_size=512, intermediate_size=1024, num_hidden_layers=layers, num_attention_heads=4,
+                          num_key_value_heads=2, vocab_size=2000, max_position_embeddings=4096, rms_norm_eps=1e-6,
+                          rope_theta=1e6, attention_bias=bias)
+
+
+def oracle_shape(config):
+    from oracle import forward as F
+    return F.Shape(hidden=config.hidden_size, intermediate=config.intermediate_size, layers=config.num_hidden_layers,
+                   heads=config.num_attention_heads, kv_heads=config.num_key_value_heads, vocab=config.vocab_size,
+                   eps=config.rms_norm_eps, theta=config.rope_theta, window=config.sliding_window,
+                   bias=config.attention_bias)
+
+
+def oracle_prompt(prompt):
+    from oracle import forward as F
+    return F.Prompt(tokens=np.asarray(prompt.tokens), query_span=(prompt.query_span.begin, prompt.query_span.end),
+                    spans=[(s.begin, s.end) for s in prompt.document_spans])
+
+
+def small_prompts(count, vocab, seed=3):
+    from attnrank import synthetic
+    shape = synthetic.PromptShape(documents=5, document_min=20, document_max=90, question=12)
+    return synthetic.prompts(count, vocab, shape, seed=seed)
+
+
+def assert_rows_close(got, want, rel=MASS_REL):
+    got, want = np.asarray(got), np.asarray(want)
+    error = np.abs(got - want) / np.maximum(np.abs(want), 1e-12)
+    assert error.max() <= rel, f"max relative error {error.max():.3e} > {rel}"
+
+
+@pytest.mark.parametrize("bias", [True, False])
+def test_small_model_rows_match_oracle(cuda, bias):
+    import attnrank as ar
+    from oracle import forward as F
+    config = small_config(bias)
+    engine = ar.Engine.synthetic(config, seed=0)
+    prompts = small_prompts(4, config.vocab_size)
+    rows, first = engine.probe_rows(prompts)
+    assert first == 0 and rows.shape == (4, config.num_hidden_layers, 5)
+    oracle = F.OracleModel(oracle_shape(config), seed=0)
+    want, _ = oracle.probe([oracle_prompt(p) for p in prompts])
+    for p in range(len(prompts)):
+        np.testing.assert_allclose(rows[p].sum(axis=1), 1.0, rtol=1e-9)
+        assert_rows_close(rows[p], want[p])
+
+
+def test_small_model_layer_range_and_length_normalisation(cuda):
+    import attnrank as ar
+    from oracle import forward as F
+    config = small_config(True, layers=4)
+    engine = ar.Engine.synthetic(config, seed=5)
+    prompts = small_prompts(2, config.vocab_size, seed=9)
+    result = engine.measure_attention_by_layer(prompts[1], layer_begin=1, layer_end=3, normalize_by_length=True)
+    assert result.layer_begin == 1 and len(result.attention_by_layer) == 2
+    oracle = F.OracleModel(oracle_shape(config), seed=5)
+    want, _ = oracle.probe([oracle_prompt(prompts[1])], 1, 3, normalize_by_length=True)
+    assert_rows_close(result.attention_by_layer, want[0])
+    # measure_attention: the layer-averaged single profile of model.cu:567-591
+    got = engine.measure_attention(prompts[0], layer_span_begin=0, layer_span_end=4)
+    assert_rows_close(got, oracle.measure_attention(oracle_prompt(prompts[0]), 0, 4))
+
+
+def test_small_model_scan_matches_host_accumulation(cuda):
+    """The device accumulator equals the sum of the per-prompt rows (attnrank.cpp:350-362)."""
+    import attnrank as ar
+    config = small_config(True)
+    engine = ar.Engine.synthetic(config, seed=1)
+    prompts = small_prompts(9, config.vocab_size, seed=4)
+    rows, _ = engine.probe_rows(prompts)
+    accumulated = engine.scan(prompts)
+    np.testing.assert_allclose(accumulated, rows.sum(axis=0), rtol=1e-6)
+    scan = ar.find_shallowest_attention_layer(engine=engine, samples=prompts,
+                                              settings=ar.LayerScanSettings(min_edge_ratio=1.0))
+    for layer, profile in enumerate(scan.profiles):
+        mean = rows[:, layer, :].mean(axis=0)
+        np.testing.assert_allclose(profile.attention, mean / mean.sum(), rtol=1e-6)
+
+
+def test_engine_rejects_bad_requests(cuda):
+    import attnrank as ar
+    config = small_config(False, layers=2)
+    engine = ar.Engine.synthetic(config, seed=0)
+    good = small_prompts(1, config.vocab_size)[0]
+    with pytest.raises(ar.AttnRankError):
+        engine.measure_attention_by_layer(good, layer_begin=0, layer_end=5)
+    bad_token = ar.StructuredPrompt(tokens=[1, 2, config.vocab_size], document_spans=[(0, 1), (1, 2), (2, 3)],
+                                    query_span=(2, 3))
+    with pytest.raises(ar.AttnRankError, match="vocabulary"):
+        engine.measure_attention_by_layer(bad_token)
+    # the engine stays usable after a reported error
+    assert engine.measure_attention_by_layer(good).layer_begin == 0
+
+
+# ---- 7B architecture against the reference's CUDA build ------------------------------------
+@pytest.fixture(scope="module")
+def qwen_pair(cuda, reference_lib):
+    if reference_lib is None:
+        pytest.skip("oracle/_ref not built")
+    import attnrank as ar
+    from attnrank import synthetic
+    from oracle.reference import ReferenceModel
+    config = synthetic.qwen2_7b()
+    engine = ar.Engine.synthetic(config, seed=0, options=ar.RuntimeOptions(max_sequence_length=4096))
+    reference = ReferenceModel(config, seed=0, max_sequence_length=2048)
+    yield config, engine, reference
+    reference.close()
+    engine.close()
+
+
+@pytest.mark.slow
+def test_qwen7b_rows_match_reference(qwen_pair):
+    from attnrank import synthetic
+    config, engine, reference = qwen_pair
+    prompts = synthetic.prompts(3, config.vocab_size)
+    rows, _ = engine.probe_rows(prompts)
+    for p, prompt in enumerate(prompts):
+        want = reference.measure_attention_by_layer(prompt)
+        assert_rows_close(rows[p], want)
+
+
+@pytest.mark.slow
+def test_qwen7b_scan_matches_reference(qwen_pair):
+    import attnrank as ar
+    from attnrank import synthetic
+    config, engine, reference = qwen_pair
+    prompts = synthetic.prompts(48, config.vocab_size)
+    scan = ar.find_shallowest_attention_layer(engine=engine, samples=prompts,
+                                              settings=ar.LayerScanSettings(min_edge_ratio=1.3))
+    want = reference.scan(prompts, min_edge_ratio=1.3)
+    assert scan.selected_layer == want.selected_layer
+    for layer, profile in enumerate(scan.profiles):
+        assert profile.layer_index == int(want.layer_index[layer])
+        assert_rows_close(profile.attention, want.attention[layer])
+        assert list(profile.position_order) == [int(v) for v in want.position_order[layer]]
