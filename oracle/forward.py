@@ -245,12 +245,14 @@ def op_rms_norm_residual(residual: np.ndarray, delta: np.ndarray, gamma: np.ndar
 
 
 def op_rotary_bias(qkv: np.ndarray, bias: np.ndarray | None, positions: np.ndarray, heads: int, kv_heads: int,
-                   head_dim: int, theta: float) -> np.ndarray:
+                   head_dim: int, theta: float, tables: tuple[np.ndarray, np.ndarray] | None = None) -> np.ndarray:
+    """Bias + rotate-half RoPE on a fused q|k|v block. `tables` (cos, sin) [positions, D/2] may be
+    given to check the rotation arithmetic independently of how the tables were computed."""
     T = qkv.shape[0]
     x = torch.from_numpy(qkv.copy())
     if bias is not None:
         x = x + torch.from_numpy(bias)
-    cos_np, sin_np = rope_tables(int(positions.max()) + 1, head_dim, theta)
+    cos_np, sin_np = tables if tables is not None else rope_tables(int(positions.max()) + 1, head_dim, theta)
     cos = torch.from_numpy(cos_np)[positions]
     sin = torch.from_numpy(sin_np)[positions]
     rotated = (heads + kv_heads) * head_dim

@@ -156,11 +156,33 @@ def test_rotary_bias(cuda, heads, kv_heads, bias):
                                                 _stream()))
     torch.cuda.synchronize()
     assert int(status.item()) == 0
-    want = F.op_rotary_bias(qkv_exact, bias_np, positions, heads, kv_heads, D, theta)
+    # the rotation arithmetic, on the kernel's own cos/sin table
+    tables = (cos.cpu().numpy(), sin.cpu().numpy())
+    want = F.op_rotary_bias(qkv_exact, bias_np, positions, heads, kv_heads, D, theta, tables=tables)
     got = _to_np(qkv_d)
-    assert_bf16_close(got, want, floor=2e-5 * np.abs(want).max())
+    assert_bf16_close(got, want, floor=1e-6 * np.abs(want).max())
     if not bias:  # value heads untouched without a bias
         assert np.array_equal(got[:, (heads + kv_heads) * D:], qkv_exact[:, (heads + kv_heads) * D:])
+
+
+@pytest.mark.parametrize("theta", [1e4, 5e5, 1e6])
+def test_rope_table(cuda, theta):
+    """cos/sin(pos * theta^(-2i/D)) against fp64. The fp32 angle carries pos x (a few ulp of the
+    fp32 inverse frequency) of rounding, exactly as the reference's per-element powf/cosf/sinf
+    (kernels.cu:95-98), so the bound grows with the position."""
+    import torch
+    native = _lib()
+    D, positions = 128, 32768
+    cos = torch.empty((positions, D // 2), dtype=torch.float32, device=cuda)
+    sin = torch.empty_like(cos)
+    native.check(native.lib.ar_rope_table(_ptr(cos), _ptr(sin), positions, D, theta, _stream()))
+    torch.cuda.synchronize()
+    index = np.arange(D // 2, dtype=np.float64)
+    inverse = theta ** (-2.0 * index / D)
+    angle = np.arange(positions, dtype=np.float64)[:, None] * inverse[None, :]
+    bound = 1e-6 + np.arange(positions)[:, None] * inverse[None, :] * 2.0 ** -21  # ~4 ulp of inv_freq, times pos
+    assert np.all(np.abs(cos.cpu().numpy() - np.cos(angle)) <= bound)
+    assert np.all(np.abs(sin.cpu().numpy() - np.sin(angle)) <= bound)
 
 
 @pytest.mark.parametrize("tokens,width", [(1, 18944), (257, 18944), (64, 14336)])

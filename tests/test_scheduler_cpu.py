@@ -1,0 +1,126 @@
+"""Multi-rank probe scheduler on CPU (gloo, world_size 2) with a host-side fake engine.
+
+Checks the host logic of the N>1 path: length-balanced sharding, one all-reduce of the
+[layers x slots] accumulator, identical profiles / basin pick on every rank, equality with the
+single-process scan, and failure propagation (a rank that raises before the all-reduce makes
+the others fail with an error instead of hanging).
+"""
+from __future__ import annotations
+
+import multiprocessing as mp
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from attnrank.scheduler import ProbeScheduler, shard_by_length
+
+
+class FakeEngine:
+    """Deterministic stand-in for the device engine: each prompt contributes a unit-sum row per
+    layer that depends on its tokens and spans."""
+
+    accumulator_device = "cpu"
+    model_directory = "fake"
+
+    def __init__(self, layers=4, fail=False):
+        self.num_layers = layers
+        self.fail = fail
+
+    @staticmethod
+    def rows(prompt, layers):
+        lengths = np.array([s.end - s.begin for s in prompt.document_spans], dtype=np.float64)
+        out = []
+        for layer in range(layers):
+            weights = lengths * (1.0 + 0.1 * layer * np.cos(np.arange(len(lengths)) + prompt.tokens[0] % 7))
+            out.append(weights / weights.sum())
+        return np.array(out)
+
+    def scan(self, prompts, layer_begin, layer_end, normalize_by_length, accumulator=None):
+        if self.fail:
+            raise RuntimeError("injected rank failure")
+        end = self.num_layers if layer_end < 0 else layer_end
+        total = sum(self.rows(p, self.num_layers)[layer_begin:end] for p in prompts)
+        accumulator += __import__("torch").from_numpy(total.reshape(-1).astype(np.float32))
+        return total
+
+
+def _prompts():
+    from attnrank import synthetic
+    shape = synthetic.PromptShape(documents=5, document_min=10, document_max=60, question=8)
+    return synthetic.prompts(37, 1000, shape, seed=2)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, fail_rank, queue):
+    import datetime
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    sys.path[:0] = [str(root / "attention-rank_b200"), str(root)]
+    import torch.distributed as dist
+
+    import attnrank as ar
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+    try:
+        engine = FakeEngine(fail=(rank == fail_rank))
+        scan = ProbeScheduler(engine).find_shallowest_attention_layer(_prompts(), ar.LayerScanSettings(min_edge_ratio=0.9))
+        queue.put((rank, "ok", scan.selected_layer, [p.attention for p in scan.profiles],
+                   [p.position_order for p in scan.profiles]))
+    except Exception as error:  # noqa: BLE001 - reported to the parent
+        queue.put((rank, "error", type(error).__name__, str(error)[:200], None))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:  # noqa: BLE001
+            pass
+
+
+def _run(world, fail_rank=-1):
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, fail_rank, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [queue.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    return sorted(results, key=lambda r: r[0])
+
+
+def test_shard_by_length_balances_and_covers():
+    lengths = [900, 100, 500, 500, 300, 800, 50]
+    shards = shard_by_length(lengths, 3)
+    assert sorted(i for s in shards for i in s) == list(range(len(lengths)))
+    loads = [sum(lengths[i] for i in s) for s in shards]
+    assert max(loads) - min(loads) <= max(lengths)
+    assert shard_by_length(lengths, 1) == [list(range(len(lengths)))]
+
+
+def test_two_rank_scan_equals_single_process():
+    import attnrank as ar
+    single = ProbeScheduler(FakeEngine()).find_shallowest_attention_layer(_prompts(), ar.LayerScanSettings(min_edge_ratio=0.9))
+    results = _run(2)
+    assert all(r[1] == "ok" for r in results), results
+    for _, _, selected, attention, order in results:
+        assert selected == single.selected_layer
+        for layer, profile in enumerate(single.profiles):
+            np.testing.assert_allclose(attention[layer], profile.attention, rtol=1e-6)
+            assert order[layer] == profile.position_order
+
+
+def test_rank_failure_propagates_without_hanging():
+    results = _run(2, fail_rank=1)
+    assert results[1][1] == "error" and "injected" in results[1][3]
+    assert results[0][1] == "error"  # the surviving rank's all-reduce fails instead of hanging
