@@ -51,6 +51,9 @@ def parse_args():
     parser.add_argument("--batch-tokens", type=int, default=16384)
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-kernels", action="store_true", help="skip the per-kernel roofline timing")
+    parser.add_argument("--kernels-only", action="store_true",
+                        help="only the per-kernel roofline timing (about 3 GB of device memory; for ncu captures)")
+    parser.add_argument("--kernel-tokens", type=int, default=16384)
     return parser.parse_args()
 
 
@@ -462,7 +465,14 @@ def run_reference(args, rank, world, local_rank):
 def main():
     args = parse_args()
     rank, world, local_rank = init_distributed(args)
-    if args.impl == "reference":
+    if args.kernels_only:
+        from attnrank import synthetic
+        peak, kind = peaks()
+        result = {"kernels": kernel_rooflines(synthetic.qwen2_7b(), peak.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]),
+                                              peak.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]),
+                                              tokens=args.kernel_tokens),
+                  "kernels_peak_source": f"{kind} hbm_gbs / bf16_tflops (burst)", "tokens": args.kernel_tokens}
+    elif args.impl == "reference":
         result = run_reference(args, rank, world, local_rank)
     else:
         result = run_b200(args, rank, world, local_rank)
