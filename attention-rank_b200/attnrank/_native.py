@@ -88,6 +88,7 @@ SIGNATURES: dict[str, list] = {
     "ar_silu_multiply": [_P, _P, _I64, _P, _I64, _I, _I, _P],
     "ar_causal_attention": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P],
     "ar_document_attention_mass": [_P, _I, _P, _P, _I, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P],
+    "ar_document_attention_mass_noalloc": [_P, _I, _P, _P, _I, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P],
     "ar_synthetic_fill": [_P, _I64, _U64, _I, _I, _F, _P],
     "ar_engine_create": [ctypes.POINTER(LlamaConfigStruct), ctypes.POINTER(RuntimeOptionsStruct), ctypes.POINTER(_P)],
     "ar_engine_destroy": [_P],

@@ -91,6 +91,10 @@ struct StreamScratch {
 
 }  // namespace
 
+namespace arb {
+void set_last_error(const std::string& message) { g_last_error = message; }
+}  // namespace arb
+
 extern "C" {
 
 const char* ar_last_error(void) { return g_last_error.c_str(); }

@@ -92,6 +92,24 @@ int ar_document_attention_mass(const void* qkv_bf16, int qkv_rows, const float* 
                                int span_count, int query_heads, int kv_heads, int head_dim, int sliding_window,
                                int prefill_chunk_tokens, int normalize_by_length, double* mass_out, void* stream);
 
+/* The same computation as ar_document_attention_mass for callers that cannot let the library
+ * allocate device memory while they run (a process holding the whole GPU under a fixed memory
+ * budget, a latency-critical serving loop where an allocator call may block or synchronise, a
+ * host framework that owns every device allocation). No counterpart in the reference. Its scratch
+ * (metadata, per-CTA partials, rows, status) comes from one fixed 8 MiB device array that every
+ * GPU loading the library keeps until the process exits; it calls no cudaMalloc, cudaFree or
+ * other allocating routine. Batches that need more than 8 MiB of scratch are rejected with
+ * AR_ERR_INVALID. The array's device address is looked up once per device by the first call
+ * made on that device (make that call before any stream capture). Calls share the array: calls
+ * whose work overlaps on the GPU race, so issue them on one stream or wait in between. The
+ * stream is synchronised before return. */
+int ar_document_attention_mass_noalloc(const void* qkv_bf16, int qkv_rows, const float* lse,
+                                       const int32_t* prompt_offsets_host, int prompt_count,
+                                       const int32_t* query_spans_host, const int32_t* spans_host, int span_count,
+                                       int query_heads, int kv_heads, int head_dim, int sliding_window,
+                                       int prefill_chunk_tokens, int normalize_by_length, double* mass_out,
+                                       void* stream);
+
 /* Seeded synthetic weights: fills count bf16 values of tensor (layer, kind) with the generator
  * documented in csrc/synthetic.h (Irwin-Hall, bf16 round-to-nearest-even). */
 int ar_synthetic_fill(void* dst_bf16, int64_t count, uint64_t seed, int layer, int kind, float standard_deviation,
