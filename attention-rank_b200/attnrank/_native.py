@@ -18,6 +18,7 @@ AR_ERR_DEVICE = 3
 AR_ERR_INTERNAL = 4
 
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
+KERNEL_CLASS_COUNT = 12  # AR_KERNEL_CLASS_COUNT
 
 
 class AttnRankError(RuntimeError):
@@ -47,6 +48,8 @@ class RuntimeOptionsStruct(ctypes.Structure):
         ("prefill_chunk_tokens", ctypes.c_int),
         ("max_batch_tokens", ctypes.c_int),
         ("max_batch_prompts", ctypes.c_int),
+        ("activation_dtype", ctypes.c_int),
+        ("attention_kernel", ctypes.c_int),
     ]
 
 
@@ -81,15 +84,16 @@ _D = ctypes.c_double
 SIGNATURES: dict[str, list] = {
     "ar_last_error": [],
     "ar_version": [],
-    "ar_embedding_rms_norm": [_P, _I, _P, _I, _I, _P, _F, _P, _P, _P, _P],
-    "ar_rms_norm_residual": [_P, _P, _P, _I, _I, _F, _P, _P],
-    "ar_rotary_embedding": [_P, _P, _P, _I, _I, _I, _I, _P, _P, _I, _P, _P],
+    "ar_embedding_rms_norm": [_P, _I, _P, _I, _I, _P, _F, _P, _P, _P, _I, _P],
+    "ar_rms_norm_residual": [_P, _P, _P, _I, _I, _F, _P, _I, _P],
+    "ar_rotary_embedding": [_P, _P, _P, _I, _I, _I, _I, _P, _P, _I, _P, _I, _P],
     "ar_rope_table": [_P, _P, _I, _I, _F, _P],
-    "ar_silu_multiply": [_P, _P, _I64, _P, _I64, _I, _I, _P],
-    "ar_causal_attention": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P],
-    "ar_document_attention_mass": [_P, _I, _P, _P, _I, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P],
-    "ar_document_attention_mass_noalloc": [_P, _I, _P, _P, _I, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P],
-    "ar_synthetic_fill": [_P, _I64, _U64, _I, _I, _F, _P],
+    "ar_silu_multiply": [_P, _P, _I64, _P, _I64, _I, _I, _I, _P],
+    "ar_causal_attention": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P],
+    "ar_causal_attention_mma": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P],
+    "ar_document_attention_mass": [_P, _I, _P, _P, _I, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _I, _P],
+    "ar_document_attention_mass_noalloc": [_P, _I, _P, _P, _I, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _I, _P],
+    "ar_synthetic_fill": [_P, _I64, _U64, _I, _I, _F, _I, _P],
     "ar_engine_create": [ctypes.POINTER(LlamaConfigStruct), ctypes.POINTER(RuntimeOptionsStruct), ctypes.POINTER(_P)],
     "ar_engine_destroy": [_P],
     "ar_engine_load_tensor": [_P, ctypes.c_char_p, _I, _P, _I, _P],
@@ -102,6 +106,10 @@ SIGNATURES: dict[str, list] = {
     "ar_prepared_scan_destroy": [_P],
     "ar_prepared_scan_bytes": [_P],
     "ar_engine_synchronize": [_P],
+    "ar_engine_set_kernel_timing": [_P, _I],
+    "ar_engine_kernel_timing": [_P, _P, _P, _P],
+    "ar_kernel_class_name": [_I],
+    "ar_kernel_class_is_tensor": [_I],
     "ar_engine_stream": [_P],
     "ar_engine_device": [_P],
     "ar_profile_from_accumulated": [_P, _I, _I64, _P, _P],
@@ -116,6 +124,7 @@ _RESTYPES = {
     "ar_engine_destroy": None,
     "ar_prepared_scan_destroy": None,
     "ar_prepared_scan_bytes": ctypes.c_int64,
+    "ar_kernel_class_name": ctypes.c_char_p,
     "ar_engine_stream": ctypes.c_void_p,
     "ar_engine_device": ctypes.c_int,
 }

@@ -144,10 +144,25 @@ class RuntimeOptions:
     prefill_chunk_tokens: int = 512
     max_batch_tokens: int = 16384
     max_batch_prompts: int = 256
+    # Additive: the 16-bit type of weights, GEMM operands and activations ("fp16", the reference's
+    # GEMM operand type, or "bf16"), and the attention kernel ("tcgen05" or "mma").
+    activation_dtype: str = "fp16"
+    attention_kernel: str = "tcgen05"
 
     def to_struct(self) -> _native.RuntimeOptionsStruct:
+        dtypes = {"fp16": _native.DTYPE_F16, "bf16": _native.DTYPE_BF16}
+        kernels = {"tcgen05": 0, "mma": 1}
+        if self.activation_dtype not in dtypes:
+            raise AttnRankError(f"activation_dtype must be one of {sorted(dtypes)}")
+        if self.attention_kernel not in kernels:
+            raise AttnRankError(f"attention_kernel must be one of {sorted(kernels)}")
         return _native.RuntimeOptionsStruct(self.device_index, self.max_sequence_length, self.prefill_chunk_tokens,
-                                            self.max_batch_tokens, self.max_batch_prompts)
+                                            self.max_batch_tokens, self.max_batch_prompts,
+                                            dtypes[self.activation_dtype], kernels[self.attention_kernel])
+
+    @property
+    def dtype_code(self) -> int:
+        return {"fp16": _native.DTYPE_F16, "bf16": _native.DTYPE_BF16}[self.activation_dtype]
 
 
 @dataclass
@@ -523,6 +538,26 @@ class Engine:
     def synchronize(self) -> None:
         """Wait for the engine's stream; raises AttnRankError on a device-reported error."""
         check(lib.ar_engine_synchronize(self._handle))
+
+    def set_kernel_timing(self, enabled: bool) -> None:
+        """Additive: bracket every engine launch with CUDA events (see kernel_timing)."""
+        check(lib.ar_engine_set_kernel_timing(self._handle, 1 if enabled else 0))
+
+    def kernel_timing(self) -> dict[str, dict]:
+        """Per kernel class since the last call: {name: {ms, work, launches, tensor}} (then cleared).
+
+        `work` is algorithmic FLOPs for tensor classes and HBM bytes for the others."""
+        count = _native.KERNEL_CLASS_COUNT
+        ms = (ctypes.c_double * count)()
+        work = (ctypes.c_double * count)()
+        launches = (ctypes.c_int64 * count)()
+        check(lib.ar_engine_kernel_timing(self._handle, ms, work, launches))
+        result = {}
+        for k in range(count):
+            name = lib.ar_kernel_class_name(k).decode()
+            result[name] = {"ms": ms[k], "work": work[k], "launches": int(launches[k]),
+                            "tensor": bool(lib.ar_kernel_class_is_tensor(k))}
+        return result
 
     def prepare_scan(self, prompts: Sequence[StructuredPrompt], layer_begin: int = 0, layer_end: int = -1,
                      normalize_by_length: bool = False) -> "PreparedScan":

@@ -21,6 +21,8 @@ class EngineSettings:
     system_prompt: str = ""
     max_batch_tokens: int = DEFAULT_MAX_BATCH_TOKENS      # additive: packed tokens per forward
     max_batch_prompts: int = DEFAULT_MAX_BATCH_PROMPTS    # additive
+    activation_dtype: str = "fp16"                        # additive: "fp16" (reference GEMM type) or "bf16"
+    attention_kernel: str = "tcgen05"                     # additive: "tcgen05" or "mma"
 
 
 @dataclass(frozen=True, slots=True)

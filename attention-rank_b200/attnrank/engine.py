@@ -39,7 +39,8 @@ def is_model_directory(*, path: Path) -> bool:
 def runtime_options(settings: EngineSettings) -> RuntimeOptions:
     return RuntimeOptions(device_index=settings.device, max_sequence_length=settings.max_sequence,
                           prefill_chunk_tokens=settings.chunk, max_batch_tokens=settings.max_batch_tokens,
-                          max_batch_prompts=settings.max_batch_prompts)
+                          max_batch_prompts=settings.max_batch_prompts, activation_dtype=settings.activation_dtype,
+                          attention_kernel=settings.attention_kernel)
 
 
 def load_model(*, model_dir: Path, settings: EngineSettings = EngineSettings()) -> Engine:

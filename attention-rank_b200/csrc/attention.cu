@@ -9,11 +9,12 @@
 // attention-mass kernel (mass.cu) uses it to turn raw scores into exact softmax probabilities
 // in a single pass, so mass capture needs no second softmax.
 //
-// Tensor-core path: mma.sync m16n8k16 bf16 with fp32 accumulation (8 warps x 16 query rows,
+// Tensor-core path: mma.sync m16n8k16 (fp16 or bf16 operands) with fp32 accumulation (8 warps x 16 query rows,
 // 64-key tiles double-buffered with cp.async, XOR-swizzled shared memory for conflict-free
 // ldmatrix). Masking follows softmax_causal_kernel (kernels.cu:117-162): key k is visible to
 // query q iff k <= q, k < prompt length, and k > q - sliding_window when a window is set.
 #include <cmath>
+#include <type_traits>
 
 #include "common.cuh"
 #include "layer_kernels.h"
@@ -29,13 +30,13 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kChunksPerRow = kHeadDim / 8;   // 16-byte chunks per row
 constexpr int kQElems = kBlockM * kHeadDim;
 constexpr int kKvElems = kBlockN * kHeadDim;
-constexpr size_t kSmemBytes = (kQElems + 4 * kKvElems) * sizeof(__nv_bfloat16);  // 96 KB
+constexpr size_t kSmemBytes = (kQElems + 4 * kKvElems) * 2;  // 96 KB of 16-bit values
 
 __device__ __forceinline__ uint32_t smem_u32(const void* pointer) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(pointer));
 }
 
-// element offset of (row, col) in a [rows][128] bf16 tile with 16-byte chunks XOR-swizzled by row
+// element offset of (row, col) in a [rows][128] 16-bit tile with 16-byte chunks XOR-swizzled by row
 __device__ __forceinline__ int swizzle(int row, int col) {
   return row * kHeadDim + ((((col >> 3) ^ (row & 7))) << 3) + (col & 7);
 }
@@ -62,28 +63,34 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t address, uint32_t& r0
                : "r"(address));
 }
 
+template <typename T>
 __device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};\n"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  if constexpr (std::is_same_v<T, __half>) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
 }
 
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<const uint32_t*>(&v);
-}
-
+template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
-    causal_attention_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out,
+    causal_attention_kernel(const T* __restrict__ qkv, T* __restrict__ out,
                             float* __restrict__ lse, const int32_t* __restrict__ prompt_offsets,
                             const int32_t* __restrict__ tiles, int query_heads, int kv_heads,
                             int sliding_window) {
-  extern __shared__ __align__(128) __nv_bfloat16 smem[];
-  __nv_bfloat16* q_smem = smem;
-  __nv_bfloat16* k_smem = smem + kQElems;                 // [2][64][128]
-  __nv_bfloat16* v_smem = smem + kQElems + 2 * kKvElems;  // [2][64][128]
+  extern __shared__ __align__(128) uint8_t smem_bytes[];
+  T* smem = reinterpret_cast<T*>(smem_bytes);
+  T* q_smem = smem;
+  T* k_smem = smem + kQElems;                 // [2][64][128]
+  T* v_smem = smem + kQElems + 2 * kKvElems;  // [2][64][128]
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -98,10 +105,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int prompt_begin = prompt_offsets[prompt];
   const int length = prompt_offsets[prompt + 1] - prompt_begin;
   const int q0 = query_tile * kBlockM;
-  const __nv_bfloat16* base = qkv + static_cast<size_t>(prompt_begin) * row_width;
-  const __nv_bfloat16* q_base = base + head * kHeadDim;
-  const __nv_bfloat16* k_base = base + (query_heads + kv_head) * kHeadDim;
-  const __nv_bfloat16* v_base = base + (query_heads + kv_heads + kv_head) * kHeadDim;
+  const T* base = qkv + static_cast<size_t>(prompt_begin) * row_width;
+  const T* q_base = base + head * kHeadDim;
+  const T* k_base = base + (query_heads + kv_head) * kHeadDim;
+  const T* v_base = base + (query_heads + kv_heads + kv_head) * kHeadDim;
 
   // ---- query tile -> shared (rows past the prompt are zero-filled)
 #pragma unroll
@@ -110,7 +117,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = id / kChunksPerRow;
     const int chunk = id % kChunksPerRow;
     const bool valid = q0 + row < length;
-    const __nv_bfloat16* src = valid ? q_base + static_cast<size_t>(q0 + row) * row_width + chunk * 8 : qkv;
+    const T* src = valid ? q_base + static_cast<size_t>(q0 + row) * row_width + chunk * 8 : qkv;
     cp_async16(smem_u32(q_smem + swizzle(row, chunk * 8)), src, valid ? 16 : 0);
   }
   cp_async_commit();
@@ -171,8 +178,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncthreads();
 
-    const __nv_bfloat16* kt = k_smem + stage * kKvElems;
-    const __nv_bfloat16* vt = v_smem + stage * kKvElems;
+    const T* kt = k_smem + stage * kKvElems;
+    const T* vt = v_smem + stage * kKvElems;
     float s[8][4];
 #pragma unroll
     for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.0f;
@@ -184,8 +191,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int col = kk * 16 + ((lane >> 3) & 1) * 8;
         uint32_t b0, b1, b2, b3;
         ldmatrix_x4(smem_u32(kt + swizzle(key_row, col)), b0, b1, b2, b3);
-        mma_16816(s[2 * np], qa[kk], b0, b1);
-        mma_16816(s[2 * np + 1], qa[kk], b2, b3);
+        mma_16816<T>(s[2 * np], qa[kk], b0, b1);
+        mma_16816<T>(s[2 * np + 1], qa[kk], b2, b3);
       }
     }
 
@@ -240,18 +247,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int kk2 = 0; kk2 < 4; ++kk2) {
       uint32_t pa[4];
-      pa[0] = pack_bf16x2(s[2 * kk2][0], s[2 * kk2][1]);
-      pa[1] = pack_bf16x2(s[2 * kk2][2], s[2 * kk2][3]);
-      pa[2] = pack_bf16x2(s[2 * kk2 + 1][0], s[2 * kk2 + 1][1]);
-      pa[3] = pack_bf16x2(s[2 * kk2 + 1][2], s[2 * kk2 + 1][3]);
+      pa[0] = pack2<T>(s[2 * kk2][0], s[2 * kk2][1]);
+      pa[1] = pack2<T>(s[2 * kk2][2], s[2 * kk2][3]);
+      pa[2] = pack2<T>(s[2 * kk2 + 1][0], s[2 * kk2 + 1][1]);
+      pa[3] = pack2<T>(s[2 * kk2 + 1][2], s[2 * kk2 + 1][3]);
       const int key_row = kk2 * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
 #pragma unroll
       for (int dp = 0; dp < 8; ++dp) {
         const int col = dp * 16 + (lane >> 4) * 8;
         uint32_t b0, b1, b2, b3;
         ldmatrix_x4_trans(smem_u32(vt + swizzle(key_row, col)), b0, b1, b2, b3);
-        mma_16816(o[2 * dp], pa, b0, b1);
-        mma_16816(o[2 * dp + 1], pa, b2, b3);
+        mma_16816<T>(o[2 * dp], pa, b0, b1);
+        mma_16816<T>(o[2 * dp + 1], pa, b2, b3);
       }
     }
     __syncthreads();  // the stage is refilled by the next iteration's prefetch
@@ -265,10 +272,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const float inv_hi = l_hi > 0.0f ? 1.0f / l_hi : 0.0f;
 
   if (row_lo < length) {
-    __nv_bfloat16* dst = out + static_cast<size_t>(prompt_begin + row_lo) * out_width + head * kHeadDim;
+    T* dst = out + static_cast<size_t>(prompt_begin + row_lo) * out_width + head * kHeadDim;
 #pragma unroll
     for (int dt = 0; dt < 16; ++dt) {
-      *reinterpret_cast<uint32_t*>(dst + dt * 8 + 2 * t) = pack_bf16x2(o[dt][0] * inv_lo, o[dt][1] * inv_lo);
+      *reinterpret_cast<uint32_t*>(dst + dt * 8 + 2 * t) = pack2<T>(o[dt][0] * inv_lo, o[dt][1] * inv_lo);
     }
     if (t == 0) {
       lse[static_cast<size_t>(prompt_begin + row_lo) * query_heads + head] =
@@ -276,10 +283,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   if (row_hi < length) {
-    __nv_bfloat16* dst = out + static_cast<size_t>(prompt_begin + row_hi) * out_width + head * kHeadDim;
+    T* dst = out + static_cast<size_t>(prompt_begin + row_hi) * out_width + head * kHeadDim;
 #pragma unroll
     for (int dt = 0; dt < 16; ++dt) {
-      *reinterpret_cast<uint32_t*>(dst + dt * 8 + 2 * t) = pack_bf16x2(o[dt][2] * inv_hi, o[dt][3] * inv_hi);
+      *reinterpret_cast<uint32_t*>(dst + dt * 8 + 2 * t) = pack2<T>(o[dt][2] * inv_hi, o[dt][3] * inv_hi);
     }
     if (t == 0) {
       lse[static_cast<size_t>(prompt_begin + row_hi) * query_heads + head] =
@@ -290,25 +297,32 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace
 
-cudaError_t launch_causal_attention(const AttentionArgs& args, cudaStream_t stream) {
-  if (args.tile_count <= 0) return cudaSuccess;
-  if (args.head_dim != kHeadDim || args.kv_heads <= 0 || args.query_heads % args.kv_heads != 0) {
-    return cudaErrorInvalidValue;
-  }
+template <typename T>
+cudaError_t launch_typed(const AttentionArgs& args, cudaStream_t stream) {
   int device = 0;
   cudaGetDevice(&device);
   static uint64_t configured_devices = 0;  // the shared-memory opt-in is a per-device attribute
   if (device >= 64 || !(configured_devices & (1ull << device))) {
     const cudaError_t status = cudaFuncSetAttribute(
-        causal_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
+        causal_attention_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
     if (status != cudaSuccess) return status;
     if (device < 64) configured_devices |= 1ull << device;
   }
   const dim3 grid(args.tile_count, args.query_heads);
-  causal_attention_kernel<<<grid, kThreads, kSmemBytes, stream>>>(
-      static_cast<const __nv_bfloat16*>(args.qkv), static_cast<__nv_bfloat16*>(args.out), args.lse,
-      args.prompt_offsets, args.tiles, args.query_heads, args.kv_heads, args.sliding_window);
+  causal_attention_kernel<T><<<grid, kThreads, kSmemBytes, stream>>>(
+      static_cast<const T*>(args.qkv), static_cast<T*>(args.out), args.lse, args.prompt_offsets, args.tiles,
+      args.query_heads, args.kv_heads, args.sliding_window);
   return cudaGetLastError();
+}
+
+cudaError_t launch_causal_attention(const AttentionArgs& args, cudaStream_t stream) {
+  if (args.tile_count <= 0) return cudaSuccess;
+  if (args.head_dim != kHeadDim || args.kv_heads <= 0 || args.query_heads % args.kv_heads != 0) {
+    return cudaErrorInvalidValue;
+  }
+  if (args.dtype == kActFp16) return launch_typed<__half>(args, stream);
+  if (args.dtype == kActBf16) return launch_typed<__nv_bfloat16>(args, stream);
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace arb

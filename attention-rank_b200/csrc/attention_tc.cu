@@ -1,0 +1,541 @@
+// Causal GQA prefill attention on tcgen05 / TMEM (sm_100a), packed variable-length prompts, with
+// per-row log-sum-exp for the attention-mass kernel.
+//
+// Same contract as the mma.sync kernel in attention.cu (which it replaces on the engine path):
+// reference semantics of LlamaForwardPass::attend (attnrank/src/model.cu:426-480) and
+// softmax_causal_kernel (attnrank/src/kernels.cu:117-162); key k is visible to query q iff
+// k <= q, k < prompt length and, with a sliding window, k > q - window.
+//
+// One CTA = one (prompt, 128-row query tile, query head). 160 threads:
+//   warps 0-3 (softmax): thread r owns query row r = TMEM lane r. For every 128-key tile it
+//     reads S = Q K^T (fp32) from TMEM, applies the mask, keeps the row's running max / sum,
+//     writes P (16-bit) back into the same TMEM columns, and signals the control warp.
+//   warp 4 (control): allocates TMEM, lane 0 issues every TMA load (no multicast) and every
+//     tcgen05.mma, and commits MMA completion to mbarriers.
+// Pipeline per key tile j (K/V double-buffered in shared memory, S double-buffered in TMEM):
+//     S_{j+1} = Q K_{j+1}^T  overlaps the softmax of tile j;
+//     O += P_j V_j  (A = P from TMEM, B = V from shared memory, MN-major) after the softmax.
+// Rescaling: exponents use a reference max m_ref that moves only when the row max exceeds it by
+// more than 8 (log2 units), so p <= 2^8 and the O accumulator in TMEM is rescaled rarely.
+// Every mbarrier wait is bounded (time and polls); on expiry the kernel records
+// kStatusWaitTimeout, waits (bounded) for its own MMAs and copies, frees TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <mutex>
+#include <type_traits>
+
+#include "common.cuh"
+#include "layer_kernels.h"
+
+namespace arb {
+namespace {
+
+constexpr int kHeadDim = 128;
+constexpr int kTile = 128;                         // query rows per CTA and keys per tile
+constexpr int kSoftmaxThreads = 128;
+constexpr int kThreads = kSoftmaxThreads + 32;     // + control warp
+constexpr uint32_t kTmemColumns = 512;             // S0 [0,128) S1 [128,256) O [256,384)
+constexpr uint32_t kTmemO = 256;
+constexpr uint32_t kHalfBytes = 128 * 128;         // 128 rows x 64 16-bit values (one 128B-swizzled half)
+constexpr uint32_t kTileBytes = 2 * kHalfBytes;    // 128 rows x 128 values
+constexpr uint32_t kSpinLimit = 1u << 26;          // hard backstop on polls per wait
+constexpr uint64_t kWaitLimitNs = 500ull * 1000 * 1000;  // a wait gives up after 0.5 s
+constexpr float kRescaleThreshold = 8.0f;          // log2 units
+
+// shared memory (1024-byte aligned): Q | K stage 0,1 | V stage 0,1 | control
+constexpr uint32_t kQOffset = 0;
+constexpr uint32_t kKOffset = kTileBytes;
+constexpr uint32_t kVOffset = 3 * kTileBytes;
+constexpr uint32_t kControlOffset = 5 * kTileBytes;
+
+struct __align__(8) Control {
+  uint64_t q_bar;
+  uint64_t kv_bar[2];
+  uint64_t s_bar[2];
+  uint64_t o_bar;
+  uint64_t p_bar[2];
+  uint64_t done_bar;  // every MMA of the CTA completed (one commit after the last P.V)
+  uint32_t tmem_base;
+  volatile int abort;
+};
+constexpr size_t kSmemBytes = kControlOffset + sizeof(Control) + 1024;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* pointer) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(pointer));
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait for the completion of phase `phase` (parity); gives up after kWaitLimitNs (or
+// kSpinLimit polls), or earlier once *abort is set by another thread of the CTA. Every caller
+// waits on a barrier at most one phase ahead of the last phase it saw complete, so the parity
+// is unambiguous.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase, const volatile int* abort = nullptr) {
+  uint64_t start = 0;
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(phase)
+        : "memory");
+    if (done) return true;
+    if ((i & 1023) == 1023) {
+      if (abort != nullptr && *abort) return false;
+      const uint64_t now = global_ns();
+      if (start == 0) {
+        start = now;
+      } else if (now - start > kWaitLimitNs) {
+        return false;
+      }
+    }
+  }
+  return false;
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// K-major 128B-swizzled operand: 128-byte rows, 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t desc_k_major(uint32_t address) {
+  return static_cast<uint64_t>((address >> 4) & 0x3FFFu) | (static_cast<uint64_t>(1) << 16) |
+         (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) | (static_cast<uint64_t>(2) << 61);
+}
+// MN-major 128B-swizzled operand (V as B of P.V): each 128-byte row holds 64 consecutive N (head
+// dim) values of one K (key); 8 rows form a 1024-byte atom; the two 64-wide N halves are 16 KB
+// apart (leading byte offset), consecutive 8-key groups 1024 bytes apart (stride byte offset).
+__device__ __forceinline__ uint64_t desc_mn_major(uint32_t address) {
+  return static_cast<uint64_t>((address >> 4) & 0x3FFFu) | (static_cast<uint64_t>(kHalfBytes >> 4) << 16) |
+         (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) | (static_cast<uint64_t>(2) << 61);
+}
+
+// kind::f16 instruction descriptor, fp32 accumulator, M = N = 128; format 0 = fp16, 1 = bf16
+// (A and B always of the same format); A K-major, B K-major or MN-major.
+constexpr uint32_t idesc(uint32_t format, bool b_mn_major) {
+  return (1u << 4) | (format << 7) | (format << 10) | (b_mn_major ? (1u << 16) : 0u) | ((128u >> 3) << 17) |
+         ((128u >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+      ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+}
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t id, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+      ::"r"(d), "r"(a_tmem), "l"(b), "r"(id), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t address, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(address));
+}
+__device__ __forceinline__ void tmem_st32(uint32_t address, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+      ::"r"(address), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+        "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+        "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void softmax_barrier() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+struct Args {
+  void* out;
+  float* lse;
+  const int32_t* prompt_offsets;
+  const int32_t* tiles;
+  int query_heads;
+  int kv_heads;
+  int sliding_window;
+  uint32_t idesc_s;
+  uint32_t idesc_pv;
+  int* status;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+    attention_tc_kernel(const __grid_constant__ CUtensorMap map, const Args args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Control& ctl = *reinterpret_cast<Control*>(smem + kControlOffset);
+  const uint32_t q_smem = smem_u32(smem + kQOffset);
+  const uint32_t k_smem = smem_u32(smem + kKOffset);
+  const uint32_t v_smem = smem_u32(smem + kVOffset);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int prompt = args.tiles[2 * blockIdx.x];
+  const int query_tile = args.tiles[2 * blockIdx.x + 1];
+  const int head = blockIdx.y;
+  const int group = args.query_heads / args.kv_heads;
+  const int kv_head = head / group;
+  const int prompt_begin = args.prompt_offsets[prompt];
+  const int length = args.prompt_offsets[prompt + 1] - prompt_begin;
+  const int q0 = query_tile * kTile;
+  const int last_query = min(q0 + kTile, length) - 1;
+  const int first_key = args.sliding_window > 0 ? max(0, q0 - args.sliding_window + 1) : 0;
+  const int tile_begin = first_key / kTile;
+  const int tile_end = last_query / kTile + 1;
+  const int tiles = tile_end - tile_begin;
+
+  if (tid == 0) {
+    mbar_init(smem_u32(&ctl.q_bar), 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&ctl.kv_bar[i]), 1);
+      mbar_init(smem_u32(&ctl.s_bar[i]), 1);
+      mbar_init(smem_u32(&ctl.p_bar[i]), kSoftmaxThreads);
+    }
+    mbar_init(smem_u32(&ctl.o_bar), 1);
+    mbar_init(smem_u32(&ctl.done_bar), 1);
+    // a CTA of a launch that already reported an error does no work (bounds a failing launch to
+    // about one wave of timed-out CTAs); read once here so that the whole CTA agrees
+    ctl.abort = (args.status != nullptr && *reinterpret_cast<volatile int*>(args.status) != 0) ? 1 : 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 4) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&ctl.tmem_base)),
+                 "r"(kTmemColumns));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = ctl.tmem_base;
+  const uint32_t q_bar = smem_u32(&ctl.q_bar);
+  const uint32_t o_bar = smem_u32(&ctl.o_bar);
+  const uint32_t done_bar = smem_u32(&ctl.done_bar);
+  const bool skip = ctl.abort != 0;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------------ control warp (lane 0)
+    if (lane == 0 && tiles > 0 && !skip) {
+      const int q_x = head * kHeadDim;
+      const int k_x = (args.query_heads + kv_head) * kHeadDim;
+      const int v_x = (args.query_heads + args.kv_heads + kv_head) * kHeadDim;
+      // last load issued on each K/V stage (tile index, -1 = none): an aborted CTA waits for it
+      // before its shared memory is released; MMAs are drained through done_bar
+      int last_kv[2] = {-1, -1};
+      auto load_kv = [&](int j) {
+        const int stage = j & 1;
+        last_kv[stage] = j;
+        const int y = prompt_begin + (tile_begin + j) * kTile;
+        const uint32_t bar = smem_u32(&ctl.kv_bar[stage]);
+        mbar_expect_tx(bar, 2 * kTileBytes);
+        tma_load_2d(k_smem + stage * kTileBytes, &map, k_x, y, bar);
+        tma_load_2d(k_smem + stage * kTileBytes + kHalfBytes, &map, k_x + 64, y, bar);
+        tma_load_2d(v_smem + stage * kTileBytes, &map, v_x, y, bar);
+        tma_load_2d(v_smem + stage * kTileBytes + kHalfBytes, &map, v_x + 64, y, bar);
+      };
+      auto issue_s = [&](int j) {
+        const int stage = j & 1;
+        fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+          const uint32_t offset = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+          mma_ss(tmem + stage * 128, desc_k_major(q_smem + offset), desc_k_major(k_smem + stage * kTileBytes + offset),
+                 args.idesc_s, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(smem_u32(&ctl.s_bar[stage]));
+      };
+      auto issue_pv = [&](int j) {
+        const int stage = j & 1;
+        fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk) {  // 16 keys per MMA: 8 packed TMEM columns of P
+          mma_ts(tmem + kTmemO, tmem + stage * 128 + kk * 8, desc_mn_major(v_smem + stage * kTileBytes + kk * 2048),
+                 args.idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(o_bar);
+      };
+      mbar_expect_tx(q_bar, kTileBytes);
+      tma_load_2d(q_smem, &map, q_x, prompt_begin + q0, q_bar);
+      tma_load_2d(q_smem + kHalfBytes, &map, q_x + 64, prompt_begin + q0, q_bar);
+      load_kv(0);
+      if (tiles > 1) load_kv(1);
+      bool ok = mbar_wait(q_bar, 0) && mbar_wait(smem_u32(&ctl.kv_bar[0]), 0);
+      if (ok) issue_s(0);
+      for (int j = 0; ok && j < tiles; ++j) {
+        if (j + 1 < tiles) {
+          // S_{j+1} needs K_{j+1} and a free S buffer: PV_{j-1} read P_{j-1} from it
+          ok = mbar_wait(smem_u32(&ctl.kv_bar[(j + 1) & 1]), ((j + 1) >> 1) & 1) &&
+               (j == 0 || mbar_wait(o_bar, (j - 1) & 1));
+          if (!ok) break;
+          issue_s(j + 1);
+        }
+        ok = mbar_wait(smem_u32(&ctl.p_bar[j & 1]), (j >> 1) & 1, &ctl.abort);  // softmax wrote P_j
+        if (!ok) break;
+        issue_pv(j);
+        if (j + 2 < tiles) {
+          ok = mbar_wait(o_bar, j & 1);  // PV_j done: K_j and V_j buffers are free
+          if (!ok) break;
+          load_kv(j + 2);
+        }
+      }
+      if (!ok) {
+        report_status(args.status, kStatusWaitTimeout);
+        ctl.abort = 1;
+        __threadfence_block();
+      }
+      // done_bar tracks every MMA this thread issued; TMEM and shared memory are released only
+      // after it completes (and, on abort, after the last load of each stage has landed)
+      mma_commit(done_bar);
+      mbar_wait(done_bar, 0);
+      if (!ok) {
+        mbar_wait(q_bar, 0);
+        for (int s = 0; s < 2; ++s) {
+          if (last_kv[s] >= 0) mbar_wait(smem_u32(&ctl.kv_bar[s]), (last_kv[s] >> 1) & 1);
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax warps
+    const int row = tid;                       // TMEM lane
+    const int query = q0 + row;                // prompt-relative
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(kHeadDim));
+    float m_ref = -INFINITY;
+    float l = 0.0f;
+    bool ok = tiles > 0 && !skip;
+    for (int j = 0; ok && j < tiles; ++j) {
+      const int stage = j & 1;
+      if (!mbar_wait(smem_u32(&ctl.s_bar[stage]), (j >> 1) & 1, &ctl.abort) || ctl.abort) {
+        ok = false;
+        break;
+      }
+      fence_after();
+      const int k0 = (tile_begin + j) * kTile;
+      float x[kTile];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t raw[32];
+        tmem_ld32(tmem + lane_base + stage * 128 + c * 32, raw);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(raw[i]) * scale_log2;
+      }
+      const bool diagonal = k0 + kTile - 1 > q0 || k0 + kTile > length || args.sliding_window > 0;
+      float m_tile = -INFINITY;
+      if (diagonal) {
+        const int key_min = args.sliding_window > 0 ? query - args.sliding_window + 1 : 0;
+        const int key_max = min(query, length - 1);
+#pragma unroll
+        for (int i = 0; i < kTile; ++i) {
+          const int key = k0 + i;
+          if (key < key_min || key > key_max) x[i] = -INFINITY;
+          m_tile = fmaxf(m_tile, x[i]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < kTile; ++i) m_tile = fmaxf(m_tile, x[i]);
+      }
+      if (m_tile > m_ref + kRescaleThreshold || (m_ref == -INFINITY && m_tile != -INFINITY)) {
+        if (j > 0 && m_ref != -INFINITY) {
+          // O (accumulated through PV_{j-1}) and l are rescaled to the new reference; PV_{j-2}
+          // completed before S_j was issued, so o_bar is at most one phase behind here
+          if (!mbar_wait(o_bar, (j - 1) & 1, &ctl.abort)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          const float factor = exp2f(m_ref - m_tile);
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t raw[32];
+            tmem_ld32(tmem + lane_base + kTmemO + c * 32, raw);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) raw[i] = __float_as_uint(__uint_as_float(raw[i]) * factor);
+            tmem_st32(tmem + lane_base + kTmemO + c * 32, raw);
+          }
+          l *= factor;
+        }
+        m_ref = m_tile;
+      }
+      const float reference = m_ref == -INFINITY ? 0.0f : m_ref;
+      float sum = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t packed[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float p0 = exp2f(x[c * 64 + 2 * i] - reference);
+          const float p1 = exp2f(x[c * 64 + 2 * i + 1] - reference);
+          sum += p0 + p1;
+          packed[i] = pack2<T>(p0, p1);
+        }
+        tmem_st32(tmem + lane_base + stage * 128 + c * 32, packed);
+      }
+      l += sum;
+      tmem_wait_st();
+      fence_before();
+      mbar_arrive(smem_u32(&ctl.p_bar[stage]));
+    }
+    // ---- epilogue: O / l -> shared (swizzled rows) -> coalesced global stores; LSE.
+    // done_bar, not o_bar: PV of tile tiles-2 may still be in flight here, two phases behind.
+    const bool done = ok && mbar_wait(done_bar, 0, &ctl.abort) && !ctl.abort;
+    if (!done && tiles > 0 && !skip) {
+      report_status(args.status, kStatusWaitTimeout);
+      ctl.abort = 1;
+    }
+    fence_after();
+    const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+    uint8_t* stage_rows = smem + kQOffset;  // the Q tile is no longer read: every MMA completed
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      uint32_t raw[32];
+      if (done) {
+        tmem_ld32(tmem + lane_base + kTmemO + c * 32, raw);
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) raw[i] = 0u;
+      }
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {  // four 16-byte chunks of 8 values
+        float y[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = __uint_as_float(raw[v * 8 + i]) * inv;
+        const int chunk = c * 4 + v;  // 0..15 across the 256-byte row
+        *reinterpret_cast<uint4*>(stage_rows + row * 256 + ((chunk ^ (row & 15)) << 4)) = pack8<T>(y);
+      }
+    }
+    if (query < length && done) {
+      args.lse[static_cast<size_t>(prompt_begin + query) * args.query_heads + head] = m_ref + log2f(l);
+    }
+    softmax_barrier();
+    const int out_width = args.query_heads * kHeadDim;
+    T* out = static_cast<T*>(args.out);
+#pragma unroll 1
+    for (int i = 0; i < 16; ++i) {  // each warp writes its 32 rows, two rows per instruction
+      const int r = warp * 32 + i * 2 + (lane >> 4);
+      const int chunk = lane & 15;
+      if (q0 + r < length) {
+        const uint4 value = *reinterpret_cast<const uint4*>(stage_rows + r * 256 + ((chunk ^ (r & 15)) << 4));
+        *reinterpret_cast<uint4*>(out + static_cast<size_t>(prompt_begin + q0 + r) * out_width + head * kHeadDim +
+                                  chunk * 8) = value;
+      }
+    }
+  }
+
+  fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemColumns));
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* pointer = nullptr;
+    cudaDriverEntryPointQueryResult result;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &pointer, cudaEnableDefault, &result) == cudaSuccess &&
+        result == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(pointer);
+    }
+  });
+  return fn;
+}
+
+template <typename T>
+cudaError_t launch_typed(const AttentionArgs& a, cudaStream_t stream) {
+  int device = 0;
+  cudaGetDevice(&device);
+  static uint64_t configured = 0;  // the shared-memory opt-in is a per-device attribute
+  if (device >= 64 || !(configured & (1ull << device))) {
+    const cudaError_t status = cudaFuncSetAttribute(attention_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                    static_cast<int>(kSmemBytes));
+    if (status != cudaSuccess) return status;
+    if (device < 64) configured |= 1ull << device;
+  }
+  PFN_cuTensorMapEncodeTiled_v12000 encode = encode_fn();
+  if (encode == nullptr) return cudaErrorNotSupported;
+  // rows beyond the batch read as zeros (the map's extent is the batch's token count)
+  const int width = (a.query_heads + 2 * a.kv_heads) * kHeadDim;
+  CUtensorMap map;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(a.rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(width) * 2};
+  const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(kTile)};
+  const cuuint32_t element_strides[2] = {1, 1};
+  const CUtensorMapDataType type =
+      std::is_same_v<T, __half> ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  if (encode(&map, type, 2, const_cast<void*>(a.qkv), dims, strides, box, element_strides,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+    return cudaErrorInvalidValue;
+  }
+  Args args;
+  args.out = a.out;
+  args.lse = a.lse;
+  args.prompt_offsets = a.prompt_offsets;
+  args.tiles = a.tiles;
+  args.query_heads = a.query_heads;
+  args.kv_heads = a.kv_heads;
+  args.sliding_window = a.sliding_window;
+  const uint32_t format = std::is_same_v<T, __half> ? 0u : 1u;
+  args.idesc_s = idesc(format, false);
+  args.idesc_pv = idesc(format, true);
+  args.status = a.status;
+  const dim3 grid(a.tile_count, a.query_heads);
+  attention_tc_kernel<T><<<grid, kThreads, kSmemBytes, stream>>>(map, args);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_causal_attention_tc(const AttentionArgs& args, cudaStream_t stream) {
+  if (args.tile_count <= 0) return cudaSuccess;
+  if (args.head_dim != kHeadDim || args.kv_heads <= 0 || args.query_heads % args.kv_heads != 0 || args.rows <= 0) {
+    return cudaErrorInvalidValue;
+  }
+  // TMA: 16-byte aligned base; every x coordinate is a multiple of 64 elements (128 bytes)
+  if ((reinterpret_cast<uintptr_t>(args.qkv) & 15) != 0) return cudaErrorInvalidValue;
+  if (args.dtype == kActFp16) return launch_typed<__half>(args, stream);
+  if (args.dtype == kActBf16) return launch_typed<__nv_bfloat16>(args, stream);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace arb

@@ -101,35 +101,36 @@ const char* ar_last_error(void) { return g_last_error.c_str(); }
 
 const char* ar_version(void) { return "attnrank-b200 0.1.0 (sm_100a)"; }
 
-int ar_embedding_rms_norm(const int32_t* token_ids, int token_count, const void* table_bf16, int vocab_size,
-                          int hidden_size, const float* gamma, float eps, float* residual, void* normed_bf16,
-                          int* device_status, void* stream) {
+int ar_embedding_rms_norm(const int32_t* token_ids, int token_count, const void* table, int vocab_size,
+                          int hidden_size, const float* gamma, float eps, float* residual, void* normed,
+                          int* device_status, int dtype, void* stream) {
   if (token_count < 0 || hidden_size <= 0 || hidden_size % 8 != 0 || vocab_size <= 0) {
     return fail(AR_ERR_INVALID, "embedding: invalid sizes (hidden_size must be a positive multiple of 8)");
   }
-  return cuda_result(arb::launch_embed_rms_norm(token_ids, token_count, table_bf16, vocab_size, hidden_size, gamma, eps,
-                                                residual, normed_bf16, device_status, as_stream(stream)),
+  return cuda_result(arb::launch_embed_rms_norm(token_ids, token_count, table, vocab_size, hidden_size, gamma, eps,
+                                                residual, normed, device_status, dtype, as_stream(stream)),
                      "embedding_rms_norm");
 }
 
-int ar_rms_norm_residual(float* residual, const void* delta_bf16, const float* gamma, int token_count, int hidden_size,
-                         float eps, void* normed_bf16, void* stream) {
+int ar_rms_norm_residual(float* residual, const void* delta, const float* gamma, int token_count, int hidden_size,
+                         float eps, void* normed, int dtype, void* stream) {
   if (token_count < 0 || hidden_size <= 0 || hidden_size % 8 != 0) {
     return fail(AR_ERR_INVALID, "rms_norm_residual: hidden_size must be a positive multiple of 8");
   }
-  return cuda_result(arb::launch_rms_norm_residual(residual, delta_bf16, gamma, token_count, hidden_size, eps,
-                                                   normed_bf16, as_stream(stream)),
+  return cuda_result(arb::launch_rms_norm_residual(residual, delta, gamma, token_count, hidden_size, eps, normed, dtype,
+                                                   as_stream(stream)),
                      "rms_norm_residual");
 }
 
-int ar_rotary_embedding(void* qkv_bf16, const float* bias, const int32_t* positions, int token_count, int query_heads,
+int ar_rotary_embedding(void* qkv, const float* bias, const int32_t* positions, int token_count, int query_heads,
                         int kv_heads, int head_dim, const float* cos_table, const float* sin_table,
-                        int table_positions, int* device_status, void* stream) {
+                        int table_positions, int* device_status, int dtype, void* stream) {
   if (token_count < 0 || query_heads <= 0 || kv_heads <= 0 || head_dim <= 0 || head_dim % 16 != 0) {
     return fail(AR_ERR_INVALID, "rotary_embedding: head_dim must be a positive multiple of 16");
   }
-  return cuda_result(arb::launch_rotary_bias(qkv_bf16, bias, positions, token_count, query_heads, kv_heads, head_dim,
-                                             cos_table, sin_table, table_positions, device_status, as_stream(stream)),
+  return cuda_result(arb::launch_rotary_bias(qkv, bias, positions, token_count, query_heads, kv_heads, head_dim,
+                                             cos_table, sin_table, table_positions, device_status, dtype,
+                                             as_stream(stream)),
                      "rotary_embedding");
 }
 
@@ -139,23 +140,28 @@ int ar_rope_table(float* cos_table, float* sin_table, int positions, int head_di
                      "rope_table");
 }
 
-int ar_silu_multiply(const void* gate_bf16, const void* up_bf16, int64_t in_row_stride, void* out_bf16,
-                     int64_t out_row_stride, int token_count, int width, void* stream) {
+int ar_silu_multiply(const void* gate, const void* up, int64_t in_row_stride, void* out, int64_t out_row_stride,
+                     int token_count, int width, int dtype, void* stream) {
   if (token_count < 0 || width <= 0 || width % 8 != 0 || in_row_stride % 8 != 0 || out_row_stride % 8 != 0) {
     return fail(AR_ERR_INVALID, "silu_multiply: width and strides must be multiples of 8");
   }
-  return cuda_result(arb::launch_silu_multiply(gate_bf16, up_bf16, in_row_stride, out_bf16, out_row_stride,
-                                               token_count, width, as_stream(stream)),
+  return cuda_result(arb::launch_silu_multiply(gate, up, in_row_stride, out, out_row_stride, token_count, width, dtype,
+                                               as_stream(stream)),
                      "silu_multiply");
 }
 
-int ar_causal_attention(const void* qkv_bf16, void* out_bf16, float* lse, const int32_t* prompt_offsets_host,
-                        const int32_t* prompt_offsets_device, int prompt_count, int query_heads, int kv_heads,
-                        int head_dim, int sliding_window, void* stream) {
+}  // extern "C"
+
+namespace {
+
+int causal_attention_call(bool tcgen05, const void* qkv, void* out, float* lse, const int32_t* prompt_offsets_host,
+                          const int32_t* prompt_offsets_device, int prompt_count, int query_heads, int kv_heads,
+                          int head_dim, int sliding_window, int dtype, void* stream) {
   return guarded([&] {
     if (prompt_count <= 0 || head_dim != 128 || kv_heads <= 0 || query_heads % kv_heads != 0) {
       throw arb::Error("causal_attention: head_dim must be 128 and query_heads a multiple of kv_heads");
     }
+    if (dtype != arb::kActFp16 && dtype != arb::kActBf16) throw arb::Error("causal_attention: dtype must be fp16 or bf16");
     std::vector<int32_t> tiles;
     int max_tiles = 0;
     for (int p = 0; p < prompt_count; ++p) {
@@ -172,14 +178,16 @@ int ar_causal_attention(const void* qkv_bf16, void* out_bf16, float* lse, const 
       }
     }
     if (tiles.empty()) return AR_OK;
-    StreamScratch scratch(as_stream(stream));
+    cudaStream_t s = as_stream(stream);
+    StreamScratch scratch(s);
     auto* tiles_device = static_cast<int32_t*>(scratch.get(tiles.size() * sizeof(int32_t)));
-    arb::check_cuda(cudaMemcpyAsync(tiles_device, tiles.data(), tiles.size() * sizeof(int32_t), cudaMemcpyHostToDevice,
-                                    as_stream(stream)),
+    auto* status = static_cast<int*>(scratch.get(sizeof(int)));
+    arb::check_cuda(cudaMemsetAsync(status, 0, sizeof(int), s), "status reset");
+    arb::check_cuda(cudaMemcpyAsync(tiles_device, tiles.data(), tiles.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s),
                     "tile upload");
     arb::AttentionArgs args;
-    args.qkv = qkv_bf16;
-    args.out = out_bf16;
+    args.qkv = qkv;
+    args.out = out;
     args.lse = lse;
     args.prompt_offsets = prompt_offsets_device;
     args.tiles = tiles_device;
@@ -188,16 +196,44 @@ int ar_causal_attention(const void* qkv_bf16, void* out_bf16, float* lse, const 
     args.kv_heads = kv_heads;
     args.head_dim = head_dim;
     args.sliding_window = sliding_window;
-    arb::check_cuda(arb::launch_causal_attention(args, as_stream(stream)), "causal_attention");
-    arb::check_cuda(cudaStreamSynchronize(as_stream(stream)), "causal_attention");  // host tile list lifetime
+    args.dtype = dtype;
+    args.rows = prompt_offsets_host[prompt_count];
+    args.status = status;
+    arb::check_cuda(tcgen05 ? arb::launch_causal_attention_tc(args, s) : arb::launch_causal_attention(args, s),
+                    "causal_attention");
+    int device_status = 0;
+    arb::check_cuda(cudaMemcpyAsync(&device_status, status, sizeof(int), cudaMemcpyDeviceToHost, s), "status read");
+    arb::check_cuda(cudaStreamSynchronize(s), "causal_attention");  // host tile list lifetime
+    if (device_status != 0) {
+      throw arb::Error("causal_attention: device reported status " + std::to_string(device_status));
+    }
     return AR_OK;
   });
 }
 
-int ar_document_attention_mass(const void* qkv_bf16, int qkv_rows, const float* lse, const int32_t* prompt_offsets_host,
+}  // namespace
+
+extern "C" {
+
+int ar_causal_attention(const void* qkv, void* out, float* lse, const int32_t* prompt_offsets_host,
+                        const int32_t* prompt_offsets_device, int prompt_count, int query_heads, int kv_heads,
+                        int head_dim, int sliding_window, int dtype, void* stream) {
+  return causal_attention_call(true, qkv, out, lse, prompt_offsets_host, prompt_offsets_device, prompt_count,
+                               query_heads, kv_heads, head_dim, sliding_window, dtype, stream);
+}
+
+int ar_causal_attention_mma(const void* qkv, void* out, float* lse, const int32_t* prompt_offsets_host,
+                            const int32_t* prompt_offsets_device, int prompt_count, int query_heads, int kv_heads,
+                            int head_dim, int sliding_window, int dtype, void* stream) {
+  return causal_attention_call(false, qkv, out, lse, prompt_offsets_host, prompt_offsets_device, prompt_count,
+                               query_heads, kv_heads, head_dim, sliding_window, dtype, stream);
+}
+
+int ar_document_attention_mass(const void* qkv, int qkv_rows, const float* lse, const int32_t* prompt_offsets_host,
                                int prompt_count, const int32_t* query_spans_host, const int32_t* spans_host,
                                int span_count, int query_heads, int kv_heads, int head_dim, int sliding_window,
-                               int prefill_chunk_tokens, int normalize_by_length, double* mass_out, void* stream) {
+                               int prefill_chunk_tokens, int normalize_by_length, double* mass_out, int dtype,
+                               void* stream) {
   return guarded([&] {
     if (prompt_count <= 0 || span_count <= 0 || span_count > arb::kMassMaxSpans) {
       throw arb::Error("document_attention_mass: 1..32 spans and at least one prompt are required");
@@ -241,7 +277,8 @@ int ar_document_attention_mass(const void* qkv_bf16, int qkv_rows, const float* 
     arb::check_cuda(cudaMemcpyAsync(meta_device, meta.data(), meta.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s),
                     "metadata upload");
     arb::MassArgs args;
-    args.qkv = qkv_bf16;
+    args.qkv = qkv;
+    args.dtype = dtype;
     args.qkv_rows_capacity = qkv_rows;
     args.lse = lse;
     args.prompt_offsets = meta_device;
@@ -283,11 +320,11 @@ int ar_document_attention_mass(const void* qkv_bf16, int qkv_rows, const float* 
   });
 }
 
-int ar_synthetic_fill(void* dst_bf16, int64_t count, uint64_t seed, int layer, int kind, float standard_deviation,
-                      void* stream) {
+int ar_synthetic_fill(void* dst, int64_t count, uint64_t seed, int layer, int kind, float standard_deviation,
+                      int dtype, void* stream) {
   if (count < 0) return fail(AR_ERR_INVALID, "synthetic_fill: negative count");
-  return cuda_result(arb::launch_synthetic_fill(dst_bf16, count, arb::synthetic_tensor_key(seed, layer, kind),
-                                                arb::synthetic_scale(standard_deviation), as_stream(stream)),
+  return cuda_result(arb::launch_synthetic_fill(dst, count, arb::synthetic_tensor_key(seed, layer, kind),
+                                                arb::synthetic_scale(standard_deviation), dtype, as_stream(stream)),
                      "synthetic_fill");
 }
 
@@ -313,6 +350,8 @@ int ar_engine_create(const ar_llama_config* config, const ar_runtime_options* op
       if (options->prefill_chunk_tokens > 0) o.prefill_chunk_tokens = options->prefill_chunk_tokens;
       if (options->max_batch_tokens > 0) o.max_batch_tokens = options->max_batch_tokens;
       if (options->max_batch_prompts > 0) o.max_batch_prompts = options->max_batch_prompts;
+      if (options->activation_dtype != 0) o.activation_dtype = options->activation_dtype;
+      o.attention_kernel = options->attention_kernel;
     }
     auto holder = std::make_unique<ar_engine>();
     holder->engine = std::make_unique<arb::Engine>(c, o);
@@ -437,6 +476,27 @@ int ar_engine_synchronize(ar_engine* engine) {
 void* ar_engine_stream(ar_engine* engine) { return engine ? static_cast<void*>(engine->engine->stream()) : nullptr; }
 
 int ar_engine_device(ar_engine* engine) { return engine ? engine->engine->options().device_index : -1; }
+
+int ar_engine_set_kernel_timing(ar_engine* engine, int enabled) {
+  return guarded([&] {
+    if (engine == nullptr) throw arb::Error("set_kernel_timing: null engine");
+    engine->engine->set_kernel_timing(enabled != 0);
+    return AR_OK;
+  });
+}
+
+int ar_engine_kernel_timing(ar_engine* engine, double* milliseconds, double* work, int64_t* launches) {
+  return guarded([&] {
+    if (engine == nullptr) throw arb::Error("kernel_timing: null engine");
+    static_assert(arb::kKernelClassCount == AR_KERNEL_CLASS_COUNT, "kernel class count");
+    engine->engine->kernel_timing(milliseconds, work, launches);
+    return AR_OK;
+  });
+}
+
+const char* ar_kernel_class_name(int kernel_class) { return arb::kernel_class_name(kernel_class); }
+
+int ar_kernel_class_is_tensor(int kernel_class) { return arb::kernel_class_is_tensor(kernel_class) ? 1 : 0; }
 
 int ar_profile_from_accumulated(const double* accumulated, int slots, int64_t sample_count, double* attention_out,
                                 int* position_order_out) {

@@ -2,9 +2,9 @@
 //
 //   positions, embed+norm                                         (layer_kernels.cu)
 //   for layer in [0, probe_end):
-//     qkv   = normed @ Wqkv^T                 cuBLASLt bf16 -> bf16
+//     qkv   = normed @ Wqkv^T                 cuBLASLt, fp16 (or bf16) operands, fp32 accumulation
 //     qkv  += bias; RoPE(q, k)                rotary_bias_kernel (in place)
-//     attn, lse = causal_attention(qkv)       attention.cu (flash, no score matrix)
+//     attn, lse = causal_attention(qkv)       attention_tc.cu (tcgen05 flash, no score matrix)
 //     partials[layer] = document_mass(qkv, lse)   mass.cu (tcgen05), probed layers only
 //     delta = attn @ Wo^T
 //     residual += delta; normed = rms(residual) * post_norm
@@ -93,7 +93,7 @@ float element_as_float(const void* data, int dtype, size_t index) {
   }
 }
 
-// Upload `count` elements of host data as bf16 into dst.
+// Upload `count` elements of host data as bf16 into dst (host-side conversion).
 void upload_bf16(void* dst, const void* host, int dtype, size_t count) {
   if (dtype == 2) {
     check_cuda(cudaMemcpy(dst, host, count * 2, cudaMemcpyHostToDevice), "weight upload");
@@ -132,12 +132,115 @@ void destroy_plans(std::map<std::tuple<int, int, int>, GemmPlan>& plans) {
 
 }  // namespace
 
+const char* kernel_class_name(int klass) {
+  static const char* names[kKernelClassCount] = {
+      "embedding_rms_norm", "gemm_qkv",      "rotary_bias", "causal_attention", "document_mass", "gemm_out",
+      "rms_norm_residual",  "gemm_gate_up",  "silu_multiply", "gemm_down",     "positions",     "finalize_mass"};
+  return klass >= 0 && klass < kKernelClassCount ? names[klass] : "";
+}
+
+bool kernel_class_is_tensor(int klass) {
+  return klass == kClassGemmQkv || klass == kClassAttention || klass == kClassMass || klass == kClassGemmOut ||
+         klass == kClassGemmGateUp || klass == kClassGemmDown;
+}
+
+struct Engine::KernelTimer {
+  struct Record {
+    int klass;
+    double work;
+  };
+  bool enabled = false;
+  std::vector<cudaEvent_t> pool;  // two events per record
+  std::vector<Record> records;
+  double milliseconds[kKernelClassCount] = {};
+  double work[kKernelClassCount] = {};
+  int64_t launches[kKernelClassCount] = {};
+  ~KernelTimer() {
+    for (cudaEvent_t event : pool) cudaEventDestroy(event);
+  }
+  cudaEvent_t event(size_t index) {
+    while (pool.size() <= index) {
+      cudaEvent_t created = nullptr;
+      check_cuda(cudaEventCreate(&created), "timing event");
+      pool.push_back(created);
+    }
+    return pool[index];
+  }
+};
+
+template <typename Launch>
+void Engine::timed(int klass, double work, Launch&& launch) {
+  KernelTimer& timer = *timer_;
+  if (!timer.enabled) {
+    launch();
+    return;
+  }
+  const size_t first = timer.records.size() * 2;
+  check_cuda(cudaEventRecord(timer.event(first), stream_), "timing event");
+  launch();
+  check_cuda(cudaEventRecord(timer.event(first + 1), stream_), "timing event");
+  timer.records.push_back({klass, work});
+}
+
+void Engine::set_kernel_timing(bool enabled) { timer_->enabled = enabled; }
+
+void Engine::kernel_timing(double* milliseconds, double* work, int64_t* launches) {
+  KernelTimer& timer = *timer_;
+  synchronize();
+  for (size_t i = 0; i < timer.records.size(); ++i) {
+    float elapsed = 0.0f;
+    check_cuda(cudaEventElapsedTime(&elapsed, timer.pool[2 * i], timer.pool[2 * i + 1]), "timing read");
+    const int klass = timer.records[i].klass;
+    timer.milliseconds[klass] += elapsed;
+    timer.work[klass] += timer.records[i].work;
+    timer.launches[klass] += 1;
+  }
+  timer.records.clear();
+  for (int k = 0; k < kKernelClassCount; ++k) {
+    if (milliseconds != nullptr) milliseconds[k] = timer.milliseconds[k];
+    if (work != nullptr) work[k] = timer.work[k];
+    if (launches != nullptr) launches[k] = timer.launches[k];
+    timer.milliseconds[k] = 0;
+    timer.work[k] = 0;
+    timer.launches[k] = 0;
+  }
+}
+
+// Upload `count` elements of host data (dtype 0 = fp32, 1 = fp16, 2 = bf16) into dst in the
+// engine's activation type. bf16 -> fp16 and fp32 -> 16-bit are converted on the device
+// (round to nearest even), so a bf16 checkpoint gives exactly the fp16 weights of the seeded
+// synthetic path.
+void Engine::upload_matrix(void* dst, const void* host, int dtype, size_t count) {
+  const int target = options_.activation_dtype;
+  if (dtype == target) {
+    check_cuda(cudaMemcpy(dst, host, count * 2, cudaMemcpyHostToDevice), "weight upload");
+    return;
+  }
+  if (target == kActBf16 && dtype == 1) {
+    upload_bf16(dst, host, dtype, count);
+    return;
+  }
+  if (dtype != 0 && dtype != 2) throw Error("unsupported tensor dtype code " + std::to_string(dtype));
+  const size_t bytes = count * (dtype == 0 ? 4 : 2);
+  void* staging = nullptr;
+  check_cuda(cudaMalloc(&staging, bytes), "weight staging allocation");
+  cudaError_t status = cudaMemcpy(staging, host, bytes, cudaMemcpyHostToDevice);
+  if (status == cudaSuccess) {
+    status = dtype == 0 ? launch_f32_to_activation(static_cast<const float*>(staging), dst, static_cast<long long>(count),
+                                                   target, stream_)
+                        : launch_bf16_to_fp16(staging, dst, static_cast<long long>(count), stream_);
+  }
+  if (status == cudaSuccess) status = cudaStreamSynchronize(stream_);
+  cudaFree(staging);
+  check_cuda(status, "weight conversion");
+}
+
 struct Engine::GemmPlans {
   std::map<std::tuple<int, int, int>, GemmPlan> by_shape;
 };
 
 Engine::Engine(const ModelConfig& config, const RuntimeOptions& options)
-    : config_(config), options_(options), plans_(new GemmPlans) {
+    : config_(config), options_(options), plans_(new GemmPlans), timer_(new KernelTimer) {
   const ModelConfig& c = config_;
   if (c.hidden_size <= 0 || c.num_attention_heads <= 0 || c.hidden_size % c.num_attention_heads != 0) {
     throw Error("invalid attention head configuration");
@@ -152,6 +255,12 @@ Engine::Engine(const ModelConfig& config, const RuntimeOptions& options)
   if (options_.prefill_chunk_tokens <= 0) throw Error("prefill_chunk_tokens must be positive");
   if (options_.max_batch_tokens <= 0) throw Error("max_batch_tokens must be positive");
   if (options_.max_batch_prompts <= 0) throw Error("max_batch_prompts must be positive");
+  if (options_.activation_dtype != kActFp16 && options_.activation_dtype != kActBf16) {
+    throw Error("activation_dtype must be 1 (fp16) or 2 (bf16)");
+  }
+  if (options_.attention_kernel != 0 && options_.attention_kernel != 1) {
+    throw Error("attention_kernel must be 0 (tcgen05) or 1 (mma.sync)");
+  }
   if (options_.max_batch_tokens < options_.max_sequence_length) options_.max_batch_tokens = options_.max_sequence_length;
   capacity_tokens_ = options_.max_batch_tokens;
 
@@ -176,6 +285,7 @@ Engine::Engine(const ModelConfig& config, const RuntimeOptions& options)
 
 Engine::~Engine() {
   if (stream_ != nullptr) cudaStreamSynchronize(stream_);
+  timer_.reset();
   destroy_plans(plans_->by_shape);
   for (void* pointer : allocations_) cudaFree(pointer);
   if (partials_ != nullptr) cudaFree(partials_);
@@ -266,7 +376,7 @@ void Engine::load_tensor(const std::string& name, int dtype, const std::vector<i
   };
   if (name == "model.embed_tokens.weight") {
     expect(V, H);
-    upload_bf16(embedding_, host, dtype, static_cast<size_t>(count));
+    upload_matrix(embedding_, host, dtype, static_cast<size_t>(count));
     embedding_loaded_ = true;
     return;
   }
@@ -285,15 +395,15 @@ void Engine::load_tensor(const std::string& name, int dtype, const std::vector<i
   auto* qkv = static_cast<uint16_t*>(layer.qkv);
   if (suffix == "self_attn.q_proj.weight") {
     expect(Hq * D, H);
-    upload_bf16(qkv, host, dtype, count);
+    upload_matrix(qkv, host, dtype, count);
     loaded_[index][kQ] = true;
   } else if (suffix == "self_attn.k_proj.weight") {
     expect(KV, H);
-    upload_bf16(qkv + Hq * D * H, host, dtype, count);
+    upload_matrix(qkv + Hq * D * H, host, dtype, count);
     loaded_[index][kK] = true;
   } else if (suffix == "self_attn.v_proj.weight") {
     expect(KV, H);
-    upload_bf16(qkv + (Hq * D + KV) * H, host, dtype, count);
+    upload_matrix(qkv + (Hq * D + KV) * H, host, dtype, count);
     loaded_[index][kV] = true;
   } else if (suffix == "self_attn.q_proj.bias" || suffix == "self_attn.k_proj.bias" ||
              suffix == "self_attn.v_proj.bias") {
@@ -305,19 +415,19 @@ void Engine::load_tensor(const std::string& name, int dtype, const std::vector<i
     loaded_[index][which == 'q' ? kQBias : which == 'k' ? kKBias : kVBias] = true;
   } else if (suffix == "self_attn.o_proj.weight") {
     expect(H, Hq * D);
-    upload_bf16(layer.out, host, dtype, count);
+    upload_matrix(layer.out, host, dtype, count);
     loaded_[index][kO] = true;
   } else if (suffix == "mlp.gate_proj.weight") {
     expect(I, H);
-    upload_bf16(layer.gate_up, host, dtype, count);
+    upload_matrix(layer.gate_up, host, dtype, count);
     loaded_[index][kGate] = true;
   } else if (suffix == "mlp.up_proj.weight") {
     expect(I, H);
-    upload_bf16(static_cast<uint16_t*>(layer.gate_up) + I * H, host, dtype, count);
+    upload_matrix(static_cast<uint16_t*>(layer.gate_up) + I * H, host, dtype, count);
     loaded_[index][kUp] = true;
   } else if (suffix == "mlp.down_proj.weight") {
     expect(H, I);
-    upload_bf16(layer.down, host, dtype, count);
+    upload_matrix(layer.down, host, dtype, count);
     loaded_[index][kDown] = true;
   } else if (suffix == "input_layernorm.weight") {
     expect(H, 1);
@@ -336,7 +446,8 @@ void Engine::init_synthetic(uint64_t seed, float standard_deviation) {
   const long long QD = static_cast<long long>(c.num_attention_heads) * c.head_dim(), KV = c.kv_width();
   const float scale = synthetic_scale(standard_deviation);
   auto fill = [&](void* dst, long long count, int layer, int kind) {
-    check_cuda(launch_synthetic_fill(dst, count, synthetic_tensor_key(seed, layer, kind), scale, stream_),
+    check_cuda(launch_synthetic_fill(dst, count, synthetic_tensor_key(seed, layer, kind), scale,
+                                     options_.activation_dtype, stream_),
                "synthetic fill");
   };
   auto ones = [&](float* dst, long long count, int layer, int kind) {
@@ -416,9 +527,10 @@ void Engine::gemm(const void* x, const void* w, void* y, int m, int n, int k) {
     check_lt(cublasLtMatmulDescSetAttribute(plan.op, CUBLASLT_MATMUL_DESC_TRANSA, &transa, sizeof(transa)), "transa");
     check_lt(cublasLtMatmulDescSetAttribute(plan.op, CUBLASLT_MATMUL_DESC_TRANSB, &transb, sizeof(transb)), "transb");
     // column-major view: D[n, m] = W[k, n]^T * X[k, m]  (row-major Y[m, n] = X[m, k] W[n, k]^T)
-    check_lt(cublasLtMatrixLayoutCreate(&plan.a, CUDA_R_16BF, k, n, k), "layout a");
-    check_lt(cublasLtMatrixLayoutCreate(&plan.b, CUDA_R_16BF, k, m, k), "layout b");
-    check_lt(cublasLtMatrixLayoutCreate(&plan.c, CUDA_R_16BF, n, m, n), "layout c");
+    const cudaDataType_t type = options_.activation_dtype == kActFp16 ? CUDA_R_16F : CUDA_R_16BF;
+    check_lt(cublasLtMatrixLayoutCreate(&plan.a, type, k, n, k), "layout a");
+    check_lt(cublasLtMatrixLayoutCreate(&plan.b, type, k, m, k), "layout b");
+    check_lt(cublasLtMatrixLayoutCreate(&plan.c, type, n, m, n), "layout c");
     cublasLtMatmulPreference_t preference = nullptr;
     check_lt(cublasLtMatmulPreferenceCreate(&preference), "preference");
     check_lt(cublasLtMatmulPreferenceSetAttribute(preference, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES,
@@ -431,7 +543,7 @@ void Engine::gemm(const void* x, const void* w, void* y, int m, int n, int k) {
     cublasLtMatmulPreferenceDestroy(preference);
     if (status != CUBLAS_STATUS_SUCCESS || returned == 0) {
       throw Error("cuBLASLt found no algorithm for a " + std::to_string(m) + "x" + std::to_string(n) + "x" +
-                  std::to_string(k) + " bf16 GEMM");
+                  std::to_string(k) + " 16-bit GEMM");
     }
     plan.algo = result.algo;
     found = cache.emplace(key, plan).first;
@@ -608,6 +720,20 @@ BatchLayout Engine::build_metadata(const std::vector<PromptView>& prompts, const
     ++cursor;
   }
   BatchLayout layout;
+  const double D = c.head_dim(), Hq = c.num_attention_heads;
+  for (int i = 0; i < P; ++i) {
+    const PromptView& p = prompts[batch.first + i];
+    const double L = p.token_count;
+    double pairs = L * (L + 1) / 2;  // causal (query, key) pairs
+    if (c.sliding_window > 0 && p.token_count > c.sliding_window) {
+      const double W = c.sliding_window;
+      pairs = W * (W + 1) / 2 + (L - W) * W;
+    }
+    layout.attention_flops += 4 * D * Hq * pairs;
+    double span_keys = 0;
+    for (int s = 0; s < S; ++s) span_keys += p.spans[2 * s + 1] - p.spans[2 * s];
+    layout.mass_flops += 2 * D * Hq * (p.query_end - p.query_begin) * span_keys;
+  }
   layout.tokens_at = tokens_at;
   layout.offsets_at = offsets_at;
   layout.queries_at = queries_at;
@@ -708,10 +834,16 @@ void Engine::execute_batch(const BatchLayout& layout, const int32_t* dev, int sp
 
   const int H = c.hidden_size, I = c.intermediate_size, Hq = c.num_attention_heads, Hkv = c.num_key_value_heads;
   const int D = c.head_dim(), Wqkv = c.qkv_width();
-  check_cuda(launch_positions(d_offsets, P, M, positions_, stream_), "positions");
-  check_cuda(launch_embed_rms_norm(d_tokens, M, embedding_, c.vocab_size, H, layers_[0].input_norm, c.rms_norm_eps,
-                                   residual_, normed_, status_, stream_),
-             "embedding");
+  const int dtype = options_.activation_dtype;
+  const double m = M;
+  timed(kClassPositions, 4.0 * M + 4.0 * (P + 1), [&] {
+    check_cuda(launch_positions(d_offsets, P, M, positions_, stream_), "positions");
+  });
+  timed(kClassEmbedding, m * H * (2 + 4 + 2) + 4.0 * M, [&] {
+    check_cuda(launch_embed_rms_norm(d_tokens, M, embedding_, c.vocab_size, H, layers_[0].input_norm, c.rms_norm_eps,
+                                     residual_, normed_, status_, dtype, stream_),
+               "embedding");
+  });
 
   AttentionArgs attention;
   attention.qkv = qkv_;
@@ -724,6 +856,9 @@ void Engine::execute_batch(const BatchLayout& layout, const int32_t* dev, int sp
   attention.kv_heads = Hkv;
   attention.head_dim = D;
   attention.sliding_window = c.sliding_window;
+  attention.dtype = dtype;
+  attention.rows = M;
+  attention.status = status_;
 
   MassArgs mass;
   mass.qkv = qkv_;
@@ -743,30 +878,48 @@ void Engine::execute_batch(const BatchLayout& layout, const int32_t* dev, int sp
   mass.reference_chunk = options_.prefill_chunk_tokens;
   mass.normalize_by_length = normalize_by_length ? 1 : 0;
   mass.status = status_;
+  mass.dtype = dtype;
 
+  // algorithmic work of each launch: FLOPs for GEMMs / attention / mass, HBM bytes otherwise
+  const double rotated_heads = Hq + Hkv + (c.attention_bias ? Hkv : 0);
+  const double rotary_bytes = m * rotated_heads * D * 2 * 2;
+  const double norm_bytes = m * H * (4 + 2 + 4 + 2);
+  const double silu_bytes = m * I * 2 * 3;
   const int last_layer = range.end - 1;
   for (int l = 0; l <= last_layer; ++l) {
     const LayerWeights& w = layers_[l];
-    gemm(normed_, w.qkv, qkv_, M, Wqkv, H);
-    check_cuda(launch_rotary_bias(qkv_, w.qkv_bias, positions_, M, Hq, Hkv, D, cos_table_, sin_table_,
-                                  options_.max_sequence_length, status_, stream_),
-               "rotary");
-    check_cuda(launch_causal_attention(attention, stream_), "attention");
+    timed(kClassGemmQkv, 2 * m * Wqkv * H, [&] { gemm(normed_, w.qkv, qkv_, M, Wqkv, H); });
+    timed(kClassRotary, rotary_bytes, [&] {
+      check_cuda(launch_rotary_bias(qkv_, w.qkv_bias, positions_, M, Hq, Hkv, D, cos_table_, sin_table_,
+                                    options_.max_sequence_length, status_, dtype, stream_),
+                 "rotary");
+    });
+    timed(kClassAttention, layout.attention_flops, [&] {
+      check_cuda(options_.attention_kernel == 0 ? launch_causal_attention_tc(attention, stream_)
+                                                : launch_causal_attention(attention, stream_),
+                 "attention");
+    });
     if (l >= range.begin) {
       mass.partials = partials_ + static_cast<size_t>(l - range.begin) * item_count * S;
-      check_cuda(launch_document_mass(mass, stream_), "document mass");
+      timed(kClassMass, layout.mass_flops, [&] { check_cuda(launch_document_mass(mass, stream_), "document mass"); });
     }
-    gemm(attn_, w.out, delta_, M, H, Hq * D);
-    check_cuda(launch_rms_norm_residual(residual_, delta_, w.post_norm, M, H, c.rms_norm_eps, normed_, stream_),
-               "post-attention norm");
-    gemm(normed_, w.gate_up, gate_up_, M, 2 * I, H);
-    check_cuda(launch_silu_multiply(gate_up_, static_cast<const uint16_t*>(gate_up_) + I, 2LL * I, act_, I, M, I,
-                                    stream_),
-               "swiglu");
-    gemm(act_, w.down, delta_, M, H, I);
+    timed(kClassGemmOut, 2 * m * H * Hq * D, [&] { gemm(attn_, w.out, delta_, M, H, Hq * D); });
+    timed(kClassNorm, norm_bytes, [&] {
+      check_cuda(launch_rms_norm_residual(residual_, delta_, w.post_norm, M, H, c.rms_norm_eps, normed_, dtype, stream_),
+                 "post-attention norm");
+    });
+    timed(kClassGemmGateUp, 2 * m * 2 * I * H, [&] { gemm(normed_, w.gate_up, gate_up_, M, 2 * I, H); });
+    timed(kClassSilu, silu_bytes, [&] {
+      check_cuda(launch_silu_multiply(gate_up_, static_cast<const uint16_t*>(gate_up_) + I, 2LL * I, act_, I, M, I,
+                                      dtype, stream_),
+                 "swiglu");
+    });
+    timed(kClassGemmDown, 2 * m * H * I, [&] { gemm(act_, w.down, delta_, M, H, I); });
     const float* next_norm = l + 1 < c.num_hidden_layers ? layers_[l + 1].input_norm : final_norm_;
-    check_cuda(launch_rms_norm_residual(residual_, delta_, next_norm, M, H, c.rms_norm_eps, normed_, stream_),
-               "pre-attention norm");
+    timed(kClassNorm, norm_bytes, [&] {
+      check_cuda(launch_rms_norm_residual(residual_, delta_, next_norm, M, H, c.rms_norm_eps, normed_, dtype, stream_),
+                 "pre-attention norm");
+    });
   }
 
   FinalizeArgs finalize;
@@ -782,7 +935,9 @@ void Engine::execute_batch(const BatchLayout& layout, const int32_t* dev, int sp
   finalize.rows = rows_device;
   finalize.raw_rows = raw_rows_device;
   finalize.accumulator = device_accumulator;
-  check_cuda(launch_finalize_mass(finalize, stream_), "finalize");
+  timed(kClassFinalize, 4.0 * layers * item_count * S, [&] {
+    check_cuda(launch_finalize_mass(finalize, stream_), "finalize");
+  });
 }
 
 }  // namespace arb

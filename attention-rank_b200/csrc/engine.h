@@ -6,8 +6,9 @@
 // are design, not semantics:
 //   * many prompts run in one forward (packed, variable length), so the projection GEMMs see
 //     thousands of rows instead of one prompt's chunk;
-//   * weights stay bf16 in HBM (q|k|v and gate|up fused into one matrix each), activations are
-//     bf16 except the fp32 residual stream;
+//   * weights stay 16-bit in HBM (q|k|v and gate|up fused into one matrix each); activations
+//     are 16-bit except the fp32 residual stream. The 16-bit type is fp16 by default -- the
+//     reference's own GEMM operand type (model.cu:353-365) -- or bf16;
 //   * attention never materialises scores; mass is captured by a tcgen05 kernel per layer and
 //     reduced on the device, with no host synchronisation until the caller asks for results.
 #pragma once
@@ -56,7 +57,28 @@ struct RuntimeOptions {
   int prefill_chunk_tokens = 512;    // the reference's chunk length (normalize_by_length divisors)
   int max_batch_tokens = 16384;      // packed tokens per forward
   int max_batch_prompts = 256;
+  int activation_dtype = 1;          // 1 = fp16 (default), 2 = bf16: weights, GEMM operands, activations
+  int attention_kernel = 0;          // 0 = tcgen05 (attention_tc.cu), 1 = mma.sync (attention.cu)
 };
+
+// Kernel classes timed by the engine's optional per-launch timing (CUDA events on stream()).
+enum KernelClass : int {
+  kClassEmbedding = 0,
+  kClassGemmQkv,
+  kClassRotary,
+  kClassAttention,
+  kClassMass,
+  kClassGemmOut,
+  kClassNorm,
+  kClassGemmGateUp,
+  kClassSilu,
+  kClassGemmDown,
+  kClassPositions,
+  kClassFinalize,
+  kKernelClassCount
+};
+const char* kernel_class_name(int klass);
+bool kernel_class_is_tensor(int klass);  // work unit: FLOPs (tensor) or bytes (HBM)
 
 // One probe prompt as the host hands it over: token ids plus prompt-relative spans.
 struct PromptView {
@@ -81,6 +103,8 @@ struct BatchLayout {
   int tokens = 0;
   int tile_count = 0;  // attention query tiles
   int item_count = 0;  // mass CTAs
+  double attention_flops = 0;  // 4 D Hq x visible causal (query, key) pairs
+  double mass_flops = 0;       // 2 D Hq x sum over prompts of query rows x document-span keys
 };
 
 // A scan whose batch metadata is resident in HBM: running it launches kernels only.
@@ -136,6 +160,12 @@ class Engine {
   static void raise_on_status(int status);
   int last_device_status() const { return last_status_; }
 
+  // Per-launch timing of the engine's kernels: while enabled every launch is bracketed by CUDA
+  // events; kernel_timing() synchronises, adds up milliseconds, algorithmic work and launches
+  // per KernelClass since the last call, and clears the record.
+  void set_kernel_timing(bool enabled);
+  void kernel_timing(double* milliseconds, double* work, int64_t* launches);
+
   // Raw access for the kernel-level tests: the device buffers of the last batch.
   const void* qkv_buffer() const { return qkv_; }
   int qkv_capacity_rows() const { return capacity_tokens_; }
@@ -144,11 +174,11 @@ class Engine {
 
  private:
   struct LayerWeights {
-    void* qkv = nullptr;     // bf16 [(Hq + 2 Hkv) D, H]
+    void* qkv = nullptr;     // 16-bit [(Hq + 2 Hkv) D, H]
     float* qkv_bias = nullptr;  // fp32 [(Hq + 2 Hkv) D] or null
-    void* out = nullptr;     // bf16 [H, Hq D]
-    void* gate_up = nullptr;  // bf16 [2 I, H]
-    void* down = nullptr;    // bf16 [H, I]
+    void* out = nullptr;     // 16-bit [H, Hq D]
+    void* gate_up = nullptr;  // 16-bit [2 I, H]
+    void* down = nullptr;    // 16-bit [H, I]
     float* input_norm = nullptr;  // fp32 [H]
     float* post_norm = nullptr;   // fp32 [H]
   };
@@ -173,6 +203,11 @@ class Engine {
   void validate(const std::vector<PromptView>& prompts, int span_count, LayerRange range) const;
   std::vector<Batch> plan_batches(const std::vector<PromptView>& prompts) const;
   void* device_alloc(size_t bytes);
+  void upload_matrix(void* dst, const void* host, int dtype, size_t count);
+  template <typename Launch>
+  void timed(int klass, double work, Launch&& launch);
+  struct KernelTimer;
+  std::unique_ptr<KernelTimer> timer_;
 
   ModelConfig config_;
   RuntimeOptions options_;
@@ -185,7 +220,7 @@ class Engine {
   std::unique_ptr<GemmPlans> plans_;  // cuBLASLt descriptors + algorithm per (m, n, k)
 
   std::vector<void*> allocations_;
-  void* embedding_ = nullptr;  // bf16 [V, H]
+  void* embedding_ = nullptr;  // 16-bit [V, H]
   std::vector<LayerWeights> layers_;
   float* final_norm_ = nullptr;
   std::vector<std::vector<bool>> loaded_;  // per layer, per tensor kind

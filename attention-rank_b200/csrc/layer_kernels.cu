@@ -8,24 +8,27 @@
 //   rotary_embedding_kernel (:85-115) + add_row_bias_kernel (:177-184) -> rotary_bias_kernel
 //   silu_multiply_kernel (:164-170)     -> silu_multiply_kernel
 // The arithmetic of each op follows the reference formula line for line (fp32 math, the same
-// order of multiplies), only the storage type of activations changes from fp32 to bf16.
+// order of multiplies), only the storage type of activations changes from fp32 to 16 bits (T =
+// __half, the default, or __nv_bfloat16).
 #include "common.cuh"
 #include "layer_kernels.h"
 
 namespace arb {
 namespace {
 
-constexpr int kRowThreadsCap = 512;
+constexpr int kRowThreadsCap = 256;
+constexpr int kRopeUnroll = 4;   // heads per rotary loop iteration (loads in flight per thread)
+constexpr int kSiluUnroll = 2;   // 8-value chunks per SwiGLU thread
 
 // ---------------------------------------------------------------------------------------------
 // Row kernels: one CTA per token row, each thread holds VPT vectors of 8 channels in registers,
 // so the row is read once, reduced, and written once.
 // ---------------------------------------------------------------------------------------------
-template <int VPT>
+template <typename T, int VPT>
 __global__ void __launch_bounds__(kRowThreadsCap) embed_rms_norm_kernel(
-    const int32_t* __restrict__ token_ids, const __nv_bfloat16* __restrict__ table, int vocab,
-    int hidden, const float* __restrict__ gamma, float eps, float* __restrict__ residual,
-    __nv_bfloat16* __restrict__ normed, int* status) {
+    const int32_t* __restrict__ token_ids, const T* __restrict__ table, int vocab, int hidden,
+    const float* __restrict__ gamma, float eps, float* __restrict__ residual, T* __restrict__ normed,
+    int* status) {
   __shared__ float scratch[32];
   const int row = blockIdx.x;
   int token = token_ids[row];
@@ -40,7 +43,7 @@ __global__ void __launch_bounds__(kRowThreadsCap) embed_rms_norm_kernel(
   for (int k = 0; k < VPT; ++k) {
     const int chunk = threadIdx.x + k * blockDim.x;
     if (chunk < chunks && token >= 0) {
-      unpack8(load_nc(table + static_cast<size_t>(token) * hidden + chunk * 8), values[k]);
+      unpack8<T>(load_nc(table + static_cast<size_t>(token) * hidden + chunk * 8), values[k]);
     } else {
 #pragma unroll
       for (int i = 0; i < 8; ++i) values[k][i] = 0.0f;
@@ -51,7 +54,7 @@ __global__ void __launch_bounds__(kRowThreadsCap) embed_rms_norm_kernel(
   const float total = block_sum(squares, scratch);
   const float scale = rsqrtf(total / static_cast<float>(hidden) + eps);
   float* residual_row = residual + static_cast<size_t>(row) * hidden;
-  __nv_bfloat16* normed_row = normed + static_cast<size_t>(row) * hidden;
+  T* normed_row = normed + static_cast<size_t>(row) * hidden;
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
     const int chunk = threadIdx.x + k * blockDim.x;
@@ -65,19 +68,19 @@ __global__ void __launch_bounds__(kRowThreadsCap) embed_rms_norm_kernel(
     float y[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) y[i] = values[k][i] * scale * g[i];
-    *reinterpret_cast<uint4*>(normed_row + chunk * 8) = pack8(y);
+    *reinterpret_cast<uint4*>(normed_row + chunk * 8) = pack8<T>(y);
   }
 }
 
-template <int VPT>
+template <typename T, int VPT>
 __global__ void __launch_bounds__(kRowThreadsCap) rms_norm_residual_kernel(
-    float* __restrict__ residual, const __nv_bfloat16* __restrict__ delta,
-    const float* __restrict__ gamma, int hidden, float eps, __nv_bfloat16* __restrict__ normed) {
+    float* __restrict__ residual, const T* __restrict__ delta, const float* __restrict__ gamma,
+    int hidden, float eps, T* __restrict__ normed) {
   __shared__ float scratch[32];
   const int row = blockIdx.x;
   const int chunks = hidden >> 3;
   float* residual_row = residual + static_cast<size_t>(row) * hidden;
-  const __nv_bfloat16* delta_row = delta + static_cast<size_t>(row) * hidden;
+  const T* delta_row = delta + static_cast<size_t>(row) * hidden;
   float values[VPT][8];
   float squares = 0.0f;
 #pragma unroll
@@ -87,7 +90,7 @@ __global__ void __launch_bounds__(kRowThreadsCap) rms_norm_residual_kernel(
       const float4 r0 = load_stream_f4(residual_row + chunk * 8);
       const float4 r1 = load_stream_f4(residual_row + chunk * 8 + 4);
       float d[8];
-      unpack8(load_stream(delta_row + chunk * 8), d);
+      unpack8<T>(load_stream(delta_row + chunk * 8), d);
       values[k][0] = r0.x + d[0];
       values[k][1] = r0.y + d[1];
       values[k][2] = r0.z + d[2];
@@ -108,7 +111,7 @@ __global__ void __launch_bounds__(kRowThreadsCap) rms_norm_residual_kernel(
   }
   const float total = block_sum(squares, scratch);
   const float scale = rsqrtf(total / static_cast<float>(hidden) + eps);
-  __nv_bfloat16* normed_row = normed + static_cast<size_t>(row) * hidden;
+  T* normed_row = normed + static_cast<size_t>(row) * hidden;
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
     const int chunk = threadIdx.x + k * blockDim.x;
@@ -119,16 +122,19 @@ __global__ void __launch_bounds__(kRowThreadsCap) rms_norm_residual_kernel(
     float y[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) y[i] = values[k][i] * scale * g[i];
-    *reinterpret_cast<uint4*>(normed_row + chunk * 8) = pack8(y);
+    *reinterpret_cast<uint4*>(normed_row + chunk * 8) = pack8<T>(y);
   }
 }
 
 // ---------------------------------------------------------------------------------------------
 // Bias + rotary embedding, in place on the fused [tokens, (Hq + 2 Hkv) * D] projection output.
-// One thread owns 8 rotation pairs (x_i, x_{i + D/2}) of one head of one token.
-// Query and key heads get bias + rotation; value heads get the bias only (skipped without bias).
+// One thread owns 8 rotation pairs (x_i, x_{i + D/2}) at one offset of one token and walks all of
+// that token's heads, so its cos/sin values are read once; kRopeUnroll heads are loaded before
+// any is stored. Query and key heads get bias + rotation; value heads get the bias only (and
+// are skipped without bias).
 // ---------------------------------------------------------------------------------------------
-__global__ void rotary_bias_kernel(__nv_bfloat16* __restrict__ qkv, const float* __restrict__ bias,
+template <typename T>
+__global__ void rotary_bias_kernel(T* __restrict__ qkv, const float* __restrict__ bias,
                                    const int32_t* __restrict__ positions, int tokens, int query_heads,
                                    int kv_heads, int head_dim, const float* __restrict__ cos_table,
                                    const float* __restrict__ sin_table, int table_positions,
@@ -138,58 +144,74 @@ __global__ void rotary_bias_kernel(__nv_bfloat16* __restrict__ qkv, const float*
   const int rotated_heads = query_heads + kv_heads;
   const int heads = bias != nullptr ? rotated_heads + kv_heads : rotated_heads;
   const int row_width = (query_heads + 2 * kv_heads) * head_dim;
-  const long long per_token = static_cast<long long>(heads) * chunks_per_head;
-  const long long total = per_token * tokens;
+  const long long total = static_cast<long long>(tokens) * chunks_per_head;
   for (long long item = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; item < total;
        item += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int token = static_cast<int>(item / per_token);
-    const int rest = static_cast<int>(item - static_cast<long long>(token) * per_token);
-    const int head = rest / chunks_per_head;
-    const int chunk = rest - head * chunks_per_head;
-    const int column = head * head_dim + chunk * 8;
-    __nv_bfloat16* low_ptr = qkv + static_cast<size_t>(token) * row_width + column;
-    __nv_bfloat16* high_ptr = low_ptr + half;
-    float low[8];
-    float high[8];
-    unpack8(*reinterpret_cast<const uint4*>(low_ptr), low);
-    unpack8(*reinterpret_cast<const uint4*>(high_ptr), high);
-    if (bias != nullptr) {
-      const float4 b0 = __ldg(reinterpret_cast<const float4*>(bias + column));
-      const float4 b1 = __ldg(reinterpret_cast<const float4*>(bias + column + 4));
-      const float4 b2 = __ldg(reinterpret_cast<const float4*>(bias + column + half));
-      const float4 b3 = __ldg(reinterpret_cast<const float4*>(bias + column + half + 4));
-      const float bl[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-      const float bh[8] = {b2.x, b2.y, b2.z, b2.w, b3.x, b3.y, b3.z, b3.w};
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        low[i] += bl[i];
-        high[i] += bh[i];
-      }
-    }
-    if (head < rotated_heads) {
-      const int position = positions[token];
-      if (position < 0 || position >= table_positions) {
-        report_status(status, kStatusPositionOutOfRange);
-        continue;
-      }
+    const int token = static_cast<int>(item / chunks_per_head);
+    const int chunk = static_cast<int>(item - static_cast<long long>(token) * chunks_per_head);
+    const int position = positions[token];
+    const bool in_table = position >= 0 && position < table_positions;
+    if (!in_table) report_status(status, kStatusPositionOutOfRange);
+    float c[8];
+    float s[8];
+    if (in_table) {
       const float* cos_row = cos_table + static_cast<size_t>(position) * half + chunk * 8;
       const float* sin_row = sin_table + static_cast<size_t>(position) * half + chunk * 8;
       const float4 c0 = __ldg(reinterpret_cast<const float4*>(cos_row));
       const float4 c1 = __ldg(reinterpret_cast<const float4*>(cos_row + 4));
       const float4 s0 = __ldg(reinterpret_cast<const float4*>(sin_row));
       const float4 s1 = __ldg(reinterpret_cast<const float4*>(sin_row + 4));
-      const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-      const float s[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+      c[0] = c0.x; c[1] = c0.y; c[2] = c0.z; c[3] = c0.w; c[4] = c1.x; c[5] = c1.y; c[6] = c1.z; c[7] = c1.w;
+      s[0] = s0.x; s[1] = s0.y; s[2] = s0.z; s[3] = s0.w; s[4] = s1.x; s[5] = s1.y; s[6] = s1.z; s[7] = s1.w;
+    }
+    // without a valid position only the bias-only value heads are written
+    const int first_head = in_table ? 0 : rotated_heads;
+    T* row = qkv + static_cast<size_t>(token) * row_width + chunk * 8;
+    for (int h0 = first_head; h0 < heads; h0 += kRopeUnroll) {
+      uint4 low_raw[kRopeUnroll];
+      uint4 high_raw[kRopeUnroll];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float l = low[i];
-        const float h = high[i];
-        low[i] = l * c[i] - h * s[i];
-        high[i] = h * c[i] + l * s[i];
+      for (int u = 0; u < kRopeUnroll; ++u) {
+        if (h0 + u < heads) {
+          low_raw[u] = *reinterpret_cast<const uint4*>(row + (h0 + u) * head_dim);
+          high_raw[u] = *reinterpret_cast<const uint4*>(row + (h0 + u) * head_dim + half);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kRopeUnroll; ++u) {
+        const int head = h0 + u;
+        if (head >= heads) break;
+        float low[8];
+        float high[8];
+        unpack8<T>(low_raw[u], low);
+        unpack8<T>(high_raw[u], high);
+        if (bias != nullptr) {
+          const float* b = bias + head * head_dim + chunk * 8;
+          const float4 b0 = __ldg(reinterpret_cast<const float4*>(b));
+          const float4 b1 = __ldg(reinterpret_cast<const float4*>(b + 4));
+          const float4 b2 = __ldg(reinterpret_cast<const float4*>(b + half));
+          const float4 b3 = __ldg(reinterpret_cast<const float4*>(b + half + 4));
+          const float bl[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+          const float bh[8] = {b2.x, b2.y, b2.z, b2.w, b3.x, b3.y, b3.z, b3.w};
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            low[i] += bl[i];
+            high[i] += bh[i];
+          }
+        }
+        if (head < rotated_heads) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float l = low[i];
+            const float h = high[i];
+            low[i] = l * c[i] - h * s[i];
+            high[i] = h * c[i] + l * s[i];
+          }
+        }
+        *reinterpret_cast<uint4*>(row + head * head_dim) = pack8<T>(low);
+        *reinterpret_cast<uint4*>(row + head * head_dim + half) = pack8<T>(high);
       }
     }
-    *reinterpret_cast<uint4*>(low_ptr) = pack8(low);
-    *reinterpret_cast<uint4*>(high_ptr) = pack8(high);
   }
 }
 
@@ -214,24 +236,41 @@ __global__ void rope_table_kernel(float* __restrict__ cos_out, float* __restrict
 // SwiGLU: a = silu(g) * u with g, u read through arbitrary row strides (the fused gate|up GEMM
 // output has g in columns [0, I) and u in [I, 2I) of each row).
 // ---------------------------------------------------------------------------------------------
-__global__ void silu_multiply_kernel(const __nv_bfloat16* __restrict__ gate,
-                                     const __nv_bfloat16* __restrict__ up, long long in_stride,
-                                     __nv_bfloat16* __restrict__ out, long long out_stride, int tokens,
-                                     int width) {
+template <typename T>
+__global__ void silu_multiply_kernel(const T* __restrict__ gate, const T* __restrict__ up, long long in_stride,
+                                     T* __restrict__ out, long long out_stride, int tokens, int width) {
   const int chunks = width >> 3;
   const long long total = static_cast<long long>(tokens) * chunks;
-  for (long long item = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; item < total;
-       item += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long token = item / chunks;
-    const int chunk = static_cast<int>(item - token * chunks);
-    float g[8];
-    float u[8];
-    unpack8(load_stream(gate + token * in_stride + chunk * 8), g);
-    unpack8(load_stream(up + token * in_stride + chunk * 8), u);
-    float a[8];
+  const long long threads = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long first = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; first < total;
+       first += threads * kSiluUnroll) {
+    uint4 g_raw[kSiluUnroll];
+    uint4 u_raw[kSiluUnroll];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) a[i] = (g[i] / (1.0f + __expf(-g[i]))) * u[i];
-    __stcs(reinterpret_cast<uint4*>(out + token * out_stride + chunk * 8), pack8(a));
+    for (int k = 0; k < kSiluUnroll; ++k) {
+      const long long item = first + k * threads;
+      if (item < total) {
+        const long long token = item / chunks;
+        const int chunk = static_cast<int>(item - token * chunks);
+        g_raw[k] = load_stream(gate + token * in_stride + chunk * 8);
+        u_raw[k] = load_stream(up + token * in_stride + chunk * 8);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kSiluUnroll; ++k) {
+      const long long item = first + k * threads;
+      if (item >= total) break;
+      const long long token = item / chunks;
+      const int chunk = static_cast<int>(item - token * chunks);
+      float g[8];
+      float u[8];
+      unpack8<T>(g_raw[k], g);
+      unpack8<T>(u_raw[k], u);
+      float a[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) a[i] = (g[i] / (1.0f + __expf(-g[i]))) * u[i];
+      __stcs(reinterpret_cast<uint4*>(out + token * out_stride + chunk * 8), pack8<T>(a));
+    }
   }
 }
 
@@ -279,52 +318,83 @@ static int stride_grid(long long items, int threads, int ctas_per_sm) {
   return static_cast<int>(needed < cap ? (needed > 0 ? needed : 1) : cap);
 }
 
-cudaError_t launch_embed_rms_norm(const int32_t* token_ids, int tokens, const void* table, int vocab,
-                                  int hidden, const float* gamma, float eps, float* residual,
-                                  void* normed, int* status, cudaStream_t stream) {
-  if (tokens <= 0) return cudaSuccess;
+template <typename T>
+cudaError_t embed_typed(const int32_t* token_ids, int tokens, const void* table, int vocab, int hidden,
+                        const float* gamma, float eps, float* residual, void* normed, int* status,
+                        cudaStream_t stream) {
   int vpt = 1;
   const int threads = row_threads(hidden, &vpt);
-  const auto* t = static_cast<const __nv_bfloat16*>(table);
-  auto* n = static_cast<__nv_bfloat16*>(normed);
+  const auto* t = static_cast<const T*>(table);
+  auto* n = static_cast<T*>(normed);
   switch (vpt) {
-    case 1: embed_rms_norm_kernel<1><<<tokens, threads, 0, stream>>>(token_ids, t, vocab, hidden, gamma, eps, residual, n, status); break;
-    case 2: embed_rms_norm_kernel<2><<<tokens, threads, 0, stream>>>(token_ids, t, vocab, hidden, gamma, eps, residual, n, status); break;
-    case 3: embed_rms_norm_kernel<3><<<tokens, threads, 0, stream>>>(token_ids, t, vocab, hidden, gamma, eps, residual, n, status); break;
-    case 4: embed_rms_norm_kernel<4><<<tokens, threads, 0, stream>>>(token_ids, t, vocab, hidden, gamma, eps, residual, n, status); break;
+    case 1: embed_rms_norm_kernel<T, 1><<<tokens, threads, 0, stream>>>(token_ids, t, vocab, hidden, gamma, eps, residual, n, status); break;
+    case 2: embed_rms_norm_kernel<T, 2><<<tokens, threads, 0, stream>>>(token_ids, t, vocab, hidden, gamma, eps, residual, n, status); break;
+    case 3: embed_rms_norm_kernel<T, 3><<<tokens, threads, 0, stream>>>(token_ids, t, vocab, hidden, gamma, eps, residual, n, status); break;
+    case 4: embed_rms_norm_kernel<T, 4><<<tokens, threads, 0, stream>>>(token_ids, t, vocab, hidden, gamma, eps, residual, n, status); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
 }
 
-cudaError_t launch_rms_norm_residual(float* residual, const void* delta, const float* gamma, int tokens,
-                                     int hidden, float eps, void* normed, cudaStream_t stream) {
-  if (tokens <= 0) return cudaSuccess;
+template <typename T>
+cudaError_t norm_typed(float* residual, const void* delta, const float* gamma, int tokens, int hidden, float eps,
+                       void* normed, cudaStream_t stream) {
   int vpt = 1;
   const int threads = row_threads(hidden, &vpt);
-  const auto* d = static_cast<const __nv_bfloat16*>(delta);
-  auto* n = static_cast<__nv_bfloat16*>(normed);
+  const auto* d = static_cast<const T*>(delta);
+  auto* n = static_cast<T*>(normed);
   switch (vpt) {
-    case 1: rms_norm_residual_kernel<1><<<tokens, threads, 0, stream>>>(residual, d, gamma, hidden, eps, n); break;
-    case 2: rms_norm_residual_kernel<2><<<tokens, threads, 0, stream>>>(residual, d, gamma, hidden, eps, n); break;
-    case 3: rms_norm_residual_kernel<3><<<tokens, threads, 0, stream>>>(residual, d, gamma, hidden, eps, n); break;
-    case 4: rms_norm_residual_kernel<4><<<tokens, threads, 0, stream>>>(residual, d, gamma, hidden, eps, n); break;
+    case 1: rms_norm_residual_kernel<T, 1><<<tokens, threads, 0, stream>>>(residual, d, gamma, hidden, eps, n); break;
+    case 2: rms_norm_residual_kernel<T, 2><<<tokens, threads, 0, stream>>>(residual, d, gamma, hidden, eps, n); break;
+    case 3: rms_norm_residual_kernel<T, 3><<<tokens, threads, 0, stream>>>(residual, d, gamma, hidden, eps, n); break;
+    case 4: rms_norm_residual_kernel<T, 4><<<tokens, threads, 0, stream>>>(residual, d, gamma, hidden, eps, n); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
+}
+
+cudaError_t launch_embed_rms_norm(const int32_t* token_ids, int tokens, const void* table, int vocab,
+                                  int hidden, const float* gamma, float eps, float* residual,
+                                  void* normed, int* status, int dtype, cudaStream_t stream) {
+  if (tokens <= 0) return cudaSuccess;
+  if (hidden % 8 != 0 || hidden > 8 * 4 * kRowThreadsCap) return cudaErrorInvalidValue;
+  if (dtype == kActFp16)
+    return embed_typed<__half>(token_ids, tokens, table, vocab, hidden, gamma, eps, residual, normed, status, stream);
+  if (dtype == kActBf16)
+    return embed_typed<__nv_bfloat16>(token_ids, tokens, table, vocab, hidden, gamma, eps, residual, normed, status,
+                                      stream);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_rms_norm_residual(float* residual, const void* delta, const float* gamma, int tokens,
+                                     int hidden, float eps, void* normed, int dtype, cudaStream_t stream) {
+  if (tokens <= 0) return cudaSuccess;
+  if (hidden % 8 != 0 || hidden > 8 * 4 * kRowThreadsCap) return cudaErrorInvalidValue;
+  if (dtype == kActFp16) return norm_typed<__half>(residual, delta, gamma, tokens, hidden, eps, normed, stream);
+  if (dtype == kActBf16) return norm_typed<__nv_bfloat16>(residual, delta, gamma, tokens, hidden, eps, normed, stream);
+  return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_rotary_bias(void* qkv, const float* bias, const int32_t* positions, int tokens,
                                int query_heads, int kv_heads, int head_dim, const float* cos_table,
-                               const float* sin_table, int table_positions, int* status,
+                               const float* sin_table, int table_positions, int* status, int dtype,
                                cudaStream_t stream) {
   if (tokens <= 0) return cudaSuccess;
-  const int heads = query_heads + kv_heads + (bias != nullptr ? kv_heads : 0);
-  const long long items = static_cast<long long>(tokens) * heads * (head_dim / 16);
+  if (head_dim % 16 != 0) return cudaErrorInvalidValue;
+  const long long items = static_cast<long long>(tokens) * (head_dim / 16);
   const int threads = 256;
-  rotary_bias_kernel<<<stride_grid(items, threads, 8), threads, 0, stream>>>(
-      static_cast<__nv_bfloat16*>(qkv), bias, positions, tokens, query_heads, kv_heads, head_dim,
-      cos_table, sin_table, table_positions, status);
+  const int grid = stride_grid(items, threads, 8);
+  if (dtype == kActFp16) {
+    rotary_bias_kernel<__half><<<grid, threads, 0, stream>>>(static_cast<__half*>(qkv), bias, positions, tokens,
+                                                             query_heads, kv_heads, head_dim, cos_table, sin_table,
+                                                             table_positions, status);
+  } else if (dtype == kActBf16) {
+    rotary_bias_kernel<__nv_bfloat16><<<grid, threads, 0, stream>>>(
+        static_cast<__nv_bfloat16*>(qkv), bias, positions, tokens, query_heads, kv_heads, head_dim, cos_table,
+        sin_table, table_positions, status);
+  } else {
+    return cudaErrorInvalidValue;
+  }
   return cudaGetLastError();
 }
 
@@ -338,13 +408,22 @@ cudaError_t launch_rope_table(float* cos_out, float* sin_out, int positions, int
 }
 
 cudaError_t launch_silu_multiply(const void* gate, const void* up, long long in_stride, void* out,
-                                 long long out_stride, int tokens, int width, cudaStream_t stream) {
+                                 long long out_stride, int tokens, int width, int dtype, cudaStream_t stream) {
   const long long items = static_cast<long long>(tokens) * (width / 8);
   if (items <= 0) return cudaSuccess;
   const int threads = 256;
-  silu_multiply_kernel<<<stride_grid(items, threads, 8), threads, 0, stream>>>(
-      static_cast<const __nv_bfloat16*>(gate), static_cast<const __nv_bfloat16*>(up), in_stride,
-      static_cast<__nv_bfloat16*>(out), out_stride, tokens, width);
+  const int grid = stride_grid((items + kSiluUnroll - 1) / kSiluUnroll, threads, 8);
+  if (dtype == kActFp16) {
+    silu_multiply_kernel<__half><<<grid, threads, 0, stream>>>(static_cast<const __half*>(gate),
+                                                               static_cast<const __half*>(up), in_stride,
+                                                               static_cast<__half*>(out), out_stride, tokens, width);
+  } else if (dtype == kActBf16) {
+    silu_multiply_kernel<__nv_bfloat16><<<grid, threads, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(gate), static_cast<const __nv_bfloat16*>(up), in_stride,
+        static_cast<__nv_bfloat16*>(out), out_stride, tokens, width);
+  } else {
+    return cudaErrorInvalidValue;
+  }
   return cudaGetLastError();
 }
 

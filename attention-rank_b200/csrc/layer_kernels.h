@@ -6,35 +6,38 @@
 
 #include <cstdint>
 
+#include "common.cuh"
+
 namespace arb {
 
 int sm_count();
 
 cudaError_t launch_embed_rms_norm(const int32_t* token_ids, int tokens, const void* table, int vocab,
                                   int hidden, const float* gamma, float eps, float* residual,
-                                  void* normed, int* status, cudaStream_t stream);
+                                  void* normed, int* status, int dtype, cudaStream_t stream);
 
 cudaError_t launch_rms_norm_residual(float* residual, const void* delta, const float* gamma, int tokens,
-                                     int hidden, float eps, void* normed, cudaStream_t stream);
+                                     int hidden, float eps, void* normed, int dtype, cudaStream_t stream);
 
 cudaError_t launch_rotary_bias(void* qkv, const float* bias, const int32_t* positions, int tokens,
                                int query_heads, int kv_heads, int head_dim, const float* cos_table,
-                               const float* sin_table, int table_positions, int* status,
+                               const float* sin_table, int table_positions, int* status, int dtype,
                                cudaStream_t stream);
 
 cudaError_t launch_rope_table(float* cos_out, float* sin_out, int positions, int head_dim, float theta,
                               cudaStream_t stream);
 
 cudaError_t launch_silu_multiply(const void* gate, const void* up, long long in_stride, void* out,
-                                 long long out_stride, int tokens, int width, cudaStream_t stream);
+                                 long long out_stride, int tokens, int width, int dtype, cudaStream_t stream);
 
 cudaError_t launch_positions(const int32_t* prompt_offsets, int prompt_count, int tokens,
                              int32_t* positions, cudaStream_t stream);
 
-// Causal prefill attention over packed prompts (attention.cu).
+// Causal prefill attention over packed prompts: attention_tc.cu (tcgen05, the engine's kernel)
+// and attention.cu (mma.sync, kept as the alternative).
 struct AttentionArgs {
-  const void* qkv = nullptr;        // bf16 [tokens, (Hq + 2 Hkv) * D], Q | K | V column blocks
-  void* out = nullptr;              // bf16 [tokens, Hq * D]
+  const void* qkv = nullptr;        // 16-bit [tokens, (Hq + 2 Hkv) * D], Q | K | V column blocks
+  void* out = nullptr;              // 16-bit [tokens, Hq * D]
   float* lse = nullptr;             // fp32 [tokens, Hq], log2-domain log-sum-exp of scaled scores
   const int32_t* prompt_offsets = nullptr;  // [prompts + 1]
   const int32_t* tiles = nullptr;   // [tile_count * 2] (prompt, query tile) pairs, heaviest first
@@ -43,8 +46,12 @@ struct AttentionArgs {
   int kv_heads = 0;
   int head_dim = 0;
   int sliding_window = 0;           // 0 = unlimited
+  int dtype = kActFp16;             // ActivationType of qkv and out
+  int rows = 0;                     // rows of qkv (tensor-map extent; tcgen05 kernel)
+  int* status = nullptr;            // device status word (tcgen05 kernel: wait timeouts)
 };
 cudaError_t launch_causal_attention(const AttentionArgs& args, cudaStream_t stream);
+cudaError_t launch_causal_attention_tc(const AttentionArgs& args, cudaStream_t stream);
 constexpr int kAttentionQueryTile = 128;
 
 // Query->document attention mass (mass.cu).
@@ -67,6 +74,7 @@ struct MassArgs {
   int normalize_by_length = 0;
   float* partials = nullptr;        // fp32 [item_count, span_count]
   int* status = nullptr;
+  int dtype = kActFp16;             // ActivationType of qkv
 };
 cudaError_t launch_document_mass(const MassArgs& args, cudaStream_t stream);
 constexpr int kMassRowTile = 128;   // GQA-stacked query rows per CTA
@@ -99,9 +107,13 @@ struct FinalizeArgs {
 };
 cudaError_t launch_finalize_mass(const FinalizeArgs& args, cudaStream_t stream);
 
-// Seeded synthetic weights (synthetic.cu).
-cudaError_t launch_synthetic_fill(void* dst_bf16, long long count, uint64_t key, float scale,
+// Seeded synthetic weights (synthetic.cu): the bf16 value of every element, stored as bf16 or
+// converted (exactly representable or round-to-nearest-even) to fp16.
+cudaError_t launch_synthetic_fill(void* dst, long long count, uint64_t key, float scale, int dtype,
                                   cudaStream_t stream);
+// In-place-free conversions used when uploading host weights.
+cudaError_t launch_bf16_to_fp16(const void* src, void* dst, long long count, cudaStream_t stream);
+cudaError_t launch_f32_to_activation(const float* src, void* dst, long long count, int dtype, cudaStream_t stream);
 cudaError_t launch_synthetic_fill_f32(float* dst, long long count, uint64_t key, float scale,
                                       float offset, cudaStream_t stream);
 

@@ -10,7 +10,7 @@
 //
 // B200 design. One CTA = (prompt, KV head, 128-row tile of GQA-stacked query rows, a run of
 // 128-key tiles). Q and K tiles arrive by TMA (128B swizzle, no multicast) into shared memory,
-// one elected thread issues tcgen05.mma (M=128, N=128, K=16 x 8, bf16 -> fp32) into a TMEM
+// one elected thread issues tcgen05.mma (M=128, N=128, K=16 x 8, fp16 or bf16 -> fp32) into a TMEM
 // accumulator, double-buffered so the MMA and TMA of tile j+1 overlap the epilogue of tile j.
 // The epilogue (4 warps, one TMEM lane = one query row per thread) turns raw scores into
 // probabilities with the row's log-sum-exp produced by the attention kernel, p = 2^(s*c - lse2),
@@ -35,8 +35,8 @@ namespace {
 constexpr int kThreads = 128;
 constexpr int kHeadDim = 128;
 constexpr uint32_t kTmemColumns = 256;          // two 128-column fp32 accumulators
-constexpr uint32_t kHalfTileBytes = 128 * 128;  // 128 rows x 64 bf16 (one 128B-swizzled column half)
-constexpr uint32_t kTileBytes = 2 * kHalfTileBytes;  // 128 rows x 128 bf16
+constexpr uint32_t kHalfTileBytes = 128 * 128;  // 128 rows x 64 16-bit values (one 128B-swizzled half)
+constexpr uint32_t kTileBytes = 2 * kHalfTileBytes;  // 128 rows x 128 16-bit values
 constexpr uint32_t kQBoxRows = 8;
 constexpr uint32_t kSpinLimit = 1u << 24;
 
@@ -107,19 +107,23 @@ __device__ __forceinline__ uint64_t smem_descriptor(uint32_t address) {
   return desc;
 }
 
-// kind::f16 instruction descriptor: bf16 x bf16 -> fp32, both operands K-major, M=128, N=128.
-constexpr uint32_t kInstrDesc = (1u << 4)            // D format fp32
-                                | (1u << 7)          // A format bf16
-                                | (1u << 10)         // B format bf16
-                                | ((128u >> 3) << 17)  // N
-                                | ((128u >> 4) << 24);  // M
+// kind::f16 instruction descriptor: fp32 accumulator, both operands K-major, M=128, N=128, A and B
+// of the same 16-bit format (0 = fp16, 1 = bf16).
+constexpr uint32_t instr_desc(uint32_t format) {
+  return (1u << 4)              // D format fp32
+         | (format << 7)        // A format
+         | (format << 10)       // B format
+         | ((128u >> 3) << 17)  // N
+         | ((128u >> 4) << 24);  // M
+}
 
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t a_desc, uint64_t b_desc, uint32_t accumulate) {
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
-      ::"r"(tmem_d), "l"(a_desc), "l"(b_desc), "r"(kInstrDesc), "r"(accumulate),
+      ::"r"(tmem_d), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate),
         "r"(0u), "r"(0u), "r"(0u), "r"(0u));
 }
 
@@ -160,6 +164,7 @@ struct KernelArgs {
   int normalize_by_length;
   float* partials;
   int* status;
+  uint32_t instr_desc;
 };
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -258,8 +263,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int kk = 0; kk < kHeadDim / 16; ++kk) {
       const uint32_t offset = (kk >> 2) * kHalfTileBytes + (kk & 3) * 32;
-      umma_bf16(tmem + stage * 128, smem_descriptor(q_smem + offset),
-                smem_descriptor(k_smem + stage * kTileBytes + offset), kk > 0 ? 1u : 0u);
+      umma_f16(tmem + stage * 128, smem_descriptor(q_smem + offset),
+               smem_descriptor(k_smem + stage * kTileBytes + offset), args.instr_desc, kk > 0 ? 1u : 0u);
     }
     umma_commit(mma_bar[stage]);
   };
@@ -450,14 +455,16 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-bool encode_rows_map(CUtensorMap* map, const void* base, int width, int rows, int box_rows) {
+bool encode_rows_map(CUtensorMap* map, const void* base, int width, int rows, int box_rows, int dtype) {
   PFN_cuTensorMapEncodeTiled_v12000 encode = encode_fn();
   if (encode == nullptr) return false;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(rows)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(width) * 2};
   const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
   const cuuint32_t element_strides[2] = {1, 1};
-  const CUresult status = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+  const CUtensorMapDataType type =
+      dtype == kActFp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const CUresult status = encode(map, type, 2, const_cast<void*>(base), dims, strides,
                                  box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return status == CUDA_SUCCESS;
@@ -473,10 +480,11 @@ cudaError_t launch_document_mass(const MassArgs& args, cudaStream_t stream) {
   }
   const int width = (args.query_heads + 2 * args.kv_heads) * kHeadDim;
   if ((reinterpret_cast<uintptr_t>(args.qkv) & 15) != 0) return cudaErrorInvalidValue;
+  if (args.dtype != kActFp16 && args.dtype != kActBf16) return cudaErrorInvalidValue;
   CUtensorMap q_map;
   CUtensorMap k_map;
-  if (!encode_rows_map(&q_map, args.qkv, width, args.qkv_rows_capacity, kQBoxRows) ||
-      !encode_rows_map(&k_map, args.qkv, width, args.qkv_rows_capacity, kMassKeyTile)) {
+  if (!encode_rows_map(&q_map, args.qkv, width, args.qkv_rows_capacity, kQBoxRows, args.dtype) ||
+      !encode_rows_map(&k_map, args.qkv, width, args.qkv_rows_capacity, kMassKeyTile, args.dtype)) {
     return cudaErrorInvalidValue;
   }
   int device = 0;
@@ -503,6 +511,7 @@ cudaError_t launch_document_mass(const MassArgs& args, cudaStream_t stream) {
   kernel_args.normalize_by_length = args.normalize_by_length;
   kernel_args.partials = args.partials;
   kernel_args.status = args.status;
+  kernel_args.instr_desc = instr_desc(args.dtype == kActFp16 ? 0u : 1u);
   document_mass_kernel<<<args.item_count, kThreads, kSmemBytes, stream>>>(q_map, k_map, kernel_args);
   return cudaGetLastError();
 }

@@ -58,12 +58,13 @@ void set_last_error(const std::string& message);  // capi.cu: the message ar_las
 
 }  // namespace arb
 
-extern "C" int ar_document_attention_mass_noalloc(const void* qkv_bf16, int qkv_rows, const float* lse,
+extern "C" int ar_document_attention_mass_noalloc(const void* qkv, int qkv_rows, const float* lse,
                                                   const int32_t* prompt_offsets_host, int prompt_count,
                                                   const int32_t* query_spans_host, const int32_t* spans_host,
                                                   int span_count, int query_heads, int kv_heads, int head_dim,
                                                   int sliding_window, int prefill_chunk_tokens,
-                                                  int normalize_by_length, double* mass_out, void* stream) {
+                                                  int normalize_by_length, double* mass_out, int dtype,
+                                                  void* stream) {
   using namespace arb;
   try {
     if (prompt_count <= 0 || span_count <= 0 || span_count > kMassMaxSpans) {
@@ -123,7 +124,8 @@ extern "C" int ar_document_attention_mass_noalloc(const void* qkv_bf16, int qkv_
     check_cuda(cudaMemcpyAsync(meta_device, meta.data(), meta.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s),
                "metadata upload");
     MassArgs args;
-    args.qkv = qkv_bf16;
+    args.qkv = qkv;
+    args.dtype = dtype;
     args.qkv_rows_capacity = qkv_rows;
     args.lse = lse;
     args.prompt_offsets = meta_device;

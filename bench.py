@@ -1,8 +1,8 @@
 #!/usr/bin/env python
 """Layer-scan throughput of the attention-profiling path on B200 (prompts/s).
 
-Workload: the Qwen2.5-7B architecture with seeded random-init bf16
-weights, 400 seeded synthetic prompts (5 documents of U[120, 240] random token ids + a 40-token
+Workload: the Qwen2.5-7B architecture with seeded random-init weights
+(bf16 values, held as fp16 -- the reference's GEMM operand type -- unless --dtype bf16), 400 seeded synthetic prompts (5 documents of U[120, 240] random token ids + a 40-token
 question), a full layer scan (prefill with per-layer query->document mass capture, cross-prompt
 accumulation, all-reduce, basin pick with min_edge_ratio 1.3). One step = the whole 400-prompt
 scan, sharded across N GPUs (strong scaling).
@@ -54,6 +54,9 @@ def parse_args():
     parser.add_argument("--kernels-only", action="store_true",
                         help="only the per-kernel roofline timing (about 3 GB of device memory; for ncu captures)")
     parser.add_argument("--kernel-tokens", type=int, default=16384)
+    parser.add_argument("--dtype", choices=["fp16", "bf16"], default="fp16",
+                        help="16-bit type of weights, GEMM operands and activations")
+    parser.add_argument("--attention", choices=["tcgen05", "mma"], default="tcgen05")
     return parser.parse_args()
 
 
@@ -169,11 +172,17 @@ def barrier(world: int):
 # ---------------------------------------------------------------------------------------------
 # per-kernel roofline timing (live, CUDA events, on the engine's kernels through the C ABI)
 # ---------------------------------------------------------------------------------------------
-def kernel_rooflines(config, hbm_peak, tensor_peak, tokens: int = 16384, repeats: int = 20) -> dict:
+def kernel_rooflines(config, hbm_peak, tensor_peak, tokens: int = 16384, repeats: int = 20,
+                     dtype: str = "fp16") -> dict:
+    """Each kernel timed alone (CUDA events over `repeats` back-to-back launches, 3 warm-up
+    launches) on a 16K-token batch; work per launch is the algorithmic HBM bytes or FLOPs."""
     import ctypes
 
     import torch
     from attnrank import _native
+
+    half = torch.float16 if dtype == "fp16" else torch.bfloat16
+    code = _native.DTYPE_F16 if dtype == "fp16" else _native.DTYPE_BF16
 
     lib = _native.lib
     dev = torch.device("cuda")
@@ -208,33 +217,33 @@ def kernel_rooflines(config, hbm_peak, tensor_peak, tokens: int = 16384, repeats
         results[name] = entry
 
     residual = torch.randn(tokens, H, device=dev, generator=gen)
-    delta = torch.randn(tokens, H, device=dev, generator=gen).to(torch.bfloat16)
+    delta = torch.randn(tokens, H, device=dev, generator=gen).to(half)
     gamma = torch.ones(H, device=dev)
-    normed = torch.empty(tokens, H, device=dev, dtype=torch.bfloat16)
+    normed = torch.empty(tokens, H, device=dev, dtype=half)
     timed("rms_norm_residual", lambda: _native.check(lib.ar_rms_norm_residual(
-        P(residual), P(delta), P(gamma), tokens, H, 1e-6, P(normed), s)), bytes_moved=12 * tokens * H + 4 * H)
+        P(residual), P(delta), P(gamma), tokens, H, 1e-6, P(normed), code, s)), bytes_moved=12 * tokens * H + 4 * H)
 
-    table = (torch.randn(V, H, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+    table = (torch.randn(V, H, device=dev, generator=gen) * 0.02).to(half)
     ids = torch.randint(0, V, (tokens,), device=dev, dtype=torch.int32, generator=gen)
     timed("embedding_rms_norm", lambda: _native.check(lib.ar_embedding_rms_norm(
-        P(ids), tokens, P(table), V, H, P(gamma), 1e-6, P(residual), P(normed), None, s)),
+        P(ids), tokens, P(table), V, H, P(gamma), 1e-6, P(residual), P(normed), None, code, s)),
         bytes_moved=tokens * (2 * H + 4 * H + 2 * H + 4))
     del table
 
-    qkv = torch.randn(tokens, W, device=dev, generator=gen).to(torch.bfloat16)
+    qkv = torch.randn(tokens, W, device=dev, generator=gen).to(half)
     bias = torch.zeros(W, device=dev)
     cos = torch.empty(8192, D // 2, device=dev)
     sin = torch.empty_like(cos)
     _native.check(lib.ar_rope_table(P(cos), P(sin), 8192, D, config.rope_theta, s))
     positions = (torch.arange(tokens, device=dev, dtype=torch.int32) % 940).contiguous()
     timed("rotary_bias", lambda: _native.check(lib.ar_rotary_embedding(
-        P(qkv), P(bias), P(positions), tokens, Hq, Hkv, D, P(cos), P(sin), 8192, None, s)),
+        P(qkv), P(bias), P(positions), tokens, Hq, Hkv, D, P(cos), P(sin), 8192, None, code, s)),
         bytes_moved=4 * tokens * W)
 
-    gate_up = torch.randn(tokens, 2 * I, device=dev, generator=gen).to(torch.bfloat16)
-    act = torch.empty(tokens, I, device=dev, dtype=torch.bfloat16)
+    gate_up = torch.randn(tokens, 2 * I, device=dev, generator=gen).to(half)
+    act = torch.empty(tokens, I, device=dev, dtype=half)
     timed("silu_multiply", lambda: _native.check(lib.ar_silu_multiply(
-        P(gate_up), ctypes.c_void_p(gate_up.data_ptr() + 2 * I), 2 * I, P(act), I, tokens, I, s)),
+        P(gate_up), ctypes.c_void_p(gate_up.data_ptr() + 2 * I), 2 * I, P(act), I, tokens, I, code, s)),
         bytes_moved=6 * tokens * I)
     del gate_up, act
 
@@ -245,13 +254,16 @@ def kernel_rooflines(config, hbm_peak, tensor_peak, tokens: int = 16384, repeats
     import numpy as np
     offsets = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
     total = int(offsets[-1])
-    qkv2 = (torch.randn(total, W, device=dev, generator=gen)).to(torch.bfloat16)
-    out = torch.empty(total, Hq * D, device=dev, dtype=torch.bfloat16)
+    qkv2 = (torch.randn(total, W, device=dev, generator=gen)).to(half)
+    out = torch.empty(total, Hq * D, device=dev, dtype=half)
     lse = torch.empty(total, Hq, device=dev)
     offsets_d = torch.from_numpy(offsets).to(dev)
     attention_flops = sum(2 * Hq * D * T * (T + 1) for T in lengths)
-    timed("causal_attention", lambda: _native.check(lib.ar_causal_attention(
-        P(qkv2), P(out), P(lse), offsets.ctypes.data, P(offsets_d), len(lengths), Hq, Hkv, D, 0, s)),
+    timed("causal_attention_mma (incl. host tile list + sync)", lambda: _native.check(lib.ar_causal_attention_mma(
+        P(qkv2), P(out), P(lse), offsets.ctypes.data, P(offsets_d), len(lengths), Hq, Hkv, D, 0, code, s)),
+        flops=attention_flops)
+    timed("causal_attention (incl. host tile list + sync)", lambda: _native.check(lib.ar_causal_attention(
+        P(qkv2), P(out), P(lse), offsets.ctypes.data, P(offsets_d), len(lengths), Hq, Hkv, D, 0, code, s)),
         flops=attention_flops)
     qs = np.ascontiguousarray(np.array([(p.query_span.begin, p.query_span.end) for p in prompts], np.int32).reshape(-1))
     sp = np.ascontiguousarray(np.array([[(d.begin, d.end) for d in p.document_spans] for p in prompts],
@@ -260,7 +272,7 @@ def kernel_rooflines(config, hbm_peak, tensor_peak, tokens: int = 16384, repeats
     mass_flops = sum(2 * Hq * (p.query_span.end - p.query_span.begin) * p.document_spans[-1].end * D for p in prompts)
     timed("document_mass (incl. host planning + sync)", lambda: _native.check(lib.ar_document_attention_mass(
         P(qkv2), total, P(lse), offsets.ctypes.data, len(prompts), qs.ctypes.data, sp.ctypes.data, 5, Hq, Hkv, D, 0,
-        512, 0, mass.ctypes.data, s)), flops=mass_flops)
+        512, 0, mass.ctypes.data, code, s)), flops=mass_flops)
     torch.cuda.synchronize()
     return results
 
@@ -299,7 +311,8 @@ def run_b200(args, rank, world, local_rank):
 
     config = synthetic.qwen2_7b()
     prompts = synthetic.prompts(args.prompts, config.vocab_size)
-    options = ar.RuntimeOptions(device_index=local_rank, max_sequence_length=4096, max_batch_tokens=args.batch_tokens)
+    options = ar.RuntimeOptions(device_index=local_rank, max_sequence_length=4096, max_batch_tokens=args.batch_tokens,
+                                activation_dtype=args.dtype, attention_kernel=args.attention)
     engine = ar.Engine.synthetic(config, seed=0, options=options)
     shard = shard_by_length([len(p.tokens) for p in prompts], world)[rank]
     mine = [prompts[i] for i in shard]
@@ -337,6 +350,13 @@ def run_b200(args, rank, world, local_rank):
     ms_per_step = elapsed_ms / args.steps
     value = args.prompts / (ms_per_step / 1000.0)
 
+    # one more (untimed) step with every engine launch bracketed by CUDA events: per-kernel
+    # device time and algorithmic work inside the real scan, and the count of our own launches
+    engine.set_kernel_timing(True)
+    step()
+    timing = engine.kernel_timing()
+    engine.set_kernel_timing(False)
+
     # the scan result of the timed steps: accumulator of the last step -> profiles, basin pick
     accumulated = accumulator.double().cpu().numpy().reshape(L, slots)
     profiles = [ar.AttentionProfile.from_accumulated("synthetic", l, args.prompts, accumulated[l]) for l in range(L)]
@@ -362,8 +382,29 @@ def run_b200(args, rank, world, local_rank):
     flops = scan_flops(config, prompts)
     achieved_tflops = flops / (ms_per_step / 1000.0) / 1e12
     tensor_peak = peak.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
-    launches_per_batch = 2 + L * 6 + 1
-    gpu_launches = args.steps * launches_per_batch * len(prepared_batches(prepared, args.batch_tokens, mine))
+    hbm_peak = peak.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+    timed_ms = sum(entry["ms"] for entry in timing.values()) or 1.0
+    kernels = {}
+    for name, entry in timing.items():
+        if entry["launches"] == 0:
+            continue
+        seconds = entry["ms"] / 1000.0
+        library = name.startswith("gemm_")
+        record = {"launches_per_step": entry["launches"],
+                  "us_per_launch": round(entry["ms"] * 1000.0 / entry["launches"], 2),
+                  "share_of_step": round(entry["ms"] / timed_ms, 4), "library": library}
+        if entry["tensor"]:
+            achieved = entry["work"] / seconds / 1e12 if seconds > 0 else 0.0
+            record.update({"bound": "tensor", "achieved": round(achieved, 1), "unit": "TFLOP/s",
+                           "frac": round(achieved / tensor_peak, 4)})
+        else:
+            achieved = entry["work"] / seconds / 1e9 if seconds > 0 else 0.0
+            record.update({"bound": "hbm", "achieved": round(achieved, 1), "unit": "GB/s",
+                           "frac": round(achieved / hbm_peak, 4)})
+        kernels[name] = record
+    own_launches_per_step = sum(entry["launches"] for name, entry in timing.items() if not name.startswith("gemm_"))
+    gpu_launches = args.steps * own_launches_per_step
+    dominant = max((n for n in kernels), key=lambda n: kernels[n]["share_of_step"])
     result = {
         "metric": METRIC,
         "value": round(value, 3),
@@ -375,8 +416,9 @@ def run_b200(args, rank, world, local_rank):
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
-        "dtype": "bf16",
-        "data": "synthetic (seeded random-init bf16 weights, seeded random token-id prompts)",
+        "dtype": args.dtype,
+        "data": "synthetic (seeded random-init weights: bf16 values, stored in the compute dtype; seeded random "
+                "token-id prompts)",
         "config": {"workload": "layer scan, Qwen2.5-7B architecture, 400 prompts x (5 docs U[120,240] + 40-token "
                                "question), min_edge_ratio 1.3", "global_batch": args.prompts,
                    "seq_len": round(sum(len(p.tokens) for p in prompts) / len(prompts), 1),
@@ -389,36 +431,28 @@ def run_b200(args, rank, world, local_rank):
                 "d2h_bytes_per_step": int(d2h), "selected_layer": scan.selected_layer,
                 "api": "attnrank.scheduler.ProbeScheduler.find_shallowest_attention_layer"},
         "roofline": {"bound": "tensor", "kernel": "whole scan step (cuBLASLt GEMMs + attention + mass)",
+                     "dominant_kernel": dominant,
                      "achieved": round(achieved_tflops, 1), "peak": tensor_peak, "unit": "TFLOP/s",
                      "frac": round(achieved_tflops / tensor_peak, 4), "traffic": None,
                      "peak_source": f"{peak_kind} bf16_tflops_sustained",
                      "algorithmic_flops_per_step": flops},
         "clocks": clocks,
         "gpu_launches": gpu_launches,
+        "attention_kernel": args.attention,
+        "kernels": kernels,
+        "kernels_peak_source": f"{peak_kind}: hbm_gbs for HBM-bound, bf16_tflops_sustained for tensor-bound; "
+                               "CUDA events around every launch on the engine stream during one extra step",
     }
     if rank == 0 and not args.no_kernels:
-        result["kernels"] = kernel_rooflines(config, peak.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]),
-                                             peak.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
-        result["kernels_peak_source"] = f"{peak_kind} hbm_gbs / bf16_tflops (burst)"
+        result["kernels_isolated"] = kernel_rooflines(config, hbm_peak, peak.get("bf16_tflops",
+                                                                                 FALLBACK_PEAKS["bf16_tflops"]),
+                                                      dtype=args.dtype)
+        result["kernels_isolated_peak_source"] = f"{peak_kind} hbm_gbs / bf16_tflops (burst)"
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(config, prompts[0])
     del prepared
     engine.close()
     return result
-
-
-def prepared_batches(prepared, batch_tokens, prompts):
-    batches, tokens, count = [], 0, 0
-    for p in prompts:
-        t = len(p.tokens)
-        if count and (tokens + t > batch_tokens or count + 1 > 256):
-            batches.append(count)
-            tokens, count = 0, 0
-        tokens += t
-        count += 1
-    if count:
-        batches.append(count)
-    return batches
 
 
 def run_reference(args, rank, world, local_rank):
@@ -470,7 +504,7 @@ def main():
         peak, kind = peaks()
         result = {"kernels": kernel_rooflines(synthetic.qwen2_7b(), peak.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]),
                                               peak.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]),
-                                              tokens=args.kernel_tokens),
+                                              tokens=args.kernel_tokens, dtype=args.dtype),
                   "kernels_peak_source": f"{kind} hbm_gbs / bf16_tflops (burst)", "tokens": args.kernel_tokens}
     elif args.impl == "reference":
         result = run_reference(args, rank, world, local_rank)

@@ -36,47 +36,56 @@ const char* ar_version(void);
 /* ------------------------------------------------------------------------------------------
  * Layer kernels. Device pointers, asynchronous on `stream` (a cudaStream_t, NULL = default).
  * They replace the reference's kernels:: launchers (attnrank/src/cuda_runtime.hpp:115-144).
- * Activations are bf16, residual stream fp32, norm weights and biases fp32.
+ * Activations are 16-bit -- `dtype` AR_DTYPE_F16 (the reference's GEMM operand type,
+ * model.cu:353-365) or AR_DTYPE_BF16 -- the residual stream fp32, norm weights and biases fp32.
  * ------------------------------------------------------------------------------------------ */
 
 /* Replaces kernels::embedding_lookup (cuda_runtime.hpp:123-124, kernels.cu:424-430) fused with
  * the first kernels::rms_norm (kernels.cu:432-439): residual[t] = table[ids[t]] (fp32),
- * normed[t] = bf16(residual[t] * rsqrt(mean(residual[t]^2) + eps) * gamma).
+ * normed[t] = 16-bit(residual[t] * rsqrt(mean(residual[t]^2) + eps) * gamma).
  * Out-of-range ids set *device_status (nullable) to 1 and produce a zero row. */
-int ar_embedding_rms_norm(const int32_t* token_ids, int token_count, const void* table_bf16, int vocab_size,
-                          int hidden_size, const float* gamma, float eps, float* residual, void* normed_bf16,
-                          int* device_status, void* stream);
+int ar_embedding_rms_norm(const int32_t* token_ids, int token_count, const void* table, int vocab_size,
+                          int hidden_size, const float* gamma, float eps, float* residual, void* normed,
+                          int* device_status, int dtype, void* stream);
 
 /* Replaces kernels::add_in_place + kernels::rms_norm (cuda_runtime.hpp:126-127, :135;
- * model.cu:398 then :408-409): residual += delta; normed = bf16(rms(residual) * gamma). */
-int ar_rms_norm_residual(float* residual, const void* delta_bf16, const float* gamma, int token_count,
-                         int hidden_size, float eps, void* normed_bf16, void* stream);
+ * model.cu:398 then :408-409): residual += delta; normed = 16-bit(rms(residual) * gamma). */
+int ar_rms_norm_residual(float* residual, const void* delta, const float* gamma, int token_count,
+                         int hidden_size, float eps, void* normed, int dtype, void* stream);
 
 /* Replaces kernels::add_row_bias (cuda_runtime.hpp:137) + kernels::rotary_embedding
  * (cuda_runtime.hpp:129, kernels.cu:85-115), in place on the fused q|k|v projection output
- * [token_count, (Hq + 2 Hkv) * head_dim] bf16. bias (nullable) is fp32 [(Hq + 2 Hkv) * head_dim];
+ * [token_count, (Hq + 2 Hkv) * head_dim] 16-bit. bias (nullable) is fp32 [(Hq + 2 Hkv) * head_dim];
  * positions are int32 per token; cos/sin tables come from ar_rope_table. */
-int ar_rotary_embedding(void* qkv_bf16, const float* bias, const int32_t* positions, int token_count,
+int ar_rotary_embedding(void* qkv, const float* bias, const int32_t* positions, int token_count,
                         int query_heads, int kv_heads, int head_dim, const float* cos_table,
-                        const float* sin_table, int table_positions, int* device_status, void* stream);
+                        const float* sin_table, int table_positions, int* device_status, int dtype, void* stream);
 
 /* cos/sin of position * theta^(-2i/head_dim), fp32 [positions, head_dim / 2] each; the values of
  * the reference's per-element computation (kernels.cu:95-98). */
 int ar_rope_table(float* cos_table, float* sin_table, int positions, int head_dim, float theta, void* stream);
 
 /* Replaces kernels::silu_multiply (cuda_runtime.hpp:131, kernels.cu:164-170):
- * out[t, i] = silu(gate[t, i]) * up[t, i], bf16, rows addressed with the given strides (elements). */
-int ar_silu_multiply(const void* gate_bf16, const void* up_bf16, int64_t in_row_stride, void* out_bf16,
-                     int64_t out_row_stride, int token_count, int width, void* stream);
+ * out[t, i] = silu(gate[t, i]) * up[t, i], 16-bit, rows addressed with the given strides (elements). */
+int ar_silu_multiply(const void* gate, const void* up, int64_t in_row_stride, void* out,
+                     int64_t out_row_stride, int token_count, int width, int dtype, void* stream);
 
 /* Replaces the materialised attention of LlamaForwardPass::attend (model.cu:426-480:
  * scatter_kv_cache, SGEMM Q K^T, softmax_causal_kernel, SGEMM P V) for packed prompts.
- * qkv: bf16 [tokens, (Hq + 2 Hkv) * 128]; out: bf16 [tokens, Hq * 128];
+ * qkv: 16-bit [tokens, (Hq + 2 Hkv) * 128]; out: 16-bit [tokens, Hq * 128];
  * lse: fp32 [tokens, Hq], log2-domain log-sum-exp of the scaled scores of each row.
- * prompt_offsets: int32 [prompt_count + 1] (device). head_dim must be 128. */
-int ar_causal_attention(const void* qkv_bf16, void* out_bf16, float* lse, const int32_t* prompt_offsets_host,
+ * prompt_offsets: int32 [prompt_count + 1] (host copy and device copy). head_dim must be 128.
+ * Runs the tcgen05/TMEM kernel; synchronises the stream and reports a device-side wait timeout
+ * as AR_ERR_DEVICE. */
+int ar_causal_attention(const void* qkv, void* out, float* lse, const int32_t* prompt_offsets_host,
                         const int32_t* prompt_offsets_device, int prompt_count, int query_heads, int kv_heads,
-                        int head_dim, int sliding_window, void* stream);
+                        int head_dim, int sliding_window, int dtype, void* stream);
+
+/* The same contract computed by the mma.sync (warp-level tensor core) kernel; kept as the
+ * engine's alternative (ar_runtime_options.attention_kernel = 1) and as a cross-check. */
+int ar_causal_attention_mma(const void* qkv, void* out, float* lse, const int32_t* prompt_offsets_host,
+                            const int32_t* prompt_offsets_device, int prompt_count, int query_heads, int kv_heads,
+                            int head_dim, int sliding_window, int dtype, void* stream);
 
 /* Replaces kernels::reduce_document_attention (cuda_runtime.hpp:139, kernels.cu:202-236) over
  * the output of softmax_causal_kernel, without any score matrix. For each prompt p and span s,
@@ -87,10 +96,11 @@ int ar_causal_attention(const void* qkv_bf16, void* out_bf16, float* lse, const 
  * Host arrays (prompt-relative): query_spans [prompt_count][2], spans [prompt_count][span_count][2].
  * lse is the output of ar_causal_attention on the same qkv. Allocates its scratch (metadata and
  * per-CTA partial sums) with cudaMallocAsync on `stream` and synchronises the stream. */
-int ar_document_attention_mass(const void* qkv_bf16, int qkv_rows, const float* lse, const int32_t* prompt_offsets_host,
+int ar_document_attention_mass(const void* qkv, int qkv_rows, const float* lse, const int32_t* prompt_offsets_host,
                                int prompt_count, const int32_t* query_spans_host, const int32_t* spans_host,
                                int span_count, int query_heads, int kv_heads, int head_dim, int sliding_window,
-                               int prefill_chunk_tokens, int normalize_by_length, double* mass_out, void* stream);
+                               int prefill_chunk_tokens, int normalize_by_length, double* mass_out, int dtype,
+                               void* stream);
 
 /* The same computation as ar_document_attention_mass for callers that cannot let the library
  * allocate device memory while they run (a process holding the whole GPU under a fixed memory
@@ -103,17 +113,18 @@ int ar_document_attention_mass(const void* qkv_bf16, int qkv_rows, const float* 
  * made on that device (make that call before any stream capture). Calls share the array: calls
  * whose work overlaps on the GPU race, so issue them on one stream or wait in between. The
  * stream is synchronised before return. */
-int ar_document_attention_mass_noalloc(const void* qkv_bf16, int qkv_rows, const float* lse,
+int ar_document_attention_mass_noalloc(const void* qkv, int qkv_rows, const float* lse,
                                        const int32_t* prompt_offsets_host, int prompt_count,
                                        const int32_t* query_spans_host, const int32_t* spans_host, int span_count,
                                        int query_heads, int kv_heads, int head_dim, int sliding_window,
                                        int prefill_chunk_tokens, int normalize_by_length, double* mass_out,
-                                       void* stream);
+                                       int dtype, void* stream);
 
-/* Seeded synthetic weights: fills count bf16 values of tensor (layer, kind) with the generator
- * documented in csrc/synthetic.h (Irwin-Hall, bf16 round-to-nearest-even). */
-int ar_synthetic_fill(void* dst_bf16, int64_t count, uint64_t seed, int layer, int kind, float standard_deviation,
-                      void* stream);
+/* Seeded synthetic weights: fills count 16-bit values of tensor (layer, kind) with the generator
+ * documented in csrc/synthetic.h (Irwin-Hall, bf16 round-to-nearest-even); with AR_DTYPE_F16
+ * each bf16 value is stored converted to fp16 (round to nearest even). */
+int ar_synthetic_fill(void* dst, int64_t count, uint64_t seed, int layer, int kind, float standard_deviation,
+                      int dtype, void* stream);
 
 /* ------------------------------------------------------------------------------------------
  * Engine: the IAttentionProvider role of CudaLlamaModel (include/attnrank/model.hpp:79-86,
@@ -144,6 +155,8 @@ typedef struct {
   int prefill_chunk_tokens;  /* the reference's chunk length; only bounds normalize_by_length divisors */
   int max_batch_tokens;      /* packed tokens per forward (>= max_sequence_length) */
   int max_batch_prompts;
+  int activation_dtype;      /* AR_DTYPE_F16 (default when 0) or AR_DTYPE_BF16 */
+  int attention_kernel;      /* 0 = tcgen05 (default), 1 = mma.sync */
 } ar_runtime_options;
 
 /* One probe prompt: StructuredPrompt (include/attnrank/prompt.hpp:12-17) as token ids + spans. */
@@ -210,6 +223,17 @@ int ar_engine_synchronize(ar_engine* engine);
 /* The engine's CUDA stream (cudaStream_t) and device index. */
 void* ar_engine_stream(ar_engine* engine);
 int ar_engine_device(ar_engine* engine);
+
+/* Per-launch kernel timing (no reference counterpart; the reference has no device profiler).
+ * While enabled, every engine launch is bracketed by CUDA events on the engine stream.
+ * ar_engine_kernel_timing synchronises and returns, per kernel class, the summed milliseconds,
+ * the summed algorithmic work (FLOPs for tensor classes, HBM bytes otherwise) and the launch
+ * count since the previous call (arrays of AR_KERNEL_CLASS_COUNT, each nullable), then clears. */
+#define AR_KERNEL_CLASS_COUNT 12
+int ar_engine_set_kernel_timing(ar_engine* engine, int enabled);
+int ar_engine_kernel_timing(ar_engine* engine, double* milliseconds, double* work, int64_t* launches);
+const char* ar_kernel_class_name(int kernel_class);
+int ar_kernel_class_is_tensor(int kernel_class);
 
 /* ------------------------------------------------------------------------------------------
  * Profile accumulator and basin pick (host functions of attnrank/src/attnrank.cpp).

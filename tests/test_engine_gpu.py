@@ -49,12 +49,12 @@ def assert_rows_close(got, want, rel=MASS_REL):
     assert error.max() <= rel, f"max relative error {error.max():.3e} > {rel}"
 
 
-@pytest.mark.parametrize("bias", [True, False])
-def test_small_model_rows_match_oracle(cuda, bias):
+@pytest.mark.parametrize("bias,dtype", [(True, "fp16"), (False, "fp16"), (True, "bf16")])
+def test_small_model_rows_match_oracle(cuda, bias, dtype):
     import attnrank as ar
     from oracle import forward as F
     config = small_config(bias)
-    engine = ar.Engine.synthetic(config, seed=0)
+    engine = ar.Engine.synthetic(config, seed=0, options=ar.RuntimeOptions(activation_dtype=dtype))
     prompts = small_prompts(4, config.vocab_size)
     rows, first = engine.probe_rows(prompts)
     assert first == 0 and rows.shape == (4, config.num_hidden_layers, 5)
@@ -153,3 +153,26 @@ def test_qwen7b_scan_matches_reference(qwen_pair):
         assert profile.layer_index == int(want.layer_index[layer])
         assert_rows_close(profile.attention, want.attention[layer])
         assert list(profile.position_order) == [int(v) for v in want.position_order[layer]]
+
+
+# ---- Llama-3-8B long-context probe (4K-token prompts, 20 document spans) against the reference build
+@pytest.mark.slow
+def test_llama3_long_context_rows_match_reference(cuda, reference_lib):
+    if reference_lib is None:
+        pytest.skip("oracle/_ref not built")
+    import attnrank as ar
+    from attnrank import synthetic
+    from oracle.reference import ReferenceModel
+    config = synthetic.llama3_8b()
+    prompts = synthetic.prompts(2, config.vocab_size, synthetic.LLAMA3_LONG_PROMPTS)
+    assert all(len(p.document_spans) == 20 for p in prompts)
+    longest = max(len(p.tokens) for p in prompts)
+    engine = ar.Engine.synthetic(config, seed=0, options=ar.RuntimeOptions(max_sequence_length=8192))
+    rows, _ = engine.probe_rows(prompts)
+    engine.close()
+    reference = ReferenceModel(config, seed=0, max_sequence_length=max(longest, 4096))
+    try:
+        for p, prompt in enumerate(prompts):
+            assert_rows_close(rows[p], reference.measure_attention_by_layer(prompt))
+    finally:
+        reference.close()

@@ -1,8 +1,9 @@
 """Kernel parity through the C ABI on a B200: each CUDA kernel against the fp32 CPU oracle.
 
-Tolerances (from the build's parity bar):
+Tolerances (from the build's parity bar), for both 16-bit activation types:
   * integer / bit work (synthetic weights, residual gather): bit-exact;
-  * bf16 activations: within 2 bf16 ulp of the oracle, i.e. |x - ref| <= 2^-7 * |ref| + tiny (rel 1e-2);
+  * 16-bit activations: within 2 ulp of the oracle, i.e. |x - ref| <= 2 ulp * |ref| + tiny
+    (2^-7 relative for bf16, 2^-10 for fp16; the bf16 bar is the rel 1e-2 of the spec);
   * fp32 attention mass: rel 1e-3;  log-sum-exp: abs 2e-3 (log2 units).
 """
 from __future__ import annotations
@@ -14,13 +15,19 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
-BF16_REL = 2.0 ** -7   # two bf16 ulp, relative
+DTYPES = ["fp16", "bf16"]
+TWO_ULP = {"bf16": 2.0 ** -7, "fp16": 2.0 ** -10}   # two ulp, relative
 MASS_REL = 1e-3
 
 
 def _lib():
     from attnrank import _native
     return _native
+
+
+def _code(dtype: str) -> int:
+    from attnrank import _native
+    return _native.DTYPE_F16 if dtype == "fp16" else _native.DTYPE_BF16
 
 
 def _ptr(tensor) -> ctypes.c_void_p:
@@ -32,9 +39,17 @@ def _stream():
     return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
 
 
-def _bf16_tensor(values: np.ndarray, device):
+def _torch_dtype(dtype: str):
+    import torch
+    return torch.float16 if dtype == "fp16" else torch.bfloat16
+
+
+def _half_tensor(values: np.ndarray, device, dtype: str):
+    """values rounded to the 16-bit type with round-to-nearest-even."""
     import torch
     from oracle import weights as W
+    if dtype == "fp16":
+        return torch.from_numpy(values.astype(np.float32).astype(np.float16)).to(device)
     bits = W.f32_to_bf16_bits(values.astype(np.float32))
     return torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).to(device)
 
@@ -44,74 +59,83 @@ def _to_np(tensor) -> np.ndarray:
     return tensor.detach().to(torch.float32).cpu().numpy()
 
 
-def assert_bf16_close(actual: np.ndarray, expected: np.ndarray, floor: float = 1e-6):
+def assert_half_close(actual: np.ndarray, expected: np.ndarray, dtype: str, floor: float = 1e-6):
     error = np.abs(actual - expected)
-    bound = BF16_REL * np.abs(expected) + floor
+    bound = TWO_ULP[dtype] * np.abs(expected) + floor
     worst = np.argmax(error - bound)
     assert np.all(error <= bound), (
-        f"bf16 mismatch at {np.unravel_index(worst, error.shape)}: got {actual.flat[worst]}, "
+        f"{dtype} mismatch at {np.unravel_index(worst, error.shape)}: got {actual.flat[worst]}, "
         f"want {expected.flat[worst]} (bound {bound.flat[worst]})")
 
 
-def test_synthetic_fill_matches_checker_bit_exact(cuda):
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_synthetic_fill_matches_checker_bit_exact(cuda, dtype):
+    """The seeded generator gives the checker's bf16 bits; the fp16 engine stores each bf16 value
+    converted to fp16 with round-to-nearest-even."""
     import torch
     from oracle import weights as W
     native = _lib()
     count = 1 << 20
     for layer, kind, std in [(-1, W.EMBEDDING, 0.02), (3, W.QUERY, 0.02), (27, W.DOWN, 0.05)]:
         out = torch.empty(count, dtype=torch.int16, device=cuda)
-        native.check(native.lib.ar_synthetic_fill(_ptr(out), count, 0, layer, kind, std, _stream()))
+        native.check(native.lib.ar_synthetic_fill(_ptr(out), count, 0, layer, kind, std, _code(dtype), _stream()))
         torch.cuda.synchronize()
         expected = W.bf16_bits(count, 0, layer, kind, std)
+        if dtype == "fp16":
+            expected = (expected.astype(np.uint32) << 16).view(np.float32).astype(np.float16).view(np.uint16)
         got = out.cpu().numpy().view(np.uint16)
         assert np.array_equal(got, expected)
 
 
+@pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("hidden", [2048, 3584, 8192])
-def test_embedding_rms_norm(cuda, hidden):
+def test_embedding_rms_norm(cuda, hidden, dtype):
     import torch
     from oracle import forward as F
     native = _lib()
     rng = np.random.default_rng(hidden)
     vocab = 1000
     table = rng.standard_normal((vocab, hidden)).astype(np.float32) * 0.02
-    table_bf = _bf16_tensor(table, cuda)
+    table_bf = _half_tensor(table, cuda, dtype)
     table_exact = _to_np(table_bf)
     ids = np.concatenate([[0, vocab - 1], rng.integers(0, vocab, 61)]).astype(np.int32)
     gamma = (1.0 + 0.1 * rng.standard_normal(hidden)).astype(np.float32)
     ids_d = torch.from_numpy(ids).to(cuda)
     gamma_d = torch.from_numpy(gamma).to(cuda)
     residual = torch.empty((ids.size, hidden), dtype=torch.float32, device=cuda)
-    normed = torch.empty((ids.size, hidden), dtype=torch.bfloat16, device=cuda)
+    normed = torch.empty((ids.size, hidden), dtype=_torch_dtype(dtype), device=cuda)
     status = torch.zeros(1, dtype=torch.int32, device=cuda)
     native.check(native.lib.ar_embedding_rms_norm(_ptr(ids_d), ids.size, _ptr(table_bf), vocab, hidden, _ptr(gamma_d),
-                                                  1e-6, _ptr(residual), _ptr(normed), _ptr(status), _stream()))
+                                                  1e-6, _ptr(residual), _ptr(normed), _ptr(status), _code(dtype),
+                                                  _stream()))
     torch.cuda.synchronize()
     want_residual, want_normed = F.op_embedding_rms_norm(table_exact, ids, gamma, 1e-6)
     assert int(status.item()) == 0
     assert np.array_equal(_to_np(residual), want_residual)
-    assert_bf16_close(_to_np(normed), want_normed)
+    assert_half_close(_to_np(normed), want_normed, dtype)
 
 
 def test_embedding_reports_out_of_range_token(cuda):
     import torch
     native = _lib()
     hidden, vocab = 256, 16
-    table = torch.zeros((vocab, hidden), dtype=torch.bfloat16, device=cuda)
+    table = torch.zeros((vocab, hidden), dtype=torch.float16, device=cuda)
     ids = torch.tensor([3, vocab, -1], dtype=torch.int32, device=cuda)
     gamma = torch.ones(hidden, dtype=torch.float32, device=cuda)
     residual = torch.full((3, hidden), 7.0, dtype=torch.float32, device=cuda)
-    normed = torch.empty((3, hidden), dtype=torch.bfloat16, device=cuda)
+    normed = torch.empty((3, hidden), dtype=torch.float16, device=cuda)
     status = torch.zeros(1, dtype=torch.int32, device=cuda)
     native.check(native.lib.ar_embedding_rms_norm(_ptr(ids), 3, _ptr(table), vocab, hidden, _ptr(gamma), 1e-6,
-                                                  _ptr(residual), _ptr(normed), _ptr(status), _stream()))
+                                                  _ptr(residual), _ptr(normed), _ptr(status), _code("fp16"),
+                                                  _stream()))
     torch.cuda.synchronize()
     assert int(status.item()) == 1
     assert float(residual[1:].abs().max()) == 0.0
 
 
+@pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("tokens,hidden", [(1, 3584), (64, 4096), (1000, 3584), (33, 8192)])
-def test_rms_norm_residual(cuda, tokens, hidden):
+def test_rms_norm_residual(cuda, tokens, hidden, dtype):
     import torch
     from oracle import forward as F
     native = _lib()
@@ -119,20 +143,21 @@ def test_rms_norm_residual(cuda, tokens, hidden):
     residual = rng.standard_normal((tokens, hidden)).astype(np.float32)
     delta = rng.standard_normal((tokens, hidden)).astype(np.float32)
     gamma = (1.0 + 0.1 * rng.standard_normal(hidden)).astype(np.float32)
-    delta_d = _bf16_tensor(delta, cuda)
+    delta_d = _half_tensor(delta, cuda, dtype)
     residual_d = torch.from_numpy(residual).to(cuda)
     gamma_d = torch.from_numpy(gamma).to(cuda)
-    normed = torch.empty((tokens, hidden), dtype=torch.bfloat16, device=cuda)
+    normed = torch.empty((tokens, hidden), dtype=_torch_dtype(dtype), device=cuda)
     native.check(native.lib.ar_rms_norm_residual(_ptr(residual_d), _ptr(delta_d), _ptr(gamma_d), tokens, hidden, 1e-6,
-                                                 _ptr(normed), _stream()))
+                                                 _ptr(normed), _code(dtype), _stream()))
     torch.cuda.synchronize()
     want_residual, want_normed = F.op_rms_norm_residual(residual, _to_np(delta_d), gamma, 1e-6)
     np.testing.assert_allclose(_to_np(residual_d), want_residual, rtol=1e-6, atol=1e-6)
-    assert_bf16_close(_to_np(normed), want_normed)
+    assert_half_close(_to_np(normed), want_normed, dtype)
 
 
-@pytest.mark.parametrize("heads,kv_heads,bias", [(28, 4, True), (32, 8, False)])
-def test_rotary_bias(cuda, heads, kv_heads, bias):
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("heads,kv_heads,bias", [(28, 4, True), (32, 8, False), (3, 1, True)])
+def test_rotary_bias(cuda, heads, kv_heads, bias, dtype):
     import torch
     from oracle import forward as F
     native = _lib()
@@ -140,7 +165,7 @@ def test_rotary_bias(cuda, heads, kv_heads, bias):
     width = (heads + 2 * kv_heads) * D
     rng = np.random.default_rng(heads)
     qkv = rng.standard_normal((tokens, width)).astype(np.float32)
-    qkv_d = _bf16_tensor(qkv, cuda)
+    qkv_d = _half_tensor(qkv, cuda, dtype)
     qkv_exact = _to_np(qkv_d)
     bias_np = (0.02 * rng.standard_normal(width)).astype(np.float32) if bias else None
     positions = np.concatenate([np.arange(100), np.arange(200) + 4000]).astype(np.int32)
@@ -153,14 +178,14 @@ def test_rotary_bias(cuda, heads, kv_heads, bias):
     status = torch.zeros(1, dtype=torch.int32, device=cuda)
     native.check(native.lib.ar_rotary_embedding(_ptr(qkv_d), _ptr(bias_d) if bias else None, _ptr(pos_d), tokens, heads,
                                                 kv_heads, D, _ptr(cos), _ptr(sin), table_positions, _ptr(status),
-                                                _stream()))
+                                                _code(dtype), _stream()))
     torch.cuda.synchronize()
     assert int(status.item()) == 0
     # the rotation arithmetic, on the kernel's own cos/sin table
     tables = (cos.cpu().numpy(), sin.cpu().numpy())
     want = F.op_rotary_bias(qkv_exact, bias_np, positions, heads, kv_heads, D, theta, tables=tables)
     got = _to_np(qkv_d)
-    assert_bf16_close(got, want, floor=1e-6 * np.abs(want).max())
+    assert_half_close(got, want, dtype, floor=1e-6 * np.abs(want).max())
     if not bias:  # value heads untouched without a bias
         assert np.array_equal(got[:, (heads + kv_heads) * D:], qkv_exact[:, (heads + kv_heads) * D:])
 
@@ -185,51 +210,58 @@ def test_rope_table(cuda, theta):
     assert np.all(np.abs(sin.cpu().numpy() - np.sin(angle)) <= bound)
 
 
-@pytest.mark.parametrize("tokens,width", [(1, 18944), (257, 18944), (64, 14336)])
-def test_silu_multiply(cuda, tokens, width):
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("tokens,width", [(1, 18944), (257, 18944), (64, 14336), (3, 8)])
+def test_silu_multiply(cuda, tokens, width, dtype):
     import torch
     from oracle import forward as F
     native = _lib()
     rng = np.random.default_rng(width + tokens)
     gate_up = rng.standard_normal((tokens, 2 * width)).astype(np.float32) * 2
-    gu_d = _bf16_tensor(gate_up, cuda)
+    gu_d = _half_tensor(gate_up, cuda, dtype)
     exact = _to_np(gu_d)
-    out = torch.empty((tokens, width), dtype=torch.bfloat16, device=cuda)
+    out = torch.empty((tokens, width), dtype=_torch_dtype(dtype), device=cuda)
     native.check(native.lib.ar_silu_multiply(_ptr(gu_d), ctypes.c_void_p(gu_d.data_ptr() + 2 * width), 2 * width,
-                                             _ptr(out), width, tokens, width, _stream()))
+                                             _ptr(out), width, tokens, width, _code(dtype), _stream()))
     torch.cuda.synchronize()
     want = F.op_silu_multiply(exact[:, :width], exact[:, width:])
-    assert_bf16_close(_to_np(out), want, floor=1e-4)
+    assert_half_close(_to_np(out), want, dtype, floor=1e-4)
 
 
-def _packed_qkv(lengths, heads, kv_heads, seed, device):
+def _packed_qkv(lengths, heads, kv_heads, seed, device, dtype="fp16"):
     rng = np.random.default_rng(seed)
     D = 128
     width = (heads + 2 * kv_heads) * D
     total = int(sum(lengths))
     qkv = rng.standard_normal((total, width)).astype(np.float32)
-    qkv_d = _bf16_tensor(qkv, device)
+    qkv_d = _half_tensor(qkv, device, dtype)
     offsets = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
     return qkv_d, _to_np(qkv_d), offsets
 
 
+@pytest.mark.parametrize("kernel", ["tcgen05", "mma"])
+@pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("heads,kv_heads,lengths,window", [
     (28, 4, [1, 200, 777], 0),
     (32, 8, [129, 64, 300], 0),
     (28, 4, [500], 96),
+    (28, 4, [940, 1240, 256, 128, 1], 0),
+    (4, 4, [385, 17], 200),
 ])
-def test_causal_attention(cuda, heads, kv_heads, lengths, window):
+def test_causal_attention(cuda, heads, kv_heads, lengths, window, dtype, kernel):
+    """Both attention kernels (tcgen05/TMEM and mma.sync) against the oracle's exact softmax."""
     import torch
     from oracle import forward as F
     native = _lib()
-    qkv_d, qkv, offsets = _packed_qkv(lengths, heads, kv_heads, sum(lengths), cuda)
+    qkv_d, qkv, offsets = _packed_qkv(lengths, heads, kv_heads, sum(lengths), cuda, dtype)
     total = int(offsets[-1])
-    out = torch.zeros((total, heads * 128), dtype=torch.bfloat16, device=cuda)
+    out = torch.zeros((total, heads * 128), dtype=_torch_dtype(dtype), device=cuda)
     lse = torch.zeros((total, heads), dtype=torch.float32, device=cuda)
     offsets_d = torch.from_numpy(offsets).to(cuda)
     host_offsets = np.ascontiguousarray(offsets)
-    native.check(native.lib.ar_causal_attention(_ptr(qkv_d), _ptr(out), _ptr(lse), host_offsets.ctypes.data,
-                                                _ptr(offsets_d), len(lengths), heads, kv_heads, 128, window, _stream()))
+    entry = native.lib.ar_causal_attention if kernel == "tcgen05" else native.lib.ar_causal_attention_mma
+    native.check(entry(_ptr(qkv_d), _ptr(out), _ptr(lse), host_offsets.ctypes.data, _ptr(offsets_d), len(lengths),
+                       heads, kv_heads, 128, window, _code(dtype), _stream()))
     torch.cuda.synchronize()
     want_out, want_lse, _ = F.op_attention(qkv, offsets, heads, kv_heads, 128, window)
     np.testing.assert_allclose(_to_np(lse), want_lse, atol=2e-3, rtol=0)
@@ -238,23 +270,25 @@ def test_causal_attention(cuda, heads, kv_heads, lengths, window):
     assert error.max() <= 2e-2 * max(1.0, np.abs(want_out).max()), error.max()
 
 
+@pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("heads,kv_heads,lengths,queries,normalize", [
     (28, 4, [940, 700], 40, False),
     (32, 8, [1200], 64, True),
     (28, 4, [130, 300, 9], 5, False),
 ])
-def test_document_mass(cuda, heads, kv_heads, lengths, queries, normalize):
+def test_document_mass(cuda, heads, kv_heads, lengths, queries, normalize, dtype):
     """The tcgen05 mass kernel against span sums of the oracle's softmax rows."""
     import torch
     from oracle import forward as F
     native = _lib()
-    qkv_d, qkv, offsets = _packed_qkv(lengths, heads, kv_heads, 7 + sum(lengths), cuda)
+    qkv_d, qkv, offsets = _packed_qkv(lengths, heads, kv_heads, 7 + sum(lengths), cuda, dtype)
     total = int(offsets[-1])
-    out = torch.zeros((total, heads * 128), dtype=torch.bfloat16, device=cuda)
+    out = torch.zeros((total, heads * 128), dtype=_torch_dtype(dtype), device=cuda)
     lse = torch.zeros((total, heads), dtype=torch.float32, device=cuda)
     offsets_d = torch.from_numpy(offsets).to(cuda)
     native.check(native.lib.ar_causal_attention(_ptr(qkv_d), _ptr(out), _ptr(lse), offsets.ctypes.data,
-                                                _ptr(offsets_d), len(lengths), heads, kv_heads, 128, 0, _stream()))
+                                                _ptr(offsets_d), len(lengths), heads, kv_heads, 128, 0, _code(dtype),
+                                                _stream()))
     rng = np.random.default_rng(len(lengths))
     span_count = 5
     query_spans, spans, prompts = [], [], []
@@ -272,7 +306,8 @@ def test_document_mass(cuda, heads, kv_heads, lengths, queries, normalize):
     mass = np.zeros((len(lengths), span_count), dtype=np.float64)
     native.check(native.lib.ar_document_attention_mass(_ptr(qkv_d), total, _ptr(lse), offsets.ctypes.data, len(lengths),
                                                        qs.ctypes.data, sp.ctypes.data, span_count, heads, kv_heads, 128,
-                                                       0, 512, int(normalize), mass.ctypes.data, _stream()))
+                                                       0, 512, int(normalize), mass.ctypes.data, _code(dtype),
+                                                       _stream()))
     _, _, probs = F.op_attention(qkv, offsets, heads, kv_heads, 128, 0)
     for p, prompt in enumerate(prompts):
         raw = F.document_mass(probs[p], prompt, 512, normalize)

@@ -29,8 +29,8 @@ def _inputs(cuda, lengths, heads=28, kv_heads=4, queries=40, span_count=5, seed=
     width = (heads + 2 * kv_heads) * D
     total = int(sum(lengths))
     gen = torch.Generator(device=cuda).manual_seed(seed)
-    qkv = torch.randn(total, width, device=cuda, generator=gen).to(torch.bfloat16)
-    out = torch.empty(total, heads * D, device=cuda, dtype=torch.bfloat16)
+    qkv = torch.randn(total, width, device=cuda, generator=gen).to(torch.float16)
+    out = torch.empty(total, heads * D, device=cuda, dtype=torch.float16)
     lse = torch.empty(total, heads, device=cuda, dtype=torch.float32)
     offsets = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
     offsets_d = torch.from_numpy(offsets).to(cuda)
@@ -38,7 +38,7 @@ def _inputs(cuda, lengths, heads=28, kv_heads=4, queries=40, span_count=5, seed=
     _native.check(_native.lib.ar_causal_attention(ctypes.c_void_p(qkv.data_ptr()), ctypes.c_void_p(out.data_ptr()),
                                                   ctypes.c_void_p(lse.data_ptr()), offsets.ctypes.data,
                                                   ctypes.c_void_p(offsets_d.data_ptr()), len(lengths), heads, kv_heads,
-                                                  D, 0, stream))
+                                                  D, 0, _native.DTYPE_F16, stream))
     rng = np.random.default_rng(seed)
     query_spans, spans = [], []
     for T in lengths:
@@ -56,12 +56,13 @@ def _inputs(cuda, lengths, heads=28, kv_heads=4, queries=40, span_count=5, seed=
 
 
 def _call(function, data, normalize=0):
+    from attnrank import _native
     prompt_count = len(data["offsets"]) - 1
     out = np.zeros((prompt_count, data["span_count"]), dtype=np.float64)
     status = function(ctypes.c_void_p(data["qkv"].data_ptr()), int(data["offsets"][-1]),
                       ctypes.c_void_p(data["lse"].data_ptr()), data["offsets"].ctypes.data, prompt_count,
                       data["query_spans"].ctypes.data, data["spans"].ctypes.data, data["span_count"], data["heads"],
-                      data["kv_heads"], 128, 0, 512, normalize, out.ctypes.data, data["stream"])
+                      data["kv_heads"], 128, 0, 512, normalize, out.ctypes.data, _native.DTYPE_F16, data["stream"])
     return status, out
 
 
