@@ -337,9 +337,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m_ref = -INFINITY;
     float l = 0.0f;
     bool ok = tiles > 0 && !skip;
+    // tcgen05.ld / tcgen05.st are warp-collective (.sync.aligned): every branch around them is
+    // decided uniformly per warp (__all_sync / __any_sync), never per row
     for (int j = 0; ok && j < tiles; ++j) {
       const int stage = j & 1;
-      if (!mbar_wait(smem_u32(&ctl.s_bar[stage]), (j >> 1) & 1, &ctl.abort) || ctl.abort) {
+      const bool ready = mbar_wait(smem_u32(&ctl.s_bar[stage]), (j >> 1) & 1, &ctl.abort) && !ctl.abort;
+      if (!__all_sync(0xffffffffu, ready)) {
         ok = false;
         break;
       }
@@ -369,29 +372,33 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < kTile; ++i) m_tile = fmaxf(m_tile, x[i]);
       }
-      if (m_tile > m_ref + kRescaleThreshold || (m_ref == -INFINITY && m_tile != -INFINITY)) {
-        if (j > 0 && m_ref != -INFINITY) {
-          // O (accumulated through PV_{j-1}) and l are rescaled to the new reference; PV_{j-2}
-          // completed before S_j was issued, so o_bar is at most one phase behind here
-          if (!mbar_wait(o_bar, (j - 1) & 1, &ctl.abort)) {
-            ok = false;
-            break;
-          }
-          fence_after();
-          const float factor = exp2f(m_ref - m_tile);
-#pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            uint32_t raw[32];
-            tmem_ld32(tmem + lane_base + kTmemO + c * 32, raw);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) raw[i] = __float_as_uint(__uint_as_float(raw[i]) * factor);
-            tmem_st32(tmem + lane_base + kTmemO + c * 32, raw);
-          }
-          l *= factor;
+      // the row's reference max moves when the tile max exceeds it by more than the threshold
+      // (or on the row's first unmasked key); O already holds earlier tiles only when j > 0
+      const bool move = m_tile > m_ref + kRescaleThreshold || (m_ref == -INFINITY && m_tile != -INFINITY);
+      const bool rescale = move && j > 0 && m_ref != -INFINITY;
+      if (__any_sync(0xffffffffu, rescale)) {
+        // O (accumulated through PV_{j-1}) is rescaled by the whole warp, factor 1 on the rows
+        // that keep their reference; PV_{j-2} completed before S_j was issued, so o_bar is at
+        // most one phase behind here
+        const bool o_ready = mbar_wait(o_bar, (j - 1) & 1, &ctl.abort);
+        if (!__all_sync(0xffffffffu, o_ready)) {
+          ok = false;
+          break;
         }
-        m_ref = m_tile;
+        fence_after();
+        const float factor = rescale ? exp2f(m_ref - m_tile) : 1.0f;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t raw[32];
+          tmem_ld32(tmem + lane_base + kTmemO + c * 32, raw);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) raw[i] = __float_as_uint(__uint_as_float(raw[i]) * factor);
+          tmem_st32(tmem + lane_base + kTmemO + c * 32, raw);
+        }
+        l *= factor;
       }
+      if (move) m_ref = m_tile;
       const float reference = m_ref == -INFINITY ? 0.0f : m_ref;
       float sum = 0.0f;
 #pragma unroll
@@ -413,7 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // ---- epilogue: O / l -> shared (swizzled rows) -> coalesced global stores; LSE.
     // done_bar, not o_bar: PV of tile tiles-2 may still be in flight here, two phases behind.
-    const bool done = ok && mbar_wait(done_bar, 0, &ctl.abort) && !ctl.abort;
+    const bool done = __all_sync(0xffffffffu, ok && mbar_wait(done_bar, 0, &ctl.abort) && !ctl.abort);
     if (!done && tiles > 0 && !skip) {
       report_status(args.status, kStatusWaitTimeout);
       ctl.abort = 1;
@@ -461,6 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   fence_before();
   __syncthreads();
   if (warp == 4) {
+    __syncwarp();
     fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemColumns));
   }

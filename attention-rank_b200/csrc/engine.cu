@@ -903,6 +903,10 @@ void Engine::execute_batch(const BatchLayout& layout, const int32_t* dev, int sp
       mass.partials = partials_ + static_cast<size_t>(l - range.begin) * item_count * S;
       timed(kClassMass, layout.mass_flops, [&] { check_cuda(launch_document_mass(mass, stream_), "document mass"); });
     }
+    // The last probed layer's attention output, o_proj and MLP feed only layers that are not run:
+    // no probe output depends on them (the reference computes them, model.cu:334-337), so the
+    // forward ends at the last mass capture.
+    if (l == last_layer) break;
     timed(kClassGemmOut, 2 * m * H * Hq * D, [&] { gemm(attn_, w.out, delta_, M, H, Hq * D); });
     timed(kClassNorm, norm_bytes, [&] {
       check_cuda(launch_rms_norm_residual(residual_, delta_, w.post_norm, M, H, c.rms_norm_eps, normed_, dtype, stream_),

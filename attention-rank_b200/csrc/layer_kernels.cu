@@ -10,6 +10,8 @@
 // The arithmetic of each op follows the reference formula line for line (fp32 math, the same
 // order of multiplies), only the storage type of activations changes from fp32 to 16 bits (T =
 // __half, the default, or __nv_bfloat16).
+#include <algorithm>
+
 #include "common.cuh"
 #include "layer_kernels.h"
 
@@ -18,7 +20,7 @@ namespace {
 
 constexpr int kRowThreadsCap = 256;
 constexpr int kRopeUnroll = 4;   // heads per rotary loop iteration (loads in flight per thread)
-constexpr int kSiluUnroll = 2;   // 8-value chunks per SwiGLU thread
+constexpr int kSiluUnroll = 4;   // 8-value chunks in flight per SwiGLU thread
 
 // ---------------------------------------------------------------------------------------------
 // Row kernels: one CTA per token row, each thread holds VPT vectors of 8 channels in registers,
@@ -144,11 +146,10 @@ __global__ void rotary_bias_kernel(T* __restrict__ qkv, const float* __restrict_
   const int rotated_heads = query_heads + kv_heads;
   const int heads = bias != nullptr ? rotated_heads + kv_heads : rotated_heads;
   const int row_width = (query_heads + 2 * kv_heads) * head_dim;
-  const long long total = static_cast<long long>(tokens) * chunks_per_head;
-  for (long long item = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; item < total;
-       item += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int token = static_cast<int>(item / chunks_per_head);
-    const int chunk = static_cast<int>(item - static_cast<long long>(token) * chunks_per_head);
+  const int total = tokens * chunks_per_head;  // < 2^31: tokens and head_dim are bounded by the launcher
+  for (int item = blockIdx.x * blockDim.x + threadIdx.x; item < total; item += gridDim.x * blockDim.x) {
+    const int token = item / chunks_per_head;
+    const int chunk = item - token * chunks_per_head;
     const int position = positions[token];
     const bool in_table = position >= 0 && position < table_positions;
     if (!in_table) report_status(status, kStatusPositionOutOfRange);
@@ -239,37 +240,38 @@ __global__ void rope_table_kernel(float* __restrict__ cos_out, float* __restrict
 template <typename T>
 __global__ void silu_multiply_kernel(const T* __restrict__ gate, const T* __restrict__ up, long long in_stride,
                                      T* __restrict__ out, long long out_stride, int tokens, int width) {
+  // CTAs walk rows; a thread handles chunks c, c + blockDim, ... of the row, kSiluUnroll of them
+  // loaded before any is computed (no integer division on the index path)
   const int chunks = width >> 3;
-  const long long total = static_cast<long long>(tokens) * chunks;
-  const long long threads = static_cast<long long>(gridDim.x) * blockDim.x;
-  for (long long first = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; first < total;
-       first += threads * kSiluUnroll) {
-    uint4 g_raw[kSiluUnroll];
-    uint4 u_raw[kSiluUnroll];
+  const int span = blockDim.x * kSiluUnroll;
+  for (int token = blockIdx.x; token < tokens; token += gridDim.x) {
+    const T* gate_row = gate + token * in_stride;
+    const T* up_row = up + token * in_stride;
+    T* out_row = out + token * out_stride;
+    for (int first = threadIdx.x; first < chunks; first += span) {
+      uint4 g_raw[kSiluUnroll];
+      uint4 u_raw[kSiluUnroll];
 #pragma unroll
-    for (int k = 0; k < kSiluUnroll; ++k) {
-      const long long item = first + k * threads;
-      if (item < total) {
-        const long long token = item / chunks;
-        const int chunk = static_cast<int>(item - token * chunks);
-        g_raw[k] = load_stream(gate + token * in_stride + chunk * 8);
-        u_raw[k] = load_stream(up + token * in_stride + chunk * 8);
+      for (int k = 0; k < kSiluUnroll; ++k) {
+        const int chunk = first + k * blockDim.x;
+        if (chunk < chunks) {
+          g_raw[k] = load_stream(gate_row + chunk * 8);
+          u_raw[k] = load_stream(up_row + chunk * 8);
+        }
       }
-    }
 #pragma unroll
-    for (int k = 0; k < kSiluUnroll; ++k) {
-      const long long item = first + k * threads;
-      if (item >= total) break;
-      const long long token = item / chunks;
-      const int chunk = static_cast<int>(item - token * chunks);
-      float g[8];
-      float u[8];
-      unpack8<T>(g_raw[k], g);
-      unpack8<T>(u_raw[k], u);
-      float a[8];
+      for (int k = 0; k < kSiluUnroll; ++k) {
+        const int chunk = first + k * blockDim.x;
+        if (chunk >= chunks) break;
+        float g[8];
+        float u[8];
+        unpack8<T>(g_raw[k], g);
+        unpack8<T>(u_raw[k], u);
+        float a[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) a[i] = (g[i] / (1.0f + __expf(-g[i]))) * u[i];
-      __stcs(reinterpret_cast<uint4*>(out + token * out_stride + chunk * 8), pack8<T>(a));
+        for (int i = 0; i < 8; ++i) a[i] = (g[i] / (1.0f + __expf(-g[i]))) * u[i];
+        __stcs(reinterpret_cast<uint4*>(out_row + chunk * 8), pack8<T>(a));
+      }
     }
   }
 }
@@ -380,7 +382,7 @@ cudaError_t launch_rotary_bias(void* qkv, const float* bias, const int32_t* posi
                                const float* sin_table, int table_positions, int* status, int dtype,
                                cudaStream_t stream) {
   if (tokens <= 0) return cudaSuccess;
-  if (head_dim % 16 != 0) return cudaErrorInvalidValue;
+  if (head_dim % 16 != 0 || head_dim > 1024 || tokens > (1 << 24)) return cudaErrorInvalidValue;
   const long long items = static_cast<long long>(tokens) * (head_dim / 16);
   const int threads = 256;
   const int grid = stride_grid(items, threads, 8);
@@ -409,10 +411,9 @@ cudaError_t launch_rope_table(float* cos_out, float* sin_out, int positions, int
 
 cudaError_t launch_silu_multiply(const void* gate, const void* up, long long in_stride, void* out,
                                  long long out_stride, int tokens, int width, int dtype, cudaStream_t stream) {
-  const long long items = static_cast<long long>(tokens) * (width / 8);
-  if (items <= 0) return cudaSuccess;
+  if (tokens <= 0 || width <= 0) return cudaSuccess;
   const int threads = 256;
-  const int grid = stride_grid((items + kSiluUnroll - 1) / kSiluUnroll, threads, 8);
+  const int grid = std::min(tokens, sm_count() * 8);
   if (dtype == kActFp16) {
     silu_multiply_kernel<__half><<<grid, threads, 0, stream>>>(static_cast<const __half*>(gate),
                                                                static_cast<const __half*>(up), in_stride,

@@ -319,7 +319,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         ctl.abort = 1;
       }
     }
-    const bool ready = mbar_wait(mma_bar[j & 1], (j >> 1) & 1);
+    // warp-uniform: the TMEM loads below are warp-collective (.sync.aligned)
+    const bool ready = __all_sync(0xffffffffu, mbar_wait(mma_bar[j & 1], (j >> 1) & 1));
     if (ready) mma_waited = j + 1;
     if (!ready) {
       report_status(args.status, kStatusWaitTimeout);

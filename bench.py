@@ -124,17 +124,21 @@ class ClockSampler:
 
 
 def scan_flops(config, prompts) -> float:
-    """Algorithmic FLOPs of one full scan (projection GEMMs + causal attention + mass scoring)."""
+    """Algorithmic FLOPs of one full scan: per layer the q|k|v GEMM, causal attention and mass
+    scoring (Q K^T of the query rows over the document-span keys); o_proj and the MLP on every
+    layer but the last (whose outputs no probe reads)."""
     H, I, L = config.hidden_size, config.intermediate_size, config.num_hidden_layers
     Hq, Hkv, D = config.num_attention_heads, config.num_key_value_heads, config.head_dim
-    per_token = 2 * (H * (Hq + 2 * Hkv) * D + Hq * D * H + 3 * H * I)
+    qkv_per_token = 2 * H * (Hq + 2 * Hkv) * D
+    rest_per_token = 2 * (Hq * D * H + 3 * H * I)
     total = 0.0
     for p in prompts:
         T = len(p.tokens)
         Tq = p.query_span.end - p.query_span.begin
+        span_keys = sum(d.end - d.begin for d in p.document_spans)
         attention = 2 * Hq * D * T * (T + 1)          # QK^T and PV over the causal half
-        mass = 2 * Hq * Tq * T * D                    # mass scoring recomputes Q K^T for the query rows
-        total += L * (per_token * T + attention + mass)
+        mass = 2 * Hq * Tq * span_keys * D
+        total += L * (qkv_per_token * T + attention + mass) + (L - 1) * rest_per_token * T
     return total
 
 

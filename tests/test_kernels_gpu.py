@@ -270,6 +270,42 @@ def test_causal_attention(cuda, heads, kv_heads, lengths, window, dtype, kernel)
     assert error.max() <= 2e-2 * max(1.0, np.abs(want_out).max()), error.max()
 
 
+@pytest.mark.parametrize("kernel", ["tcgen05", "mma"])
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_causal_attention_rescale_on_some_rows(cuda, dtype, kernel):
+    """Rows of one 32-row group whose running max jumps at a later key tile while their
+    neighbours' does not: even query rows >= 260 align with keys 260..270, which score
+    ~12 log2 units above everything before them; odd rows see ordinary scores. The tcgen05
+    kernel rescales its TMEM accumulator for some rows of a warp only (a warp-collective step),
+    and both kernels must still match the exact softmax."""
+    import torch
+    from oracle import forward as F
+    native = _lib()
+    heads, kv_heads, D, T = 4, 1, 128, 700
+    width = (heads + 2 * kv_heads) * D
+    rng = np.random.default_rng(11)
+    qkv = rng.standard_normal((T, width)).astype(np.float32)
+    direction = np.full(D, 1.0 / np.sqrt(D), dtype=np.float32)
+    k_col = heads * D
+    qkv[260:271, k_col:k_col + D] = 12.0 * direction
+    for h in range(heads):
+        qkv[260::2, h * D:(h + 1) * D] = 12.0 * direction
+    qkv_d = _half_tensor(qkv, cuda, dtype)
+    exact = _to_np(qkv_d)
+    offsets = np.array([0, T], dtype=np.int32)
+    out = torch.zeros((T, heads * D), dtype=_torch_dtype(dtype), device=cuda)
+    lse = torch.zeros((T, heads), dtype=torch.float32, device=cuda)
+    offsets_d = torch.from_numpy(offsets).to(cuda)
+    entry = native.lib.ar_causal_attention if kernel == "tcgen05" else native.lib.ar_causal_attention_mma
+    native.check(entry(_ptr(qkv_d), _ptr(out), _ptr(lse), offsets.ctypes.data, _ptr(offsets_d), 1, heads, kv_heads,
+                       D, 0, _code(dtype), _stream()))
+    torch.cuda.synchronize()
+    want_out, want_lse, _ = F.op_attention(exact, offsets, heads, kv_heads, D, 0)
+    np.testing.assert_allclose(_to_np(lse), want_lse, atol=2e-3, rtol=0)
+    error = np.abs(_to_np(out) - want_out)
+    assert error.max() <= 2e-2 * max(1.0, np.abs(want_out).max()), error.max()
+
+
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("heads,kv_heads,lengths,queries,normalize", [
     (28, 4, [940, 700], 40, False),
