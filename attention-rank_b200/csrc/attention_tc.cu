@@ -7,7 +7,7 @@
 // k <= q, k < prompt length and, with a sliding window, k > q - window.
 //
 // One CTA = one (prompt, 128-row query tile, query head). 160 threads:
-//   warps 0-3 (softmax): thread r owns query row r = TMEM lane r. For every 128-key tile it
+//   warps 0-3 (softmax): thread r owns query row r = TMEM lane r. For every 64-key tile it
 //     reads S = Q K^T (fp32) from TMEM, applies the mask, keeps the row's running max / sum,
 //     writes P (16-bit) back into the same TMEM columns, and signals the control warp.
 //   warp 4 (control): allocates TMEM, lane 0 issues every TMA load (no multicast) and every
@@ -15,6 +15,8 @@
 // Pipeline per key tile j (K/V double-buffered in shared memory, S double-buffered in TMEM):
 //     S_{j+1} = Q K_{j+1}^T  overlaps the softmax of tile j;
 //     O += P_j V_j  (A = P from TMEM, B = V from shared memory, MN-major) after the softmax.
+// A CTA holds 256 TMEM columns (S0 | S1 | O) and 96 KB of shared memory, so two CTAs share an
+// SM: one's softmax, set-up and epilogue overlap the other's MMAs.
 // Rescaling: exponents use a reference max m_ref that moves only when the row max exceeds it by
 // more than 8 (log2 units), so p <= 2^8 and the O accumulator in TMEM is rescaled rarely.
 // Every mbarrier wait is bounded (time and polls); on expiry the kernel records
@@ -33,22 +35,26 @@ namespace arb {
 namespace {
 
 constexpr int kHeadDim = 128;
-constexpr int kTile = 128;                         // query rows per CTA and keys per tile
+constexpr int kTile = 128;                         // query rows per CTA
+constexpr int kKeys = 64;                          // keys per tile
 constexpr int kSoftmaxThreads = 128;
 constexpr int kThreads = kSoftmaxThreads + 32;     // + control warp
-constexpr uint32_t kTmemColumns = 512;             // S0 [0,128) S1 [128,256) O [256,384)
-constexpr uint32_t kTmemO = 256;
-constexpr uint32_t kHalfBytes = 128 * 128;         // 128 rows x 64 16-bit values (one 128B-swizzled half)
-constexpr uint32_t kTileBytes = 2 * kHalfBytes;    // 128 rows x 128 values
+constexpr uint32_t kTmemColumns = 256;             // S0 [0,64) S1 [64,128) O [128,256)
+constexpr uint32_t kTmemO = 2 * kKeys;
+constexpr uint32_t kRowBytes = 128;                // 64 16-bit values: one 128B-swizzled row of a half
+constexpr uint32_t kQHalfBytes = kTile * kRowBytes;      // 128 rows x 64 values (16 KB)
+constexpr uint32_t kQBytes = 2 * kQHalfBytes;            // 128 rows x 128 values
+constexpr uint32_t kKvHalfBytes = kKeys * kRowBytes;     // 64 rows x 64 values (8 KB)
+constexpr uint32_t kKvBytes = 2 * kKvHalfBytes;          // 64 rows x 128 values
 constexpr uint32_t kSpinLimit = 1u << 26;          // hard backstop on polls per wait
 constexpr uint64_t kWaitLimitNs = 500ull * 1000 * 1000;  // a wait gives up after 0.5 s
 constexpr float kRescaleThreshold = 8.0f;          // log2 units
 
 // shared memory (1024-byte aligned): Q | K stage 0,1 | V stage 0,1 | control
 constexpr uint32_t kQOffset = 0;
-constexpr uint32_t kKOffset = kTileBytes;
-constexpr uint32_t kVOffset = 3 * kTileBytes;
-constexpr uint32_t kControlOffset = 5 * kTileBytes;
+constexpr uint32_t kKOffset = kQBytes;
+constexpr uint32_t kVOffset = kQBytes + 2 * kKvBytes;
+constexpr uint32_t kControlOffset = kQBytes + 4 * kKvBytes;
 
 struct __align__(8) Control {
   uint64_t q_bar;
@@ -120,17 +126,17 @@ __device__ __forceinline__ uint64_t desc_k_major(uint32_t address) {
          (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) | (static_cast<uint64_t>(2) << 61);
 }
 // MN-major 128B-swizzled operand (V as B of P.V): each 128-byte row holds 64 consecutive N (head
-// dim) values of one K (key); 8 rows form a 1024-byte atom; the two 64-wide N halves are 16 KB
+// dim) values of one K (key); 8 rows form a 1024-byte atom; the two 64-wide N halves are 8 KB
 // apart (leading byte offset), consecutive 8-key groups 1024 bytes apart (stride byte offset).
 __device__ __forceinline__ uint64_t desc_mn_major(uint32_t address) {
-  return static_cast<uint64_t>((address >> 4) & 0x3FFFu) | (static_cast<uint64_t>(kHalfBytes >> 4) << 16) |
+  return static_cast<uint64_t>((address >> 4) & 0x3FFFu) | (static_cast<uint64_t>(kKvHalfBytes >> 4) << 16) |
          (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) | (static_cast<uint64_t>(2) << 61);
 }
 
-// kind::f16 instruction descriptor, fp32 accumulator, M = N = 128; format 0 = fp16, 1 = bf16
+// kind::f16 instruction descriptor, fp32 accumulator, M = 128, N = n; format 0 = fp16, 1 = bf16
 // (A and B always of the same format); A K-major, B K-major or MN-major.
-constexpr uint32_t idesc(uint32_t format, bool b_mn_major) {
-  return (1u << 4) | (format << 7) | (format << 10) | (b_mn_major ? (1u << 16) : 0u) | ((128u >> 3) << 17) |
+constexpr uint32_t idesc(uint32_t format, bool b_mn_major, uint32_t n) {
+  return (1u << 4) | (format << 7) | (format << 10) | (b_mn_major ? (1u << 16) : 0u) | ((n >> 3) << 17) |
          ((128u >> 4) << 24);
 }
 
@@ -193,7 +199,7 @@ struct Args {
 };
 
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     attention_tc_kernel(const __grid_constant__ CUtensorMap map, const Args args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -215,8 +221,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int q0 = query_tile * kTile;
   const int last_query = min(q0 + kTile, length) - 1;
   const int first_key = args.sliding_window > 0 ? max(0, q0 - args.sliding_window + 1) : 0;
-  const int tile_begin = first_key / kTile;
-  const int tile_end = last_query / kTile + 1;
+  const int tile_begin = first_key / kKeys;
+  const int tile_end = last_query / kKeys + 1;
   const int tiles = tile_end - tile_begin;
 
   if (tid == 0) {
@@ -259,22 +265,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto load_kv = [&](int j) {
         const int stage = j & 1;
         last_kv[stage] = j;
-        const int y = prompt_begin + (tile_begin + j) * kTile;
+        const int y = prompt_begin + (tile_begin + j) * kKeys;
         const uint32_t bar = smem_u32(&ctl.kv_bar[stage]);
-        mbar_expect_tx(bar, 2 * kTileBytes);
-        tma_load_2d(k_smem + stage * kTileBytes, &map, k_x, y, bar);
-        tma_load_2d(k_smem + stage * kTileBytes + kHalfBytes, &map, k_x + 64, y, bar);
-        tma_load_2d(v_smem + stage * kTileBytes, &map, v_x, y, bar);
-        tma_load_2d(v_smem + stage * kTileBytes + kHalfBytes, &map, v_x + 64, y, bar);
+        mbar_expect_tx(bar, 2 * kKvBytes);
+        tma_load_2d(k_smem + stage * kKvBytes, &map, k_x, y, bar);
+        tma_load_2d(k_smem + stage * kKvBytes + kKvHalfBytes, &map, k_x + 64, y, bar);
+        tma_load_2d(v_smem + stage * kKvBytes, &map, v_x, y, bar);
+        tma_load_2d(v_smem + stage * kKvBytes + kKvHalfBytes, &map, v_x + 64, y, bar);
       };
       auto issue_s = [&](int j) {
         const int stage = j & 1;
         fence_after();
 #pragma unroll
-        for (int kk = 0; kk < kHeadDim / 16; ++kk) {
-          const uint32_t offset = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-          mma_ss(tmem + stage * 128, desc_k_major(q_smem + offset), desc_k_major(k_smem + stage * kTileBytes + offset),
-                 args.idesc_s, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < kHeadDim / 16; ++kk) {  // 16 head-dim values per MMA (32 bytes of a row)
+          const uint32_t q_offset = (kk >> 2) * kQHalfBytes + (kk & 3) * 32;
+          const uint32_t k_offset = (kk >> 2) * kKvHalfBytes + (kk & 3) * 32;
+          mma_ss(tmem + stage * kKeys, desc_k_major(q_smem + q_offset),
+                 desc_k_major(k_smem + stage * kKvBytes + k_offset), args.idesc_s, kk > 0 ? 1u : 0u);
         }
         mma_commit(smem_u32(&ctl.s_bar[stage]));
       };
@@ -282,15 +289,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int stage = j & 1;
         fence_after();
 #pragma unroll
-        for (int kk = 0; kk < kTile / 16; ++kk) {  // 16 keys per MMA: 8 packed TMEM columns of P
-          mma_ts(tmem + kTmemO, tmem + stage * 128 + kk * 8, desc_mn_major(v_smem + stage * kTileBytes + kk * 2048),
-                 args.idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < kKeys / 16; ++kk) {  // 16 keys per MMA: 8 packed TMEM columns of P
+          mma_ts(tmem + kTmemO, tmem + stage * kKeys + kk * 8,
+                 desc_mn_major(v_smem + stage * kKvBytes + kk * 16 * kRowBytes), args.idesc_pv,
+                 (j > 0 || kk > 0) ? 1u : 0u);
         }
         mma_commit(o_bar);
       };
-      mbar_expect_tx(q_bar, kTileBytes);
-      tma_load_2d(q_smem, &map, q_x, prompt_begin + q0, q_bar);
-      tma_load_2d(q_smem + kHalfBytes, &map, q_x + 64, prompt_begin + q0, q_bar);
+      mbar_expect_tx(q_bar, kQBytes);
+      for (int half = 0; half < 2; ++half) {     // four 64 x 64 boxes: (column half, row half)
+        for (int rows = 0; rows < 2; ++rows) {
+          tma_load_2d(q_smem + half * kQHalfBytes + rows * kKvHalfBytes, &map, q_x + 64 * half,
+                      prompt_begin + q0 + rows * kKeys, q_bar);
+        }
+      }
       load_kv(0);
       if (tiles > 1) load_kv(1);
       bool ok = mbar_wait(q_bar, 0) && mbar_wait(smem_u32(&ctl.kv_bar[0]), 0);
@@ -347,30 +359,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       fence_after();
-      const int k0 = (tile_begin + j) * kTile;
-      float x[kTile];
+      const int k0 = (tile_begin + j) * kKeys;
+      float x[kKeys];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < kKeys / 32; ++c) {
         uint32_t raw[32];
-        tmem_ld32(tmem + lane_base + stage * 128 + c * 32, raw);
+        tmem_ld32(tmem + lane_base + stage * kKeys + c * 32, raw);
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(raw[i]) * scale_log2;
       }
-      const bool diagonal = k0 + kTile - 1 > q0 || k0 + kTile > length || args.sliding_window > 0;
+      const bool diagonal = k0 + kKeys - 1 > q0 || k0 + kKeys > length || args.sliding_window > 0;
       float m_tile = -INFINITY;
       if (diagonal) {
         const int key_min = args.sliding_window > 0 ? query - args.sliding_window + 1 : 0;
         const int key_max = min(query, length - 1);
 #pragma unroll
-        for (int i = 0; i < kTile; ++i) {
+        for (int i = 0; i < kKeys; ++i) {
           const int key = k0 + i;
           if (key < key_min || key > key_max) x[i] = -INFINITY;
           m_tile = fmaxf(m_tile, x[i]);
         }
       } else {
 #pragma unroll
-        for (int i = 0; i < kTile; ++i) m_tile = fmaxf(m_tile, x[i]);
+        for (int i = 0; i < kKeys; ++i) m_tile = fmaxf(m_tile, x[i]);
       }
       // the row's reference max moves when the tile max exceeds it by more than the threshold
       // (or on the row's first unmasked key); O already holds earlier tiles only when j > 0
@@ -401,17 +413,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (move) m_ref = m_tile;
       const float reference = m_ref == -INFINITY ? 0.0f : m_ref;
       float sum = 0.0f;
+      {
+        uint32_t packed[kKeys / 2];  // 64 probabilities -> 32 TMEM columns of 16-bit pairs
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t packed[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float p0 = exp2f(x[c * 64 + 2 * i] - reference);
-          const float p1 = exp2f(x[c * 64 + 2 * i + 1] - reference);
+        for (int i = 0; i < kKeys / 2; ++i) {
+          const float p0 = exp2f(x[2 * i] - reference);
+          const float p1 = exp2f(x[2 * i + 1] - reference);
           sum += p0 + p1;
           packed[i] = pack2<T>(p0, p1);
         }
-        tmem_st32(tmem + lane_base + stage * 128 + c * 32, packed);
+        tmem_st32(tmem + lane_base + stage * kKeys, packed);
       }
       l += sum;
       tmem_wait_st();
@@ -506,7 +517,7 @@ cudaError_t launch_typed(const AttentionArgs& a, cudaStream_t stream) {
   CUtensorMap map;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(a.rows)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(width) * 2};
-  const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(kTile)};
+  const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(kKeys)};  // 64 x 64 boxes for Q, K and V
   const cuuint32_t element_strides[2] = {1, 1};
   const CUtensorMapDataType type =
       std::is_same_v<T, __half> ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -524,8 +535,8 @@ cudaError_t launch_typed(const AttentionArgs& a, cudaStream_t stream) {
   args.kv_heads = a.kv_heads;
   args.sliding_window = a.sliding_window;
   const uint32_t format = std::is_same_v<T, __half> ? 0u : 1u;
-  args.idesc_s = idesc(format, false);
-  args.idesc_pv = idesc(format, true);
+  args.idesc_s = idesc(format, false, kKeys);     // S = Q K^T: 128 x 64 per tile
+  args.idesc_pv = idesc(format, true, kHeadDim);  // O += P V: 128 x 128
   args.status = a.status;
   const dim3 grid(a.tile_count, a.query_heads);
   attention_tc_kernel<T><<<grid, kThreads, kSmemBytes, stream>>>(map, args);

@@ -19,8 +19,9 @@ namespace arb {
 namespace {
 
 constexpr int kRowThreadsCap = 256;
-constexpr int kRopeUnroll = 4;   // heads per rotary loop iteration (loads in flight per thread)
-constexpr int kSiluUnroll = 4;   // 8-value chunks in flight per SwiGLU thread
+constexpr int kRopeTokens = 2;       // tokens per rotary step (loads in flight per thread)
+constexpr int kRopeMaxThreads = 512;
+constexpr int kSiluUnroll = 2;   // 8-value chunks in flight per SwiGLU thread
 
 // ---------------------------------------------------------------------------------------------
 // Row kernels: one CTA per token row, each thread holds VPT vectors of 8 channels in registers,
@@ -130,64 +131,52 @@ __global__ void __launch_bounds__(kRowThreadsCap) rms_norm_residual_kernel(
 
 // ---------------------------------------------------------------------------------------------
 // Bias + rotary embedding, in place on the fused [tokens, (Hq + 2 Hkv) * D] projection output.
-// One thread owns 8 rotation pairs (x_i, x_{i + D/2}) at one offset of one token and walks all of
-// that token's heads, so its cos/sin values are read once; kRopeUnroll heads are loaded before
-// any is stored. Query and key heads get bias + rotation; value heads get the bias only (and
-// are skipped without bias).
+// A CTA walks tokens (kRopeTokens per step, all loaded before any is stored); its threads tile one
+// token row: thread i owns 8 rotation pairs (x_j, x_{j + D/2}) of one head, so a token's row is
+// read and written with 256-byte coalesced segments and its cos/sin row (shared by every head)
+// comes from L1. Query and key heads get bias + rotation; value heads get the bias only (and are
+// skipped without bias).
 // ---------------------------------------------------------------------------------------------
 template <typename T>
-__global__ void rotary_bias_kernel(T* __restrict__ qkv, const float* __restrict__ bias,
-                                   const int32_t* __restrict__ positions, int tokens, int query_heads,
-                                   int kv_heads, int head_dim, const float* __restrict__ cos_table,
-                                   const float* __restrict__ sin_table, int table_positions,
-                                   int* status) {
+__global__ void __launch_bounds__(kRopeMaxThreads) rotary_bias_kernel(
+    T* __restrict__ qkv, const float* __restrict__ bias, const int32_t* __restrict__ positions, int tokens,
+    int query_heads, int kv_heads, int head_dim, const float* __restrict__ cos_table,
+    const float* __restrict__ sin_table, int table_positions, int* status) {
   const int half = head_dim >> 1;
   const int chunks_per_head = half >> 3;
   const int rotated_heads = query_heads + kv_heads;
   const int heads = bias != nullptr ? rotated_heads + kv_heads : rotated_heads;
   const int row_width = (query_heads + 2 * kv_heads) * head_dim;
-  const int total = tokens * chunks_per_head;  // < 2^31: tokens and head_dim are bounded by the launcher
-  for (int item = blockIdx.x * blockDim.x + threadIdx.x; item < total; item += gridDim.x * blockDim.x) {
-    const int token = item / chunks_per_head;
-    const int chunk = item - token * chunks_per_head;
-    const int position = positions[token];
-    const bool in_table = position >= 0 && position < table_positions;
-    if (!in_table) report_status(status, kStatusPositionOutOfRange);
-    float c[8];
-    float s[8];
-    if (in_table) {
-      const float* cos_row = cos_table + static_cast<size_t>(position) * half + chunk * 8;
-      const float* sin_row = sin_table + static_cast<size_t>(position) * half + chunk * 8;
-      const float4 c0 = __ldg(reinterpret_cast<const float4*>(cos_row));
-      const float4 c1 = __ldg(reinterpret_cast<const float4*>(cos_row + 4));
-      const float4 s0 = __ldg(reinterpret_cast<const float4*>(sin_row));
-      const float4 s1 = __ldg(reinterpret_cast<const float4*>(sin_row + 4));
-      c[0] = c0.x; c[1] = c0.y; c[2] = c0.z; c[3] = c0.w; c[4] = c1.x; c[5] = c1.y; c[6] = c1.z; c[7] = c1.w;
-      s[0] = s0.x; s[1] = s0.y; s[2] = s0.z; s[3] = s0.w; s[4] = s1.x; s[5] = s1.y; s[6] = s1.z; s[7] = s1.w;
-    }
-    // without a valid position only the bias-only value heads are written
-    const int first_head = in_table ? 0 : rotated_heads;
-    T* row = qkv + static_cast<size_t>(token) * row_width + chunk * 8;
-    for (int h0 = first_head; h0 < heads; h0 += kRopeUnroll) {
-      uint4 low_raw[kRopeUnroll];
-      uint4 high_raw[kRopeUnroll];
+  const int slots = heads * chunks_per_head;
+  for (int slot = threadIdx.x; slot < slots; slot += blockDim.x) {
+    const int head = slot / chunks_per_head;
+    const int chunk = slot - head * chunks_per_head;
+    const int column = head * head_dim + chunk * 8;
+    const bool rotate = head < rotated_heads;
+    for (int first = blockIdx.x * kRopeTokens; first < tokens; first += gridDim.x * kRopeTokens) {
+      uint4 low_raw[kRopeTokens];
+      uint4 high_raw[kRopeTokens];
+      int position[kRopeTokens];
 #pragma unroll
-      for (int u = 0; u < kRopeUnroll; ++u) {
-        if (h0 + u < heads) {
-          low_raw[u] = *reinterpret_cast<const uint4*>(row + (h0 + u) * head_dim);
-          high_raw[u] = *reinterpret_cast<const uint4*>(row + (h0 + u) * head_dim + half);
+      for (int k = 0; k < kRopeTokens; ++k) {
+        const int token = first + k;
+        if (token < tokens) {
+          const T* at = qkv + static_cast<size_t>(token) * row_width + column;
+          low_raw[k] = *reinterpret_cast<const uint4*>(at);
+          high_raw[k] = *reinterpret_cast<const uint4*>(at + half);
+          position[k] = positions[token];
         }
       }
 #pragma unroll
-      for (int u = 0; u < kRopeUnroll; ++u) {
-        const int head = h0 + u;
-        if (head >= heads) break;
+      for (int k = 0; k < kRopeTokens; ++k) {
+        const int token = first + k;
+        if (token >= tokens) break;
         float low[8];
         float high[8];
-        unpack8<T>(low_raw[u], low);
-        unpack8<T>(high_raw[u], high);
+        unpack8<T>(low_raw[k], low);
+        unpack8<T>(high_raw[k], high);
         if (bias != nullptr) {
-          const float* b = bias + head * head_dim + chunk * 8;
+          const float* b = bias + column;
           const float4 b0 = __ldg(reinterpret_cast<const float4*>(b));
           const float4 b1 = __ldg(reinterpret_cast<const float4*>(b + 4));
           const float4 b2 = __ldg(reinterpret_cast<const float4*>(b + half));
@@ -200,7 +189,20 @@ __global__ void rotary_bias_kernel(T* __restrict__ qkv, const float* __restrict_
             high[i] += bh[i];
           }
         }
-        if (head < rotated_heads) {
+        if (rotate) {
+          const int p = position[k];
+          if (p < 0 || p >= table_positions) {  // the row keeps its input values; the call fails
+            report_status(status, kStatusPositionOutOfRange);
+            continue;
+          }
+          const float* cos_row = cos_table + static_cast<size_t>(p) * half + chunk * 8;
+          const float* sin_row = sin_table + static_cast<size_t>(p) * half + chunk * 8;
+          const float4 c0 = __ldg(reinterpret_cast<const float4*>(cos_row));
+          const float4 c1 = __ldg(reinterpret_cast<const float4*>(cos_row + 4));
+          const float4 s0 = __ldg(reinterpret_cast<const float4*>(sin_row));
+          const float4 s1 = __ldg(reinterpret_cast<const float4*>(sin_row + 4));
+          const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+          const float s[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const float l = low[i];
@@ -209,8 +211,9 @@ __global__ void rotary_bias_kernel(T* __restrict__ qkv, const float* __restrict_
             high[i] = h * c[i] + l * s[i];
           }
         }
-        *reinterpret_cast<uint4*>(row + head * head_dim) = pack8<T>(low);
-        *reinterpret_cast<uint4*>(row + head * head_dim + half) = pack8<T>(high);
+        T* at = qkv + static_cast<size_t>(token) * row_width + column;
+        *reinterpret_cast<uint4*>(at) = pack8<T>(low);
+        *reinterpret_cast<uint4*>(at + half) = pack8<T>(high);
       }
     }
   }
@@ -238,7 +241,7 @@ __global__ void rope_table_kernel(float* __restrict__ cos_out, float* __restrict
 // output has g in columns [0, I) and u in [I, 2I) of each row).
 // ---------------------------------------------------------------------------------------------
 template <typename T>
-__global__ void silu_multiply_kernel(const T* __restrict__ gate, const T* __restrict__ up, long long in_stride,
+__global__ void __launch_bounds__(256, 6) silu_multiply_kernel(const T* __restrict__ gate, const T* __restrict__ up, long long in_stride,
                                      T* __restrict__ out, long long out_stride, int tokens, int width) {
   // CTAs walk rows; a thread handles chunks c, c + blockDim, ... of the row, kSiluUnroll of them
   // loaded before any is computed (no integer division on the index path)
@@ -317,6 +320,16 @@ int sm_count() {
   return cached;
 }
 
+// CTAs of `kernel` that fit on one SM at `threads` threads (registers and shared memory decide).
+template <typename Kernel>
+static int resident_per_sm(Kernel kernel, int threads) {
+  int blocks = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, threads, 0) != cudaSuccess || blocks <= 0) {
+    blocks = 1;
+  }
+  return blocks;
+}
+
 static int stride_grid(long long items, int threads, int ctas_per_sm) {
   const long long needed = (items + threads - 1) / threads;
   const long long cap = static_cast<long long>(sm_count()) * ctas_per_sm;
@@ -385,10 +398,14 @@ cudaError_t launch_rotary_bias(void* qkv, const float* bias, const int32_t* posi
                                const float* sin_table, int table_positions, int* status, int dtype,
                                cudaStream_t stream) {
   if (tokens <= 0) return cudaSuccess;
-  if (head_dim % 16 != 0 || head_dim > 1024 || tokens > (1 << 24)) return cudaErrorInvalidValue;
-  const long long items = static_cast<long long>(tokens) * (head_dim / 16);
-  const int threads = 256;
-  const int grid = stride_grid(items, threads, 8);
+  if (head_dim % 16 != 0 || head_dim > 1024) return cudaErrorInvalidValue;
+  const int heads = query_heads + kv_heads + (bias != nullptr ? kv_heads : 0);
+  const int slots = heads * (head_dim / 16);
+  const int threads = std::min(kRopeMaxThreads, (slots + 31) & ~31);
+  const int per_sm = dtype == kActFp16 ? resident_per_sm(rotary_bias_kernel<__half>, threads)
+                                       : resident_per_sm(rotary_bias_kernel<__nv_bfloat16>, threads);
+  // one wave of resident CTAs walks all tokens (no tail wave)
+  const int grid = std::max(1, std::min((tokens + kRopeTokens - 1) / kRopeTokens, sm_count() * per_sm));
   if (dtype == kActFp16) {
     rotary_bias_kernel<__half><<<grid, threads, 0, stream>>>(static_cast<__half*>(qkv), bias, positions, tokens,
                                                              query_heads, kv_heads, head_dim, cos_table, sin_table,
@@ -416,7 +433,9 @@ cudaError_t launch_silu_multiply(const void* gate, const void* up, long long in_
                                  long long out_stride, int tokens, int width, int dtype, cudaStream_t stream) {
   if (tokens <= 0 || width <= 0) return cudaSuccess;
   const int threads = 256;
-  const int grid = std::min(tokens, sm_count() * 8);
+  const int per_sm = dtype == kActFp16 ? resident_per_sm(silu_multiply_kernel<__half>, threads)
+                                       : resident_per_sm(silu_multiply_kernel<__nv_bfloat16>, threads);
+  const int grid = std::min(tokens, sm_count() * per_sm);  // one wave of resident CTAs walks all rows
   if (dtype == kActFp16) {
     silu_multiply_kernel<__half><<<grid, threads, 0, stream>>>(static_cast<const __half*>(gate),
                                                                static_cast<const __half*>(up), in_stride,
