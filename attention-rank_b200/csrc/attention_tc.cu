@@ -17,6 +17,14 @@
 //     O += P_j V_j  (A = P from TMEM, B = V from shared memory, MN-major) after the softmax.
 // A CTA holds 256 TMEM columns (S0 | S1 | O) and 96 KB of shared memory, so two CTAs share an
 // SM: one's softmax, set-up and epilogue overlap the other's MMAs.
+//
+// Fused attention mass (optional, `mass_partials` non-null): for the query rows of the probe
+// (the prompt's query span) the softmax warps also add each tile's probabilities into per-span
+// sums, kept relative to the same running reference as O and l (rescaled with them) and divided
+// by l at the end, so each row contributes sum_{k in span} softmax(q.k / sqrt(D)) exactly
+// (reference: reduce_document_attention over softmax_causal_kernel's output, kernels.cu:202-236,
+// :117-162, with the normalize_by_length divisor of kernels.cu:211). Each CTA writes one partial
+// per span: the fixed-order sum over its rows.
 // Rescaling: exponents use a reference max m_ref that moves only when the row max exceeds it by
 // more than 8 (log2 units), so p <= 2^8 and the O accumulator in TMEM is rescaled rarely.
 // Every mbarrier wait is bounded (time and polls); on expiry the kernel records
@@ -56,7 +64,9 @@ constexpr uint32_t kKOffset = kQBytes;
 constexpr uint32_t kVOffset = kQBytes + 2 * kKvBytes;
 constexpr uint32_t kControlOffset = kQBytes + 4 * kKvBytes;
 
-struct __align__(8) Control {
+constexpr int kMaxSpans = kMassMaxSpans;
+
+struct __align__(16) Control {
   uint64_t q_bar;
   uint64_t kv_bar[2];
   uint64_t s_bar[2];
@@ -65,8 +75,14 @@ struct __align__(8) Control {
   uint64_t done_bar;  // every MMA of the CTA completed (one commit after the last P.V)
   uint32_t tmem_base;
   volatile int abort;
+  int span_lo[kMaxSpans];  // fused mass: the prompt's document spans
+  int span_hi[kMaxSpans];
+  float warp_sums[4][kMaxSpans];
 };
-constexpr size_t kSmemBytes = kControlOffset + sizeof(Control) + 1024;
+// dynamic shared memory: the fixed part, then (fused mass only) float sigma[span_count][128]
+constexpr size_t kSigmaOffset = kControlOffset + ((sizeof(Control) + 15) & ~size_t(15));
+constexpr size_t kSmemBytes = kSigmaOffset + 1024;
+constexpr size_t smem_bytes(int span_count) { return kSmemBytes + static_cast<size_t>(span_count) * kTile * 4; }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* pointer) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(pointer));
@@ -196,6 +212,14 @@ struct Args {
   uint32_t idesc_s;
   uint32_t idesc_pv;
   int* status;
+  // fused mass (mass_partials == nullptr: attention only)
+  const int32_t* query_spans;  // [prompts][2], prompt-relative
+  const int32_t* spans;        // [prompts][span_count][2]
+  const int32_t* mass_items;   // [prompts + 1] partial slots per prompt: Hq x query tiles in the span
+  float* mass_partials;        // [items][span_count]
+  int span_count;
+  int normalize_by_length;
+  int reference_chunk;
 };
 
 template <typename T>
@@ -224,6 +248,22 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int tile_begin = first_key / kKeys;
   const int tile_end = last_query / kKeys + 1;
   const int tiles = tile_end - tile_begin;
+
+  // fused mass: does this query tile hold rows of the probe's query span?
+  int query_lo = 0, query_hi = 0;
+  if (args.mass_partials != nullptr) {
+    query_lo = max(args.query_spans[2 * prompt], 0);
+    query_hi = min(args.query_spans[2 * prompt + 1], length);
+  }
+  const bool capture = args.mass_partials != nullptr && query_hi > query_lo && q0 < query_hi && q0 + kTile > query_lo;
+  const int S = capture ? args.span_count : 0;
+  float* sigma = reinterpret_cast<float*>(smem + kSigmaOffset);
+  if (tid < S) {
+    const int32_t* span = args.spans + 2 * (static_cast<size_t>(prompt) * args.span_count + tid);
+    ctl.span_lo[tid] = max(span[0], 0);
+    ctl.span_hi[tid] = span[1];
+  }
+  for (int i = tid; i < S * kTile; i += kThreads) sigma[i] = 0.0f;
 
   if (tid == 0) {
     mbar_init(smem_u32(&ctl.q_bar), 1);
@@ -344,6 +384,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // ------------------------------------------------------------------ softmax warps
     const int row = tid;                       // TMEM lane
     const int query = q0 + row;                // prompt-relative
+    const bool row_in = capture && query >= query_lo && query < query_hi;  // a probe row
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
     const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(kHeadDim));
     float m_ref = -INFINITY;
@@ -409,6 +450,9 @@ __global__ void __launch_bounds__(kThreads, 2)
           tmem_st32(tmem + lane_base + kTmemO + c * 32, raw);
         }
         l *= factor;
+        if (row_in && factor != 1.0f) {
+          for (int s = 0; s < S; ++s) sigma[s * kTile + row] *= factor;
+        }
       }
       if (move) m_ref = m_tile;
       const float reference = m_ref == -INFINITY ? 0.0f : m_ref;
@@ -421,8 +465,20 @@ __global__ void __launch_bounds__(kThreads, 2)
           const float p1 = exp2f(x[2 * i + 1] - reference);
           sum += p0 + p1;
           packed[i] = pack2<T>(p0, p1);
+          x[2 * i] = p0;
+          x[2 * i + 1] = p1;
         }
         tmem_st32(tmem + lane_base + stage * kKeys, packed);
+      }
+      // fused mass: span sums of this tile's fp32 probabilities (spans and k0 are CTA-uniform)
+      for (int s = 0; s < S; ++s) {
+        const int lo = max(ctl.span_lo[s], k0) - k0;
+        const int hi = min(ctl.span_hi[s], k0 + kKeys) - k0;
+        if (lo >= hi) continue;
+        float acc = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kKeys; ++i) acc += (i >= lo && i < hi) ? x[i] : 0.0f;
+        if (row_in) sigma[s * kTile + row] += acc;
       }
       l += sum;
       tmem_wait_st();
@@ -461,7 +517,34 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (query < length && done) {
       args.lse[static_cast<size_t>(prompt_begin + query) * args.query_heads + head] = m_ref + log2f(l);
     }
+    if (S > 0) {
+      // fused mass: row values = span sums / l, with the reference's per-(row, span) length divisor
+      int chunk_end = length;
+      if (args.normalize_by_length) {
+        const int chunk = args.reference_chunk > 0 ? args.reference_chunk : length;
+        chunk_end = min((query / chunk + 1) * chunk, length);
+      }
+      for (int s = 0; s < S; ++s) {
+        float v = 0.0f;
+        if (row_in && done) {
+          v = sigma[s * kTile + row] * inv;
+          if (args.normalize_by_length) {
+            const int divisor = min(ctl.span_hi[s], chunk_end) - ctl.span_lo[s];
+            if (divisor > 0) v /= static_cast<float>(divisor);
+          }
+        }
+        v = warp_sum(v);
+        if (lane == 0) ctl.warp_sums[warp][s] = v;
+      }
+    }
     softmax_barrier();
+    if (S > 0 && tid < S) {
+      const int first_tile = query_lo / kTile;
+      const int query_tiles = (query_hi - 1) / kTile - first_tile + 1;
+      const int item = args.mass_items[prompt] + head * query_tiles + (query_tile - first_tile);
+      const float total = ctl.warp_sums[0][tid] + ctl.warp_sums[1][tid] + ctl.warp_sums[2][tid] + ctl.warp_sums[3][tid];
+      args.mass_partials[static_cast<size_t>(item) * S + tid] = total;
+    }
     const int out_width = args.query_heads * kHeadDim;
     T* out = static_cast<T*>(args.out);
 #pragma unroll 1
@@ -506,7 +589,7 @@ cudaError_t launch_typed(const AttentionArgs& a, cudaStream_t stream) {
   static uint64_t configured = 0;  // the shared-memory opt-in is a per-device attribute
   if (device >= 64 || !(configured & (1ull << device))) {
     const cudaError_t status = cudaFuncSetAttribute(attention_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                    static_cast<int>(kSmemBytes));
+                                                    static_cast<int>(smem_bytes(kMaxSpans)));
     if (status != cudaSuccess) return status;
     if (device < 64) configured |= 1ull << device;
   }
@@ -538,8 +621,15 @@ cudaError_t launch_typed(const AttentionArgs& a, cudaStream_t stream) {
   args.idesc_s = idesc(format, false, kKeys);     // S = Q K^T: 128 x 64 per tile
   args.idesc_pv = idesc(format, true, kHeadDim);  // O += P V: 128 x 128
   args.status = a.status;
+  args.query_spans = a.query_spans;
+  args.spans = a.spans;
+  args.mass_items = a.mass_items;
+  args.mass_partials = a.mass_partials;
+  args.span_count = a.mass_partials != nullptr ? a.span_count : 0;
+  args.normalize_by_length = a.normalize_by_length;
+  args.reference_chunk = a.reference_chunk;
   const dim3 grid(a.tile_count, a.query_heads);
-  attention_tc_kernel<T><<<grid, kThreads, kSmemBytes, stream>>>(map, args);
+  attention_tc_kernel<T><<<grid, kThreads, smem_bytes(args.span_count), stream>>>(map, args);
   return cudaGetLastError();
 }
 
@@ -552,6 +642,11 @@ cudaError_t launch_causal_attention_tc(const AttentionArgs& args, cudaStream_t s
   }
   // TMA: 16-byte aligned base; every x coordinate is a multiple of 64 elements (128 bytes)
   if ((reinterpret_cast<uintptr_t>(args.qkv) & 15) != 0) return cudaErrorInvalidValue;
+  if (args.mass_partials != nullptr &&
+      (args.span_count <= 0 || args.span_count > kMaxSpans || args.query_spans == nullptr || args.spans == nullptr ||
+       args.mass_items == nullptr)) {
+    return cudaErrorInvalidValue;
+  }
   if (args.dtype == kActFp16) return launch_typed<__half>(args, stream);
   if (args.dtype == kActBf16) return launch_typed<__nv_bfloat16>(args, stream);
   return cudaErrorInvalidValue;

@@ -345,7 +345,7 @@ void Engine::allocate() {
   lt_workspace_ = device_alloc(lt_workspace_bytes_);
 
   const size_t P = options_.max_batch_prompts;
-  meta_capacity_ = T + (P + 1) + 2 * P + 2 * P * kMassMaxSpans + 2 * (T / kAttentionQueryTile + P) + (P + 1) + 64;
+  meta_capacity_ = T + (P + 1) + 2 * P + 2 * P * kMassMaxSpans + 2 * (T / kAttentionQueryTile + P) + 2 * (P + 1) + 64;
   for (int i = 0; i < 2; ++i) {
     meta_device_[i] = static_cast<int32_t*>(device_alloc(meta_capacity_ * 4));
     check_cuda(cudaHostAlloc(reinterpret_cast<void**>(&meta_host_[i]), meta_capacity_ * 4, cudaHostAllocDefault),
@@ -668,7 +668,7 @@ BatchLayout Engine::build_metadata(const std::vector<PromptView>& prompts, const
   const int P = batch.count;
   const int S = span_count;
   const int group = c.num_attention_heads / c.num_key_value_heads;
-  size_t needed = static_cast<size_t>(batch.tokens) + (P + 1) + 2 * P + 2 * static_cast<size_t>(P) * S + (P + 1);
+  size_t needed = static_cast<size_t>(batch.tokens) + (P + 1) + 2 * P + 2 * static_cast<size_t>(P) * S + 2 * (P + 1);
   for (int i = 0; i < P; ++i) {
     needed += 2 * ((prompts[batch.first + i].token_count + kAttentionQueryTile - 1) / kAttentionQueryTile);
   }
@@ -719,6 +719,13 @@ BatchLayout Engine::build_metadata(const std::vector<PromptView>& prompts, const
     host[cursor] = host[cursor - 1] + mass_items_for_prompt(shape, c.num_key_value_heads);
     ++cursor;
   }
+  const size_t fused_items_at = cursor;
+  host[cursor++] = 0;
+  for (int i = 0; i < P; ++i) {
+    const int tiles = fused_mass_tiles(host + queries_at + 2 * i, prompts[batch.first + i].token_count);
+    host[cursor] = host[cursor - 1] + c.num_attention_heads * tiles;
+    ++cursor;
+  }
   BatchLayout layout;
   const double D = c.head_dim(), Hq = c.num_attention_heads;
   for (int i = 0; i < P; ++i) {
@@ -740,12 +747,14 @@ BatchLayout Engine::build_metadata(const std::vector<PromptView>& prompts, const
   layout.spans_at = spans_at;
   layout.tiles_at = tiles_at;
   layout.items_at = items_at;
+  layout.fused_items_at = fused_items_at;
   layout.size = cursor;
   layout.first = batch.first;
   layout.prompts = P;
   layout.tokens = batch.tokens;
   layout.tile_count = tile_count;
-  layout.item_count = host[cursor - 1];
+  layout.item_count = host[items_at + P];
+  layout.fused_item_count = host[cursor - 1];
   return layout;
 }
 
@@ -759,7 +768,8 @@ void Engine::run_batch(const std::vector<PromptView>& prompts, const Batch& batc
                              cudaMemcpyHostToDevice, stream_),
              "metadata upload");
   check_cuda(cudaEventRecord(meta_free_[slot], stream_), "cudaEventRecord");
-  ensure_partials(static_cast<size_t>(layout.item_count), span_count, range.count());
+  ensure_partials(static_cast<size_t>(std::max(layout.item_count, layout.fused_item_count)), span_count,
+                  range.count());
   execute_batch(layout, meta_device_[slot], span_count, range, normalize_by_length, rows_device, raw_rows_device,
                 device_accumulator);
 }
@@ -785,7 +795,8 @@ std::unique_ptr<PreparedScan> Engine::prepare_scan(const std::vector<PromptView>
     layout.spans_at += base;
     layout.tiles_at += base;
     layout.items_at += base;
-    max_items = std::max(max_items, static_cast<size_t>(layout.item_count));
+    layout.fused_items_at += base;
+    max_items = std::max(max_items, static_cast<size_t>(std::max(layout.item_count, layout.fused_item_count)));
     prepared->batches.push_back(layout);
   }
   ensure_partials(max_items, span_count, range.count());
@@ -829,7 +840,9 @@ void Engine::execute_batch(const BatchLayout& layout, const int32_t* dev, int sp
   const int32_t* d_queries = dev + layout.queries_at;
   const int32_t* d_spans = dev + layout.spans_at;
   const int32_t* d_tiles = dev + layout.tiles_at;
-  const int32_t* d_items = dev + layout.items_at;
+  const bool fused = options_.attention_kernel == 0;  // tcgen05 attention captures the mass itself
+  const int32_t* d_items = dev + (fused ? layout.fused_items_at : layout.items_at);
+  const int mass_items = fused ? layout.fused_item_count : item_count;
   const int layers = range.count();
 
   const int H = c.hidden_size, I = c.intermediate_size, Hq = c.num_attention_heads, Hkv = c.num_key_value_heads;
@@ -859,6 +872,12 @@ void Engine::execute_batch(const BatchLayout& layout, const int32_t* dev, int sp
   attention.dtype = dtype;
   attention.rows = M;
   attention.status = status_;
+  attention.query_spans = d_queries;
+  attention.spans = d_spans;
+  attention.mass_items = d_items;
+  attention.span_count = S;
+  attention.normalize_by_length = normalize_by_length ? 1 : 0;
+  attention.reference_chunk = options_.prefill_chunk_tokens;
 
   MassArgs mass;
   mass.qkv = qkv_;
@@ -867,7 +886,7 @@ void Engine::execute_batch(const BatchLayout& layout, const int32_t* dev, int sp
   mass.prompt_offsets = d_offsets;
   mass.query_spans = d_queries;
   mass.spans = d_spans;
-  mass.item_offsets = d_items;
+  mass.item_offsets = dev + layout.items_at;
   mass.prompt_count = P;
   mass.span_count = S;
   mass.item_count = item_count;
@@ -894,13 +913,15 @@ void Engine::execute_batch(const BatchLayout& layout, const int32_t* dev, int sp
                                     options_.max_sequence_length, status_, dtype, stream_),
                  "rotary");
     });
+    const bool probed = l >= range.begin;
+    float* layer_partials = probed ? partials_ + static_cast<size_t>(l - range.begin) * mass_items * S : nullptr;
+    attention.mass_partials = fused ? layer_partials : nullptr;
     timed(kClassAttention, layout.attention_flops, [&] {
-      check_cuda(options_.attention_kernel == 0 ? launch_causal_attention_tc(attention, stream_)
-                                                : launch_causal_attention(attention, stream_),
+      check_cuda(fused ? launch_causal_attention_tc(attention, stream_) : launch_causal_attention(attention, stream_),
                  "attention");
     });
-    if (l >= range.begin) {
-      mass.partials = partials_ + static_cast<size_t>(l - range.begin) * item_count * S;
+    if (probed && !fused) {
+      mass.partials = layer_partials;
       timed(kClassMass, layout.mass_flops, [&] { check_cuda(launch_document_mass(mass, stream_), "document mass"); });
     }
     // The last probed layer's attention output, o_proj and MLP feed only layers that are not run:
@@ -933,13 +954,13 @@ void Engine::execute_batch(const BatchLayout& layout, const int32_t* dev, int sp
   finalize.prompt_offsets = d_offsets;
   finalize.prompt_count = P;
   finalize.span_count = S;
-  finalize.item_count = item_count;
+  finalize.item_count = mass_items;
   finalize.layers = layers;
   finalize.query_heads = Hq;
   finalize.rows = rows_device;
   finalize.raw_rows = raw_rows_device;
   finalize.accumulator = device_accumulator;
-  timed(kClassFinalize, 4.0 * layers * item_count * S, [&] {
+  timed(kClassFinalize, 4.0 * layers * mass_items * S, [&] {
     check_cuda(launch_finalize_mass(finalize, stream_), "finalize");
   });
 }

@@ -97,12 +97,14 @@ struct LayerRange {
 
 // Offsets (int32 elements) of one batch's metadata inside a metadata buffer.
 struct BatchLayout {
-  size_t tokens_at = 0, offsets_at = 0, queries_at = 0, spans_at = 0, tiles_at = 0, items_at = 0, size = 0;
+  size_t tokens_at = 0, offsets_at = 0, queries_at = 0, spans_at = 0, tiles_at = 0, items_at = 0, fused_items_at = 0,
+         size = 0;
   int first = 0;       // index of the batch's first prompt
   int prompts = 0;
   int tokens = 0;
   int tile_count = 0;  // attention query tiles
-  int item_count = 0;  // mass CTAs
+  int item_count = 0;  // mass CTAs (separate mass kernel)
+  int fused_item_count = 0;  // mass partial slots of the fused attention (Hq x query tiles in the span)
   double attention_flops = 0;  // 4 D Hq x visible causal (query, key) pairs
   double mass_flops = 0;       // 2 D Hq x sum over prompts of query rows x document-span keys
 };

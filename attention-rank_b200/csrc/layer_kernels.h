@@ -49,10 +49,30 @@ struct AttentionArgs {
   int dtype = kActFp16;             // ActivationType of qkv and out
   int rows = 0;                     // rows of qkv (tensor-map extent; tcgen05 kernel)
   int* status = nullptr;            // device status word (tcgen05 kernel: wait timeouts)
+  // Fused attention mass (tcgen05 kernel only; mass_partials == nullptr: none). Partial slot of
+  // (prompt p, query head h, query tile t): mass_items[p] + h * tiles_p + (t - first_p), where
+  // first_p.. are the query tiles that hold rows of p's query span (fused_mass_tiles).
+  const int32_t* query_spans = nullptr;   // [prompts * 2], prompt-relative
+  const int32_t* spans = nullptr;         // [prompts * span_count * 2], prompt-relative
+  const int32_t* mass_items = nullptr;    // [prompts + 1]
+  float* mass_partials = nullptr;         // [items * span_count], each the sum over the tile's rows
+  int span_count = 0;
+  int normalize_by_length = 0;
+  int reference_chunk = 0;
 };
+
 cudaError_t launch_causal_attention(const AttentionArgs& args, cudaStream_t stream);
 cudaError_t launch_causal_attention_tc(const AttentionArgs& args, cudaStream_t stream);
 constexpr int kAttentionQueryTile = 128;
+
+// Query tiles (kAttentionQueryTile rows) that hold rows of a prompt's query span: the fused mass
+// writes one partial per (query head, such tile).
+inline int fused_mass_tiles(const int32_t* query_span, int length) {
+  const int begin = query_span[0] < 0 ? 0 : query_span[0];
+  const int end = query_span[1] > length ? length : query_span[1];
+  if (end <= begin) return 0;
+  return (end - 1) / kAttentionQueryTile - begin / kAttentionQueryTile + 1;
+}
 
 // Query->document attention mass (mass.cu).
 struct MassArgs {

@@ -49,12 +49,16 @@ def assert_rows_close(got, want, rel=MASS_REL):
     assert error.max() <= rel, f"max relative error {error.max():.3e} > {rel}"
 
 
-@pytest.mark.parametrize("bias,dtype", [(True, "fp16"), (False, "fp16"), (True, "bf16")])
-def test_small_model_rows_match_oracle(cuda, bias, dtype):
+@pytest.mark.parametrize("bias,dtype,kernel", [(True, "fp16", "tcgen05"), (False, "fp16", "tcgen05"),
+                                               (True, "bf16", "tcgen05"), (True, "fp16", "mma")])
+def test_small_model_rows_match_oracle(cuda, bias, dtype, kernel):
+    """tcgen05: attention with the mass fused into its softmax; mma: attention + the separate
+    tcgen05 mass kernel."""
     import attnrank as ar
     from oracle import forward as F
     config = small_config(bias)
-    engine = ar.Engine.synthetic(config, seed=0, options=ar.RuntimeOptions(activation_dtype=dtype))
+    engine = ar.Engine.synthetic(config, seed=0,
+                                 options=ar.RuntimeOptions(activation_dtype=dtype, attention_kernel=kernel))
     prompts = small_prompts(4, config.vocab_size)
     rows, first = engine.probe_rows(prompts)
     assert first == 0 and rows.shape == (4, config.num_hidden_layers, 5)
@@ -79,6 +83,26 @@ def test_small_model_layer_range_and_length_normalisation(cuda):
     # measure_attention: the layer-averaged single profile of model.cu:567-591
     got = engine.measure_attention(prompts[0], layer_span_begin=0, layer_span_end=4)
     assert_rows_close(got, oracle.measure_attention(oracle_prompt(prompts[0]), 0, 4))
+
+
+@pytest.mark.parametrize("kernel", ["tcgen05", "mma"])
+@pytest.mark.parametrize("normalize", [False, True])
+def test_long_question_over_several_query_tiles(cuda, kernel, normalize):
+    """A 300-token question starting mid-tile: the probe rows span three 128-row query tiles, so
+    the fused mass writes several partials per head, and length normalisation crosses the
+    reference's 512-token chunk boundary."""
+    import attnrank as ar
+    from attnrank import synthetic
+    from oracle import forward as F
+    config = small_config(True, layers=2)
+    engine = ar.Engine.synthetic(config, seed=2, options=ar.RuntimeOptions(attention_kernel=kernel))
+    shape = synthetic.PromptShape(documents=4, document_min=60, document_max=110, question=300)
+    prompts = synthetic.prompts(3, config.vocab_size, shape, seed=21)
+    rows, _ = engine.probe_rows(prompts, normalize_by_length=normalize)
+    oracle = F.OracleModel(oracle_shape(config), seed=2)
+    want, _ = oracle.probe([oracle_prompt(p) for p in prompts], normalize_by_length=normalize)
+    for p in range(len(prompts)):
+        assert_rows_close(rows[p], want[p])
 
 
 def test_small_model_scan_matches_host_accumulation(cuda):
