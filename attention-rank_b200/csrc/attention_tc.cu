@@ -470,15 +470,21 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         tmem_st32(tmem + lane_base + stage * kKeys, packed);
       }
-      // fused mass: span sums of this tile's fp32 probabilities (spans and k0 are CTA-uniform)
-      for (int s = 0; s < S; ++s) {
-        const int lo = max(ctl.span_lo[s], k0) - k0;
-        const int hi = min(ctl.span_hi[s], k0 + kKeys) - k0;
-        if (lo >= hi) continue;
-        float acc = 0.0f;
+      // fused mass: span sums of this tile's fp32 probabilities, by the warps that hold probe rows
+      // (spans and k0 are CTA-uniform); a span that covers the whole tile takes the tile's sum
+      if (S > 0 && __any_sync(0xffffffffu, row_in)) {
+        for (int s = 0; s < S; ++s) {
+          const int lo = max(ctl.span_lo[s], k0) - k0;
+          const int hi = min(ctl.span_hi[s], k0 + kKeys) - k0;
+          if (lo >= hi) continue;
+          float acc = sum;
+          if (lo > 0 || hi < kKeys) {
+            acc = 0.0f;
 #pragma unroll
-        for (int i = 0; i < kKeys; ++i) acc += (i >= lo && i < hi) ? x[i] : 0.0f;
-        if (row_in) sigma[s * kTile + row] += acc;
+            for (int i = 0; i < kKeys; ++i) acc += (i >= lo && i < hi) ? x[i] : 0.0f;
+          }
+          if (row_in) sigma[s * kTile + row] += acc;
+        }
       }
       l += sum;
       tmem_wait_st();

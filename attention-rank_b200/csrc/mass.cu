@@ -407,39 +407,32 @@ __global__ void finalize_mass_kernel(const float* __restrict__ partials, const i
                                      int prompt_count, int span_count, int item_count, int layers, int query_heads,
                                      double* __restrict__ rows_out, double* __restrict__ raw_rows_out,
                                      float* __restrict__ accumulator) {
-  for (int layer = threadIdx.x; layer < layers; layer += blockDim.x) {
-    double total[kMassMaxSpans];
-    for (int s = 0; s < span_count; ++s) total[s] = 0.0;
-    const float* layer_partials = partials + static_cast<size_t>(layer) * item_count * span_count;
-    for (int p = 0; p < prompt_count; ++p) {
-      const int length = prompt_offsets[p + 1] - prompt_offsets[p];
-      const ProbeRows rows = probe_rows(query_spans + 2 * p, length);
-      const double observations = static_cast<double>(rows.query_end - rows.query_begin) * query_heads;
-      double row[kMassMaxSpans];
-      double sum = 0.0;
-      for (int s = 0; s < span_count; ++s) {
-        double raw = 0.0;
-        for (int item = item_offsets[p]; item < item_offsets[p + 1]; ++item) {
-          raw += static_cast<double>(layer_partials[static_cast<size_t>(item) * span_count + s]);
-        }
-        row[s] = observations > 0.0 ? raw / observations : 0.0;
-        if (raw_rows_out != nullptr) raw_rows_out[(static_cast<size_t>(p) * layers + layer) * span_count + s] = row[s];
-        sum += row[s];
-      }
-      if (sum > 0.0) {
-        for (int s = 0; s < span_count; ++s) row[s] /= sum;
-      }
-      for (int s = 0; s < span_count; ++s) {
-        if (rows_out != nullptr) rows_out[(static_cast<size_t>(p) * layers + layer) * span_count + s] = row[s];
-        total[s] += row[s];
+  // one warp per layer, lane s owns span s; every sum runs in a fixed order
+  const int layer = blockIdx.x;
+  const int s = threadIdx.x;
+  const bool active = s < span_count;
+  const float* layer_partials = partials + static_cast<size_t>(layer) * item_count * span_count;
+  double total = 0.0;
+  for (int p = 0; p < prompt_count; ++p) {
+    const int length = prompt_offsets[p + 1] - prompt_offsets[p];
+    const ProbeRows rows = probe_rows(query_spans + 2 * p, length);
+    const double observations = static_cast<double>(rows.query_end - rows.query_begin) * query_heads;
+    double raw = 0.0;
+    if (active) {
+      for (int item = item_offsets[p]; item < item_offsets[p + 1]; ++item) {
+        raw += static_cast<double>(layer_partials[static_cast<size_t>(item) * span_count + s]);
       }
     }
-    if (accumulator != nullptr) {
-      for (int s = 0; s < span_count; ++s) {
-        accumulator[layer * span_count + s] += static_cast<float>(total[s]);
-      }
-    }
+    double row = observations > 0.0 ? raw / observations : 0.0;
+    if (active && raw_rows_out != nullptr) raw_rows_out[(static_cast<size_t>(p) * layers + layer) * span_count + s] = row;
+    double sum = row;  // inactive lanes hold 0
+#pragma unroll
+    for (int offset = 16; offset > 0; offset >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, offset);
+    if (sum > 0.0) row /= sum;
+    if (active && rows_out != nullptr) rows_out[(static_cast<size_t>(p) * layers + layer) * span_count + s] = row;
+    total += row;
   }
+  if (active && accumulator != nullptr) accumulator[layer * span_count + s] += static_cast<float>(total);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -520,7 +513,7 @@ cudaError_t launch_document_mass(const MassArgs& args, cudaStream_t stream) {
 cudaError_t launch_finalize_mass(const FinalizeArgs& args, cudaStream_t stream) {
   if (args.prompt_count <= 0 || args.layers <= 0) return cudaSuccess;
   if (args.span_count <= 0 || args.span_count > kMassMaxSpans) return cudaErrorInvalidValue;
-  finalize_mass_kernel<<<1, 64, 0, stream>>>(args.partials, args.item_offsets, args.query_spans, args.prompt_offsets,
+  finalize_mass_kernel<<<args.layers, 32, 0, stream>>>(args.partials, args.item_offsets, args.query_spans, args.prompt_offsets,
                                              args.prompt_count, args.span_count, args.item_count, args.layers,
                                              args.query_heads, args.rows, args.raw_rows, args.accumulator);
   return cudaGetLastError();
