@@ -19,8 +19,8 @@ namespace arb {
 namespace {
 
 constexpr int kRowThreadsCap = 256;
-constexpr int kRopeGroup = 4;        // tokens staged per rotary step (32 bytes each per thread)
-constexpr int kRopeMaxThreads = 1024;
+constexpr int kRopeTokens = 2;       // tokens per rotary step (loads in flight per thread)
+constexpr int kRopeMaxThreads = 512;
 constexpr int kSiluUnroll = 2;   // 8-value chunks in flight per SwiGLU thread
 
 // ---------------------------------------------------------------------------------------------
@@ -131,116 +131,90 @@ __global__ void __launch_bounds__(kRowThreadsCap) rms_norm_residual_kernel(
 
 // ---------------------------------------------------------------------------------------------
 // Bias + rotary embedding, in place on the fused [tokens, (Hq + 2 Hkv) * D] projection output.
-// Thread i of a CTA owns slot i of a token row: 8 rotation pairs (x_j, x_{j + D/2}) of one head.
-// A CTA walks groups of kRopeGroup consecutive tokens; each thread stages its slot of the next
-// group into shared memory with cp.async while it rotates the current one, so every thread keeps
-// kRopeGroup x 32 bytes in flight without spending registers on them (and reads back only what it
-// copied itself, so no CTA barrier is needed). Query and key heads get bias + rotation; value heads
-// get the bias only (and are skipped without bias). The slot's bias lives in registers; its cos/sin
-// row (shared by every head of the token) comes from L1.
+// A CTA walks tokens (kRopeTokens per step, all loaded before any is stored); its threads tile one
+// token row: thread i owns 8 rotation pairs (x_j, x_{j + D/2}) of one head, so a token's row is
+// read and written with 256-byte coalesced segments and its cos/sin row (shared by every head)
+// comes from L1. Query and key heads get bias + rotation; value heads get the bias only (and are
+// skipped without bias).
 // ---------------------------------------------------------------------------------------------
-__device__ __forceinline__ void cp_async16(void* smem_dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
-               "l"(src));
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
-__device__ __forceinline__ void cp_async_wait_one() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
-
 template <typename T>
 __global__ void __launch_bounds__(kRopeMaxThreads) rotary_bias_kernel(
     T* __restrict__ qkv, const float* __restrict__ bias, const int32_t* __restrict__ positions, int tokens,
     int query_heads, int kv_heads, int head_dim, const float* __restrict__ cos_table,
     const float* __restrict__ sin_table, int table_positions, int* status) {
-  extern __shared__ uint4 staged[];  // [2 stages][kRopeGroup tokens][slots][low, high]
   const int half = head_dim >> 1;
   const int chunks_per_head = half >> 3;
   const int rotated_heads = query_heads + kv_heads;
   const int heads = bias != nullptr ? rotated_heads + kv_heads : rotated_heads;
   const int row_width = (query_heads + 2 * kv_heads) * head_dim;
-  const int slots = heads * chunks_per_head;  // == blockDim.x rounded up to a warp
-  const int slot = threadIdx.x;
-  const bool active = slot < slots;
-  const int head = slot / chunks_per_head;
-  const int chunk = slot - head * chunks_per_head;
-  const int column = head * head_dim + chunk * 8;
-  const bool rotate = head < rotated_heads;
-  float bl[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  float bh[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  if (active && bias != nullptr) {
-    const float* b = bias + column;
-    const float4 b0 = __ldg(reinterpret_cast<const float4*>(b));
-    const float4 b1 = __ldg(reinterpret_cast<const float4*>(b + 4));
-    const float4 b2 = __ldg(reinterpret_cast<const float4*>(b + half));
-    const float4 b3 = __ldg(reinterpret_cast<const float4*>(b + half + 4));
-    bl[0] = b0.x; bl[1] = b0.y; bl[2] = b0.z; bl[3] = b0.w; bl[4] = b1.x; bl[5] = b1.y; bl[6] = b1.z; bl[7] = b1.w;
-    bh[0] = b2.x; bh[1] = b2.y; bh[2] = b2.z; bh[3] = b2.w; bh[4] = b3.x; bh[5] = b3.y; bh[6] = b3.z; bh[7] = b3.w;
-  }
-  const int groups = (tokens + kRopeGroup - 1) / kRopeGroup;
-  auto prefetch = [&](int group, int stage) {
-    if (active) {
+  const int slots = heads * chunks_per_head;
+  for (int slot = threadIdx.x; slot < slots; slot += blockDim.x) {
+    const int head = slot / chunks_per_head;
+    const int chunk = slot - head * chunks_per_head;
+    const int column = head * head_dim + chunk * 8;
+    const bool rotate = head < rotated_heads;
+    for (int first = blockIdx.x * kRopeTokens; first < tokens; first += gridDim.x * kRopeTokens) {
+      uint4 low_raw[kRopeTokens];
+      uint4 high_raw[kRopeTokens];
+      int position[kRopeTokens];
 #pragma unroll
-      for (int r = 0; r < kRopeGroup; ++r) {
-        const int token = group * kRopeGroup + r;
+      for (int k = 0; k < kRopeTokens; ++k) {
+        const int token = first + k;
         if (token < tokens) {
-          const T* src = qkv + static_cast<size_t>(token) * row_width + column;
-          uint4* dst = staged + (static_cast<size_t>(stage * kRopeGroup + r) * slots + slot) * 2;
-          cp_async16(dst, src);
-          cp_async16(dst + 1, src + half);
+          const T* at = qkv + static_cast<size_t>(token) * row_width + column;
+          low_raw[k] = *reinterpret_cast<const uint4*>(at);
+          high_raw[k] = *reinterpret_cast<const uint4*>(at + half);
+          position[k] = positions[token];
         }
       }
-    }
-    cp_async_commit();  // every thread commits one group per step (possibly empty)
-  };
-  int stage = 0;
-  if (blockIdx.x < groups) prefetch(blockIdx.x, 0);
-  for (int group = blockIdx.x; group < groups; group += gridDim.x, stage ^= 1) {
-    const int next = group + gridDim.x;
-    if (next < groups) {
-      prefetch(next, stage ^ 1);
-    } else {
-      cp_async_commit();
-    }
-    cp_async_wait_one();  // this thread's copies of `group` have landed
-    if (!active) continue;
 #pragma unroll
-    for (int r = 0; r < kRopeGroup; ++r) {
-      const int token = group * kRopeGroup + r;
-      if (token >= tokens) break;
-      const uint4* src = staged + (static_cast<size_t>(stage * kRopeGroup + r) * slots + slot) * 2;
-      float low[8];
-      float high[8];
-      unpack8<T>(src[0], low);
-      unpack8<T>(src[1], high);
+      for (int k = 0; k < kRopeTokens; ++k) {
+        const int token = first + k;
+        if (token >= tokens) break;
+        float low[8];
+        float high[8];
+        unpack8<T>(low_raw[k], low);
+        unpack8<T>(high_raw[k], high);
+        if (bias != nullptr) {
+          const float* b = bias + column;
+          const float4 b0 = __ldg(reinterpret_cast<const float4*>(b));
+          const float4 b1 = __ldg(reinterpret_cast<const float4*>(b + 4));
+          const float4 b2 = __ldg(reinterpret_cast<const float4*>(b + half));
+          const float4 b3 = __ldg(reinterpret_cast<const float4*>(b + half + 4));
+          const float bl[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+          const float bh[8] = {b2.x, b2.y, b2.z, b2.w, b3.x, b3.y, b3.z, b3.w};
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        low[i] += bl[i];
-        high[i] += bh[i];
-      }
-      if (rotate) {
-        const int p = positions[token];
-        if (p < 0 || p >= table_positions) {  // the row keeps its input values; the call fails
-          report_status(status, kStatusPositionOutOfRange);
-          continue;
+          for (int i = 0; i < 8; ++i) {
+            low[i] += bl[i];
+            high[i] += bh[i];
+          }
         }
-        const float* cos_row = cos_table + static_cast<size_t>(p) * half + chunk * 8;
-        const float* sin_row = sin_table + static_cast<size_t>(p) * half + chunk * 8;
-        const float4 c0 = __ldg(reinterpret_cast<const float4*>(cos_row));
-        const float4 c1 = __ldg(reinterpret_cast<const float4*>(cos_row + 4));
-        const float4 s0 = __ldg(reinterpret_cast<const float4*>(sin_row));
-        const float4 s1 = __ldg(reinterpret_cast<const float4*>(sin_row + 4));
-        const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-        const float s[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+        if (rotate) {
+          const int p = position[k];
+          if (p < 0 || p >= table_positions) {  // the row keeps its input values; the call fails
+            report_status(status, kStatusPositionOutOfRange);
+            continue;
+          }
+          const float* cos_row = cos_table + static_cast<size_t>(p) * half + chunk * 8;
+          const float* sin_row = sin_table + static_cast<size_t>(p) * half + chunk * 8;
+          const float4 c0 = __ldg(reinterpret_cast<const float4*>(cos_row));
+          const float4 c1 = __ldg(reinterpret_cast<const float4*>(cos_row + 4));
+          const float4 s0 = __ldg(reinterpret_cast<const float4*>(sin_row));
+          const float4 s1 = __ldg(reinterpret_cast<const float4*>(sin_row + 4));
+          const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+          const float s[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float l = low[i];
-          const float h = high[i];
-          low[i] = l * c[i] - h * s[i];
-          high[i] = h * c[i] + l * s[i];
+          for (int i = 0; i < 8; ++i) {
+            const float l = low[i];
+            const float h = high[i];
+            low[i] = l * c[i] - h * s[i];
+            high[i] = h * c[i] + l * s[i];
+          }
         }
+        T* at = qkv + static_cast<size_t>(token) * row_width + column;
+        *reinterpret_cast<uint4*>(at) = pack8<T>(low);
+        *reinterpret_cast<uint4*>(at + half) = pack8<T>(high);
       }
-      T* at = qkv + static_cast<size_t>(token) * row_width + column;
-      *reinterpret_cast<uint4*>(at) = pack8<T>(low);
-      *reinterpret_cast<uint4*>(at + half) = pack8<T>(high);
     }
   }
 }
@@ -427,32 +401,17 @@ cudaError_t launch_rotary_bias(void* qkv, const float* bias, const int32_t* posi
   if (head_dim % 16 != 0 || head_dim > 1024) return cudaErrorInvalidValue;
   const int heads = query_heads + kv_heads + (bias != nullptr ? kv_heads : 0);
   const int slots = heads * (head_dim / 16);
-  if (slots > kRopeMaxThreads) return cudaErrorInvalidValue;  // one thread per slot of a row
-  const int threads = (slots + 31) & ~31;
-  const size_t smem = static_cast<size_t>(2 * kRopeGroup) * slots * 32;
-  if (smem > 48 * 1024) {
-    const cudaError_t status =
-        dtype == kActFp16
-            ? cudaFuncSetAttribute(rotary_bias_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   static_cast<int>(smem))
-            : cudaFuncSetAttribute(rotary_bias_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   static_cast<int>(smem));
-    if (status != cudaSuccess) return status;
-  }
-  int per_sm = 0;
-  const cudaError_t occupancy =
-      dtype == kActFp16
-          ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rotary_bias_kernel<__half>, threads, smem)
-          : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rotary_bias_kernel<__nv_bfloat16>, threads, smem);
-  if (occupancy != cudaSuccess || per_sm <= 0) per_sm = 1;
-  // one wave of resident CTAs walks all token groups (no tail wave)
-  const int grid = std::max(1, std::min((tokens + kRopeGroup - 1) / kRopeGroup, sm_count() * per_sm));
+  const int threads = std::min(kRopeMaxThreads, (slots + 31) & ~31);
+  const int per_sm = dtype == kActFp16 ? resident_per_sm(rotary_bias_kernel<__half>, threads)
+                                       : resident_per_sm(rotary_bias_kernel<__nv_bfloat16>, threads);
+  // one wave of resident CTAs walks all tokens (no tail wave)
+  const int grid = std::max(1, std::min((tokens + kRopeTokens - 1) / kRopeTokens, sm_count() * per_sm));
   if (dtype == kActFp16) {
-    rotary_bias_kernel<__half><<<grid, threads, smem, stream>>>(static_cast<__half*>(qkv), bias, positions, tokens,
-                                                                query_heads, kv_heads, head_dim, cos_table, sin_table,
-                                                                table_positions, status);
+    rotary_bias_kernel<__half><<<grid, threads, 0, stream>>>(static_cast<__half*>(qkv), bias, positions, tokens,
+                                                             query_heads, kv_heads, head_dim, cos_table, sin_table,
+                                                             table_positions, status);
   } else if (dtype == kActBf16) {
-    rotary_bias_kernel<__nv_bfloat16><<<grid, threads, smem, stream>>>(
+    rotary_bias_kernel<__nv_bfloat16><<<grid, threads, 0, stream>>>(
         static_cast<__nv_bfloat16*>(qkv), bias, positions, tokens, query_heads, kv_heads, head_dim, cos_table,
         sin_table, table_positions, status);
   } else {
