@@ -536,16 +536,46 @@ void Engine::gemm(const void* x, const void* w, void* y, int m, int n, int k) {
     check_lt(cublasLtMatmulPreferenceSetAttribute(preference, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES,
                                                   &lt_workspace_bytes_, sizeof(lt_workspace_bytes_)),
              "preference workspace");
-    cublasLtMatmulHeuristicResult_t result{};
+    constexpr int kCandidates = 8;
+    cublasLtMatmulHeuristicResult_t results[kCandidates] = {};
     int returned = 0;
     const cublasStatus_t status = cublasLtMatmulAlgoGetHeuristic(lt_, plan.op, plan.a, plan.b, plan.c, plan.c,
-                                                                 preference, 1, &result, &returned);
+                                                                 preference, kCandidates, results, &returned);
     cublasLtMatmulPreferenceDestroy(preference);
     if (status != CUBLAS_STATUS_SUCCESS || returned == 0) {
       throw Error("cuBLASLt found no algorithm for a " + std::to_string(m) + "x" + std::to_string(n) + "x" +
                   std::to_string(k) + " 16-bit GEMM");
     }
-    plan.algo = result.algo;
+    // Time each candidate once on this call's own buffers (y is overwritten by the real launch
+    // below) and keep the fastest; the first call of a shape happens in warm-up, not in a timed scan.
+    plan.algo = results[0].algo;
+    if (returned > 1) {
+      cudaEvent_t start = nullptr, stop = nullptr;
+      check_cuda(cudaEventCreate(&start), "autotune event");
+      check_cuda(cudaEventCreate(&stop), "autotune event");
+      const float one = 1.0f, zero = 0.0f;
+      float best = 0.0f;
+      for (int i = 0; i < returned; ++i) {
+        if (results[i].state != CUBLAS_STATUS_SUCCESS) continue;
+        bool ok = cublasLtMatmul(lt_, plan.op, &one, w, plan.a, x, plan.b, &zero, y, plan.c, y, plan.c, &results[i].algo,
+                                 lt_workspace_, lt_workspace_bytes_, stream_) == CUBLAS_STATUS_SUCCESS;  // warm
+        check_cuda(cudaEventRecord(start, stream_), "autotune event");
+        for (int r = 0; ok && r < 3; ++r) {
+          ok = cublasLtMatmul(lt_, plan.op, &one, w, plan.a, x, plan.b, &zero, y, plan.c, y, plan.c, &results[i].algo,
+                              lt_workspace_, lt_workspace_bytes_, stream_) == CUBLAS_STATUS_SUCCESS;
+        }
+        check_cuda(cudaEventRecord(stop, stream_), "autotune event");
+        check_cuda(cudaEventSynchronize(stop), "autotune event");
+        float ms = 0.0f;
+        check_cuda(cudaEventElapsedTime(&ms, start, stop), "autotune event");
+        if (ok && (best == 0.0f || ms < best)) {
+          best = ms;
+          plan.algo = results[i].algo;
+        }
+      }
+      cudaEventDestroy(start);
+      cudaEventDestroy(stop);
+    }
     found = cache.emplace(key, plan).first;
   }
   const float alpha = 1.0f, beta = 0.0f;

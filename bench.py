@@ -57,6 +57,8 @@ def parse_args():
     parser.add_argument("--dtype", choices=["fp16", "bf16"], default="fp16",
                         help="16-bit type of weights, GEMM operands and activations")
     parser.add_argument("--attention", choices=["tcgen05", "mma"], default="tcgen05")
+    parser.add_argument("--sweep", action="store_true",
+                        help="only the fused-kernel bandwidth sweep of BASELINE config 5 (one GPU)")
     return parser.parse_args()
 
 
@@ -152,6 +154,8 @@ def init_distributed(args):
         import datetime
         import torch.distributed as dist
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        # NCCL's own log lines (its version banner included) go to stderr: stdout carries the JSON line
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device(f"cuda:{local_rank}"))
     return rank, world, local_rank
@@ -281,6 +285,85 @@ def kernel_rooflines(config, hbm_peak, tensor_peak, tokens: int = 16384, repeats
     return results
 
 
+SWEEP_TOKENS = (1, 64, 1024, 8192, 32768)
+SWEEP_HIDDEN = (2048, 3584, 4096, 8192)
+SWEEP_KV_HEADS = {2048: 4, 3584: 4, 4096: 8, 8192: 8}
+
+
+def bandwidth_sweep(hbm_peak: float, dtype: str = "fp16", repeats: int = 20) -> list[dict]:
+    """the fused elementwise kernels over tokens x hidden (head_dim 128,
+    intermediate 3.5 x hidden, vocab 152064), N(0,1) activations, N(0,0.02) table, each timed alone
+    with CUDA events (3 warm-up + `repeats` launches) against its algorithmic HBM bytes. Small
+    sizes fit in L2 and are launch-bound; the large ones measure HBM."""
+    import ctypes
+
+    import torch
+    from attnrank import _native
+
+    lib = _native.lib
+    dev = torch.device("cuda")
+    stream = torch.cuda.current_stream()
+    s = ctypes.c_void_p(stream.cuda_stream)
+    half = torch.float16 if dtype == "fp16" else torch.bfloat16
+    code = _native.DTYPE_F16 if dtype == "fp16" else _native.DTYPE_BF16
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    gen = torch.Generator(device=dev).manual_seed(5)
+    vocab, D = 152064, 128
+    rows = []
+
+    def timed(kernel, tokens, hidden, launch, bytes_moved):
+        for _ in range(3):
+            launch()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(repeats):
+            launch()
+        stop.record(stream)
+        stop.synchronize()
+        seconds = start.elapsed_time(stop) / 1000 / repeats
+        achieved = bytes_moved / seconds / 1e9
+        rows.append({"kernel": kernel, "tokens": tokens, "hidden": hidden, "us": round(seconds * 1e6, 2),
+                     "bytes": int(bytes_moved), "gbs": round(achieved, 1), "frac": round(achieved / hbm_peak, 4)})
+
+    cos = torch.empty(32768, D // 2, device=dev)
+    sin = torch.empty_like(cos)
+    _native.check(lib.ar_rope_table(P(cos), P(sin), 32768, D, 1e6, s))
+    for hidden in SWEEP_HIDDEN:
+        intermediate = int(hidden * 3.5)
+        heads, kv_heads = hidden // D, SWEEP_KV_HEADS[hidden]
+        width = (heads + 2 * kv_heads) * D
+        gamma = torch.ones(hidden, device=dev)
+        table = (torch.randn(vocab, hidden, device=dev, generator=gen) * 0.02).to(half)
+        bias = (torch.randn(width, device=dev, generator=gen) * 0.02)
+        for tokens in SWEEP_TOKENS:
+            residual = torch.randn(tokens, hidden, device=dev, generator=gen)
+            delta = torch.randn(tokens, hidden, device=dev, generator=gen).to(half)
+            normed = torch.empty(tokens, hidden, device=dev, dtype=half)
+            timed("rms_norm_residual", tokens, hidden, lambda: _native.check(lib.ar_rms_norm_residual(
+                P(residual), P(delta), P(gamma), tokens, hidden, 1e-6, P(normed), code, s)),
+                12 * tokens * hidden + 4 * hidden)
+            ids = torch.randint(0, vocab, (tokens,), device=dev, dtype=torch.int32, generator=gen)
+            timed("embedding_rms_norm", tokens, hidden, lambda: _native.check(lib.ar_embedding_rms_norm(
+                P(ids), tokens, P(table), vocab, hidden, P(gamma), 1e-6, P(residual), P(normed), None, code, s)),
+                tokens * (8 * hidden + 4))
+            del residual, delta, normed, ids
+            qkv = torch.randn(tokens, width, device=dev, generator=gen).to(half)
+            positions = (torch.arange(tokens, device=dev, dtype=torch.int32) % 32768).contiguous()
+            timed("rotary_bias", tokens, hidden, lambda: _native.check(lib.ar_rotary_embedding(
+                P(qkv), P(bias), P(positions), tokens, heads, kv_heads, D, P(cos), P(sin), 32768, None, code, s)),
+                4 * tokens * width)
+            del qkv, positions
+            gate_up = torch.randn(tokens, 2 * intermediate, device=dev, generator=gen).to(half)
+            act = torch.empty(tokens, intermediate, device=dev, dtype=half)
+            timed("silu_multiply", tokens, hidden, lambda: _native.check(lib.ar_silu_multiply(
+                P(gate_up), ctypes.c_void_p(gate_up.data_ptr() + 2 * intermediate), 2 * intermediate, P(act),
+                intermediate, tokens, intermediate, code, s)), 6 * tokens * intermediate)
+            del gate_up, act
+        del table
+        torch.cuda.empty_cache()
+    return rows
+
+
 def cpu_baseline(config, prompt, layers: int = 4) -> dict:
     """The oracle port (fp32 torch on the host cores) on a bounded sample: one prompt through the
     first `layers` layers, scaled to the full depth."""
@@ -299,9 +382,22 @@ def cpu_baseline(config, prompt, layers: int = 4) -> dict:
     start = time.perf_counter()
     model.probe([sample])
     seconds = (time.perf_counter() - start) * config.num_hidden_layers / layers
+    # BASELINE config 1 in full: a TinyLlama-1.1B-shaped single layer, 256 tokens, 16 query
+    # tokens over 5 document spans of 48 tokens
+    tiny = F.Shape(hidden=2048, intermediate=5632, layers=1, heads=32, kv_heads=4, vocab=32000, eps=1e-5,
+                   theta=1e4)
+    import numpy as np
+    tokens = np.random.default_rng(0).integers(0, 32000, 256).astype(np.int32)
+    c1 = F.Prompt(tokens=tokens, query_span=(240, 256), spans=[(48 * i, 48 * i + 48) for i in range(5)])
+    start = time.perf_counter()
+    F.OracleModel(tiny, seed=0).probe([c1])
+    c1_seconds = time.perf_counter() - start
     return {"value": round(1.0 / seconds, 5), "unit": "prompts/s", "cores": cores, "kind": "port",
             "sample": f"1 prompt ({len(prompt.tokens)} tokens) x {layers} of {config.num_hidden_layers} layers, "
-                      f"fp32 torch-CPU oracle incl. weight generation, scaled to all layers"}
+                      f"fp32 torch-CPU oracle incl. weight generation, scaled to all layers",
+            "config1_seconds": round(c1_seconds, 4),
+            "config1": "TinyLlama-1.1B-shaped single layer, 256 tokens, mass of 16 query tokens over 5 spans "
+                       "of 48 (weight generation included)"}
 
 
 # ---------------------------------------------------------------------------------------------
@@ -386,6 +482,7 @@ def run_b200(args, rank, world, local_rank):
     flops = scan_flops(config, prompts)
     achieved_tflops = flops / (ms_per_step / 1000.0) / 1e12
     tensor_peak = peak.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
+    job_peak = tensor_peak * world  # the whole job's FLOPs against the peak of all its GPUs
     hbm_peak = peak.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
     timed_ms = sum(entry["ms"] for entry in timing.values()) or 1.0
     kernels = {}
@@ -436,9 +533,9 @@ def run_b200(args, rank, world, local_rank):
                 "api": "attnrank.scheduler.ProbeScheduler.find_shallowest_attention_layer"},
         "roofline": {"bound": "tensor", "kernel": "whole scan step (cuBLASLt GEMMs + attention + mass)",
                      "dominant_kernel": dominant,
-                     "achieved": round(achieved_tflops, 1), "peak": tensor_peak, "unit": "TFLOP/s",
-                     "frac": round(achieved_tflops / tensor_peak, 4), "traffic": None,
-                     "peak_source": f"{peak_kind} bf16_tflops_sustained",
+                     "achieved": round(achieved_tflops, 1), "peak": round(job_peak, 1), "unit": "TFLOP/s",
+                     "frac": round(achieved_tflops / job_peak, 4), "traffic": None,
+                     "peak_source": f"{peak_kind} bf16_tflops_sustained x {world} GPU(s)",
                      "algorithmic_flops_per_step": flops},
         "clocks": clocks,
         "gpu_launches": gpu_launches,
@@ -503,7 +600,13 @@ def run_reference(args, rank, world, local_rank):
 def main():
     args = parse_args()
     rank, world, local_rank = init_distributed(args)
-    if args.kernels_only:
+    if args.sweep:
+        peak, kind = peaks()
+        result = {"sweep": bandwidth_sweep(peak.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]), dtype=args.dtype),
+                  "peak_source": f"{kind} hbm_gbs", "dtype": args.dtype,
+                  "config": "tokens {1,64,1024,8192,32768} x hidden {2048,3584,4096,8192}, head_dim 128, "
+                            "intermediate 3.5 x hidden, vocab 152064"}
+    elif args.kernels_only:
         from attnrank import synthetic
         peak, kind = peaks()
         result = {"kernels": kernel_rooflines(synthetic.qwen2_7b(), peak.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]),
