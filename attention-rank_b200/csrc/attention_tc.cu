@@ -402,13 +402,16 @@ __global__ void __launch_bounds__(kThreads, 2)
       fence_after();
       const int k0 = (tile_begin + j) * kKeys;
       float x[kKeys];
-#pragma unroll
-      for (int c = 0; c < kKeys / 32; ++c) {
-        uint32_t raw[32];
-        tmem_ld32(tmem + lane_base + stage * kKeys + c * 32, raw);
+      {
+        uint32_t raw[2][32];  // both 32-column loads in flight before one wait
+        tmem_ld32(tmem + lane_base + stage * kKeys, raw[0]);
+        tmem_ld32(tmem + lane_base + stage * kKeys + 32, raw[1]);
         tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(raw[i]) * scale_log2;
+        for (int i = 0; i < 32; ++i) {
+          x[i] = __uint_as_float(raw[0][i]) * scale_log2;
+          x[32 + i] = __uint_as_float(raw[1][i]) * scale_log2;
+        }
       }
       const bool diagonal = k0 + kKeys - 1 > q0 || k0 + kKeys > length || args.sliding_window > 0;
       float m_tile = -INFINITY;

@@ -118,9 +118,12 @@ struct GemmPlan {
   cublasLtMatmulDesc_t op = nullptr;
   cublasLtMatrixLayout_t a = nullptr, b = nullptr, c = nullptr;
   cublasLtMatmulAlgo_t algo;
+  bool bias = false;  // the fp32 bias epilogue is part of the plan
 };
 
-void destroy_plans(std::map<std::tuple<int, int, int>, GemmPlan>& plans) {
+using GemmKey = std::tuple<int, int, int, int>;  // m, n, k, bias requested
+
+void destroy_plans(std::map<GemmKey, GemmPlan>& plans) {
   for (auto& entry : plans) {
     cublasLtMatmulDescDestroy(entry.second.op);
     cublasLtMatrixLayoutDestroy(entry.second.a);
@@ -236,7 +239,7 @@ void Engine::upload_matrix(void* dst, const void* host, int dtype, size_t count)
 }
 
 struct Engine::GemmPlans {
-  std::map<std::tuple<int, int, int>, GemmPlan> by_shape;
+  std::map<GemmKey, GemmPlan> by_shape;
 };
 
 Engine::Engine(const ModelConfig& config, const RuntimeOptions& options)
@@ -512,9 +515,9 @@ LayerRange Engine::resolve_layers(int layer_begin, int layer_end) const {
   return range;
 }
 
-void Engine::gemm(const void* x, const void* w, void* y, int m, int n, int k) {
+bool Engine::gemm(const void* x, const void* w, void* y, int m, int n, int k, const float* bias) {
   auto& cache = plans_->by_shape;
-  const auto key = std::make_tuple(m, n, k);
+  const auto key = std::make_tuple(m, n, k, bias != nullptr ? 1 : 0);
   auto found = cache.find(key);
   if (found == cache.end()) {
     if (cache.size() > 512) {
@@ -539,8 +542,32 @@ void Engine::gemm(const void* x, const void* w, void* y, int m, int n, int k) {
     constexpr int kCandidates = 8;
     cublasLtMatmulHeuristicResult_t results[kCandidates] = {};
     int returned = 0;
-    const cublasStatus_t status = cublasLtMatmulAlgoGetHeuristic(lt_, plan.op, plan.a, plan.b, plan.c, plan.c,
-                                                                 preference, kCandidates, results, &returned);
+    cublasStatus_t status = CUBLAS_STATUS_NOT_SUPPORTED;
+    if (bias != nullptr) {
+      // y = x W^T + b with b fp32, added to the fp32 accumulator before the one rounding to 16 bits
+      const cublasLtEpilogue_t epilogue = CUBLASLT_EPILOGUE_BIAS;
+      const cudaDataType_t bias_type = CUDA_R_32F;
+      if (cublasLtMatmulDescSetAttribute(plan.op, CUBLASLT_MATMUL_DESC_EPILOGUE, &epilogue, sizeof(epilogue)) ==
+              CUBLAS_STATUS_SUCCESS &&
+          cublasLtMatmulDescSetAttribute(plan.op, CUBLASLT_MATMUL_DESC_BIAS_DATA_TYPE, &bias_type,
+                                         sizeof(bias_type)) == CUBLAS_STATUS_SUCCESS &&
+          cublasLtMatmulDescSetAttribute(plan.op, CUBLASLT_MATMUL_DESC_BIAS_POINTER, &bias, sizeof(bias)) ==
+              CUBLAS_STATUS_SUCCESS) {
+        status = cublasLtMatmulAlgoGetHeuristic(lt_, plan.op, plan.a, plan.b, plan.c, plan.c, preference, kCandidates,
+                                                results, &returned);
+      }
+      plan.bias = status == CUBLAS_STATUS_SUCCESS && returned > 0;
+      if (!plan.bias) {  // no algorithm with this epilogue: plain GEMM, the caller adds the bias
+        const cublasLtEpilogue_t none = CUBLASLT_EPILOGUE_DEFAULT;
+        check_lt(cublasLtMatmulDescSetAttribute(plan.op, CUBLASLT_MATMUL_DESC_EPILOGUE, &none, sizeof(none)),
+                 "epilogue");
+      }
+    }
+    if (!plan.bias) {
+      returned = 0;
+      status = cublasLtMatmulAlgoGetHeuristic(lt_, plan.op, plan.a, plan.b, plan.c, plan.c, preference, kCandidates,
+                                              results, &returned);
+    }
     cublasLtMatmulPreferenceDestroy(preference);
     if (status != CUBLAS_STATUS_SUCCESS || returned == 0) {
       throw Error("cuBLASLt found no algorithm for a " + std::to_string(m) + "x" + std::to_string(n) + "x" +
@@ -580,9 +607,14 @@ void Engine::gemm(const void* x, const void* w, void* y, int m, int n, int k) {
   }
   const float alpha = 1.0f, beta = 0.0f;
   const GemmPlan& plan = found->second;
+  if (plan.bias) {
+    check_lt(cublasLtMatmulDescSetAttribute(plan.op, CUBLASLT_MATMUL_DESC_BIAS_POINTER, &bias, sizeof(bias)),
+             "bias pointer");
+  }
   check_lt(cublasLtMatmul(lt_, plan.op, &alpha, w, plan.a, x, plan.b, &beta, y, plan.c, y, plan.c, &plan.algo,
                           lt_workspace_, lt_workspace_bytes_, stream_),
            "cublasLtMatmul");
+  return plan.bias;
 }
 
 std::vector<Engine::Batch> Engine::plan_batches(const std::vector<PromptView>& prompts) const {
@@ -930,16 +962,19 @@ void Engine::execute_batch(const BatchLayout& layout, const int32_t* dev, int sp
   mass.dtype = dtype;
 
   // algorithmic work of each launch: FLOPs for GEMMs / attention / mass, HBM bytes otherwise
-  const double rotated_heads = Hq + Hkv + (c.attention_bias ? Hkv : 0);
-  const double rotary_bytes = m * rotated_heads * D * 2 * 2;
   const double norm_bytes = m * H * (4 + 2 + 4 + 2);
   const double silu_bytes = m * I * 2 * 3;
   const int last_layer = range.end - 1;
   for (int l = 0; l <= last_layer; ++l) {
     const LayerWeights& w = layers_[l];
-    timed(kClassGemmQkv, 2 * m * Wqkv * H, [&] { gemm(normed_, w.qkv, qkv_, M, Wqkv, H); });
-    timed(kClassRotary, rotary_bytes, [&] {
-      check_cuda(launch_rotary_bias(qkv_, w.qkv_bias, positions_, M, Hq, Hkv, D, cos_table_, sin_table_,
+    // q|k|v GEMM with the fp32 bias in its epilogue when cuBLASLt offers it; otherwise the bias
+    // is added by the RoPE kernel
+    bool bias_done = false;
+    timed(kClassGemmQkv, 2 * m * Wqkv * H, [&] { bias_done = gemm(normed_, w.qkv, qkv_, M, Wqkv, H, w.qkv_bias); });
+    const float* rotary_bias = bias_done ? nullptr : w.qkv_bias;
+    const double rotated = Hq + Hkv + (rotary_bias != nullptr ? Hkv : 0);
+    timed(kClassRotary, m * rotated * D * 2 * 2, [&] {
+      check_cuda(launch_rotary_bias(qkv_, rotary_bias, positions_, M, Hq, Hkv, D, cos_table_, sin_table_,
                                     options_.max_sequence_length, status_, dtype, stream_),
                  "rotary");
     });

@@ -193,7 +193,9 @@ class Engine {
 
   void allocate();
   void ensure_partials(size_t items, int span_count, int layers);
-  void gemm(const void* x, const void* w, void* y, int m, int n, int k);
+  // y[m, n] = x[m, k] w[n, k]^T (+ bias[n], fp32, when given and cuBLASLt offers the epilogue;
+  // returns whether the bias was applied)
+  bool gemm(const void* x, const void* w, void* y, int m, int n, int k, const float* bias = nullptr);
   void run_batch(const std::vector<PromptView>& prompts, const Batch& batch, int span_count, LayerRange range,
                  bool normalize_by_length, double* rows_device, double* raw_rows_device, float* device_accumulator,
                  int slot);

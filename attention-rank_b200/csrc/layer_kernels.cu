@@ -19,8 +19,7 @@ namespace arb {
 namespace {
 
 constexpr int kRowThreadsCap = 256;
-constexpr int kRopeTokens = 2;       // tokens per rotary step (loads in flight per thread)
-constexpr int kRopeMaxThreads = 512;
+constexpr int kRopeUnroll = 4;       // heads loaded per rotary step (loads in flight per thread)
 constexpr int kSiluUnroll = 2;   // 8-value chunks in flight per SwiGLU thread
 
 // ---------------------------------------------------------------------------------------------
@@ -131,52 +130,65 @@ __global__ void __launch_bounds__(kRowThreadsCap) rms_norm_residual_kernel(
 
 // ---------------------------------------------------------------------------------------------
 // Bias + rotary embedding, in place on the fused [tokens, (Hq + 2 Hkv) * D] projection output.
-// A CTA walks tokens (kRopeTokens per step, all loaded before any is stored); its threads tile one
-// token row: thread i owns 8 rotation pairs (x_j, x_{j + D/2}) of one head, so a token's row is
-// read and written with 256-byte coalesced segments and its cos/sin row (shared by every head)
-// comes from L1. Query and key heads get bias + rotation; value heads get the bias only (and are
-// skipped without bias).
+// One thread owns 8 rotation pairs (x_i, x_{i + D/2}) at one offset of one token and walks all of
+// that token's heads, so its cos/sin values are loaded once (not once per head, which made the
+// kernel L1-bound); kRopeUnroll heads are loaded before any is stored. Query and key heads get
+// bias + rotation; value heads get the bias only (and are skipped without bias). The engine
+// applies the bias in the q|k|v GEMM epilogue and passes none.
 // ---------------------------------------------------------------------------------------------
-template <typename T>
-__global__ void __launch_bounds__(kRopeMaxThreads) rotary_bias_kernel(
-    T* __restrict__ qkv, const float* __restrict__ bias, const int32_t* __restrict__ positions, int tokens,
-    int query_heads, int kv_heads, int head_dim, const float* __restrict__ cos_table,
-    const float* __restrict__ sin_table, int table_positions, int* status) {
+template <typename T, bool kBias>
+__global__ void __launch_bounds__(256, kBias ? 2 : 3) rotary_bias_kernel(T* __restrict__ qkv, const float* __restrict__ bias,
+                                   const int32_t* __restrict__ positions, int tokens, int query_heads,
+                                   int kv_heads, int head_dim, const float* __restrict__ cos_table,
+                                   const float* __restrict__ sin_table, int table_positions,
+                                   int* status) {
   const int half = head_dim >> 1;
   const int chunks_per_head = half >> 3;
   const int rotated_heads = query_heads + kv_heads;
-  const int heads = bias != nullptr ? rotated_heads + kv_heads : rotated_heads;
+  const int heads = kBias ? rotated_heads + kv_heads : rotated_heads;
   const int row_width = (query_heads + 2 * kv_heads) * head_dim;
-  const int slots = heads * chunks_per_head;
-  for (int slot = threadIdx.x; slot < slots; slot += blockDim.x) {
-    const int head = slot / chunks_per_head;
-    const int chunk = slot - head * chunks_per_head;
-    const int column = head * head_dim + chunk * 8;
-    const bool rotate = head < rotated_heads;
-    for (int first = blockIdx.x * kRopeTokens; first < tokens; first += gridDim.x * kRopeTokens) {
-      uint4 low_raw[kRopeTokens];
-      uint4 high_raw[kRopeTokens];
-      int position[kRopeTokens];
+  const int total = tokens * chunks_per_head;  // < 2^31: the launcher bounds tokens
+  for (int item = blockIdx.x * blockDim.x + threadIdx.x; item < total; item += gridDim.x * blockDim.x) {
+    const int token = item / chunks_per_head;
+    const int chunk = item - token * chunks_per_head;
+    const int position = positions[token];
+    const bool in_table = position >= 0 && position < table_positions;
+    if (!in_table) report_status(status, kStatusPositionOutOfRange);
+    float c[8];
+    float s[8];
+    if (in_table) {
+      const float* cos_row = cos_table + static_cast<size_t>(position) * half + chunk * 8;
+      const float* sin_row = sin_table + static_cast<size_t>(position) * half + chunk * 8;
+      const float4 c0 = __ldg(reinterpret_cast<const float4*>(cos_row));
+      const float4 c1 = __ldg(reinterpret_cast<const float4*>(cos_row + 4));
+      const float4 s0 = __ldg(reinterpret_cast<const float4*>(sin_row));
+      const float4 s1 = __ldg(reinterpret_cast<const float4*>(sin_row + 4));
+      c[0] = c0.x; c[1] = c0.y; c[2] = c0.z; c[3] = c0.w; c[4] = c1.x; c[5] = c1.y; c[6] = c1.z; c[7] = c1.w;
+      s[0] = s0.x; s[1] = s0.y; s[2] = s0.z; s[3] = s0.w; s[4] = s1.x; s[5] = s1.y; s[6] = s1.z; s[7] = s1.w;
+    }
+    // without a valid position only the bias-only value heads are written
+    const int first_head = in_table ? 0 : rotated_heads;
+    T* row = qkv + static_cast<size_t>(token) * row_width + chunk * 8;
+    for (int h0 = first_head; h0 < heads; h0 += kRopeUnroll) {
+      uint4 low_raw[kRopeUnroll];
+      uint4 high_raw[kRopeUnroll];
 #pragma unroll
-      for (int k = 0; k < kRopeTokens; ++k) {
-        const int token = first + k;
-        if (token < tokens) {
-          const T* at = qkv + static_cast<size_t>(token) * row_width + column;
-          low_raw[k] = *reinterpret_cast<const uint4*>(at);
-          high_raw[k] = *reinterpret_cast<const uint4*>(at + half);
-          position[k] = positions[token];
+      for (int u = 0; u < kRopeUnroll; ++u) {
+        if (h0 + u < heads) {
+          low_raw[u] = *reinterpret_cast<const uint4*>(row + (h0 + u) * head_dim);
+          high_raw[u] = *reinterpret_cast<const uint4*>(row + (h0 + u) * head_dim + half);
         }
       }
 #pragma unroll
-      for (int k = 0; k < kRopeTokens; ++k) {
-        const int token = first + k;
-        if (token >= tokens) break;
+      for (int u = 0; u < kRopeUnroll; ++u) {
+        const int head = h0 + u;
+        if (head >= heads) break;
         float low[8];
         float high[8];
-        unpack8<T>(low_raw[k], low);
-        unpack8<T>(high_raw[k], high);
-        if (bias != nullptr) {
-          const float* b = bias + column;
+        unpack8<T>(low_raw[u], low);
+        unpack8<T>(high_raw[u], high);
+        if constexpr (kBias) {
+          const float* b = bias + head * head_dim + chunk * 8;
           const float4 b0 = __ldg(reinterpret_cast<const float4*>(b));
           const float4 b1 = __ldg(reinterpret_cast<const float4*>(b + 4));
           const float4 b2 = __ldg(reinterpret_cast<const float4*>(b + half));
@@ -189,20 +201,7 @@ __global__ void __launch_bounds__(kRopeMaxThreads) rotary_bias_kernel(
             high[i] += bh[i];
           }
         }
-        if (rotate) {
-          const int p = position[k];
-          if (p < 0 || p >= table_positions) {  // the row keeps its input values; the call fails
-            report_status(status, kStatusPositionOutOfRange);
-            continue;
-          }
-          const float* cos_row = cos_table + static_cast<size_t>(p) * half + chunk * 8;
-          const float* sin_row = sin_table + static_cast<size_t>(p) * half + chunk * 8;
-          const float4 c0 = __ldg(reinterpret_cast<const float4*>(cos_row));
-          const float4 c1 = __ldg(reinterpret_cast<const float4*>(cos_row + 4));
-          const float4 s0 = __ldg(reinterpret_cast<const float4*>(sin_row));
-          const float4 s1 = __ldg(reinterpret_cast<const float4*>(sin_row + 4));
-          const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-          const float s[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+        if (head < rotated_heads) {
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const float l = low[i];
@@ -211,9 +210,8 @@ __global__ void __launch_bounds__(kRopeMaxThreads) rotary_bias_kernel(
             high[i] = h * c[i] + l * s[i];
           }
         }
-        T* at = qkv + static_cast<size_t>(token) * row_width + column;
-        *reinterpret_cast<uint4*>(at) = pack8<T>(low);
-        *reinterpret_cast<uint4*>(at + half) = pack8<T>(high);
+        *reinterpret_cast<uint4*>(row + head * head_dim) = pack8<T>(low);
+        *reinterpret_cast<uint4*>(row + head * head_dim + half) = pack8<T>(high);
       }
     }
   }
@@ -398,24 +396,24 @@ cudaError_t launch_rotary_bias(void* qkv, const float* bias, const int32_t* posi
                                const float* sin_table, int table_positions, int* status, int dtype,
                                cudaStream_t stream) {
   if (tokens <= 0) return cudaSuccess;
-  if (head_dim % 16 != 0 || head_dim > 1024) return cudaErrorInvalidValue;
-  const int heads = query_heads + kv_heads + (bias != nullptr ? kv_heads : 0);
-  const int slots = heads * (head_dim / 16);
-  const int threads = std::min(kRopeMaxThreads, (slots + 31) & ~31);
-  const int per_sm = dtype == kActFp16 ? resident_per_sm(rotary_bias_kernel<__half>, threads)
-                                       : resident_per_sm(rotary_bias_kernel<__nv_bfloat16>, threads);
-  // one wave of resident CTAs walks all tokens (no tail wave)
-  const int grid = std::max(1, std::min((tokens + kRopeTokens - 1) / kRopeTokens, sm_count() * per_sm));
+  if (head_dim % 16 != 0 || head_dim > 1024 || tokens > (1 << 24)) return cudaErrorInvalidValue;
+  const int items = tokens * (head_dim / 16);
+  const int threads = 256;
+  if (dtype != kActFp16 && dtype != kActBf16) return cudaErrorInvalidValue;
+  auto launch = [&](auto kernel, auto* data) {
+    // one wave of resident CTAs walks all (token, chunk) items (no tail wave)
+    const int per_sm = resident_per_sm(kernel, threads);
+    const int grid = std::max(1, std::min((items + threads - 1) / threads, sm_count() * per_sm));
+    kernel<<<grid, threads, 0, stream>>>(data, bias, positions, tokens, query_heads, kv_heads, head_dim, cos_table,
+                                         sin_table, table_positions, status);
+  };
   if (dtype == kActFp16) {
-    rotary_bias_kernel<__half><<<grid, threads, 0, stream>>>(static_cast<__half*>(qkv), bias, positions, tokens,
-                                                             query_heads, kv_heads, head_dim, cos_table, sin_table,
-                                                             table_positions, status);
-  } else if (dtype == kActBf16) {
-    rotary_bias_kernel<__nv_bfloat16><<<grid, threads, 0, stream>>>(
-        static_cast<__nv_bfloat16*>(qkv), bias, positions, tokens, query_heads, kv_heads, head_dim, cos_table,
-        sin_table, table_positions, status);
+    auto* data = static_cast<__half*>(qkv);
+    if (bias != nullptr) launch(rotary_bias_kernel<__half, true>, data); else launch(rotary_bias_kernel<__half, false>, data);
   } else {
-    return cudaErrorInvalidValue;
+    auto* data = static_cast<__nv_bfloat16*>(qkv);
+    if (bias != nullptr) launch(rotary_bias_kernel<__nv_bfloat16, true>, data);
+    else launch(rotary_bias_kernel<__nv_bfloat16, false>, data);
   }
   return cudaGetLastError();
 }
