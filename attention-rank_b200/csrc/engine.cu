@@ -323,7 +323,10 @@ void Engine::allocate() {
   loaded_.assign(c.num_hidden_layers, std::vector<bool>(kLayerTensorCount, false));
   for (auto& layer : layers_) {
     layer.qkv = device_alloc(Wqkv * H * 2);
-    if (c.attention_bias) layer.qkv_bias = static_cast<float*>(device_alloc(Wqkv * 4));
+    if (c.attention_bias) {
+      layer.qkv_bias = static_cast<float*>(device_alloc(Wqkv * 4));
+      layer.qkv_bias_half = device_alloc(Wqkv * 2);
+    }
     layer.out = device_alloc(H * Hq * D * 2);
     layer.gate_up = device_alloc(2 * I * H * 2);
     layer.down = device_alloc(H * I * 2);
@@ -415,6 +418,7 @@ void Engine::load_tensor(const std::string& name, int dtype, const std::vector<i
     const int64_t offset = which == 'q' ? 0 : which == 'k' ? Hq * D : Hq * D + KV;
     expect(which == 'q' ? Hq * D : KV, 1);
     upload_f32(layer.qkv_bias + offset, host, dtype, count);
+    refresh_half_bias(index);
     loaded_[index][which == 'q' ? kQBias : which == 'k' ? kKBias : kVBias] = true;
   } else if (suffix == "self_attn.o_proj.weight") {
     expect(H, Hq * D);
@@ -471,6 +475,7 @@ void Engine::init_synthetic(uint64_t seed, float standard_deviation) {
       check_cuda(launch_synthetic_fill_f32(layer.qkv_bias, QD, keys[0], scale, 0.0f, stream_), "synthetic fill");
       check_cuda(launch_synthetic_fill_f32(layer.qkv_bias + QD, KV, keys[1], scale, 0.0f, stream_), "synthetic fill");
       check_cuda(launch_synthetic_fill_f32(layer.qkv_bias + QD + KV, KV, keys[2], scale, 0.0f, stream_), "synthetic fill");
+      refresh_half_bias(l);
     }
     fill(layer.out, H * QD, l, kTensorOutput);
     fill(layer.gate_up, I * H, l, kTensorGate);
@@ -515,7 +520,16 @@ LayerRange Engine::resolve_layers(int layer_begin, int layer_end) const {
   return range;
 }
 
-bool Engine::gemm(const void* x, const void* w, void* y, int m, int n, int k, const float* bias) {
+void Engine::refresh_half_bias(int layer) {
+  LayerWeights& w = layers_[layer];
+  if (w.qkv_bias == nullptr) return;
+  check_cuda(launch_f32_to_activation(w.qkv_bias, w.qkv_bias_half, config_.qkv_width(), options_.activation_dtype,
+                                      stream_),
+             "bias conversion");
+  synchronize();
+}
+
+bool Engine::gemm(const void* x, const void* w, void* y, int m, int n, int k, const void* bias) {
   auto& cache = plans_->by_shape;
   const auto key = std::make_tuple(m, n, k, bias != nullptr ? 1 : 0);
   auto found = cache.find(key);
@@ -525,10 +539,15 @@ bool Engine::gemm(const void* x, const void* w, void* y, int m, int n, int k, co
       destroy_plans(cache);
     }
     GemmPlan plan;
-    check_lt(cublasLtMatmulDescCreate(&plan.op, CUBLAS_COMPUTE_32F, CUDA_R_32F), "matmul desc");
-    const cublasOperation_t transa = CUBLAS_OP_T, transb = CUBLAS_OP_N;
-    check_lt(cublasLtMatmulDescSetAttribute(plan.op, CUBLASLT_MATMUL_DESC_TRANSA, &transa, sizeof(transa)), "transa");
-    check_lt(cublasLtMatmulDescSetAttribute(plan.op, CUBLASLT_MATMUL_DESC_TRANSB, &transb, sizeof(transb)), "transb");
+    auto create_op = [&] {
+      check_lt(cublasLtMatmulDescCreate(&plan.op, CUBLAS_COMPUTE_32F, CUDA_R_32F), "matmul desc");
+      const cublasOperation_t transa = CUBLAS_OP_T, transb = CUBLAS_OP_N;
+      check_lt(cublasLtMatmulDescSetAttribute(plan.op, CUBLASLT_MATMUL_DESC_TRANSA, &transa, sizeof(transa)),
+               "transa");
+      check_lt(cublasLtMatmulDescSetAttribute(plan.op, CUBLASLT_MATMUL_DESC_TRANSB, &transb, sizeof(transb)),
+               "transb");
+    };
+    create_op();
     // column-major view: D[n, m] = W[k, n]^T * X[k, m]  (row-major Y[m, n] = X[m, k] W[n, k]^T)
     const cudaDataType_t type = options_.activation_dtype == kActFp16 ? CUDA_R_16F : CUDA_R_16BF;
     check_lt(cublasLtMatrixLayoutCreate(&plan.a, type, k, n, k), "layout a");
@@ -544,23 +563,19 @@ bool Engine::gemm(const void* x, const void* w, void* y, int m, int n, int k, co
     int returned = 0;
     cublasStatus_t status = CUBLAS_STATUS_NOT_SUPPORTED;
     if (bias != nullptr) {
-      // y = x W^T + b with b fp32, added to the fp32 accumulator before the one rounding to 16 bits
+      // y = x W^T + b, b in y's 16-bit type, added to the fp32 accumulator before the rounding of y
       const cublasLtEpilogue_t epilogue = CUBLASLT_EPILOGUE_BIAS;
-      const cudaDataType_t bias_type = CUDA_R_32F;
       if (cublasLtMatmulDescSetAttribute(plan.op, CUBLASLT_MATMUL_DESC_EPILOGUE, &epilogue, sizeof(epilogue)) ==
               CUBLAS_STATUS_SUCCESS &&
-          cublasLtMatmulDescSetAttribute(plan.op, CUBLASLT_MATMUL_DESC_BIAS_DATA_TYPE, &bias_type,
-                                         sizeof(bias_type)) == CUBLAS_STATUS_SUCCESS &&
           cublasLtMatmulDescSetAttribute(plan.op, CUBLASLT_MATMUL_DESC_BIAS_POINTER, &bias, sizeof(bias)) ==
               CUBLAS_STATUS_SUCCESS) {
         status = cublasLtMatmulAlgoGetHeuristic(lt_, plan.op, plan.a, plan.b, plan.c, plan.c, preference, kCandidates,
                                                 results, &returned);
       }
       plan.bias = status == CUBLAS_STATUS_SUCCESS && returned > 0;
-      if (!plan.bias) {  // no algorithm with this epilogue: plain GEMM, the caller adds the bias
-        const cublasLtEpilogue_t none = CUBLASLT_EPILOGUE_DEFAULT;
-        check_lt(cublasLtMatmulDescSetAttribute(plan.op, CUBLASLT_MATMUL_DESC_EPILOGUE, &none, sizeof(none)),
-                 "epilogue");
+      if (!plan.bias) {  // no algorithm with this epilogue: a plain GEMM, and the caller adds the bias
+        cublasLtMatmulDescDestroy(plan.op);
+        create_op();
       }
     }
     if (!plan.bias) {
@@ -967,10 +982,12 @@ void Engine::execute_batch(const BatchLayout& layout, const int32_t* dev, int sp
   const int last_layer = range.end - 1;
   for (int l = 0; l <= last_layer; ++l) {
     const LayerWeights& w = layers_[l];
-    // q|k|v GEMM with the fp32 bias in its epilogue when cuBLASLt offers it; otherwise the bias
-    // is added by the RoPE kernel
+    // fp16 engine: the q|k|v bias (rounded once to fp16) is added in the GEMM epilogue when
+    // cuBLASLt offers it; otherwise, and for bf16 (whose rounding of the bias would be 16x
+    // coarser), the RoPE kernel adds the fp32 bias
     bool bias_done = false;
-    timed(kClassGemmQkv, 2 * m * Wqkv * H, [&] { bias_done = gemm(normed_, w.qkv, qkv_, M, Wqkv, H, w.qkv_bias); });
+    const void* epilogue_bias = dtype == kActFp16 ? w.qkv_bias_half : nullptr;
+    timed(kClassGemmQkv, 2 * m * Wqkv * H, [&] { bias_done = gemm(normed_, w.qkv, qkv_, M, Wqkv, H, epilogue_bias); });
     const float* rotary_bias = bias_done ? nullptr : w.qkv_bias;
     const double rotated = Hq + Hkv + (rotary_bias != nullptr ? Hkv : 0);
     timed(kClassRotary, m * rotated * D * 2 * 2, [&] {

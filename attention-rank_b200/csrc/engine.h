@@ -178,6 +178,7 @@ class Engine {
   struct LayerWeights {
     void* qkv = nullptr;     // 16-bit [(Hq + 2 Hkv) D, H]
     float* qkv_bias = nullptr;  // fp32 [(Hq + 2 Hkv) D] or null
+    void* qkv_bias_half = nullptr;  // the same in the 16-bit type (the GEMM's bias epilogue) or null
     void* out = nullptr;     // 16-bit [H, Hq D]
     void* gate_up = nullptr;  // 16-bit [2 I, H]
     void* down = nullptr;    // 16-bit [H, I]
@@ -193,9 +194,10 @@ class Engine {
 
   void allocate();
   void ensure_partials(size_t items, int span_count, int layers);
-  // y[m, n] = x[m, k] w[n, k]^T (+ bias[n], fp32, when given and cuBLASLt offers the epilogue;
-  // returns whether the bias was applied)
-  bool gemm(const void* x, const void* w, void* y, int m, int n, int k, const float* bias = nullptr);
+  // y[m, n] = x[m, k] w[n, k]^T (+ bias[n], 16-bit like y, when given and cuBLASLt offers the
+  // epilogue; returns whether the bias was applied)
+  bool gemm(const void* x, const void* w, void* y, int m, int n, int k, const void* bias = nullptr);
+  void refresh_half_bias(int layer);
   void run_batch(const std::vector<PromptView>& prompts, const Batch& batch, int span_count, LayerRange range,
                  bool normalize_by_length, double* rows_device, double* raw_rows_device, float* device_accumulator,
                  int slot);
