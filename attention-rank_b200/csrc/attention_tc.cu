@@ -200,6 +200,13 @@ __device__ __forceinline__ void tmem_st32(uint32_t address, const uint32_t (&r)[
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void softmax_barrier() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// 2^x with the SFU's ex2 instruction, results below 2^-126 flushed to zero: a row's largest
+// probability relative to its reference is at least 1, so those vanish in O, l and the span sums
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 struct Args {
   void* out;
@@ -408,9 +415,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         tmem_ld32(tmem + lane_base + stage * kKeys + 32, raw[1]);
         tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          x[i] = __uint_as_float(raw[0][i]) * scale_log2;
-          x[32 + i] = __uint_as_float(raw[1][i]) * scale_log2;
+        for (int i = 0; i < 32; ++i) {  // raw scores; the log2-domain scale is folded into the exponent
+          x[i] = __uint_as_float(raw[0][i]);
+          x[32 + i] = __uint_as_float(raw[1][i]);
         }
       }
       const bool diagonal = k0 + kKeys - 1 > q0 || k0 + kKeys > length || args.sliding_window > 0;
@@ -428,6 +435,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int i = 0; i < kKeys; ++i) m_tile = fmaxf(m_tile, x[i]);
       }
+      m_tile *= scale_log2;  // the tile max in log2 units (the scale is positive)
       // the row's reference max moves when the tile max exceeds it by more than the threshold
       // (or on the row's first unmasked key); O already holds earlier tiles only when j > 0
       const bool move = m_tile > m_ref + kRescaleThreshold || (m_ref == -INFINITY && m_tile != -INFINITY);
@@ -458,14 +466,14 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
       }
       if (move) m_ref = m_tile;
-      const float reference = m_ref == -INFINITY ? 0.0f : m_ref;
+      const float neg_reference = m_ref == -INFINITY ? 0.0f : -m_ref;
       float sum = 0.0f;
       {
         uint32_t packed[kKeys / 2];  // 64 probabilities -> 32 TMEM columns of 16-bit pairs
 #pragma unroll
-        for (int i = 0; i < kKeys / 2; ++i) {
-          const float p0 = exp2f(x[2 * i] - reference);
-          const float p1 = exp2f(x[2 * i + 1] - reference);
+        for (int i = 0; i < kKeys / 2; ++i) {  // p = 2^(s * log2(e) / sqrt(D) - m_ref): one FFMA + one ex2
+          const float p0 = ex2_ftz(fmaf(x[2 * i], scale_log2, neg_reference));
+          const float p1 = ex2_ftz(fmaf(x[2 * i + 1], scale_log2, neg_reference));
           sum += p0 + p1;
           packed[i] = pack2<T>(p0, p1);
           x[2 * i] = p0;
@@ -505,22 +513,26 @@ __global__ void __launch_bounds__(kThreads, 2)
     const float inv = l > 0.0f ? 1.0f / l : 0.0f;
     uint8_t* stage_rows = smem + kQOffset;  // the Q tile is no longer read: every MMA completed
 #pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
-      uint32_t raw[32];
+    for (int c2 = 0; c2 < 2; ++c2) {  // 64 O columns per step: two TMEM loads in flight before one wait
+      uint32_t raw[2][32];
       if (done) {
-        tmem_ld32(tmem + lane_base + kTmemO + c * 32, raw);
+        tmem_ld32(tmem + lane_base + kTmemO + c2 * 64, raw[0]);
+        tmem_ld32(tmem + lane_base + kTmemO + c2 * 64 + 32, raw[1]);
         tmem_wait_ld();
       } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) raw[i] = 0u;
+        for (int i = 0; i < 32; ++i) raw[0][i] = raw[1][i] = 0u;
       }
 #pragma unroll
-      for (int v = 0; v < 4; ++v) {  // four 16-byte chunks of 8 values
-        float y[8];
+      for (int h = 0; h < 2; ++h) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) y[i] = __uint_as_float(raw[v * 8 + i]) * inv;
-        const int chunk = c * 4 + v;  // 0..15 across the 256-byte row
-        *reinterpret_cast<uint4*>(stage_rows + row * 256 + ((chunk ^ (row & 15)) << 4)) = pack8<T>(y);
+        for (int v = 0; v < 4; ++v) {  // four 16-byte chunks of 8 values
+          float y[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) y[i] = __uint_as_float(raw[h][v * 8 + i]) * inv;
+          const int chunk = (c2 * 2 + h) * 4 + v;  // 0..15 across the 256-byte row
+          *reinterpret_cast<uint4*>(stage_rows + row * 256 + ((chunk ^ (row & 15)) << 4)) = pack8<T>(y);
+        }
       }
     }
     if (query < length && done) {
