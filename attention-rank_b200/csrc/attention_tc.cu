@@ -207,26 +207,6 @@ __device__ __forceinline__ float ex2_ftz(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-// 2^t on the FMA pipe, for t <= 8 (the softmax exponents), so that a share of the exponentials
-// leaves the SFU, which otherwise limits the softmax. Range reduction t = n + f with n = rint(t)
-// from the fp32 magic-number add (1.5 * 2^23) and f in [-0.5, 0.5]; 2^f by a degree-4 polynomial
-// (Horner) whose coefficients are a relative-error least-squares fit on [-0.5, 0.5] made for this
-// kernel (max relative error 2.9e-6 in fp32, below the 16-bit rounding of P); 2^n is added to the
-// exponent field. t is clamped at -125, so a masked score gives 2^-125 instead of 0 (negligible
-// next to the row's largest probability, which is at least 1, and 0 after rounding to 16 bits).
-__device__ __forceinline__ float ex2_poly(float t) {
-  constexpr float kMagic = 12582912.0f;
-  t = fmaxf(t, -125.0f);
-  const float j = t + kMagic;
-  const float f = t - (j - kMagic);
-  float p = fmaf(0.009574029594659805f, f, 0.0559295192360878f);
-  p = fmaf(p, f, 0.240247443318367f);
-  p = fmaf(p, f, 0.6931200623512268f);
-  p = fmaf(p, f, 0.9999992251396179f);
-  // j's bits are 0x4B400000 + n; shifted left by 23 (mod 2^32) they are n << 23
-  return __uint_as_float(__float_as_uint(p) + (__float_as_uint(j) << 23));
-}
-constexpr int kPolyEvery = 4;  // one pair of scores in every kPolyEvery takes ex2_poly
 
 struct Args {
   void* out;
@@ -492,11 +472,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         uint32_t packed[kKeys / 2];  // 64 probabilities -> 32 TMEM columns of 16-bit pairs
 #pragma unroll
         for (int i = 0; i < kKeys / 2; ++i) {  // p = 2^(s * log2(e) / sqrt(D) - m_ref): one FFMA + one ex2
-          const float t0 = fmaf(x[2 * i], scale_log2, neg_reference);
-          const float t1 = fmaf(x[2 * i + 1], scale_log2, neg_reference);
-          const bool poly = (i % kPolyEvery) == kPolyEvery - 1;  // compile-time after unrolling
-          const float p0 = poly ? ex2_poly(t0) : ex2_ftz(t0);
-          const float p1 = poly ? ex2_poly(t1) : ex2_ftz(t1);
+          const float p0 = ex2_ftz(fmaf(x[2 * i], scale_log2, neg_reference));
+          const float p1 = ex2_ftz(fmaf(x[2 * i + 1], scale_log2, neg_reference));
           sum += p0 + p1;
           packed[i] = pack2<T>(p0, p1);
           x[2 * i] = p0;
