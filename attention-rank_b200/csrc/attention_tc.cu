@@ -57,6 +57,7 @@ constexpr uint32_t kKvBytes = 2 * kKvHalfBytes;          // 64 rows x 128 values
 constexpr uint32_t kSpinLimit = 1u << 26;          // hard backstop on polls per wait
 constexpr uint64_t kWaitLimitNs = 500ull * 1000 * 1000;  // a wait gives up after 0.5 s
 constexpr float kRescaleThreshold = 8.0f;          // log2 units
+constexpr int kChains = 4;                         // independent accumulators per row reduction
 
 // shared memory (1024-byte aligned): Q | K stage 0,1 | V stage 0,1 | control
 constexpr uint32_t kQOffset = 0;
@@ -421,7 +422,6 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
       }
       const bool diagonal = k0 + kKeys - 1 > q0 || k0 + kKeys > length || args.sliding_window > 0;
-      float m_tile = -INFINITY;
       if (diagonal) {
         const int key_min = args.sliding_window > 0 ? query - args.sliding_window + 1 : 0;
         const int key_max = min(query, length - 1);
@@ -429,13 +429,17 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int i = 0; i < kKeys; ++i) {
           const int key = k0 + i;
           if (key < key_min || key > key_max) x[i] = -INFINITY;
-          m_tile = fmaxf(m_tile, x[i]);
         }
-      } else {
-#pragma unroll
-        for (int i = 0; i < kKeys; ++i) m_tile = fmaxf(m_tile, x[i]);
       }
-      m_tile *= scale_log2;  // the tile max in log2 units (the scale is positive)
+      // row max and (below) row sum with kChains independent accumulators: short dependency chains
+      float m_part[kChains];
+#pragma unroll
+      for (int c = 0; c < kChains; ++c) m_part[c] = x[c];
+#pragma unroll
+      for (int i = kChains; i < kKeys; ++i) m_part[i % kChains] = fmaxf(m_part[i % kChains], x[i]);
+#pragma unroll
+      for (int c = 1; c < kChains; ++c) m_part[0] = fmaxf(m_part[0], m_part[c]);
+      const float m_tile = m_part[0] * scale_log2;  // the tile max in log2 units (the scale is positive)
       // the row's reference max moves when the tile max exceeds it by more than the threshold
       // (or on the row's first unmasked key); O already holds earlier tiles only when j > 0
       const bool move = m_tile > m_ref + kRescaleThreshold || (m_ref == -INFINITY && m_tile != -INFINITY);
@@ -470,16 +474,19 @@ __global__ void __launch_bounds__(kThreads, 2)
       float sum = 0.0f;
       {
         uint32_t packed[kKeys / 2];  // 64 probabilities -> 32 TMEM columns of 16-bit pairs
+        float s_part[kChains] = {};
 #pragma unroll
         for (int i = 0; i < kKeys / 2; ++i) {  // p = 2^(s * log2(e) / sqrt(D) - m_ref): one FFMA + one ex2
           const float p0 = ex2_ftz(fmaf(x[2 * i], scale_log2, neg_reference));
           const float p1 = ex2_ftz(fmaf(x[2 * i + 1], scale_log2, neg_reference));
-          sum += p0 + p1;
+          s_part[i % kChains] += p0 + p1;
           packed[i] = pack2<T>(p0, p1);
           x[2 * i] = p0;
           x[2 * i + 1] = p1;
         }
         tmem_st32(tmem + lane_base + stage * kKeys, packed);
+#pragma unroll
+        for (int c = 0; c < kChains; ++c) sum += s_part[c];
       }
       // fused mass: span sums of this tile's fp32 probabilities, by the warps that hold probe rows
       // (spans and k0 are CTA-uniform); a span that covers the whole tile takes the tile's sum
@@ -490,9 +497,12 @@ __global__ void __launch_bounds__(kThreads, 2)
           if (lo >= hi) continue;
           float acc = sum;
           if (lo > 0 || hi < kKeys) {
+            float a_part[kChains] = {};
+#pragma unroll
+            for (int i = 0; i < kKeys; ++i) a_part[i % kChains] += (i >= lo && i < hi) ? x[i] : 0.0f;
             acc = 0.0f;
 #pragma unroll
-            for (int i = 0; i < kKeys; ++i) acc += (i >= lo && i < hi) ? x[i] : 0.0f;
+            for (int c = 0; c < kChains; ++c) acc += a_part[c];
           }
           if (row_in) sigma[s * kTile + row] += acc;
         }
