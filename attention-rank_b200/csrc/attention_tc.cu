@@ -69,7 +69,8 @@ constexpr int kMaxSpans = kMassMaxSpans;
 
 struct __align__(16) Control {
   uint64_t q_bar;
-  uint64_t kv_bar[2];
+  uint64_t k_bar[2];  // K and V stages load separately: K_{j+2} as soon as S_j has read K_j
+  uint64_t v_bar[2];
   uint64_t s_bar[2];
   uint64_t o_bar;
   uint64_t p_bar[2];
@@ -276,7 +277,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (tid == 0) {
     mbar_init(smem_u32(&ctl.q_bar), 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(smem_u32(&ctl.kv_bar[i]), 1);
+      mbar_init(smem_u32(&ctl.k_bar[i]), 1);
+      mbar_init(smem_u32(&ctl.v_bar[i]), 1);
       mbar_init(smem_u32(&ctl.s_bar[i]), 1);
       mbar_init(smem_u32(&ctl.p_bar[i]), kSoftmaxThreads);
     }
@@ -307,19 +309,25 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int q_x = head * kHeadDim;
       const int k_x = (args.query_heads + kv_head) * kHeadDim;
       const int v_x = (args.query_heads + args.kv_heads + kv_head) * kHeadDim;
-      // last load issued on each K/V stage (tile index, -1 = none): an aborted CTA waits for it
-      // before its shared memory is released; MMAs are drained through done_bar
-      int last_kv[2] = {-1, -1};
-      auto load_kv = [&](int j) {
+      // last load issued on each K and V stage (tile index, -1 = none): an aborted CTA waits for
+      // them before its shared memory is released; MMAs are drained through done_bar
+      int last_k[2] = {-1, -1};
+      int last_v[2] = {-1, -1};
+      auto load_tile = [&](int j, uint32_t smem_base, int x, uint64_t* bars) {
         const int stage = j & 1;
-        last_kv[stage] = j;
         const int y = prompt_begin + (tile_begin + j) * kKeys;
-        const uint32_t bar = smem_u32(&ctl.kv_bar[stage]);
-        mbar_expect_tx(bar, 2 * kKvBytes);
-        tma_load_2d(k_smem + stage * kKvBytes, &map, k_x, y, bar);
-        tma_load_2d(k_smem + stage * kKvBytes + kKvHalfBytes, &map, k_x + 64, y, bar);
-        tma_load_2d(v_smem + stage * kKvBytes, &map, v_x, y, bar);
-        tma_load_2d(v_smem + stage * kKvBytes + kKvHalfBytes, &map, v_x + 64, y, bar);
+        const uint32_t bar = smem_u32(&bars[stage]);
+        mbar_expect_tx(bar, kKvBytes);
+        tma_load_2d(smem_base + stage * kKvBytes, &map, x, y, bar);
+        tma_load_2d(smem_base + stage * kKvBytes + kKvHalfBytes, &map, x + 64, y, bar);
+      };
+      auto load_k = [&](int j) {
+        last_k[j & 1] = j;
+        load_tile(j, k_smem, k_x, ctl.k_bar);
+      };
+      auto load_v = [&](int j) {
+        last_v[j & 1] = j;
+        load_tile(j, v_smem, v_x, ctl.v_bar);
       };
       auto issue_s = [&](int j) {
         const int stage = j & 1;
@@ -351,25 +359,36 @@ __global__ void __launch_bounds__(kThreads, 2)
                       prompt_begin + q0 + rows * kKeys, q_bar);
         }
       }
-      load_kv(0);
-      if (tiles > 1) load_kv(1);
-      bool ok = mbar_wait(q_bar, 0) && mbar_wait(smem_u32(&ctl.kv_bar[0]), 0);
+      load_k(0);
+      load_v(0);
+      if (tiles > 1) {
+        load_k(1);
+        load_v(1);
+      }
+      bool ok = mbar_wait(q_bar, 0) && mbar_wait(smem_u32(&ctl.k_bar[0]), 0);
       if (ok) issue_s(0);
       for (int j = 0; ok && j < tiles; ++j) {
         if (j + 1 < tiles) {
           // S_{j+1} needs K_{j+1} and a free S buffer: PV_{j-1} read P_{j-1} from it
-          ok = mbar_wait(smem_u32(&ctl.kv_bar[(j + 1) & 1]), ((j + 1) >> 1) & 1) &&
+          ok = mbar_wait(smem_u32(&ctl.k_bar[(j + 1) & 1]), ((j + 1) >> 1) & 1) &&
                (j == 0 || mbar_wait(o_bar, (j - 1) & 1));
           if (!ok) break;
           issue_s(j + 1);
         }
-        ok = mbar_wait(smem_u32(&ctl.p_bar[j & 1]), (j >> 1) & 1, &ctl.abort);  // softmax wrote P_j
+        if (j + 2 < tiles) {
+          // S_j has read K_j (its completion is what the softmax of tile j waits for): refill
+          ok = mbar_wait(smem_u32(&ctl.s_bar[j & 1]), (j >> 1) & 1);
+          if (!ok) break;
+          load_k(j + 2);
+        }
+        ok = mbar_wait(smem_u32(&ctl.p_bar[j & 1]), (j >> 1) & 1, &ctl.abort) &&  // softmax wrote P_j
+             mbar_wait(smem_u32(&ctl.v_bar[j & 1]), (j >> 1) & 1);
         if (!ok) break;
         issue_pv(j);
         if (j + 2 < tiles) {
-          ok = mbar_wait(o_bar, j & 1);  // PV_j done: K_j and V_j buffers are free
+          ok = mbar_wait(o_bar, j & 1);  // PV_j done: V_j's buffer is free
           if (!ok) break;
-          load_kv(j + 2);
+          load_v(j + 2);
         }
       }
       if (!ok) {
@@ -384,7 +403,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (!ok) {
         mbar_wait(q_bar, 0);
         for (int s = 0; s < 2; ++s) {
-          if (last_kv[s] >= 0) mbar_wait(smem_u32(&ctl.kv_bar[s]), (last_kv[s] >> 1) & 1);
+          if (last_k[s] >= 0) mbar_wait(smem_u32(&ctl.k_bar[s]), (last_k[s] >> 1) & 1);
+          if (last_v[s] >= 0) mbar_wait(smem_u32(&ctl.v_bar[s]), (last_v[s] >> 1) & 1);
         }
       }
     }
