@@ -365,16 +365,17 @@ __global__ void __launch_bounds__(kThreads, 2)
         load_k(1);
         load_v(1);
       }
+      // S_0 and S_1 go out at once (both S buffers are free). Afterwards S_{j+2} is issued right
+      // behind PV_j: it overwrites the TMEM columns from which PV_j reads P_j, and the tensor pipe
+      // executes one thread's tcgen05.mma operations in issue order, so no completion wait sits
+      // between them and S_{j+2} is ready when the softmax of tile j+1 ends.
       bool ok = mbar_wait(q_bar, 0) && mbar_wait(smem_u32(&ctl.k_bar[0]), 0);
       if (ok) issue_s(0);
+      if (ok && tiles > 1) {
+        ok = mbar_wait(smem_u32(&ctl.k_bar[1]), 0);
+        if (ok) issue_s(1);
+      }
       for (int j = 0; ok && j < tiles; ++j) {
-        if (j + 1 < tiles) {
-          // S_{j+1} needs K_{j+1} and a free S buffer: PV_{j-1} read P_{j-1} from it
-          ok = mbar_wait(smem_u32(&ctl.k_bar[(j + 1) & 1]), ((j + 1) >> 1) & 1) &&
-               (j == 0 || mbar_wait(o_bar, (j - 1) & 1));
-          if (!ok) break;
-          issue_s(j + 1);
-        }
         if (j + 2 < tiles) {
           // S_j has read K_j (its completion is what the softmax of tile j waits for): refill
           ok = mbar_wait(smem_u32(&ctl.s_bar[j & 1]), (j >> 1) & 1);
@@ -386,6 +387,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (!ok) break;
         issue_pv(j);
         if (j + 2 < tiles) {
+          ok = mbar_wait(smem_u32(&ctl.k_bar[j & 1]), ((j + 2) >> 1) & 1);
+          if (!ok) break;
+          issue_s(j + 2);
           ok = mbar_wait(o_bar, j & 1);  // PV_j done: V_j's buffer is free
           if (!ok) break;
           load_v(j + 2);
@@ -466,8 +470,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       const bool rescale = move && j > 0 && m_ref != -INFINITY;
       if (__any_sync(0xffffffffu, rescale)) {
         // O (accumulated through PV_{j-1}) is rescaled by the whole warp, factor 1 on the rows
-        // that keep their reference; PV_{j-2} completed before S_j was issued, so o_bar is at
-        // most one phase behind here
+        // that keep their reference; S_j was issued behind PV_{j-2} and has completed, so o_bar
+        // is at most one phase behind here
         const bool o_ready = mbar_wait(o_bar, (j - 1) & 1, &ctl.abort);
         if (!__all_sync(0xffffffffu, o_ready)) {
           ok = false;
