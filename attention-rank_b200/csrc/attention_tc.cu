@@ -6,14 +6,11 @@
 // softmax_causal_kernel (attnrank/src/kernels.cu:117-162); key k is visible to query q iff
 // k <= q, k < prompt length and, with a sliding window, k > q - window.
 //
-// One CTA = one (prompt, 128-row query tile, query head). 288 threads:
-//   warps 0-7 (softmax): warps q and q + 4 own query rows 32q..32q+31 (TMEM lanes); warp q takes
-//     the first 32 keys of each 64-key tile, warp q + 4 the last 32. For every tile a thread reads
-//     its 32 scores of S = Q K^T (fp32) from TMEM, applies the mask, agrees on the row's tile
-//     maximum with its partner (shared memory + a 64-thread named barrier), writes its 32
-//     probabilities (16-bit) back into the same TMEM columns, and signals the control warp.
-//     Row sums stay per half until the epilogue.
-//   warp 8 (control): allocates TMEM, lane 0 issues every TMA load (no multicast) and every
+// One CTA = one (prompt, 128-row query tile, query head). 160 threads:
+//   warps 0-3 (softmax): thread r owns query row r = TMEM lane r. For every 64-key tile it
+//     reads S = Q K^T (fp32) from TMEM, applies the mask, keeps the row's running max / sum,
+//     writes P (16-bit) back into the same TMEM columns, and signals the control warp.
+//   warp 4 (control): allocates TMEM, lane 0 issues every TMA load (no multicast) and every
 //     tcgen05.mma, and commits MMA completion to mbarriers.
 // Pipeline per key tile j (K/V double-buffered in shared memory, S double-buffered in TMEM):
 //     S_{j+1} = Q K_{j+1}^T  overlaps the softmax of tile j;
@@ -48,11 +45,8 @@ namespace {
 constexpr int kHeadDim = 128;
 constexpr int kTile = 128;                         // query rows per CTA
 constexpr int kKeys = 64;                          // keys per tile
-constexpr int kSoftmaxWarps = 8;                   // two per 32-row TMEM lane quarter: one per key half
-constexpr int kSoftmaxThreads = 32 * kSoftmaxWarps;
-constexpr int kControlWarp = kSoftmaxWarps;        // the warp after the softmax warps
-constexpr int kThreads = kSoftmaxThreads + 32;
-constexpr int kHalfKeys = 32;                      // key columns of a 64-key tile per softmax half
+constexpr int kSoftmaxThreads = 128;
+constexpr int kThreads = kSoftmaxThreads + 32;     // + control warp
 constexpr uint32_t kTmemColumns = 256;             // S0 [0,64) S1 [64,128) O [128,256)
 constexpr uint32_t kTmemO = 2 * kKeys;
 constexpr uint32_t kRowBytes = 128;                // 64 16-bit values: one 128B-swizzled row of a half
@@ -86,14 +80,11 @@ struct __align__(16) Control {
   int span_lo[kMaxSpans];  // fused mass: the prompt's document spans
   int span_hi[kMaxSpans];
   float warp_sums[4][kMaxSpans];
-  float row_max[2][2][kTile];  // [tile parity][key half][row]: the halves' tile maxima
-  float row_sum[2][kTile];     // [key half][row]: the halves' probability sums, for the epilogue
 };
-// dynamic shared memory: the fixed part, then (fused mass only) float sigma[2][span_count][128]
-// (one span-sum array per key half, combined in a fixed order at the end)
+// dynamic shared memory: the fixed part, then (fused mass only) float sigma[span_count][128]
 constexpr size_t kSigmaOffset = kControlOffset + ((sizeof(Control) + 15) & ~size_t(15));
 constexpr size_t kSmemBytes = kSigmaOffset + 1024;
-constexpr size_t smem_bytes(int span_count) { return kSmemBytes + static_cast<size_t>(span_count) * 2 * kTile * 4; }
+constexpr size_t smem_bytes(int span_count) { return kSmemBytes + static_cast<size_t>(span_count) * kTile * 4; }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* pointer) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(pointer));
@@ -208,30 +199,9 @@ __device__ __forceinline__ void tmem_st32(uint32_t address, const uint32_t (&r)[
         "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
-__device__ __forceinline__ void tmem_st16(uint32_t address, const uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
-      ::"r"(address), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
-        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
-      : "memory");
-}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void softmax_barrier() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
-// The two softmax warps of one 32-row lane quarter (warps q and q + 4) meet at named barrier
-// 2 + q, which also ANDs their flags: both warps take every exit together, so neither can be left
-// waiting at a barrier its partner no longer reaches.
-__device__ __forceinline__ bool pair_barrier_all(int quarter, bool value) {
-  uint32_t result;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.and.pred q, %2, 64, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(result)
-      : "r"(value ? 1u : 0u), "r"(2 + quarter)
-      : "memory");
-  return result != 0;
-}
+__device__ __forceinline__ void softmax_barrier() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 // 2^x with the SFU's ex2 instruction, results below 2^-126 flushed to zero: a row's largest
 // probability relative to its reference is at least 1, so those vanish in O, l and the span sums
 __device__ __forceinline__ float ex2_ftz(float x) {
@@ -262,7 +232,7 @@ struct Args {
 };
 
 template <typename T>
-__global__ void __maxnreg__(112)  // 288 threads x 112 x 2 CTAs fit the SM's registers
+__global__ void __launch_bounds__(kThreads, 2)
     attention_tc_kernel(const __grid_constant__ CUtensorMap map, const Args args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -302,7 +272,7 @@ __global__ void __maxnreg__(112)  // 288 threads x 112 x 2 CTAs fit the SM's reg
     ctl.span_lo[tid] = max(span[0], 0);
     ctl.span_hi[tid] = span[1];
   }
-  for (int i = tid; i < 2 * S * kTile; i += kThreads) sigma[i] = 0.0f;
+  for (int i = tid; i < S * kTile; i += kThreads) sigma[i] = 0.0f;
 
   if (tid == 0) {
     mbar_init(smem_u32(&ctl.q_bar), 1);
@@ -319,7 +289,7 @@ __global__ void __maxnreg__(112)  // 288 threads x 112 x 2 CTAs fit the SM's reg
     ctl.abort = (args.status != nullptr && *reinterpret_cast<volatile int*>(args.status) != 0) ? 1 : 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == kControlWarp) {
+  if (warp == 4) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&ctl.tmem_base)),
                  "r"(kTmemColumns));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
@@ -333,7 +303,7 @@ __global__ void __maxnreg__(112)  // 288 threads x 112 x 2 CTAs fit the SM's reg
   const uint32_t done_bar = smem_u32(&ctl.done_bar);
   const bool skip = ctl.abort != 0;
 
-  if (warp == kControlWarp) {
+  if (warp == 4) {
     // ------------------------------------------------------------------ control warp (lane 0)
     if (lane == 0 && tiles > 0 && !skip) {
       const int q_x = head * kHeadDim;
@@ -444,98 +414,93 @@ __global__ void __maxnreg__(112)  // 288 threads x 112 x 2 CTAs fit the SM's reg
     }
   } else {
     // ------------------------------------------------------------------ softmax warps
-    const int quarter = warp & 3;              // TMEM lane quarter
-    const int half = warp >> 2;                // key half of each tile
-    const int row = tid & (kTile - 1);         // TMEM lane
+    const int row = tid;                       // TMEM lane
     const int query = q0 + row;                // prompt-relative
     const bool row_in = capture && query >= query_lo && query < query_hi;  // a probe row
-    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    const int col0 = half * kHalfKeys;
-    float* my_sigma = sigma + half * S * kTile;
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
     const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(kHeadDim));
     float m_ref = -INFINITY;
-    float l = 0.0f;  // this half's share of the row sum
+    float l = 0.0f;
     bool ok = tiles > 0 && !skip;
     // tcgen05.ld / tcgen05.st are warp-collective (.sync.aligned): every branch around them is
-    // decided uniformly per warp (__all_sync / __any_sync), never per row; the two warps of a
-    // lane quarter see the same rows and take the same decisions
+    // decided uniformly per warp (__all_sync / __any_sync), never per row
     for (int j = 0; ok && j < tiles; ++j) {
       const int stage = j & 1;
-      const bool ready = __all_sync(
-          0xffffffffu, mbar_wait(smem_u32(&ctl.s_bar[stage]), (j >> 1) & 1, &ctl.abort) && !ctl.abort);
-      const int k0 = (tile_begin + j) * kKeys + col0;  // first key of this half
-      float x[kHalfKeys];
-      if (ready) {
-        fence_after();
-        uint32_t raw[32];
-        tmem_ld32(tmem + lane_base + stage * kKeys + col0, raw);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < kHalfKeys; ++i) x[i] = __uint_as_float(raw[i]);  // scale folded into the exponent
-        const bool diagonal = k0 + kHalfKeys - 1 > q0 || k0 + kHalfKeys > length || args.sliding_window > 0;
-        if (diagonal) {
-          const int key_min = args.sliding_window > 0 ? query - args.sliding_window + 1 : 0;
-          const int key_max = min(query, length - 1);
-#pragma unroll
-          for (int i = 0; i < kHalfKeys; ++i) {
-            const int key = k0 + i;
-            if (key < key_min || key > key_max) x[i] = -INFINITY;
-          }
-        }
-        // the half's maximum in kChains independent chains
-        float m_part[kChains];
-#pragma unroll
-        for (int c = 0; c < kChains; ++c) m_part[c] = x[c];
-#pragma unroll
-        for (int i = kChains; i < kHalfKeys; ++i) m_part[i % kChains] = fmaxf(m_part[i % kChains], x[i]);
-#pragma unroll
-        for (int c = 1; c < kChains; ++c) m_part[0] = fmaxf(m_part[0], m_part[c]);
-        ctl.row_max[stage][half][row] = m_part[0];  // parity-indexed slots: the next tile writes the other
-      }
-      // the pair meets (its row maxima are then visible to both) and leaves together on a timeout
-      if (!pair_barrier_all(quarter, ready)) {
+      const bool ready = mbar_wait(smem_u32(&ctl.s_bar[stage]), (j >> 1) & 1, &ctl.abort) && !ctl.abort;
+      if (!__all_sync(0xffffffffu, ready)) {
         ok = false;
         break;
       }
-      const float m_tile = fmaxf(ctl.row_max[stage][0][row], ctl.row_max[stage][1][row]) * scale_log2;
+      fence_after();
+      const int k0 = (tile_begin + j) * kKeys;
+      float x[kKeys];
+      {
+        uint32_t raw[2][32];  // both 32-column loads in flight before one wait
+        tmem_ld32(tmem + lane_base + stage * kKeys, raw[0]);
+        tmem_ld32(tmem + lane_base + stage * kKeys + 32, raw[1]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {  // raw scores; the log2-domain scale is folded into the exponent
+          x[i] = __uint_as_float(raw[0][i]);
+          x[32 + i] = __uint_as_float(raw[1][i]);
+        }
+      }
+      const bool diagonal = k0 + kKeys - 1 > q0 || k0 + kKeys > length || args.sliding_window > 0;
+      if (diagonal) {
+        const int key_min = args.sliding_window > 0 ? query - args.sliding_window + 1 : 0;
+        const int key_max = min(query, length - 1);
+#pragma unroll
+        for (int i = 0; i < kKeys; ++i) {
+          const int key = k0 + i;
+          if (key < key_min || key > key_max) x[i] = -INFINITY;
+        }
+      }
+      // row max and (below) row sum with kChains independent accumulators: short dependency chains
+      float m_part[kChains];
+#pragma unroll
+      for (int c = 0; c < kChains; ++c) m_part[c] = x[c];
+#pragma unroll
+      for (int i = kChains; i < kKeys; ++i) m_part[i % kChains] = fmaxf(m_part[i % kChains], x[i]);
+#pragma unroll
+      for (int c = 1; c < kChains; ++c) m_part[0] = fmaxf(m_part[0], m_part[c]);
+      const float m_tile = m_part[0] * scale_log2;  // the tile max in log2 units (the scale is positive)
       // the row's reference max moves when the tile max exceeds it by more than the threshold
       // (or on the row's first unmasked key); O already holds earlier tiles only when j > 0
       const bool move = m_tile > m_ref + kRescaleThreshold || (m_ref == -INFINITY && m_tile != -INFINITY);
       const bool rescale = move && j > 0 && m_ref != -INFINITY;
       if (__any_sync(0xffffffffu, rescale)) {
-        // this half's 64 columns of O (accumulated through PV_{j-1}) are rescaled by the whole
-        // warp, factor 1 on the rows that keep their reference; S_j was issued behind PV_{j-2}
-        // and has completed, so o_bar is at most one phase behind here
-        const bool o_ready = __all_sync(0xffffffffu, mbar_wait(o_bar, (j - 1) & 1, &ctl.abort));
-        if (!pair_barrier_all(quarter, o_ready)) {  // the partner takes the same branch (same rows)
+        // O (accumulated through PV_{j-1}) is rescaled by the whole warp, factor 1 on the rows
+        // that keep their reference; S_j was issued behind PV_{j-2} and has completed, so o_bar
+        // is at most one phase behind here
+        const bool o_ready = mbar_wait(o_bar, (j - 1) & 1, &ctl.abort);
+        if (!__all_sync(0xffffffffu, o_ready)) {
           ok = false;
           break;
         }
         fence_after();
         const float factor = rescale ? exp2f(m_ref - m_tile) : 1.0f;
 #pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
+        for (int c = 0; c < 4; ++c) {
           uint32_t raw[32];
-          const uint32_t address = tmem + lane_base + kTmemO + half * 64 + c * 32;
-          tmem_ld32(address, raw);
+          tmem_ld32(tmem + lane_base + kTmemO + c * 32, raw);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) raw[i] = __float_as_uint(__uint_as_float(raw[i]) * factor);
-          tmem_st32(address, raw);
+          tmem_st32(tmem + lane_base + kTmemO + c * 32, raw);
         }
         l *= factor;
         if (row_in && factor != 1.0f) {
-          for (int s = 0; s < S; ++s) my_sigma[s * kTile + row] *= factor;
+          for (int s = 0; s < S; ++s) sigma[s * kTile + row] *= factor;
         }
       }
       if (move) m_ref = m_tile;
       const float neg_reference = m_ref == -INFINITY ? 0.0f : -m_ref;
       float sum = 0.0f;
       {
-        uint32_t packed[kHalfKeys / 2];  // 32 probabilities -> 16 TMEM columns of 16-bit pairs
+        uint32_t packed[kKeys / 2];  // 64 probabilities -> 32 TMEM columns of 16-bit pairs
         float s_part[kChains] = {};
 #pragma unroll
-        for (int i = 0; i < kHalfKeys / 2; ++i) {  // p = 2^(s * log2(e) / sqrt(D) - m_ref): one FFMA + one ex2
+        for (int i = 0; i < kKeys / 2; ++i) {  // p = 2^(s * log2(e) / sqrt(D) - m_ref): one FFMA + one ex2
           const float p0 = ex2_ftz(fmaf(x[2 * i], scale_log2, neg_reference));
           const float p1 = ex2_ftz(fmaf(x[2 * i + 1], scale_log2, neg_reference));
           s_part[i % kChains] += p0 + p1;
@@ -543,27 +508,27 @@ __global__ void __maxnreg__(112)  // 288 threads x 112 x 2 CTAs fit the SM's reg
           x[2 * i] = p0;
           x[2 * i + 1] = p1;
         }
-        tmem_st16(tmem + lane_base + stage * kKeys + half * (kHalfKeys / 2), packed);
+        tmem_st32(tmem + lane_base + stage * kKeys, packed);
 #pragma unroll
         for (int c = 0; c < kChains; ++c) sum += s_part[c];
       }
-      // fused mass: span sums of this half's fp32 probabilities, by the warps that hold probe rows
-      // (spans and k0 are CTA-uniform); a span that covers all 32 keys takes the half's sum
+      // fused mass: span sums of this tile's fp32 probabilities, by the warps that hold probe rows
+      // (spans and k0 are CTA-uniform); a span that covers the whole tile takes the tile's sum
       if (S > 0 && __any_sync(0xffffffffu, row_in)) {
         for (int s = 0; s < S; ++s) {
           const int lo = max(ctl.span_lo[s], k0) - k0;
-          const int hi = min(ctl.span_hi[s], k0 + kHalfKeys) - k0;
+          const int hi = min(ctl.span_hi[s], k0 + kKeys) - k0;
           if (lo >= hi) continue;
           float acc = sum;
-          if (lo > 0 || hi < kHalfKeys) {
+          if (lo > 0 || hi < kKeys) {
             float a_part[kChains] = {};
 #pragma unroll
-            for (int i = 0; i < kHalfKeys; ++i) a_part[i % kChains] += (i >= lo && i < hi) ? x[i] : 0.0f;
+            for (int i = 0; i < kKeys; ++i) a_part[i % kChains] += (i >= lo && i < hi) ? x[i] : 0.0f;
             acc = 0.0f;
 #pragma unroll
             for (int c = 0; c < kChains; ++c) acc += a_part[c];
           }
-          if (row_in) my_sigma[s * kTile + row] += acc;
+          if (row_in) sigma[s * kTile + row] += acc;
         }
       }
       l += sum;
@@ -578,17 +543,15 @@ __global__ void __maxnreg__(112)  // 288 threads x 112 x 2 CTAs fit the SM's reg
       report_status(args.status, kStatusWaitTimeout);
       ctl.abort = 1;
     }
-    ctl.row_sum[half][row] = l;
-    softmax_barrier();
-    l = ctl.row_sum[0][row] + ctl.row_sum[1][row];  // the same order in both halves
     fence_after();
     const float inv = l > 0.0f ? 1.0f / l : 0.0f;
     uint8_t* stage_rows = smem + kQOffset;  // the Q tile is no longer read: every MMA completed
-    {  // this half's 64 O columns: two TMEM loads in flight before one wait
+#pragma unroll 1
+    for (int c2 = 0; c2 < 2; ++c2) {  // 64 O columns per step: two TMEM loads in flight before one wait
       uint32_t raw[2][32];
       if (done) {
-        tmem_ld32(tmem + lane_base + kTmemO + half * 64, raw[0]);
-        tmem_ld32(tmem + lane_base + kTmemO + half * 64 + 32, raw[1]);
+        tmem_ld32(tmem + lane_base + kTmemO + c2 * 64, raw[0]);
+        tmem_ld32(tmem + lane_base + kTmemO + c2 * 64 + 32, raw[1]);
         tmem_wait_ld();
       } else {
 #pragma unroll
@@ -601,15 +564,15 @@ __global__ void __maxnreg__(112)  // 288 threads x 112 x 2 CTAs fit the SM's reg
           float y[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) y[i] = __uint_as_float(raw[h][v * 8 + i]) * inv;
-          const int chunk = (half * 2 + h) * 4 + v;  // 0..15 across the 256-byte row
+          const int chunk = (c2 * 2 + h) * 4 + v;  // 0..15 across the 256-byte row
           *reinterpret_cast<uint4*>(stage_rows + row * 256 + ((chunk ^ (row & 15)) << 4)) = pack8<T>(y);
         }
       }
     }
-    if (half == 0 && query < length && done) {
+    if (query < length && done) {
       args.lse[static_cast<size_t>(prompt_begin + query) * args.query_heads + head] = m_ref + log2f(l);
     }
-    if (S > 0 && half == 0) {
+    if (S > 0) {
       // fused mass: row values = span sums / l, with the reference's per-(row, span) length divisor
       int chunk_end = length;
       if (args.normalize_by_length) {
@@ -619,14 +582,14 @@ __global__ void __maxnreg__(112)  // 288 threads x 112 x 2 CTAs fit the SM's reg
       for (int s = 0; s < S; ++s) {
         float v = 0.0f;
         if (row_in && done) {
-          v = (sigma[s * kTile + row] + sigma[(S + s) * kTile + row]) * inv;
+          v = sigma[s * kTile + row] * inv;
           if (args.normalize_by_length) {
             const int divisor = min(ctl.span_hi[s], chunk_end) - ctl.span_lo[s];
             if (divisor > 0) v /= static_cast<float>(divisor);
           }
         }
         v = warp_sum(v);
-        if (lane == 0) ctl.warp_sums[quarter][s] = v;
+        if (lane == 0) ctl.warp_sums[warp][s] = v;
       }
     }
     softmax_barrier();
@@ -640,8 +603,8 @@ __global__ void __maxnreg__(112)  // 288 threads x 112 x 2 CTAs fit the SM's reg
     const int out_width = args.query_heads * kHeadDim;
     T* out = static_cast<T*>(args.out);
 #pragma unroll 1
-    for (int i = 0; i < 8; ++i) {  // each softmax warp writes 16 rows, two rows per instruction
-      const int r = warp * 16 + i * 2 + (lane >> 4);
+    for (int i = 0; i < 16; ++i) {  // each warp writes its 32 rows, two rows per instruction
+      const int r = warp * 32 + i * 2 + (lane >> 4);
       const int chunk = lane & 15;
       if (q0 + r < length) {
         const uint4 value = *reinterpret_cast<const uint4*>(stage_rows + r * 256 + ((chunk ^ (r & 15)) << 4));
@@ -653,7 +616,7 @@ __global__ void __maxnreg__(112)  // 288 threads x 112 x 2 CTAs fit the SM's reg
 
   fence_before();
   __syncthreads();
-  if (warp == kControlWarp) {
+  if (warp == 4) {
     __syncwarp();
     fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemColumns));
