@@ -274,7 +274,33 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
   for (int i = tid; i < S * kTile; i += kThreads) sigma[i] = 0.0f;
 
-  if (tid == 0) {
+  // The control lane initialises the barriers and issues the Q, K and V loads of the first two
+  // tiles before the TMEM allocation and the CTA barrier, so their latency overlaps the set-up.
+  const bool control_lane = warp == 4 && lane == 0;
+  const int q_x = head * kHeadDim;
+  const int k_x = (args.query_heads + kv_head) * kHeadDim;
+  const int v_x = (args.query_heads + args.kv_heads + kv_head) * kHeadDim;
+  // last load issued on each K and V stage (tile index, -1 = none): an aborted CTA waits for them
+  // before its shared memory is released; MMAs are drained through done_bar
+  int last_k[2] = {-1, -1};
+  int last_v[2] = {-1, -1};
+  auto load_tile = [&](int j, uint32_t smem_base, int x, uint64_t* bars) {
+    const int stage = j & 1;
+    const int y = prompt_begin + (tile_begin + j) * kKeys;
+    const uint32_t bar = smem_u32(&bars[stage]);
+    mbar_expect_tx(bar, kKvBytes);
+    tma_load_2d(smem_base + stage * kKvBytes, &map, x, y, bar);
+    tma_load_2d(smem_base + stage * kKvBytes + kKvHalfBytes, &map, x + 64, y, bar);
+  };
+  auto load_k = [&](int j) {
+    last_k[j & 1] = j;
+    load_tile(j, k_smem, k_x, ctl.k_bar);
+  };
+  auto load_v = [&](int j) {
+    last_v[j & 1] = j;
+    load_tile(j, v_smem, v_x, ctl.v_bar);
+  };
+  if (control_lane) {
     mbar_init(smem_u32(&ctl.q_bar), 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&ctl.k_bar[i]), 1);
@@ -286,10 +312,28 @@ __global__ void __launch_bounds__(kThreads, 2)
     mbar_init(smem_u32(&ctl.done_bar), 1);
     // a CTA of a launch that already reported an error does no work (bounds a failing launch to
     // about one wave of timed-out CTAs); read once here so that the whole CTA agrees
-    ctl.abort = (args.status != nullptr && *reinterpret_cast<volatile int*>(args.status) != 0) ? 1 : 0;
+    const int abort = (args.status != nullptr && *reinterpret_cast<volatile int*>(args.status) != 0) ? 1 : 0;
+    ctl.abort = abort;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    if (tiles > 0 && !abort) {
+      const uint32_t bar = smem_u32(&ctl.q_bar);
+      mbar_expect_tx(bar, kQBytes);
+      for (int half = 0; half < 2; ++half) {  // four 64 x 64 boxes: (column half, row half)
+        for (int rows = 0; rows < 2; ++rows) {
+          tma_load_2d(q_smem + half * kQHalfBytes + rows * kKvHalfBytes, &map, q_x + 64 * half,
+                      prompt_begin + q0 + rows * kKeys, bar);
+        }
+      }
+      load_k(0);
+      load_v(0);
+      if (tiles > 1) {
+        load_k(1);
+        load_v(1);
+      }
+    }
   }
   if (warp == 4) {
+    __syncwarp();
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&ctl.tmem_base)),
                  "r"(kTmemColumns));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
@@ -306,29 +350,6 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (warp == 4) {
     // ------------------------------------------------------------------ control warp (lane 0)
     if (lane == 0 && tiles > 0 && !skip) {
-      const int q_x = head * kHeadDim;
-      const int k_x = (args.query_heads + kv_head) * kHeadDim;
-      const int v_x = (args.query_heads + args.kv_heads + kv_head) * kHeadDim;
-      // last load issued on each K and V stage (tile index, -1 = none): an aborted CTA waits for
-      // them before its shared memory is released; MMAs are drained through done_bar
-      int last_k[2] = {-1, -1};
-      int last_v[2] = {-1, -1};
-      auto load_tile = [&](int j, uint32_t smem_base, int x, uint64_t* bars) {
-        const int stage = j & 1;
-        const int y = prompt_begin + (tile_begin + j) * kKeys;
-        const uint32_t bar = smem_u32(&bars[stage]);
-        mbar_expect_tx(bar, kKvBytes);
-        tma_load_2d(smem_base + stage * kKvBytes, &map, x, y, bar);
-        tma_load_2d(smem_base + stage * kKvBytes + kKvHalfBytes, &map, x + 64, y, bar);
-      };
-      auto load_k = [&](int j) {
-        last_k[j & 1] = j;
-        load_tile(j, k_smem, k_x, ctl.k_bar);
-      };
-      auto load_v = [&](int j) {
-        last_v[j & 1] = j;
-        load_tile(j, v_smem, v_x, ctl.v_bar);
-      };
       auto issue_s = [&](int j) {
         const int stage = j & 1;
         fence_after();
@@ -352,19 +373,6 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         mma_commit(o_bar);
       };
-      mbar_expect_tx(q_bar, kQBytes);
-      for (int half = 0; half < 2; ++half) {     // four 64 x 64 boxes: (column half, row half)
-        for (int rows = 0; rows < 2; ++rows) {
-          tma_load_2d(q_smem + half * kQHalfBytes + rows * kKvHalfBytes, &map, q_x + 64 * half,
-                      prompt_begin + q0 + rows * kKeys, q_bar);
-        }
-      }
-      load_k(0);
-      load_v(0);
-      if (tiles > 1) {
-        load_k(1);
-        load_v(1);
-      }
       // S_0 and S_1 go out at once (both S buffers are free). Afterwards S_{j+2} is issued right
       // behind PV_j: it overwrites the TMEM columns from which PV_j reads P_j, and the tensor pipe
       // executes one thread's tcgen05.mma operations in issue order, so no completion wait sits
