@@ -5,7 +5,9 @@ names (model.cu:120-166) and a config.json, then loaded with `from_pretrained`, 
 shard and uploads every tensor with ar_engine_load_tensor. That is host data -> device, with the
 engine's conversions: bf16 or fp32 matrices -> fp16 by round-to-nearest-even, fp32 biases and
 norms, and the fp16 copy of the q|k|v bias used by the GEMM epilogue. The engine built on the
-synthetic generator converts the same values by the same rule, so mass rows must be identical.
+synthetic generator converts the same values by the same rule. The two engines may still pick
+different cuBLASLt algorithms (each times its candidates), which changes GEMM rounding in the last
+bits, so rows are compared at rel 1e-4: a wrong tensor, shape or conversion moves them by O(1).
 """
 from __future__ import annotations
 
@@ -81,7 +83,7 @@ def test_from_pretrained_equals_synthetic_engine(cuda, tmp_path, matrix_dtype):
     prompts = synthetic.prompts(4, config.vocab_size, shape, seed=8)
     got, _ = loaded.probe_rows(prompts)
     want, _ = reference.probe_rows(prompts)
-    assert np.array_equal(got, want)
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-9)
     loaded.close()
     reference.close()
 
