@@ -93,21 +93,29 @@ float element_as_float(const void* data, int dtype, size_t index) {
   }
 }
 
+// Host -> device copy ordered on the engine's stream and complete on return. A plain cudaMemcpy
+// from pageable memory may return before its DMA lands, and it is not ordered with the engine's
+// non-blocking stream, so a kernel there could read the destination too early.
+void copy_to_device(void* dst, const void* host, size_t bytes, cudaStream_t stream, const char* what) {
+  check_cuda(cudaMemcpyAsync(dst, host, bytes, cudaMemcpyHostToDevice, stream), what);
+  check_cuda(cudaStreamSynchronize(stream), what);
+}
+
 // Upload `count` elements of host data as bf16 into dst (host-side conversion).
-void upload_bf16(void* dst, const void* host, int dtype, size_t count) {
+void upload_bf16(void* dst, const void* host, int dtype, size_t count, cudaStream_t stream) {
   if (dtype == 2) {
-    check_cuda(cudaMemcpy(dst, host, count * 2, cudaMemcpyHostToDevice), "weight upload");
+    copy_to_device(dst, host, count * 2, stream, "weight upload");
     return;
   }
   std::vector<uint16_t> staged(count);
   for (size_t i = 0; i < count; ++i) staged[i] = float_to_bf16_bits(element_as_float(host, dtype, i));
-  check_cuda(cudaMemcpy(dst, staged.data(), count * 2, cudaMemcpyHostToDevice), "weight upload");
+  copy_to_device(dst, staged.data(), count * 2, stream, "weight upload");
 }
 
-void upload_f32(float* dst, const void* host, int dtype, size_t count) {
+void upload_f32(float* dst, const void* host, int dtype, size_t count, cudaStream_t stream) {
   std::vector<float> staged(count);
   for (size_t i = 0; i < count; ++i) staged[i] = element_as_float(host, dtype, i);
-  check_cuda(cudaMemcpy(dst, staged.data(), count * 4, cudaMemcpyHostToDevice), "weight upload");
+  copy_to_device(dst, staged.data(), count * 4, stream, "weight upload");
 }
 
 enum LayerTensor : int {
@@ -216,18 +224,18 @@ void Engine::kernel_timing(double* milliseconds, double* work, int64_t* launches
 void Engine::upload_matrix(void* dst, const void* host, int dtype, size_t count) {
   const int target = options_.activation_dtype;
   if (dtype == target) {
-    check_cuda(cudaMemcpy(dst, host, count * 2, cudaMemcpyHostToDevice), "weight upload");
+    copy_to_device(dst, host, count * 2, stream_, "weight upload");
     return;
   }
   if (target == kActBf16 && dtype == 1) {
-    upload_bf16(dst, host, dtype, count);
+    upload_bf16(dst, host, dtype, count, stream_);
     return;
   }
   if (dtype != 0 && dtype != 2) throw Error("unsupported tensor dtype code " + std::to_string(dtype));
   const size_t bytes = count * (dtype == 0 ? 4 : 2);
   void* staging = nullptr;
   check_cuda(cudaMalloc(&staging, bytes), "weight staging allocation");
-  cudaError_t status = cudaMemcpy(staging, host, bytes, cudaMemcpyHostToDevice);
+  cudaError_t status = cudaMemcpyAsync(staging, host, bytes, cudaMemcpyHostToDevice, stream_);  // ordered before the conversion
   if (status == cudaSuccess) {
     status = dtype == 0 ? launch_f32_to_activation(static_cast<const float*>(staging), dst, static_cast<long long>(count),
                                                    target, stream_)
@@ -388,7 +396,7 @@ void Engine::load_tensor(const std::string& name, int dtype, const std::vector<i
   }
   if (name == "model.norm.weight") {
     expect(H, 1);
-    upload_f32(final_norm_, host, dtype, static_cast<size_t>(count));
+    upload_f32(final_norm_, host, dtype, static_cast<size_t>(count), stream_);
     return;
   }
   static const std::regex layer_pattern(R"(model\.layers\.(\d+)\.(.+))");
@@ -417,7 +425,7 @@ void Engine::load_tensor(const std::string& name, int dtype, const std::vector<i
     const char which = suffix[10];
     const int64_t offset = which == 'q' ? 0 : which == 'k' ? Hq * D : Hq * D + KV;
     expect(which == 'q' ? Hq * D : KV, 1);
-    upload_f32(layer.qkv_bias + offset, host, dtype, count);
+    upload_f32(layer.qkv_bias + offset, host, dtype, count, stream_);
     refresh_half_bias(index);
     loaded_[index][which == 'q' ? kQBias : which == 'k' ? kKBias : kVBias] = true;
   } else if (suffix == "self_attn.o_proj.weight") {
@@ -438,11 +446,11 @@ void Engine::load_tensor(const std::string& name, int dtype, const std::vector<i
     loaded_[index][kDown] = true;
   } else if (suffix == "input_layernorm.weight") {
     expect(H, 1);
-    upload_f32(layer.input_norm, host, dtype, count);
+    upload_f32(layer.input_norm, host, dtype, count, stream_);
     loaded_[index][kInputNorm] = true;
   } else if (suffix == "post_attention_layernorm.weight") {
     expect(H, 1);
-    upload_f32(layer.post_norm, host, dtype, count);
+    upload_f32(layer.post_norm, host, dtype, count, stream_);
     loaded_[index][kPostNorm] = true;
   }
 }
@@ -879,8 +887,7 @@ std::unique_ptr<PreparedScan> Engine::prepare_scan(const std::vector<PromptView>
   ensure_partials(max_items, span_count, range.count());
   check_cuda(cudaMalloc(reinterpret_cast<void**>(&prepared->device), host.size() * sizeof(int32_t)),
              "prepared scan allocation");
-  check_cuda(cudaMemcpy(prepared->device, host.data(), host.size() * sizeof(int32_t), cudaMemcpyHostToDevice),
-             "prepared scan upload");
+  copy_to_device(prepared->device, host.data(), host.size() * sizeof(int32_t), stream_, "prepared scan upload");
   prepared->device_bytes = host.size() * sizeof(int32_t);
   return prepared;
 }
