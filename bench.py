@@ -34,9 +34,31 @@ sys.path.insert(0, str(ROOT / "attention-rank_b200"))
 sys.path.insert(0, str(ROOT))
 
 METRIC = "profiled prompts/s (7B arch, 1/2/4/8 B200); fused-kernel HBM GB/s vs peak"
-PROMPT_COUNT = 400
 MIN_EDGE_RATIO = 1.3
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+# The scan workloads: BASELINE config 3 (the default bench line) and config 4.
+WORKLOADS = {
+    "qwen-scan": {"model": "qwen2_7b", "shape": "QWEN_PROMPTS", "prompts": 400, "max_sequence": 4096,
+                  "reference_sample": 128,
+                  "text": "layer scan, Qwen2.5-7B architecture, {n} prompts x (5 docs U[120,240] + 40-token question), "
+                          "min_edge_ratio 1.3"},
+    "llama3-long": {"model": "llama3_8b", "shape": "LLAMA3_LONG_PROMPTS", "prompts": 256, "max_sequence": 8192,
+                    "reference_sample": 16,
+                    "text": "long-context layer scan, Llama-3-8B architecture, {n} prompts x (20 docs U[150,250] + "
+                            "64-token question), min_edge_ratio 1.3"},
+}
+
+
+def workload(args):
+    """(LlamaConfig, prompts, spec) of the chosen workload."""
+    from attnrank import synthetic
+    spec = WORKLOADS[args.config]
+    config = getattr(synthetic, spec["model"])()
+    count = args.prompts if args.prompts is not None else spec["prompts"]
+    prompts = synthetic.prompts(count, config.vocab_size, getattr(synthetic, spec["shape"]))
+    return config, prompts, spec
 
 
 def parse_args():
@@ -45,9 +67,11 @@ def parse_args():
     parser.add_argument("--steps", type=int, default=3)
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    parser.add_argument("--prompts", type=int, default=PROMPT_COUNT)
-    parser.add_argument("--reference-sample", type=int, default=128,
-                        help="prompts per reference step (a bounded sample of the 400-prompt scan)")
+    parser.add_argument("--config", choices=sorted(WORKLOADS), default="qwen-scan",
+                        help="qwen-scan: BASELINE config 3 (the bench line); llama3-long: config 4")
+    parser.add_argument("--prompts", type=int, default=None, help="prompts per scan (default: the workload's)")
+    parser.add_argument("--reference-sample", type=int, default=None,
+                        help="prompts per reference step (a bounded sample of the scan; default: the workload's)")
     parser.add_argument("--batch-tokens", type=int, default=16384)
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-kernels", action="store_true", help="skip the per-kernel roofline timing")
@@ -409,14 +433,15 @@ def run_b200(args, rank, world, local_rank):
     from attnrank import synthetic
     from attnrank.scheduler import ProbeScheduler, shard_by_length
 
-    config = synthetic.qwen2_7b()
-    prompts = synthetic.prompts(args.prompts, config.vocab_size)
-    options = ar.RuntimeOptions(device_index=local_rank, max_sequence_length=4096, max_batch_tokens=args.batch_tokens,
+    config, prompts, spec = workload(args)
+    prompt_count = len(prompts)
+    options = ar.RuntimeOptions(device_index=local_rank, max_sequence_length=spec["max_sequence"],
+                                max_batch_tokens=args.batch_tokens,
                                 activation_dtype=args.dtype, attention_kernel=args.attention)
     engine = ar.Engine.synthetic(config, seed=0, options=options)
     shard = shard_by_length([len(p.tokens) for p in prompts], world)[rank]
     mine = [prompts[i] for i in shard]
-    slots = 5
+    slots = len(prompts[0].document_spans)
     L = config.num_hidden_layers
     prepared = engine.prepare_scan(mine)
     accumulator = torch.zeros(L * slots, dtype=torch.float32, device=f"cuda:{local_rank}")
@@ -448,7 +473,7 @@ def run_b200(args, rank, world, local_rank):
     engine.synchronize()  # raises on any device-reported error
     elapsed_ms = max_over_ranks(start.elapsed_time(stop), world)
     ms_per_step = elapsed_ms / args.steps
-    value = args.prompts / (ms_per_step / 1000.0)
+    value = prompt_count / (ms_per_step / 1000.0)
 
     # one more (untimed) step with every engine launch bracketed by CUDA events: per-kernel
     # device time and algorithmic work inside the real scan, and the count of our own launches
@@ -459,7 +484,7 @@ def run_b200(args, rank, world, local_rank):
 
     # the scan result of the timed steps: accumulator of the last step -> profiles, basin pick
     accumulated = accumulator.double().cpu().numpy().reshape(L, slots)
-    profiles = [ar.AttentionProfile.from_accumulated("synthetic", l, args.prompts, accumulated[l]) for l in range(L)]
+    profiles = [ar.AttentionProfile.from_accumulated("synthetic", l, prompt_count, accumulated[l]) for l in range(L)]
     selected = ar.select_shallowest_basin_layer(profiles=profiles, min_edge_ratio=MIN_EDGE_RATIO)
 
     # end to end through the public API (host prompts in, H2D + D2H inside the timed region)
@@ -520,15 +545,14 @@ def run_b200(args, rank, world, local_rank):
         "dtype": args.dtype,
         "data": "synthetic (seeded random-init weights: bf16 values, stored in the compute dtype; seeded random "
                 "token-id prompts)",
-        "config": {"workload": "layer scan, Qwen2.5-7B architecture, 400 prompts x (5 docs U[120,240] + 40-token "
-                               "question), min_edge_ratio 1.3", "global_batch": args.prompts,
+        "config": {"workload": spec["text"].format(n=prompt_count), "global_batch": prompt_count,
                    "seq_len": round(sum(len(p.tokens) for p in prompts) / len(prompts), 1),
                    "parallelism": f"dp{world} (prompt shards, one NCCL all-reduce)",
                    "batch_tokens": args.batch_tokens,
-                   "l2": "inputs larger than L2 (15.2 GB of weights streamed per batch); no flush"},
+                   "l2": "inputs larger than L2 (15-16 GB of weights streamed per batch); no flush"},
         "selected_layer": selected,
         "slot_order_selected": profiles[selected].position_order if selected >= 0 else None,
-        "e2e": {"value": round(args.prompts / e2e_step, 3), "unit": "prompts/s", "h2d_bytes_per_step": int(h2d),
+        "e2e": {"value": round(prompt_count / e2e_step, 3), "unit": "prompts/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h), "selected_layer": scan.selected_layer,
                 "api": "attnrank.scheduler.ProbeScheduler.find_shallowest_attention_layer"},
         "roofline": {"bound": "tensor", "kernel": "whole scan step (cuBLASLt GEMMs + attention + mass)",
@@ -563,11 +587,13 @@ def run_reference(args, rank, world, local_rank):
 
     if reference.load_or_none() is None:
         return {"impl": "reference", "unavailable": "oracle/_ref/libattnrank_ref.so was not built (make -C oracle reference)"}
-    config = synthetic.qwen2_7b()
-    prompts = synthetic.prompts(args.reference_sample, config.vocab_size)
+    spec = WORKLOADS[args.config]
+    sample = args.reference_sample if args.reference_sample is not None else spec["reference_sample"]
+    config, prompts, spec = workload(argparse.Namespace(config=args.config, prompts=sample))
     shard = shard_by_length([len(p.tokens) for p in prompts], world)[rank]
     mine = [prompts[i] for i in shard]
-    model = reference.ReferenceModel(config, seed=0, max_sequence_length=2048, device=local_rank)
+    longest = max(len(p.tokens) for p in prompts)
+    model = reference.ReferenceModel(config, seed=0, max_sequence_length=max(2048, longest), device=local_rank)
     for _ in range(args.warmup):
         model.scan(mine[: max(1, len(mine) // 8)], min_edge_ratio=MIN_EDGE_RATIO)
     barrier(world)
@@ -577,7 +603,7 @@ def run_reference(args, rank, world, local_rank):
         result = model.scan(mine, min_edge_ratio=MIN_EDGE_RATIO)
         seconds.append(result.seconds)
     step_seconds = max_over_ranks(sum(seconds) / len(seconds), world)
-    value = args.reference_sample / step_seconds
+    value = sample / step_seconds
     cores = os.cpu_count() or 1
     model.close()
     return {
@@ -585,13 +611,13 @@ def run_reference(args, rank, world, local_rank):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_seconds * 1000, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16/fp32",
         "data": "synthetic (seeded random-init weights, seeded random token-id prompts)",
-        "config": {"workload": "layer scan, Qwen2.5-7B architecture, reference CudaLlamaModel + "
-                               "AttentionLayerScanner (stock path), min_edge_ratio 1.3",
-                   "global_batch": args.reference_sample, "parallelism": f"{world} independent processes on "
+        "config": {"workload": spec["text"].format(n=sample) + "; reference CudaLlamaModel + "
+                               "AttentionLayerScanner (stock path)",
+                   "global_batch": sample, "parallelism": f"{world} independent processes on "
                    "prompt shards (the reference's multi-GPU practice)"},
         "selected_layer": result.selected_layer if result else None,
         "cpu_baseline": {"value": round(value, 3), "unit": "prompts/s", "cores": cores, "kind": "reference",
-                         "sample": f"first {args.reference_sample} of the 400 prompts per step; the reference's "
+                         "sample": f"first {sample} of the {spec['prompts']} prompts per step; the reference's "
                                    "path is CUDA, so it runs on the GPU (wall clock around its synchronous scan)"},
         "e2e": {"value": round(value, 3), "unit": "prompts/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
