@@ -7,11 +7,13 @@ token-id prompts (``StructuredPrompt``). All probing runs in libattnrank_b200.so
 package without the built library raises ImportError.
 """
 from attnrank import core
-from attnrank.core import (AttentionProfile, AttnRankError, BasinCriterion, BasinStatistics, Engine, LayerProbeResult,
-                           LayerScanConfig, LlamaConfig, ProfilerConfig, RuntimeOptions, StructuredPrompt, TokenSpan)
-from attnrank.data.classes import EngineSettings, LayerScanSettings, ProfileSettings
+from attnrank.core import (AttentionProfile, AttnRankError, BasinCriterion, BasinStatistics, Engine, GenerationResult,
+                           LayerProbeResult, LayerScanConfig, LlamaConfig, ProfilerConfig, RuntimeOptions,
+                           StructuredPrompt, TokenSampler, TokenSpan, make_sampler)
+from attnrank.data.classes import EngineSettings, GenerationSettings, LayerScanSettings, ProfileSettings
 from attnrank.engine import (LayerScan, attention_slot_order, basin_statistics, extract_attention_profile,
-                             find_shallowest_attention_layer, from_pretrained, is_model_directory,
+                             find_shallowest_attention_layer, from_pretrained, generate_from_prompt,
+                             is_model_directory,
                              load_attention_profile, load_model, make_prompt, make_reranker,
                              measure_attention_by_layer, measure_document_attention, profile_to_dict,
                              rerank_baseline, rerank_documents, rerank_with_profile, reranker_names,
@@ -22,6 +24,7 @@ __version__ = "0.1.0"
 
 __all__ = [
     "AttentionProfile", "AttnRankError", "BasinCriterion", "BasinStatistics", "Engine", "EngineSettings",
+    "GenerationResult", "GenerationSettings", "TokenSampler", "generate_from_prompt", "make_sampler",
     "LayerProbeResult", "LayerScan", "LayerScanConfig", "LayerScanSettings", "LlamaConfig", "ProfileSettings",
     "ProfilerConfig", "RuntimeOptions", "StructuredPrompt", "TokenSpan", "attention_slot_order", "basin_statistics",
     "core", "extract_attention_profile", "find_shallowest_attention_layer", "from_pretrained", "is_model_directory",

@@ -38,6 +38,7 @@ class LlamaConfigStruct(ctypes.Structure):
         ("rope_theta", ctypes.c_float),
         ("sliding_window", ctypes.c_int),
         ("attention_bias", ctypes.c_int),
+        ("tie_word_embeddings", ctypes.c_int),
     ]
 
 
@@ -50,6 +51,15 @@ class RuntimeOptionsStruct(ctypes.Structure):
         ("max_batch_prompts", ctypes.c_int),
         ("activation_dtype", ctypes.c_int),
         ("attention_kernel", ctypes.c_int),
+    ]
+
+
+class SamplerConfigStruct(ctypes.Structure):
+    _fields_ = [
+        ("temperature", ctypes.c_float),
+        ("top_p", ctypes.c_float),
+        ("top_k", ctypes.c_int),
+        ("seed", ctypes.c_uint64),
     ]
 
 
@@ -112,6 +122,16 @@ SIGNATURES: dict[str, list] = {
     "ar_kernel_class_is_tensor": [_I],
     "ar_engine_stream": [_P],
     "ar_engine_device": [_P],
+    "ar_engine_generate": [_P, _P, _I, _I, _I, ctypes.POINTER(SamplerConfigStruct), _P, _P],
+    "ar_engine_generation_begin": [_P, _P, _I, _P],
+    "ar_engine_generation_step": [_P, ctypes.c_int32, _P],
+    "ar_engine_generation_position": [_P],
+    "ar_sampler_create": [ctypes.POINTER(SamplerConfigStruct), ctypes.POINTER(_P)],
+    "ar_sampler_select": [_P, _P, _I, _P],
+    "ar_sampler_destroy": [_P],
+    "ar_decode_gemv": [_P, _P, _I, _I, _P, _I, _I, _P],
+    "ar_decode_gate_up": [_P, _P, _I, _I, _P, _I, _P],
+    "ar_decode_attention": [_P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _I, _P],
     "ar_profile_from_accumulated": [_P, _I, _I64, _P, _P],
     "ar_position_order": [_P, _I, _P],
     "ar_basin_statistics": [_P, _I, _D, ctypes.POINTER(BasinStatsStruct)],
@@ -123,6 +143,7 @@ _RESTYPES = {
     "ar_version": ctypes.c_char_p,
     "ar_engine_destroy": None,
     "ar_prepared_scan_destroy": None,
+    "ar_sampler_destroy": None,
     "ar_prepared_scan_bytes": ctypes.c_int64,
     "ar_kernel_class_name": ctypes.c_char_p,
     "ar_engine_stream": ctypes.c_void_p,

@@ -132,7 +132,8 @@ class LlamaConfig:
         return _native.LlamaConfigStruct(
             self.hidden_size, self.intermediate_size, self.num_hidden_layers, self.num_attention_heads,
             self.num_key_value_heads, self.vocab_size, self.max_position_embeddings, self.rms_norm_eps,
-            self.rope_theta, self.sliding_window, 1 if self.attention_bias else 0)
+            self.rope_theta, self.sliding_window, 1 if self.attention_bias else 0,
+            1 if self.tie_word_embeddings else 0)
 
 
 @dataclass
@@ -163,6 +164,64 @@ class RuntimeOptions:
     @property
     def dtype_code(self) -> int:
         return {"fp16": _native.DTYPE_F16, "bf16": _native.DTYPE_BF16}[self.activation_dtype]
+
+
+@dataclass
+class GenerationResult:
+    """GenerationResult (model.hpp:124-129; Python fields of bindings.cpp:286-291)."""
+
+    generated_tokens: list[int]
+    text: str = ""
+    prompt_token_count: int = 0
+    hit_stop_sequence: bool = False
+
+    @property
+    def raw_bytes(self) -> bytes:
+        return self.text.encode("utf-8", "surrogateescape")
+
+
+class TokenSampler:
+    """GreedySampler (temperature <= 0) or NucleusSampler (model.hpp:88-116, model.cpp:70-127),
+    the library's host implementation: the same logits and seed give the reference's token ids."""
+
+    def __init__(self, temperature: float = 0.0, top_p: float = 0.9, top_k: int = 0, seed: int = 1234):
+        self.config = _native.SamplerConfigStruct(float(temperature), float(top_p), int(top_k), int(seed))
+        handle = ctypes.c_void_p()
+        check(lib.ar_sampler_create(ctypes.byref(self.config), ctypes.byref(handle)))
+        self._handle = handle
+
+    @property
+    def greedy(self) -> bool:
+        return self.config.temperature <= 0.0
+
+    def select(self, logits) -> int:
+        values = np.ascontiguousarray(logits, dtype=np.float32)
+        token = ctypes.c_int32(0)
+        check(lib.ar_sampler_select(self._handle, values.ctypes.data, values.size, ctypes.byref(token)))
+        return int(token.value)
+
+    def __del__(self):
+        handle = getattr(self, "_handle", None)
+        if handle is not None and handle.value:
+            lib.ar_sampler_destroy(handle)
+            self._handle = None
+
+
+def make_sampler(temperature: float = 0.0, top_p: float = 0.9, top_k: int = 0, seed: int = 1234) -> TokenSampler:
+    """make_sampler (model.cpp:124-127)."""
+    return TokenSampler(temperature, top_p, top_k, seed)
+
+
+def _apply_stop_sequence(decoded: str, stops: Sequence[str]) -> tuple[bool, str]:
+    """apply_stop_sequence (model.cu:490-501): the first stop string (in list order) found
+    anywhere in the text cuts it at its first occurrence."""
+    for stop in stops:
+        if not stop:
+            continue
+        found = decoded.find(stop)
+        if found >= 0:
+            return True, decoded[:found]
+    return False, decoded
 
 
 @dataclass
@@ -558,6 +617,74 @@ class Engine:
             result[name] = {"ms": ms[k], "work": work[k], "launches": int(launches[k]),
                             "tensor": bool(lib.ar_kernel_class_is_tensor(k))}
         return result
+
+    # -- generation ----------------------------------------------------------------------------
+    def generate(self, prompt_tokens: Sequence[int], max_new_tokens: int = 128, stop_sequences: Sequence[str] = (),
+                 temperature: float = 0.0, top_p: float = 0.9, top_k: int = 0, seed: int = 1234, *,
+                 decode: Callable[[list[int]], str] | None = None) -> GenerationResult:
+        """Engine.generate (bindings.cpp:360-363 -> CudaLlamaModel::generate, model.cu:532-565).
+
+        Stops at the config's eos_token_id (not returned), max_new_tokens or the end of the context
+        (RuntimeOptions.max_sequence_length). Text needs a tokenizer, which this library does not
+        carry: pass ``decode`` (token ids -> str) to get ``text`` and to use ``stop_sequences``.
+        Without stop strings the whole loop runs in the library (greedy selection on the device);
+        with them the loop runs here, one library step per token, testing the decoded text after
+        every token as the reference does."""
+        tokens = np.ascontiguousarray(np.asarray(prompt_tokens, dtype=np.int32).ravel())
+        stops = [stop for stop in stop_sequences if stop]
+        if stops and decode is None:
+            raise AttnRankError("stop_sequences need a decode function (token ids -> text)")
+        eos = int(self.config.eos_token_id)
+        if not stops:
+            config = _native.SamplerConfigStruct(float(temperature), float(top_p), int(top_k), int(seed))
+            out = np.zeros(max(int(max_new_tokens), 1), dtype=np.int32)
+            count = ctypes.c_int(0)
+            with self._lock:
+                check(lib.ar_engine_generate(self._handle, tokens.ctypes.data, tokens.size, int(max_new_tokens), eos,
+                                             ctypes.byref(config), out.ctypes.data, ctypes.byref(count)))
+            generated = [int(t) for t in out[:count.value]]
+            text = decode(generated) if decode is not None and generated else ""
+            return GenerationResult(generated, text, int(tokens.size), False)
+
+        sampler = make_sampler(temperature, top_p, top_k, seed)
+        logits = np.empty(self.config.vocab_size, dtype=np.float32)
+        generated: list[int] = []
+        decoded, hit = "", False
+        with self._lock:
+            check(lib.ar_engine_generation_begin(self._handle, tokens.ctypes.data, tokens.size, logits.ctypes.data))
+            limit = min(int(max_new_tokens), self.options.max_sequence_length - int(tokens.size))
+            for step in range(limit):
+                token = sampler.select(logits)
+                if token == eos:
+                    break
+                generated.append(token)
+                decoded = decode(generated)
+                hit, text = _apply_stop_sequence(decoded, stops)
+                if hit:
+                    return GenerationResult(generated, text, int(tokens.size), True)
+                if step + 1 >= limit:
+                    break
+                check(lib.ar_engine_generation_step(self._handle, token, logits.ctypes.data))
+        return GenerationResult(generated, decoded, int(tokens.size), False)
+
+    def generation_begin(self, prompt_tokens: Sequence[int]) -> np.ndarray:
+        """Additive: prefill a prompt into the KV cache; returns the next-token logits (fp32 [vocab])."""
+        tokens = np.ascontiguousarray(np.asarray(prompt_tokens, dtype=np.int32).ravel())
+        logits = np.empty(self.config.vocab_size, dtype=np.float32)
+        with self._lock:
+            check(lib.ar_engine_generation_begin(self._handle, tokens.ctypes.data, tokens.size, logits.ctypes.data))
+        return logits
+
+    def generation_step(self, token: int) -> np.ndarray:
+        """Additive: feed one token at the next position; returns the next-token logits."""
+        logits = np.empty(self.config.vocab_size, dtype=np.float32)
+        with self._lock:
+            check(lib.ar_engine_generation_step(self._handle, int(token), logits.ctypes.data))
+        return logits
+
+    @property
+    def generation_position(self) -> int:
+        return int(lib.ar_engine_generation_position(self._handle))
 
     def prepare_scan(self, prompts: Sequence[StructuredPrompt], layer_begin: int = 0, layer_end: int = -1,
                      normalize_by_length: bool = False) -> "PreparedScan":

@@ -26,6 +26,18 @@ class EngineSettings:
 
 
 @dataclass(frozen=True, slots=True)
+class GenerationSettings:
+    """GenerationSettings (attnrank/data/classes.py:61-67 of the reference)."""
+
+    max_new_tokens: int = 128
+    temperature: float = 0.0
+    top_p: float = 0.9
+    top_k: int = 0
+    seed: int = DEFAULT_SEED
+    extra_stop_sequences: tuple[str, ...] = ()
+
+
+@dataclass(frozen=True, slots=True)
 class LayerScanSettings:
     layer_begin: int = 0
     layer_end: int | None = None

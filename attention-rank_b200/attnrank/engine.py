@@ -21,7 +21,8 @@ from typing import Any, Callable, Sequence
 from attnrank import core
 from attnrank.core import (AttentionProfile, AttnRankError, Engine, LlamaConfig, RuntimeOptions, StructuredPrompt,
                            TokenSpan)
-from attnrank.data.classes import DEFAULT_MIN_EDGE_RATIO, DEFAULT_SEED, EngineSettings, LayerScanSettings, ProfileSettings
+from attnrank.data.classes import (DEFAULT_MIN_EDGE_RATIO, DEFAULT_SEED, EngineSettings, GenerationSettings,
+                                   LayerScanSettings, ProfileSettings)
 
 MODEL_CONFIG_FILE = "config.json"
 WEIGHT_FILE_PATTERNS = ("*.safetensors",)
@@ -205,6 +206,18 @@ def rerank_documents(*, documents_by_relevance: Sequence[Any], position_order: S
 
 def rerank_with_profile(*, documents_by_relevance: Sequence[Any], profile: AttentionProfile) -> list[Any]:
     return rerank_documents(documents_by_relevance=documents_by_relevance, position_order=profile.position_order)
+
+
+def generate_from_prompt(*, engine: Engine, prompt: Any, settings: GenerationSettings = GenerationSettings(),
+                         decode: Callable[[list[int]], str] | None = None) -> core.GenerationResult:
+    """generate_from_prompt (reference engine.py:504-514) on a StructuredPrompt or token ids.
+
+    The reference adds its prompt builder's stop strings; this library has no tokenizer or chat
+    formatter, so only ``settings.extra_stop_sequences`` apply, and they need ``decode``."""
+    tokens = prompt.tokens if hasattr(prompt, "tokens") else prompt
+    return engine.generate(tokens, max_new_tokens=settings.max_new_tokens,
+                           stop_sequences=list(settings.extra_stop_sequences), temperature=settings.temperature,
+                           top_p=settings.top_p, top_k=settings.top_k, seed=settings.seed, decode=decode)
 
 
 def make_reranker(*, strategy: str, position_order: Sequence[int] | None = None, seed: int = DEFAULT_SEED,

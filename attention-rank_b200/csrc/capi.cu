@@ -11,6 +11,7 @@
 #include <vector>
 
 #include "../../include/attnrank_b200.h"
+#include "decode.h"
 #include "engine.h"
 #include "layer_kernels.h"
 #include "mass_plan.h"
@@ -23,6 +24,10 @@ struct ar_engine {
 
 struct ar_prepared_scan {
   std::unique_ptr<arb::PreparedScan> scan;
+};
+
+struct ar_sampler {
+  std::unique_ptr<arb::TokenSampler> sampler;
 };
 
 namespace {
@@ -343,6 +348,7 @@ int ar_engine_create(const ar_llama_config* config, const ar_runtime_options* op
     c.rope_theta = config->rope_theta;
     c.sliding_window = config->sliding_window;
     c.attention_bias = config->attention_bias != 0;
+    c.tie_word_embeddings = config->tie_word_embeddings != 0;
     arb::RuntimeOptions o;
     if (options != nullptr) {
       o.device_index = options->device_index;
@@ -497,6 +503,132 @@ int ar_engine_kernel_timing(ar_engine* engine, double* milliseconds, double* wor
 const char* ar_kernel_class_name(int kernel_class) { return arb::kernel_class_name(kernel_class); }
 
 int ar_kernel_class_is_tensor(int kernel_class) { return arb::kernel_class_is_tensor(kernel_class) ? 1 : 0; }
+
+// ---- generation ----------------------------------------------------------------------------
+
+namespace {
+arb::SamplerConfig sampler_config(const ar_sampler_config* config) {
+  arb::SamplerConfig c;
+  if (config != nullptr) {
+    c.temperature = config->temperature;
+    c.top_p = config->top_p;
+    c.top_k = config->top_k;
+    c.seed = config->seed;
+  }
+  return c;
+}
+}  // namespace
+
+int ar_engine_generate(ar_engine* engine, const int32_t* prompt, int prompt_count, int max_new_tokens,
+                       int eos_token_id, const ar_sampler_config* sampler, int32_t* tokens_out, int* token_count_out) {
+  return guarded([&] {
+    if (engine == nullptr || token_count_out == nullptr || (max_new_tokens > 0 && tokens_out == nullptr)) {
+      throw arb::Error("generate: null argument");
+    }
+    const std::vector<int32_t> tokens = engine->engine->generate(prompt, prompt_count, max_new_tokens, eos_token_id,
+                                                                 sampler_config(sampler));
+    std::copy(tokens.begin(), tokens.end(), tokens_out);
+    *token_count_out = static_cast<int>(tokens.size());
+    return AR_OK;
+  });
+}
+
+int ar_engine_generation_begin(ar_engine* engine, const int32_t* prompt, int prompt_count, float* logits_out) {
+  return guarded([&] {
+    if (engine == nullptr) throw arb::Error("generation_begin: null engine");
+    engine->engine->begin_generation(prompt, prompt_count);
+    if (logits_out != nullptr) engine->engine->read_logits(logits_out);
+    return AR_OK;
+  });
+}
+
+int ar_engine_generation_step(ar_engine* engine, int32_t token, float* logits_out) {
+  return guarded([&] {
+    if (engine == nullptr) throw arb::Error("generation_step: null engine");
+    engine->engine->decode_token(token);
+    if (logits_out != nullptr) {
+      engine->engine->read_logits(logits_out);
+    } else {
+      const int status = engine->engine->read_status();  // synchronises
+      if (status != 0) {
+        engine->engine->reset_status();
+        arb::Engine::raise_on_status(status);
+      }
+    }
+    return AR_OK;
+  });
+}
+
+int ar_engine_generation_position(ar_engine* engine) {
+  return engine ? engine->engine->generation_position() : -1;
+}
+
+int ar_sampler_create(const ar_sampler_config* config, ar_sampler** sampler) {
+  return guarded([&] {
+    if (config == nullptr || sampler == nullptr) throw arb::Error("sampler_create: null argument");
+    auto holder = std::make_unique<ar_sampler>();
+    holder->sampler = arb::make_token_sampler(sampler_config(config));
+    *sampler = holder.release();
+    return AR_OK;
+  });
+}
+
+int ar_sampler_select(ar_sampler* sampler, const float* logits, int count, int32_t* token_out) {
+  return guarded([&] {
+    if (sampler == nullptr || token_out == nullptr) throw arb::Error("sampler_select: null argument");
+    *token_out = sampler->sampler->select(logits, count);
+    return AR_OK;
+  });
+}
+
+void ar_sampler_destroy(ar_sampler* sampler) { delete sampler; }
+
+int ar_decode_gemv(const void* w, const void* x, int rows, int k, void* y, int f32_out, int dtype, void* stream) {
+  if (rows <= 0 || k <= 0 || k % 8 != 0) return fail(AR_ERR_INVALID, "decode_gemv: k must be a positive multiple of 8");
+  return cuda_result(arb::launch_decode_gemv(w, x, rows, k, y, f32_out != 0, dtype, as_stream(stream)),
+                     "decode_gemv");
+}
+
+int ar_decode_gate_up(const void* w, const void* x, int inter, int k, void* act, int dtype, void* stream) {
+  if (inter <= 0 || k <= 0 || k % 8 != 0) {
+    return fail(AR_ERR_INVALID, "decode_gate_up: k must be a positive multiple of 8");
+  }
+  return cuda_result(arb::launch_decode_gate_up(w, x, inter, k, act, dtype, as_stream(stream)), "decode_gate_up");
+}
+
+int ar_decode_attention(const void* q, const void* k_cache, const void* v_cache, int context, int position,
+                        int query_heads, int kv_heads, int head_dim, int sliding_window, void* out, int dtype,
+                        void* stream) {
+  return guarded([&] {
+    if (head_dim != 128 || kv_heads <= 0 || query_heads % kv_heads != 0 ||
+        query_heads / kv_heads > arb::kDecodeMaxGroup) {
+      throw arb::Error("decode_attention: head_dim must be 128 and query_heads a multiple (<= 16x) of kv_heads");
+    }
+    if (position < 0 || position >= context) throw arb::Error("decode_attention: position outside the cache");
+    cudaStream_t s = as_stream(stream);
+    StreamScratch scratch(s);
+    auto* state = static_cast<int32_t*>(scratch.get(2 * sizeof(int32_t)));
+    const int32_t host_state[2] = {0, position};
+    arb::check_cuda(cudaMemcpyAsync(state, host_state, sizeof(host_state), cudaMemcpyHostToDevice, s), "state upload");
+    arb::DecodeAttentionArgs args;
+    args.q = q;
+    args.k_cache = k_cache;
+    args.v_cache = v_cache;
+    args.context = context;
+    args.state = state;
+    args.query_heads = query_heads;
+    args.kv_heads = kv_heads;
+    args.head_dim = head_dim;
+    args.sliding_window = sliding_window;
+    args.partials = static_cast<float*>(scratch.get(static_cast<size_t>(query_heads) * arb::kDecodeSplits * head_dim * 4));
+    args.stats = static_cast<float*>(scratch.get(static_cast<size_t>(query_heads) * arb::kDecodeSplits * 2 * 4));
+    args.out = out;
+    args.dtype = dtype;
+    arb::check_cuda(arb::launch_decode_attention(args, s), "decode_attention");
+    arb::check_cuda(cudaStreamSynchronize(s), "decode_attention");  // host_state outlives the copy
+    return AR_OK;
+  });
+}
 
 int ar_profile_from_accumulated(const double* accumulated, int slots, int64_t sample_count, double* attention_out,
                                 int* position_order_out) {

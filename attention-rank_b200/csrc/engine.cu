@@ -296,6 +296,7 @@ Engine::Engine(const ModelConfig& config, const RuntimeOptions& options)
 
 Engine::~Engine() {
   if (stream_ != nullptr) cudaStreamSynchronize(stream_);
+  generation_.reset();
   timer_.reset();
   destroy_plans(plans_->by_shape);
   for (void* pointer : allocations_) cudaFree(pointer);
@@ -399,9 +400,19 @@ void Engine::load_tensor(const std::string& name, int dtype, const std::vector<i
     upload_f32(final_norm_, host, dtype, static_cast<size_t>(count), stream_);
     return;
   }
+  if (name == "lm_head.weight") {
+    // the output head (model.cu:140-146); only generation reads it
+    expect(V, H);
+    if (lm_head_ == nullptr) {
+      lm_head_ = device_alloc(static_cast<size_t>(V) * H * 2);
+      release_decode_graphs();  // captured steps hold the head's address
+    }
+    upload_matrix(lm_head_, host, dtype, static_cast<size_t>(count));
+    return;
+  }
   static const std::regex layer_pattern(R"(model\.layers\.(\d+)\.(.+))");
   std::smatch match;
-  if (!std::regex_match(name, match, layer_pattern)) return;  // lm_head, rotary buffers, ...: not used by probing
+  if (!std::regex_match(name, match, layer_pattern)) return;  // rotary buffers and the like: unused
   const int index = std::stoi(match[1].str());
   if (index < 0 || index >= c.num_hidden_layers) throw Error("tensor '" + name + "' names a layer out of range");
   const std::string suffix = match[2].str();
@@ -471,6 +482,13 @@ void Engine::init_synthetic(uint64_t seed, float standard_deviation) {
   };
   fill(embedding_, V * H, -1, kTensorEmbedding);
   ones(final_norm_, H, -1, kTensorFinalNorm);
+  if (!c.tie_word_embeddings) {
+    if (lm_head_ == nullptr) {
+      lm_head_ = device_alloc(static_cast<size_t>(V) * H * 2);
+      release_decode_graphs();
+    }
+    fill(lm_head_, V * H, -1, kTensorLmHead);
+  }
   for (int l = 0; l < c.num_hidden_layers; ++l) {
     LayerWeights& layer = layers_[l];
     auto* qkv = static_cast<uint16_t*>(layer.qkv);

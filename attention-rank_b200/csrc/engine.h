@@ -24,6 +24,8 @@
 #include <tuple>
 #include <vector>
 
+#include "sampler.h"
+
 namespace arb {
 
 class Error : public std::runtime_error {
@@ -45,6 +47,7 @@ struct ModelConfig {
   float rope_theta = 10000.0f;
   int sliding_window = 0;
   bool attention_bias = false;
+  bool tie_word_embeddings = false;  // the output head is the embedding table (no lm_head.weight)
 
   int head_dim() const { return hidden_size / num_attention_heads; }
   int kv_width() const { return num_key_value_heads * head_dim(); }
@@ -121,6 +124,29 @@ struct PreparedScan {
   ~PreparedScan();
 };
 
+// Buffers of generation, allocated at the first begin_generation. Device arrays are engine
+// allocations (freed with the engine); pinned host memory, events and graphs are freed here.
+struct GenerationState {
+  int context = 0;                // positions the KV cache holds (max_sequence_length)
+  size_t layer_elements = 0;      // Hkv * context * D: one layer's K (or V) cache
+  void* k_cache = nullptr;        // 16-bit [layers][Hkv][context][D]
+  void* v_cache = nullptr;
+  void* q = nullptr;              // 16-bit [Hq D]: the step's rotated query
+  float* partials = nullptr;      // fp32 [Hq][kDecodeSplits][D]
+  float* stats = nullptr;         // fp32 [Hq][kDecodeSplits][2]
+  float* logits = nullptr;        // fp32 [vocab]
+  int32_t* state = nullptr;       // device {token, position}
+  int32_t* meta = nullptr;        // device: prompt tokens | offsets [2] | attention tiles
+  size_t meta_capacity = 0;       // int32 elements of meta (and of the staging area behind the slots)
+  int32_t* staging = nullptr;     // pinned: state upload [2], two download slots [2][2], metadata
+  float* logits_host = nullptr;   // pinned [vocab], allocated by the first host read
+  cudaEvent_t slot_ready[2] = {nullptr, nullptr};
+  cudaGraphExec_t graphs[2] = {nullptr, nullptr};  // decode step: [0] logits only, [1] + greedy pick
+  bool warmed[2] = {false, false};  // the first step of each kind runs eagerly, later ones replay
+  int position = -1;              // position of the next token fed; -1: no prompt
+  ~GenerationState();
+};
+
 class Engine {
  public:
   Engine(const ModelConfig& config, const RuntimeOptions& options);
@@ -168,6 +194,29 @@ class Engine {
   void set_kernel_timing(bool enabled);
   void kernel_timing(double* milliseconds, double* work, int64_t* launches);
 
+  // ---- generation: CudaLlamaModel::generate (model.hpp:131-136, 156; model.cu:532-565) ----
+  // The KV cache ([layers][Hkv][context][D] 16-bit K and V, context = max_sequence_length) and
+  // the decode buffers are allocated at the first call.
+  // Prefills `prompt` through every layer (the probe's batched kernels, K/V stored into the
+  // cache) and computes the next-token logits (fp32 [vocab], on the device). The prompt must be
+  // non-empty, fit one forward (max_batch_tokens) and leave room in the context.
+  void begin_generation(const int32_t* prompt, int count);
+  // Feeds `token` at the next position through one decode step: every layer on one token, the
+  // KV cache extended by one row, new logits. Replays a captured CUDA graph of the step.
+  void decode_token(int32_t token);
+  // Copies the current logits to host memory (fp32 [vocab]); synchronises.
+  void read_logits(float* host);
+  // The generate loop (model.cu:537-562 without the text/stop-sequence part, which needs a
+  // tokenizer): select a token from the logits, stop at eos_token_id (not returned), else keep
+  // it and decode it, up to max_new_tokens or the end of the context. temperature <= 0 selects
+  // greedily on the device (the first maximum, GreedySampler::select) with one step in flight;
+  // otherwise NucleusTokenSampler selects on the host.
+  std::vector<int32_t> generate(const int32_t* prompt, int count, int max_new_tokens, int eos_token_id,
+                                const SamplerConfig& sampler);
+  // Position the next decoded token takes (prompt length + tokens fed so far); -1 before a prompt.
+  int generation_position() const;
+  int generation_context() const { return options_.max_sequence_length; }
+
   // Raw access for the kernel-level tests: the device buffers of the last batch.
   const void* qkv_buffer() const { return qkv_; }
   int qkv_capacity_rows() const { return capacity_tokens_; }
@@ -175,6 +224,13 @@ class Engine {
   void synchronize();
 
  private:
+  void ensure_generation();
+  void prefill_generation(int tokens);  // metadata already uploaded
+  void launch_decode_step(bool greedy);  // the step's kernels, in order, on stream_
+  void run_decode_step(bool greedy);     // eager on first use, then a CUDA graph replay
+  void release_decode_graphs();
+  const void* output_head() const;
+
   struct LayerWeights {
     void* qkv = nullptr;     // 16-bit [(Hq + 2 Hkv) D, H]
     float* qkv_bias = nullptr;  // fp32 [(Hq + 2 Hkv) D] or null
@@ -227,6 +283,8 @@ class Engine {
 
   std::vector<void*> allocations_;
   void* embedding_ = nullptr;  // 16-bit [V, H]
+  void* lm_head_ = nullptr;    // 16-bit [V, H] when loaded or synthesised; else the embedding is the head
+  std::unique_ptr<GenerationState> generation_;
   std::vector<LayerWeights> layers_;
   float* final_norm_ = nullptr;
   std::vector<std::vector<bool>> loaded_;  // per layer, per tensor kind

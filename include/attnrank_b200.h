@@ -146,6 +146,7 @@ typedef struct {
   float rope_theta;
   int sliding_window;    /* 0 = none (kernels.cu:125-126) */
   int attention_bias;    /* 1 when q/k/v projections have biases (Qwen2) */
+  int tie_word_embeddings; /* 1: the output head is the embedding (model.cu:140-146); generation only */
 } ar_llama_config;
 
 /* LlamaRuntimeOptions (model.hpp:138-142) plus the batching limits of this build. */
@@ -173,7 +174,7 @@ int ar_engine_create(const ar_llama_config* config, const ar_runtime_options* op
 void ar_engine_destroy(ar_engine* engine);
 
 /* Uploads one checkpoint tensor by its Hugging Face name (DeviceWeights, model.cu:113-174).
- * Unknown names (lm_head, rotary buffers) are accepted and ignored. */
+ * lm_head.weight is kept for generation; unknown names (rotary buffers) are accepted and ignored. */
 int ar_engine_load_tensor(ar_engine* engine, const char* name, int dtype, const int64_t* shape, int rank,
                           const void* host_data);
 
@@ -234,6 +235,61 @@ int ar_engine_set_kernel_timing(ar_engine* engine, int enabled);
 int ar_engine_kernel_timing(ar_engine* engine, double* milliseconds, double* work, int64_t* launches);
 const char* ar_kernel_class_name(int kernel_class);
 int ar_kernel_class_is_tensor(int kernel_class);
+
+/* ------------------------------------------------------------------------------------------
+ * Generation: CudaLlamaModel::generate (include/attnrank/model.hpp:118-136, :156;
+ * attnrank/src/model.cu:532-565), the answering step after reranking, and the samplers of
+ * model.hpp:88-116 (attnrank/src/model.cpp:70-127).
+ * ------------------------------------------------------------------------------------------ */
+
+/* NucleusSamplerConfig (model.hpp:99-104). temperature <= 0 selects greedily (make_sampler,
+ * model.cpp:124-127): the first index of the largest logit. */
+typedef struct {
+  float temperature;
+  float top_p;
+  int top_k;       /* 0 = every token is a candidate */
+  uint64_t seed;
+} ar_sampler_config;
+
+/* The generate loop for one prompt (GenerationRequest / GenerationResult, model.hpp:118-129):
+ * prefill, then select -> stop at eos_token_id (not returned) -> decode, until max_new_tokens or
+ * the end of the context (max_sequence_length). Stop strings need a tokenizer and stay with the
+ * caller (ar_engine_generation_begin/_step hand out the logits step by step). tokens_out has
+ * room for max_new_tokens ids; *token_count_out receives the count. The prompt must fit one
+ * forward (max_batch_tokens). */
+int ar_engine_generate(ar_engine* engine, const int32_t* prompt, int prompt_count, int max_new_tokens,
+                       int eos_token_id, const ar_sampler_config* sampler, int32_t* tokens_out, int* token_count_out);
+
+/* Step-wise generation. _begin prefills the prompt (restarting the position at its length);
+ * _step feeds one token at the next position. Both leave the next-token logits on the device
+ * and copy them to logits_out (host fp32 [vocab]) when it is not NULL. */
+int ar_engine_generation_begin(ar_engine* engine, const int32_t* prompt, int prompt_count, float* logits_out);
+int ar_engine_generation_step(ar_engine* engine, int32_t token, float* logits_out);
+/* Position of the next token fed (prompt length + steps), -1 before a prompt. */
+int ar_engine_generation_position(ar_engine* engine);
+
+/* Host samplers: GreedySampler / NucleusSampler (model.cpp:70-127). The same logits and
+ * config give the reference's token ids; a nucleus sampler's draws advance its own
+ * std::mt19937_64 seeded with config->seed. */
+typedef struct ar_sampler ar_sampler;
+int ar_sampler_create(const ar_sampler_config* config, ar_sampler** sampler);
+int ar_sampler_select(ar_sampler* sampler, const float* logits, int count, int32_t* token_out);
+void ar_sampler_destroy(ar_sampler* sampler);
+
+/* Decode kernels (device pointers, asynchronous on `stream`); the single-token forms of the
+ * reference's cuBLAS projections at m = 1 (LlamaForwardPass::matmul, model.cu:353-365).
+ * y[n] = w[n, :] . x for n < rows: w 16-bit [rows, k] row-major, x 16-bit [k], k % 8 == 0;
+ * y 16-bit, or fp32 when f32_out (the lm_head logits, model.cu:341-350). */
+int ar_decode_gemv(const void* w, const void* x, int rows, int k, void* y, int f32_out, int dtype, void* stream);
+/* act[j] = silu(g_j) * u_j over the fused gate|up matrix w [2 inter, k] (model.cu:410-415). */
+int ar_decode_gate_up(const void* w, const void* x, int inter, int k, void* act, int dtype, void* stream);
+/* Attention of one query token at `position` over a KV cache (keys 0 .. position, or the last
+ * sliding_window of them): q 16-bit [Hq, 128]; k_cache, v_cache 16-bit [Hkv, context, 128];
+ * out 16-bit [Hq, 128]. The decode form of LlamaForwardPass::attend (model.cu:426-480).
+ * Allocates its scratch with cudaMallocAsync on `stream` and synchronises the stream. */
+int ar_decode_attention(const void* q, const void* k_cache, const void* v_cache, int context, int position,
+                        int query_heads, int kv_heads, int head_dim, int sliding_window, void* out, int dtype,
+                        void* stream);
 
 /* ------------------------------------------------------------------------------------------
  * Profile accumulator and basin pick (host functions of attnrank/src/attnrank.cpp).

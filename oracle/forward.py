@@ -222,6 +222,47 @@ class OracleModel:
             rows.append(np.where(sums > 0, r / np.where(sums > 0, sums, 1.0), r))
         return rows, raw_rows
 
+    def next_token_logits(self, tokens: np.ndarray, tied: bool = True) -> np.ndarray:
+        """The logits generation reads after a prompt (CudaLlamaModel::generate, model.cu:532-565):
+        every layer over the whole sequence (the reference's chunked prefill and one-token decode
+        steps against its KV cache compute this same causal forward), the final RMSNorm
+        (model.norm.weight) and the output head on the last row (read_logits, model.cu:341-350):
+        the embedding when tied (tie_word_embeddings), else lm_head.weight. fp32 [vocab]."""
+        s = self.shape
+        ids = np.asarray(tokens, dtype=np.int32)
+        T = ids.size
+        cos_np, sin_np = rope_tables(T, s.head_dim, s.theta)
+        cos, sin = torch.from_numpy(cos_np), torch.from_numpy(sin_np)
+        h = torch.from_numpy(W.gather_rows(ids, s.hidden, self.seed, -1, W.EMBEDDING, self.std))
+        scale = 1.0 / math.sqrt(float(s.head_dim))
+        group = s.heads // s.kv_heads
+        key = torch.arange(T)[None, :]
+        query = torch.arange(T)[:, None]
+        visible = key <= query
+        if s.window > 0:
+            visible &= key >= query + 1 - s.window
+        for layer in range(s.layers):
+            w = self.layer_weights(layer)
+            x = rms_norm(h, w["input_norm"], s.eps)
+            q, k, v = self._linear(x, w["q"]), self._linear(x, w["k"]), self._linear(x, w["v"])
+            if s.bias:
+                q, k, v = q + w["q_bias"], k + w["k_bias"], v + w["v_bias"]
+            q = apply_rope(q.view(T, s.heads, s.head_dim), cos, sin)
+            k = apply_rope(k.view(T, s.kv_heads, s.head_dim), cos, sin)
+            v = v.view(T, s.kv_heads, s.head_dim)
+            kq = k.repeat_interleave(group, dim=1)
+            vq = v.repeat_interleave(group, dim=1)
+            scores = torch.einsum("qhd,khd->hqk", q, kq) * scale
+            probs = torch.softmax(scores.masked_fill(~visible[None], float("-inf")), dim=-1)
+            attn = torch.einsum("hqk,khd->qhd", probs, vq).reshape(T, s.heads * s.head_dim)
+            h = h + self._linear(attn, w["o"])
+            x = rms_norm(h, w["post_norm"], s.eps)
+            h = h + self._linear(silu_multiply(self._linear(x, w["gate"]), self._linear(x, w["up"])), w["down"])
+        final = torch.from_numpy(W.f32(s.hidden, self.seed, -1, W.FINAL_NORM, 0.0, 1.0))
+        last = rms_norm(h[-1:], final, s.eps)
+        head = self._matrix(s.vocab, s.hidden, -1, W.EMBEDDING if tied else W.LM_HEAD)
+        return self._linear(last, head)[0].numpy().astype(np.float32)
+
     def measure_attention(self, prompt: Prompt, layer_begin: int, layer_end: int,
                           normalize_by_length: bool = False) -> np.ndarray:
         """CudaLlamaModel::measure_attention (model.cu:567-591)."""

@@ -12,8 +12,9 @@
 //     AttentionLayerScanner::scan (attnrank.cpp:364-375) + select_shallowest_basin_layer
 //     (attnrank.cpp:257-265), fed token-id prompts through an IPromptBuilder (prompt.hpp:25-30)
 //     that returns the given StructuredPrompt for each sample;
-//   * the reference's host functions (profile, basin statistics, position order), which run
-//     without a GPU and produce the golden fixtures under tests/golden/.
+//   * its generate (model.cu:532-565), the answering step, with the reference's samplers;
+//   * the reference's host functions (profile, basin statistics, position order, the samplers of
+//     model.cpp:70-127), which run without a GPU and produce the golden fixtures under tests/golden/.
 #include <chrono>
 #include <cstdint>
 #include <cstring>
@@ -307,7 +308,60 @@ int ref_scan(void* handle, const ref_prompt* prompts, int prompt_count, int span
   }
 }
 
+// CudaLlamaModel::generate (model.cu:532-565) with the sampler of make_sampler (model.cpp:124-127).
+// tokens_out has room for max_new_tokens ids; seconds_out: wall time of the generate call.
+int ref_generate(void* handle, const int32_t* prompt, int prompt_count, int max_new_tokens, float temperature,
+                 float top_p, int top_k, uint64_t seed, int32_t* tokens_out, int* token_count_out,
+                 double* seconds_out) {
+  try {
+    auto* holder = static_cast<Holder*>(handle);
+    GenerationRequest request;
+    request.prompt_tokens.assign(prompt, prompt + prompt_count);
+    request.max_new_tokens = max_new_tokens;
+    NucleusSamplerConfig config;
+    config.temperature = temperature;
+    config.top_p = top_p;
+    config.top_k = top_k;
+    config.seed = seed;
+    const std::unique_ptr<ISampler> sampler = make_sampler(config);
+    cudaDeviceSynchronize();
+    const auto start = std::chrono::steady_clock::now();
+    const GenerationResult result = holder->shared->generate(request, *sampler);
+    cudaDeviceSynchronize();
+    const auto stop = std::chrono::steady_clock::now();
+    for (size_t i = 0; i < result.generated_tokens.size(); ++i) tokens_out[i] = result.generated_tokens[i];
+    *token_count_out = static_cast<int>(result.generated_tokens.size());
+    if (seconds_out) *seconds_out = std::chrono::duration<double>(stop - start).count();
+    return 0;
+  } catch (const std::exception& error) {
+    g_error = error.what();
+    return 1;
+  }
+}
+
 // ---- host-only entry points (no GPU) --------------------------------------------------------
+
+// make_sampler (model.cpp:124-127) + select (model.cpp:70-122): `draws` selections by one sampler
+// (its generator advances between them), draw d over logits[d * count, (d + 1) * count).
+int ref_sample(float temperature, float top_p, int top_k, uint64_t seed, const float* logits, int count, int draws,
+               int* out) {
+  try {
+    NucleusSamplerConfig config;
+    config.temperature = temperature;
+    config.top_p = top_p;
+    config.top_k = top_k;
+    config.seed = seed;
+    const std::unique_ptr<ISampler> sampler = make_sampler(config);
+    for (int d = 0; d < draws; ++d) {
+      const std::vector<float> row(logits + static_cast<size_t>(d) * count, logits + static_cast<size_t>(d + 1) * count);
+      out[d] = sampler->select(row);
+    }
+    return 0;
+  } catch (const std::exception& error) {
+    g_error = error.what();
+    return 1;
+  }
+}
 
 int ref_from_accumulated(const double* accumulated, int slots, int64_t sample_count, double* attention_out,
                          int* order_out) {

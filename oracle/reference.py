@@ -52,6 +52,8 @@ def load_or_none():
     lib.ref_basin_statistics.argtypes = [P, I, D, P]
     lib.ref_select_shallowest.argtypes = [P, P, I, I, D]
     lib.ref_resolve_position_order.argtypes = [P, I, I, P]
+    lib.ref_generate.argtypes = [P, P, I, I, ctypes.c_float, ctypes.c_float, I, ctypes.c_uint64, P, P, P]
+    lib.ref_sample.argtypes = [ctypes.c_float, ctypes.c_float, I, ctypes.c_uint64, P, I, I, P]
     _lib = lib
     return lib
 
@@ -135,6 +137,19 @@ class ReferenceModel:
         return ScanResult(attention[:n], order[:n], layer_index[:n], selected.value, seconds.value)
 
 
+    def generate(self, prompt_tokens, max_new_tokens: int, temperature: float = 0.0, top_p: float = 0.9,
+                 top_k: int = 0, seed: int = 1234) -> tuple[list[int], float]:
+        """CudaLlamaModel::generate with make_sampler's sampler: (generated ids, seconds)."""
+        lib = _require()
+        tokens = np.ascontiguousarray(np.asarray(prompt_tokens, dtype=np.int32))
+        out = np.zeros(max(max_new_tokens, 1), dtype=np.int32)
+        count, seconds = ctypes.c_int(), ctypes.c_double()
+        if lib.ref_generate(self.handle, tokens.ctypes.data, tokens.size, max_new_tokens, temperature, top_p, top_k,
+                            seed, out.ctypes.data, ctypes.byref(count), ctypes.byref(seconds)) != 0:
+            raise RuntimeError(lib.ref_last_error().decode())
+        return [int(t) for t in out[:count.value]], seconds.value
+
+
 @dataclass
 class ScanResult:
     attention: np.ndarray
@@ -175,4 +190,17 @@ def resolve_position_order(preferred: Sequence[int], count: int) -> list[int]:
     pref = np.ascontiguousarray(np.asarray(preferred, dtype=np.int32))
     out = np.zeros(count, dtype=np.int32)
     lib.ref_resolve_position_order(pref.ctypes.data if pref.size else None, pref.size, count, out.ctypes.data)
+    return [int(v) for v in out]
+
+
+def sample(logits_rows: np.ndarray, temperature: float, top_p: float, top_k: int, seed: int) -> list[int]:
+    """The reference's make_sampler(config)->select over each row of logits_rows, one sampler."""
+    lib = _require()
+    rows = np.ascontiguousarray(np.asarray(logits_rows, dtype=np.float32))
+    if rows.ndim == 1:
+        rows = rows[None, :]
+    out = np.zeros(rows.shape[0], dtype=np.int32)
+    if lib.ref_sample(temperature, top_p, top_k, seed, rows.ctypes.data, rows.shape[1], rows.shape[0],
+                      out.ctypes.data) != 0:
+        raise RuntimeError(lib.ref_last_error().decode())
     return [int(v) for v in out]

@@ -1,0 +1,341 @@
+"""Generation on the B200 engine (CudaLlamaModel::generate, attnrank/src/model.cu:532-565) and the
+decode kernels it runs, through the C ABI.
+
+Kernel parity (same 16-bit inputs, float64 torch as the checker):
+  * ar_decode_gemv / ar_decode_gate_up: 16-bit outputs within 2 ulp (+ a floor of 1e-6 x sum|w x|
+    for fp32 accumulation order); fp32 outputs (logits) within rel 1e-5 + the same floor;
+  * ar_decode_attention: one query over a KV cache at several positions, sliding windows and GQA
+    groups; 16-bit outputs within 2 ulp.
+Engine parity (small Llama/Qwen-shaped model, seeded synthetic weights):
+  * next-token logits after the prefill and after every decode step (teacher-forced) against the
+    fp32 CPU oracle's full-sequence forward (oracle/forward.py:next_token_logits):
+    max |d| <= LOGIT_TOL * max |logit| (16-bit activations against fp32);
+  * decode-step logits against a fresh prefill of the same sequence, same bound;
+  * greedy generate == the first maximum of the step-wise logits; nucleus generate == the host
+    sampler over them (bit-exact: the same kernels on the same inputs);
+  * eos / max_new_tokens / context-window stops and the reference's error messages;
+  * greedy tokens against the reference's own generate (oracle/_ref, when built).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+TWO_ULP = {"bf16": 2.0 ** -7, "fp16": 2.0 ** -10}
+LOGIT_TOL = {"fp16": 1e-2, "bf16": 4e-2}
+
+
+def _native():
+    from attnrank import _native
+    return _native
+
+
+def _code(dtype):
+    return _native().DTYPE_F16 if dtype == "fp16" else _native().DTYPE_BF16
+
+
+def _torch_dtype(dtype):
+    import torch
+    return torch.float16 if dtype == "fp16" else torch.bfloat16
+
+
+def _p(tensor):
+    return ctypes.c_void_p(tensor.data_ptr())
+
+
+def _stream():
+    import torch
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _check(status):
+    _native().check(status)
+
+
+def assert_within(actual, expected, rel, floor, what):
+    actual = np.asarray(actual, dtype=np.float64)
+    expected = np.asarray(expected, dtype=np.float64)
+    error = np.abs(actual - expected)
+    bound = rel * np.abs(expected) + floor
+    worst = int(np.argmax(error - bound))
+    assert np.all(error <= bound), (f"{what}: index {worst} got {actual.flat[worst]} want {expected.flat[worst]} "
+                                    f"(bound {np.broadcast_to(bound, error.shape).flat[worst]})")
+
+
+# ---- kernels -------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+@pytest.mark.parametrize("rows,k,f32_out", [(1, 512, False), (7, 1024, False), (4608, 3584, False),
+                                            (3584, 18944, False), (3584, 3584, True), (152064, 3584, True)])
+def test_decode_gemv(cuda, rows, k, f32_out, dtype):
+    import torch
+    g = torch.Generator(device=cuda).manual_seed(rows + k)
+    w = (torch.randn(rows, k, device=cuda, generator=g) * 0.02).to(_torch_dtype(dtype))
+    x = torch.randn(k, device=cuda, generator=g).to(_torch_dtype(dtype))
+    y = torch.empty(rows, device=cuda, dtype=torch.float32 if f32_out else _torch_dtype(dtype))
+    _check(_native().lib.ar_decode_gemv(_p(w), _p(x), rows, k, _p(y), int(f32_out), _code(dtype), _stream()))
+    torch.cuda.synchronize()
+    want = (w.double() @ x.double()).cpu().numpy()
+    floor = 1e-6 * (w.double().abs() @ x.double().abs()).cpu().numpy()
+    got = y.double().cpu().numpy()
+    assert_within(got, want, 1e-5 if f32_out else TWO_ULP[dtype], floor, "gemv")
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+@pytest.mark.parametrize("inter,k", [(1, 512), (37, 1024), (18944, 3584)])
+def test_decode_gate_up(cuda, inter, k, dtype):
+    import torch
+    g = torch.Generator(device=cuda).manual_seed(inter * 7 + k)
+    w = (torch.randn(2 * inter, k, device=cuda, generator=g) * 0.05).to(_torch_dtype(dtype))
+    x = torch.randn(k, device=cuda, generator=g).to(_torch_dtype(dtype))
+    act = torch.empty(inter, device=cuda, dtype=_torch_dtype(dtype))
+    _check(_native().lib.ar_decode_gate_up(_p(w), _p(x), inter, k, _p(act), _code(dtype), _stream()))
+    torch.cuda.synchronize()
+    both = (w.double() @ x.double()).to(_torch_dtype(dtype)).double().cpu().numpy()  # the 16-bit projections
+    g, u = both[:inter], both[inter:]
+    sigmoid = 1.0 / (1.0 + np.exp(-g))
+    want = g * sigmoid * u
+    # a projection whose fp32 sum sits at a 16-bit rounding boundary may round the other way: its
+    # 2-ulp change, carried through d(silu(g) u) = u silu'(g) dg + silu(g) du, widens the bound
+    derivative = sigmoid * (1.0 + g * (1.0 - sigmoid))
+    floor = TWO_ULP[dtype] * (np.abs(u * derivative * g) + np.abs(g * sigmoid * u)) + 1e-6
+    assert_within(act.double().cpu().numpy(), want, TWO_ULP[dtype], floor, "gate_up")
+
+
+def _attention_reference(q, k_cache, v_cache, position, window, group):
+    import torch
+    first = max(0, position + 1 - window) if window > 0 else 0
+    keys = k_cache[:, first:position + 1].double()    # [Hkv, n, D]
+    values = v_cache[:, first:position + 1].double()
+    hq = q.shape[0]
+    out = torch.empty(hq, q.shape[1], dtype=torch.float64, device=q.device)
+    for h in range(hq):
+        scores = keys[h // group] @ q[h].double() / np.sqrt(q.shape[1])
+        probs = torch.softmax(scores, dim=0)
+        out[h] = probs @ values[h // group]
+    return out
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+@pytest.mark.parametrize("heads,kv_heads", [(28, 4), (32, 8), (4, 4), (16, 1)])
+@pytest.mark.parametrize("window", [0, 100])
+def test_decode_attention(cuda, heads, kv_heads, window, dtype):
+    import torch
+    context = 4096
+    g = torch.Generator(device=cuda).manual_seed(heads * 131 + kv_heads + window)
+    k_cache = torch.randn(kv_heads, context, 128, device=cuda, generator=g).to(_torch_dtype(dtype))
+    v_cache = torch.randn(kv_heads, context, 128, device=cuda, generator=g).to(_torch_dtype(dtype))
+    q = (torch.randn(heads, 128, device=cuda, generator=g) * 2.0).to(_torch_dtype(dtype))
+    out = torch.empty(heads, 128, device=cuda, dtype=_torch_dtype(dtype))
+    for position in [0, 1, 31, 63, 64, 65, 500, 2047, context - 1]:
+        _check(_native().lib.ar_decode_attention(_p(q), _p(k_cache), _p(v_cache), context, position, heads, kv_heads,
+                                                 128, window, _p(out), _code(dtype), _stream()))
+        want = _attention_reference(q, k_cache, v_cache, position, window, heads // kv_heads).cpu().numpy()
+        assert_within(out.double().cpu().numpy(), want, TWO_ULP[dtype], 1e-5, f"attention at {position}")
+
+
+def test_decode_attention_rejects_bad_arguments(cuda):
+    import torch
+    import attnrank as ar
+    k = torch.zeros(2, 64, 128, device=cuda, dtype=torch.float16)
+    q = torch.zeros(4, 128, device=cuda, dtype=torch.float16)
+    lib = _native().lib
+    with pytest.raises(ar.AttnRankError, match="position outside the cache"):
+        _check(lib.ar_decode_attention(_p(q), _p(k), _p(k), 64, 64, 4, 2, 128, 0, _p(q), _code("fp16"), _stream()))
+    with pytest.raises(ar.AttnRankError, match="head_dim must be 128"):
+        _check(lib.ar_decode_attention(_p(q), _p(k), _p(k), 64, 3, 4, 2, 64, 0, _p(q), _code("fp16"), _stream()))
+
+
+# ---- engine --------------------------------------------------------------------------------
+
+def small_config(bias=True, tie=True, layers=2, window=0):
+    import attnrank as ar
+    return ar.LlamaConfig(hidden_size=512, intermediate_size=1024, num_hidden_layers=layers, num_attention_heads=4,
+                          num_key_value_heads=2, vocab_size=2000, max_position_embeddings=4096, rms_norm_eps=1e-6,
+                          rope_theta=1e6, sliding_window=window, tie_word_embeddings=tie, attention_bias=bias)
+
+
+def oracle_for(config, dtype):
+    from oracle import forward as F
+    shape = F.Shape(hidden=config.hidden_size, intermediate=config.intermediate_size, layers=config.num_hidden_layers,
+                    heads=config.num_attention_heads, kv_heads=config.num_key_value_heads, vocab=config.vocab_size,
+                    eps=config.rms_norm_eps, theta=config.rope_theta, window=config.sliding_window,
+                    bias=config.attention_bias)
+    return F.OracleModel(shape, seed=0, gemm_inputs=dtype)
+
+
+def make_engine(config, dtype="fp16", context=1024):
+    import attnrank as ar
+    return ar.Engine.synthetic(config, seed=0, options=ar.RuntimeOptions(activation_dtype=dtype,
+                                                                         max_sequence_length=context))
+
+
+def prompt_tokens(count, vocab, seed=1):
+    return np.random.default_rng(seed).integers(0, vocab, size=count).astype(np.int32)
+
+
+def assert_logits_close(got, want, dtype, what):
+    error = np.abs(np.asarray(got, np.float64) - np.asarray(want, np.float64)).max()
+    scale = np.abs(want).max()
+    assert error <= LOGIT_TOL[dtype] * scale, f"{what}: max |d| {error:.3e} > {LOGIT_TOL[dtype]} x {scale:.3e}"
+
+
+@pytest.mark.parametrize("bias,tie,dtype,window", [(True, True, "fp16", 0), (False, False, "fp16", 0),
+                                                   (True, True, "bf16", 0), (True, False, "fp16", 160)])
+def test_generation_logits_match_oracle(cuda, bias, tie, dtype, window):
+    config = small_config(bias, tie, window=window)
+    engine = make_engine(config, dtype)
+    oracle = oracle_for(config, dtype)
+    prompt = prompt_tokens(300, config.vocab_size)
+    logits = engine.generation_begin(prompt)
+    assert engine.generation_position == prompt.size
+    assert_logits_close(logits, oracle.next_token_logits(prompt, tied=tie), dtype, "prefill")
+    sequence = list(prompt)
+    for step in range(6):
+        token = int(np.argmax(logits))
+        sequence.append(token)
+        logits = engine.generation_step(token)
+        assert engine.generation_position == prompt.size + step + 1
+        assert_logits_close(logits, oracle.next_token_logits(np.array(sequence), tied=tie), dtype, f"step {step}")
+    engine.close()
+
+
+def test_decode_steps_match_a_fresh_prefill(cuda):
+    config = small_config(layers=3)
+    engine = make_engine(config)
+    prompt = prompt_tokens(200, config.vocab_size, seed=4)
+    logits = engine.generation_begin(prompt)
+    sequence = list(prompt)
+    for _ in range(10):
+        token = int(np.argmax(logits))
+        sequence.append(token)
+        logits = engine.generation_step(token)
+    again = engine.generation_begin(np.array(sequence))
+    assert_logits_close(logits, again, "fp16", "decode vs prefill")
+    engine.close()
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+def test_greedy_generate_follows_the_step_logits(cuda, dtype):
+    config = small_config()
+    engine = make_engine(config, dtype)
+    engine.config.eos_token_id = -1
+    prompt = prompt_tokens(150, config.vocab_size, seed=2)
+    result = engine.generate(prompt, max_new_tokens=24)
+    assert result.prompt_token_count == prompt.size and not result.hit_stop_sequence
+    assert len(result.generated_tokens) == 24
+    logits = engine.generation_begin(prompt)
+    expected = []
+    for _ in range(24):
+        token = int(np.argmax(logits))  # the first maximum, like std::max_element
+        expected.append(token)
+        logits = engine.generation_step(token)
+    assert result.generated_tokens == expected
+    engine.close()
+
+
+def test_nucleus_generate_follows_the_host_sampler(cuda):
+    import attnrank as ar
+    config = small_config()
+    engine = make_engine(config)
+    engine.config.eos_token_id = -1
+    prompt = prompt_tokens(120, config.vocab_size, seed=5)
+    result = engine.generate(prompt, max_new_tokens=16, temperature=0.8, top_p=0.9, top_k=50, seed=99)
+    sampler = ar.make_sampler(0.8, 0.9, 50, 99)
+    logits = engine.generation_begin(prompt)
+    expected = []
+    for step in range(16):
+        token = sampler.select(logits)
+        expected.append(token)
+        if step + 1 < 16:
+            logits = engine.generation_step(token)
+    assert result.generated_tokens == expected
+    engine.close()
+
+
+def test_generation_stops(cuda):
+    config = small_config()
+    engine = make_engine(config, context=320)
+    engine.config.eos_token_id = -1
+    prompt = prompt_tokens(300, config.vocab_size, seed=6)
+    # the context window bounds the new tokens: 320 - 300
+    tokens = engine.generate(prompt, max_new_tokens=50).generated_tokens
+    assert len(tokens) == 20
+    assert engine.generate(prompt, max_new_tokens=0).generated_tokens == []
+    assert engine.generate(prompt, max_new_tokens=1).generated_tokens == tokens[:1]
+    # eos ends generation without being returned
+    stop = next(i for i in range(1, 20) if tokens[i] not in tokens[:i])
+    engine.config.eos_token_id = tokens[stop]
+    assert engine.generate(prompt, max_new_tokens=50).generated_tokens == tokens[:stop]
+    engine.config.eos_token_id = tokens[0]
+    assert engine.generate(prompt, max_new_tokens=50).generated_tokens == []
+    engine.close()
+
+
+def test_generation_stop_strings_use_the_decoder(cuda):
+    config = small_config()
+    engine = make_engine(config)
+    engine.config.eos_token_id = -1
+    prompt = prompt_tokens(100, config.vocab_size, seed=7)
+    plain = engine.generate(prompt, max_new_tokens=12).generated_tokens
+    decode = lambda ids: " ".join(f"t{t}" for t in ids)  # noqa: E731
+    stop = f"t{plain[5]}"
+    # the reference tests the decoded text after every token (model.cu:546-548)
+    cut = next(i for i in range(12) if stop in decode(plain[:i + 1]))
+    result = engine.generate(prompt, max_new_tokens=12, stop_sequences=["", stop], decode=decode)
+    assert result.hit_stop_sequence
+    assert result.generated_tokens == plain[:cut + 1]
+    text = decode(plain[:cut + 1])
+    assert result.text == text[:text.find(stop)]
+    engine.close()
+
+
+def test_generation_errors(cuda):
+    import attnrank as ar
+    config = small_config()
+    engine = make_engine(config, context=256)
+    with pytest.raises(ar.AttnRankError, match="decode_token needs a prompt"):
+        engine.generation_step(5)
+    with pytest.raises(ar.AttnRankError, match="non-empty prompt"):
+        engine.generate([], max_new_tokens=4)
+    with pytest.raises(ar.AttnRankError, match="exceeds the 256 token window"):
+        engine.generate(prompt_tokens(256, config.vocab_size), max_new_tokens=4)
+    engine.generation_begin(prompt_tokens(10, config.vocab_size))
+    with pytest.raises(ar.AttnRankError, match="out of range"):
+        engine.generation_step(config.vocab_size)
+    with pytest.raises(ar.AttnRankError, match="stop_sequences need a decode"):
+        engine.generate(prompt_tokens(10, config.vocab_size), stop_sequences=["x"])
+    # the engine still works after the errors
+    assert len(engine.generate(prompt_tokens(10, config.vocab_size), max_new_tokens=3).generated_tokens) <= 3
+    untied = make_engine(small_config(tie=False))
+    untied.generate(prompt_tokens(10, config.vocab_size), max_new_tokens=2)
+    engine.close()
+    untied.close()
+
+
+def test_greedy_tokens_match_the_reference_generate(cuda, reference_lib):
+    """The reference's own CudaLlamaModel::generate on this GPU (oracle/_ref), greedy, tied head."""
+    if reference_lib is None:
+        pytest.skip("oracle/_ref is not built")
+    from oracle import reference
+    config = small_config(bias=True, tie=True, layers=3)
+    engine = make_engine(config, context=1024)
+    ref = reference.ReferenceModel(config, seed=0, max_sequence_length=1024)
+    oracle = oracle_for(config, "fp16")
+    for seed in (11, 12):
+        prompt = prompt_tokens(260, config.vocab_size, seed=seed)
+        want, _ = ref.generate(prompt, max_new_tokens=16)
+        got = engine.generate(prompt, max_new_tokens=16).generated_tokens
+        if got != want:
+            # only a near-tie of the top two logits may separate them: check the first difference
+            step = next(i for i in range(min(len(got), len(want))) if got[i] != want[i])
+            logits = oracle.next_token_logits(np.concatenate([prompt, np.array(want[:step], np.int32)]))
+            top = np.sort(logits)[-2:]
+            assert top[1] - top[0] <= LOGIT_TOL["fp16"] * np.abs(logits).max(), (
+                f"tokens differ at step {step} with a clear top-1 margin: got {got}, want {want}")
+    ref.close()
+    engine.close()
