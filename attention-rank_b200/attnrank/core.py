@@ -686,6 +686,11 @@ class Engine:
     def generation_position(self) -> int:
         return int(lib.ar_engine_generation_position(self._handle))
 
+    @property
+    def decode_programmatic(self) -> bool:
+        """Additive: whether decode steps use programmatic dependent launch."""
+        return bool(lib.ar_engine_decode_programmatic(self._handle))
+
     def prepare_scan(self, prompts: Sequence[StructuredPrompt], layer_begin: int = 0, layer_end: int = -1,
                      normalize_by_length: bool = False) -> "PreparedScan":
         return PreparedScan(self, prompts, layer_begin, layer_end, normalize_by_length)

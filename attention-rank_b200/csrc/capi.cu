@@ -563,6 +563,10 @@ int ar_engine_generation_position(ar_engine* engine) {
   return engine ? engine->engine->generation_position() : -1;
 }
 
+int ar_engine_decode_programmatic(ar_engine* engine) {
+  return engine != nullptr && engine->engine->decode_programmatic() ? 1 : 0;
+}
+
 int ar_sampler_create(const ar_sampler_config* config, ar_sampler** sampler) {
   return guarded([&] {
     if (config == nullptr || sampler == nullptr) throw arb::Error("sampler_create: null argument");
@@ -585,15 +589,30 @@ void ar_sampler_destroy(ar_sampler* sampler) { delete sampler; }
 
 int ar_decode_gemv(const void* w, const void* x, int rows, int k, void* y, int f32_out, int dtype, void* stream) {
   if (rows <= 0 || k <= 0 || k % 8 != 0) return fail(AR_ERR_INVALID, "decode_gemv: k must be a positive multiple of 8");
-  return cuda_result(arb::launch_decode_gemv(w, x, rows, k, y, f32_out != 0, dtype, as_stream(stream)),
-                     "decode_gemv");
+  arb::DecodeGemvArgs args;
+  args.kind = f32_out ? arb::kDecodeLogits : arb::kDecodePlain;
+  args.w = w;
+  args.rows = rows;
+  args.k = k;
+  args.x = x;
+  args.y = y;
+  args.dtype = dtype;
+  return cuda_result(arb::launch_decode_gemv(args, false, as_stream(stream)), "decode_gemv");
 }
 
 int ar_decode_gate_up(const void* w, const void* x, int inter, int k, void* act, int dtype, void* stream) {
   if (inter <= 0 || k <= 0 || k % 8 != 0) {
     return fail(AR_ERR_INVALID, "decode_gate_up: k must be a positive multiple of 8");
   }
-  return cuda_result(arb::launch_decode_gate_up(w, x, inter, k, act, dtype, as_stream(stream)), "decode_gate_up");
+  arb::DecodeGemvArgs args;
+  args.kind = arb::kDecodeGateUp;
+  args.w = w;
+  args.rows = inter;
+  args.k = k;
+  args.x = x;
+  args.y = act;
+  args.dtype = dtype;
+  return cuda_result(arb::launch_decode_gemv(args, false, as_stream(stream)), "decode_gate_up");
 }
 
 int ar_decode_attention(const void* q, const void* k_cache, const void* v_cache, int context, int position,
@@ -622,9 +641,11 @@ int ar_decode_attention(const void* q, const void* k_cache, const void* v_cache,
     args.sliding_window = sliding_window;
     args.partials = static_cast<float*>(scratch.get(static_cast<size_t>(query_heads) * arb::kDecodeSplits * head_dim * 4));
     args.stats = static_cast<float*>(scratch.get(static_cast<size_t>(query_heads) * arb::kDecodeSplits * 2 * 4));
+    args.tickets = static_cast<unsigned*>(scratch.get(static_cast<size_t>(kv_heads) * sizeof(unsigned)));
+    arb::check_cuda(cudaMemsetAsync(args.tickets, 0, static_cast<size_t>(kv_heads) * sizeof(unsigned), s), "tickets");
     args.out = out;
     args.dtype = dtype;
-    arb::check_cuda(arb::launch_decode_attention(args, s), "decode_attention");
+    arb::check_cuda(arb::launch_decode_attention(args, false, s), "decode_attention");
     arb::check_cuda(cudaStreamSynchronize(s), "decode_attention");  // host_state outlives the copy
     return AR_OK;
   });

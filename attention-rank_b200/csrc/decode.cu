@@ -1,12 +1,16 @@
 // Single-token decode kernels (declarations and the reference mapping in decode.h).
 //
-// Matrix-vector products: a CTA of 8 warps stages x in shared memory once, then every warp
-// walks work items (2 or 4 weight rows) with a grid stride. A lane keeps kLoadsInFlight
-// 16-byte streaming loads (ld.global.nc.L1::no_allocate) outstanding before its first FMA, so an
-// SM holds 32 KB per resident CTA in flight -- the weights are read once per step and never
-// cached. Accumulation is fp32; each row ends with a warp butterfly sum.
+// Matrix-vector products (decode_gemv_kernel): a CTA of 8 warps works on kItems = 8 / kSplit
+// items (2 or 4 weight rows each); the kSplit warps of an item take equal slices of the K range,
+// so a warp's chain of dependent loads is short, and their partial sums meet in shared memory in
+// a fixed order. A lane keeps 8 or 16 16-byte streaming loads (ld.global.nc.L1::no_allocate)
+// outstanding before its first FMA (kInFlight). Before waiting for its producer a CTA sends its first
+// slice of weights towards L2 (cp.async.bulk.prefetch.L2), since weights never depend on the
+// previous kernel; x is then staged in shared memory once per CTA (or built there by the fused
+// RMSNorm prologue). Accumulation is fp32; 16-bit outputs are rounded once.
 #include <cfloat>
 #include <climits>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "decode.h"
@@ -20,8 +24,8 @@ namespace {
 
 constexpr int kGemvThreads = 256;
 constexpr int kGemvWarps = kGemvThreads / 32;
-constexpr int kLoadsInFlight = 8;  // 16-byte weight loads per lane before the first FMA
-constexpr int kDecodeThreads = 128;
+constexpr int kNormVpt = kDecodeMaxNormHidden / (kGemvThreads * 8);  // 8-value chunks per thread
+constexpr int kDecodeThreads = 256;
 constexpr int kDecodeKeys = 64;    // keys staged in shared memory per pass
 constexpr int kDecodeDim = 128;    // head_dim the decode attention is written for
 constexpr int kKeyStride = kDecodeDim + 8;  // padded K row (halves): 16-byte reads of 8 rows hit 32 banks
@@ -45,22 +49,139 @@ __device__ __forceinline__ float round16(float v) {
   return Scalar<T>::to(Scalar<T>::from(v));
 }
 
+// Programmatic dependent launch: wait until the preceding kernel on the stream has completed and
+// its writes are visible (a no-op for kernels launched without the attribute) ...
+__device__ __forceinline__ void wait_for_producer() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// ... and let the next kernel on the stream be scheduled while this one runs.
+__device__ __forceinline__ void release_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+__device__ __forceinline__ void prefetch_l2(const void* address, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(__cvta_generic_to_global(address)), "r"(bytes)
+               : "memory");
+}
+
+// larger value first; equal values: the smaller index (the first maximum)
+__device__ __forceinline__ bool better(float value, int index, float than_value, int than_index) {
+  return value > than_value || (value == than_value && index < than_index);
+}
+
+template <int kKind>
+struct GemvShape {
+  static constexpr int kRows = (kKind == kDecodeGateUp || kKind == kDecodeQkv) ? 4 : 2;
+};
+
+template <int kKind>
+__device__ __forceinline__ int item_count(const DecodeGemvArgs& a) {
+  if constexpr (kKind == kDecodeQkv) return a.rows / 4;
+  return (a.rows + 1) / 2;
+}
+
+// Weight rows of work item `item`.
+//   plain / logits: 2i, 2i + 1;  gate|up: gate rows 2i, 2i + 1 and their up rows inter + 2i, +1;
+//   q|k|v: for query and key heads the rotation pairs (2j, 2j + D/2), (2j + 1, 2j + 1 + D/2) of
+//   head h, for value heads rows 4j .. 4j + 3 (item = h * D/4 + j).
+// A row past the end repeats the last row; its result is not stored.
+template <int kKind>
+__device__ __forceinline__ void item_rows(const DecodeGemvArgs& a, int item, int (&row)[GemvShape<kKind>::kRows]) {
+  if constexpr (kKind == kDecodePlain || kKind == kDecodeLogits) {
+    row[0] = 2 * item;
+    row[1] = min(2 * item + 1, a.rows - 1);
+  } else if constexpr (kKind == kDecodeGateUp) {
+    const int j0 = 2 * item;
+    const int j1 = min(j0 + 1, a.rows - 1);
+    row[0] = j0;
+    row[1] = j1;
+    row[2] = a.rows + j0;
+    row[3] = a.rows + j1;
+  } else {
+    const int per_head = a.head_dim >> 2;
+    const int head = item / per_head;
+    const int j = item - head * per_head;
+    if (head < a.query_heads + a.kv_heads) {
+      row[0] = head * a.head_dim + 2 * j;
+      row[1] = row[0] + 1;
+      row[2] = row[0] + (a.head_dim >> 1);
+      row[3] = row[2] + 1;
+    } else {
+#pragma unroll
+      for (int r = 0; r < 4; ++r) row[r] = head * a.head_dim + 4 * j + r;
+    }
+  }
+}
+
+// x into shared memory: copied, or built by the RMSNorm prologue (the formula of the engine's
+// rms_norm_residual_kernel: v = residual + delta, y = v * rsqrt(sum(v^2) / k + eps) * gamma).
 template <typename T>
-__device__ __forceinline__ void stage_vector(const T* __restrict__ x, int chunks, uint4* xs) {
-  for (int i = threadIdx.x; i < chunks; i += blockDim.x) xs[i] = load_nc(x + 8 * static_cast<size_t>(i));
+__device__ __forceinline__ void stage_x(const DecodeGemvArgs& a, uint4* xs, float* scratch) {
+  const int chunks = a.k >> 3;
+  if (a.residual_in == nullptr) {
+    const T* x = static_cast<const T*>(a.x);
+    for (int i = threadIdx.x; i < chunks; i += kGemvThreads) {
+      xs[i] = __ldcg(reinterpret_cast<const uint4*>(x + 8 * static_cast<size_t>(i)));
+    }
+    __syncthreads();
+    return;
+  }
+  const T* delta = static_cast<const T*>(a.delta);
+  float values[kNormVpt][8];
+  float squares = 0.0f;
+#pragma unroll
+  for (int v = 0; v < kNormVpt; ++v) {
+    const int chunk = threadIdx.x + v * kGemvThreads;
+    if (chunk < chunks) {
+      const float4 r0 = __ldcg(reinterpret_cast<const float4*>(a.residual_in + 8 * chunk));
+      const float4 r1 = __ldcg(reinterpret_cast<const float4*>(a.residual_in + 8 * chunk + 4));
+      float d[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+      if (delta != nullptr) unpack8<T>(__ldcg(reinterpret_cast<const uint4*>(delta + 8 * chunk)), d);
+      values[v][0] = r0.x + d[0];
+      values[v][1] = r0.y + d[1];
+      values[v][2] = r0.z + d[2];
+      values[v][3] = r0.w + d[3];
+      values[v][4] = r1.x + d[4];
+      values[v][5] = r1.y + d[5];
+      values[v][6] = r1.z + d[6];
+      values[v][7] = r1.w + d[7];
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) values[v][i] = 0.0f;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) squares += values[v][i] * values[v][i];
+  }
+  const float total = block_sum(squares, scratch);
+  const float scale = rsqrtf(total / static_cast<float>(a.k) + a.eps);
+  const bool keep = a.residual_out != nullptr && blockIdx.x == 0;
+#pragma unroll
+  for (int v = 0; v < kNormVpt; ++v) {
+    const int chunk = threadIdx.x + v * kGemvThreads;
+    if (chunk >= chunks) continue;
+    const float4 g0 = __ldg(reinterpret_cast<const float4*>(a.gamma + 8 * chunk));
+    const float4 g1 = __ldg(reinterpret_cast<const float4*>(a.gamma + 8 * chunk + 4));
+    const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+    if (keep) {
+      float4* out = reinterpret_cast<float4*>(a.residual_out + 8 * chunk);
+      out[0] = make_float4(values[v][0], values[v][1], values[v][2], values[v][3]);
+      out[1] = make_float4(values[v][4], values[v][5], values[v][6], values[v][7]);
+    }
+    float y[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) y[i] = values[v][i] * scale * g[i];
+    xs[chunk] = pack8<T>(y);
+  }
   __syncthreads();
 }
 
-// acc[r] = rows[r][0, 8 chunks) . x for the whole warp (every lane receives the sums)
-template <typename T, int kRows>
-__device__ __forceinline__ void warp_dot(const T* (&rows)[kRows], const uint4* __restrict__ xs, int chunks,
-                                         float (&acc)[kRows]) {
-  constexpr int kUnroll = kLoadsInFlight / kRows;
+// acc[r] = rows[r][8 c] . x over chunks c in [begin, end), summed over the warp (all lanes);
+// kInFlight 16-byte weight loads per lane are issued before the first FMA of a batch
+template <typename T, int kRows, int kInFlight>
+__device__ __forceinline__ void warp_dot_range(const T* (&rows)[kRows], const uint4* __restrict__ xs, int begin,
+                                               int end, float (&acc)[kRows]) {
+  constexpr int kUnroll = kInFlight / kRows;
   const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int r = 0; r < kRows; ++r) acc[r] = 0.0f;
-  int c = lane;
-  for (; c + 32 * (kUnroll - 1) < chunks; c += 32 * kUnroll) {
+  int c = begin + lane;
+  for (; c + 32 * (kUnroll - 1) < end; c += 32 * kUnroll) {
     uint4 w[kRows][kUnroll];
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
@@ -80,7 +201,7 @@ __device__ __forceinline__ void warp_dot(const T* (&rows)[kRows], const uint4* _
       }
     }
   }
-  for (; c < chunks; c += 32) {
+  for (; c < end; c += 32) {
     float xv[8];
     unpack8<T>(xs[c], xv);
 #pragma unroll
@@ -95,143 +216,288 @@ __device__ __forceinline__ void warp_dot(const T* (&rows)[kRows], const uint4* _
   for (int r = 0; r < kRows; ++r) acc[r] = warp_sum(acc[r]);
 }
 
-template <typename T, bool kF32Out>
-__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const T* __restrict__ w, const T* __restrict__ x,
-                                                            int rows, int k, void* __restrict__ y) {
-  extern __shared__ uint4 xs[];
-  const int chunks = k >> 3;
-  stage_vector<T>(x, chunks, xs);
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int items = (rows + 1) >> 1;
-  for (int item = blockIdx.x * kGemvWarps + warp; item < items; item += gridDim.x * kGemvWarps) {
+// Epilogue of one item (lane 0 of the item's first warp); `best` tracks the greedy pick.
+template <typename T, int kKind>
+__device__ __forceinline__ void finish_item(const DecodeGemvArgs& a, int item, const float (&sum)[GemvShape<kKind>::kRows],
+                                            float& best, int& best_at) {
+  if constexpr (kKind == kDecodePlain || kKind == kDecodeLogits) {
     const int r0 = 2 * item;
-    const bool pair = r0 + 1 < rows;
-    const T* row_ptr[2] = {w + static_cast<size_t>(r0) * k, w + static_cast<size_t>(pair ? r0 + 1 : r0) * k};
-    float acc[2];
-    warp_dot<T, 2>(row_ptr, xs, chunks, acc);
-    if (lane == 0) {
-      if constexpr (kF32Out) {
-        float* out = static_cast<float*>(y);
-        out[r0] = acc[0];
-        if (pair) out[r0 + 1] = acc[1];
-      } else {
-        T* out = static_cast<T*>(y);
-        if (pair) {
-          *reinterpret_cast<uint32_t*>(out + r0) = pack2<T>(acc[0], acc[1]);
-        } else {
-          out[r0] = Scalar<T>::from(acc[0]);
-        }
+    const bool pair = r0 + 1 < a.rows;
+    if constexpr (kKind == kDecodeLogits) {
+      float* out = static_cast<float*>(a.y);
+      out[r0] = sum[0];
+      if (pair) out[r0 + 1] = sum[1];
+      if (sum[0] > best) {
+        best = sum[0];
+        best_at = r0;
       }
-    }
-  }
-}
-
-template <typename T>
-__global__ void __launch_bounds__(kGemvThreads) gate_up_kernel(const T* __restrict__ w, const T* __restrict__ x,
-                                                               int inter, int k, T* __restrict__ act) {
-  extern __shared__ uint4 xs[];
-  const int chunks = k >> 3;
-  stage_vector<T>(x, chunks, xs);
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int items = (inter + 1) >> 1;
-  for (int item = blockIdx.x * kGemvWarps + warp; item < items; item += gridDim.x * kGemvWarps) {
-    const int j0 = 2 * item;
-    const bool pair = j0 + 1 < inter;
-    const int j1 = pair ? j0 + 1 : j0;
-    const T* row_ptr[4] = {w + static_cast<size_t>(j0) * k, w + static_cast<size_t>(j1) * k,
-                           w + static_cast<size_t>(inter + j0) * k, w + static_cast<size_t>(inter + j1) * k};
-    float acc[4];
-    warp_dot<T, 4>(row_ptr, xs, chunks, acc);
-    if (lane == 0) {
-      // silu(g) * u = g / (1 + e^-g) * u on the 16-bit projections, as the prefill's SwiGLU kernel
-      float a[2];
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const float g = round16<T>(acc[i]);
-        const float u = round16<T>(acc[2 + i]);
-        a[i] = __fdividef(g, 1.0f + __expf(-g)) * u;
+      if (pair && sum[1] > best) {
+        best = sum[1];
+        best_at = r0 + 1;
       }
+    } else {
+      T* out = static_cast<T*>(a.y);
       if (pair) {
-        *reinterpret_cast<uint32_t*>(act + j0) = pack2<T>(a[0], a[1]);
+        *reinterpret_cast<uint32_t*>(out + r0) = pack2<T>(sum[0], sum[1]);
       } else {
-        act[j0] = Scalar<T>::from(a[0]);
+        out[r0] = Scalar<T>::from(sum[0]);
       }
+    }
+  } else if constexpr (kKind == kDecodeGateUp) {
+    // silu(g) * u = g / (1 + e^-g) * u on the 16-bit projections, as the prefill's SwiGLU kernel
+    const int j0 = 2 * item;
+    const bool pair = j0 + 1 < a.rows;
+    float value[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float g = round16<T>(sum[i]);
+      const float u = round16<T>(sum[2 + i]);
+      value[i] = __fdividef(g, 1.0f + __expf(-g)) * u;
+    }
+    T* out = static_cast<T*>(a.y);
+    if (pair) {
+      *reinterpret_cast<uint32_t*>(out + j0) = pack2<T>(value[0], value[1]);
+    } else {
+      out[j0] = Scalar<T>::from(value[0]);
     }
   }
 }
 
-// q|k|v projection of the step's token. Work item = 4 rows of one head: for query and key heads
-// the rotation pairs (2j, 2j + D/2) and (2j + 1, 2j + 1 + D/2), for value heads rows 4j .. 4j + 3.
+// Operands of a q|k|v item's epilogue (bias, rotation), loaded before its dot products so that
+// their latency hides behind the weight stream.
+struct QkvOperands {
+  float bias_half[4];
+  float bias[4];
+  float c0, c1, s0, s1;
+};
+
 template <typename T>
-__global__ void __launch_bounds__(kGemvThreads) qkv_rope_kernel(DecodeQkvArgs a) {
-  extern __shared__ uint4 xs[];
-  const int chunks = a.hidden >> 3;
-  stage_vector<T>(static_cast<const T*>(a.x), chunks, xs);
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
+__device__ __forceinline__ void load_qkv_operands(const DecodeGemvArgs& a, int item, int position, QkvOperands& o) {
+  int row[4];
+  item_rows<kDecodeQkv>(a, item, row);
+  const T* bias_half = static_cast<const T*>(a.bias_half);
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    o.bias_half[r] = bias_half != nullptr ? Scalar<T>::to(bias_half[row[r]]) : 0.0f;
+    o.bias[r] = a.bias != nullptr ? a.bias[row[r]] : 0.0f;
+  }
+  o.c0 = o.c1 = 1.0f;
+  o.s0 = o.s1 = 0.0f;
+  const int per_head = a.head_dim >> 2;
+  const int head = item / per_head;
+  const int j = item - head * per_head;
+  if (head < a.query_heads + a.kv_heads && position >= 0 && position < a.table_positions) {
+    const size_t at = static_cast<size_t>(position) * (a.head_dim >> 1) + 2 * j;
+    o.c0 = a.cos_table[at];
+    o.c1 = a.cos_table[at + 1];
+    o.s0 = a.sin_table[at];
+    o.s1 = a.sin_table[at + 1];
+  }
+}
+
+// q|k|v epilogue: bias where the prefill adds it, RoPE on query and key heads (the prefill's
+// rotary expression), the query to q_out, key and value rows to the cache at `position`.
+template <typename T>
+__device__ __forceinline__ void finish_qkv(const DecodeGemvArgs& a, int item, int position, const float (&sum)[4],
+                                           const QkvOperands& o) {
   const int D = a.head_dim;
   const int half = D >> 1;
   const int per_head = D >> 2;
+  const int head = item / per_head;
+  const int j = item - head * per_head;
   const int rotated = a.query_heads + a.kv_heads;
-  const int heads = rotated + a.kv_heads;
-  const int items = heads * per_head;
-  const int position = a.state[1];
-  const bool valid = position >= 0 && position < a.table_positions && position < a.context;
-  if (!valid && blockIdx.x == 0 && threadIdx.x == 0) report_status(a.status, kStatusPositionOutOfRange);
+  if (position < 0 || position >= a.table_positions || position >= a.context) return;  // reported once per launch
+  float v[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    float value = sum[r];
+    if (a.bias_half != nullptr) value += o.bias_half[r];
+    value = round16<T>(value);
+    if (a.bias != nullptr) value += o.bias[r];
+    v[r] = value;
+  }
+  if (head < rotated) {
+    const float lo0 = v[0] * o.c0 - v[2] * o.s0;
+    const float hi0 = v[2] * o.c0 + v[0] * o.s0;
+    const float lo1 = v[1] * o.c1 - v[3] * o.s1;
+    const float hi1 = v[3] * o.c1 + v[1] * o.s1;
+    T* dst = head < a.query_heads
+                 ? static_cast<T*>(a.q_out) + static_cast<size_t>(head) * D
+                 : static_cast<T*>(a.k_cache) + (static_cast<size_t>(head - a.query_heads) * a.context + position) * D;
+    *reinterpret_cast<uint32_t*>(dst + 2 * j) = pack2<T>(lo0, lo1);
+    *reinterpret_cast<uint32_t*>(dst + half + 2 * j) = pack2<T>(hi0, hi1);
+  } else {
+    T* dst = static_cast<T*>(a.v_cache) + (static_cast<size_t>(head - rotated) * a.context + position) * D + 4 * j;
+    uint2 packed;
+    packed.x = pack2<T>(v[0], v[1]);
+    packed.y = pack2<T>(v[2], v[3]);
+    *reinterpret_cast<uint2*>(dst) = packed;
+  }
+}
+
+// The CTA's best (value, index) into its slot; the last CTA to finish reduces the slots into
+// state = {index, position + 1}. No CTA waits for another: the last one is found by a ticket.
+__device__ void finish_pick(const DecodeGemvArgs& a, float best, int best_at) {
+  __shared__ float values[kGemvWarps];
+  __shared__ int indices[kGemvWarps];
+  __shared__ bool last;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (lane == 0) {
+    values[warp] = best;
+    indices[warp] = best_at;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float v = values[0];
+    int at = indices[0];
+    for (int w = 1; w < kGemvWarps; ++w) {
+      if (better(values[w], indices[w], v, at)) {
+        v = values[w];
+        at = indices[w];
+      }
+    }
+    a.pick_values[blockIdx.x] = v;
+    a.pick_indices[blockIdx.x] = at;
+    __threadfence();
+    last = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  float v = -INFINITY;
+  int at = INT_MAX;
+  for (int s = threadIdx.x; s < static_cast<int>(gridDim.x); s += kGemvThreads) {
+    const float sv = __ldcg(a.pick_values + s);
+    const int si = __ldcg(a.pick_indices + s);
+    if (better(sv, si, v, at)) {
+      v = sv;
+      at = si;
+    }
+  }
+#pragma unroll
+  for (int offset = 16; offset > 0; offset >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, offset);
+    const int oi = __shfl_xor_sync(0xffffffffu, at, offset);
+    if (better(ov, oi, v, at)) {
+      v = ov;
+      at = oi;
+    }
+  }
+  __syncthreads();  // values / indices reused
+  if (lane == 0) {
+    values[warp] = v;
+    indices[warp] = at;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kGemvWarps; ++w) {
+      if (better(values[w], indices[w], values[0], indices[0])) {
+        values[0] = values[w];
+        indices[0] = indices[w];
+      }
+    }
+    a.state[0] = indices[0] == INT_MAX ? 0 : indices[0];
+    a.state[1] = a.state[1] + 1;
+    *a.ticket = 0u;
+  }
+}
+
+template <typename T, int kKind, int kSplit, int kInFlight>
+__global__ void __launch_bounds__(kGemvThreads) decode_gemv_kernel(const DecodeGemvArgs a) {
+  constexpr int kRows = GemvShape<kKind>::kRows;
+  constexpr int kItems = kGemvWarps / kSplit;
+  extern __shared__ uint4 xs[];
+  __shared__ float partial[kGemvWarps][kRows];
+  __shared__ float scratch[32];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int local = warp / kSplit;
+  const int slice = warp - local * kSplit;
+  const int chunks = a.k >> 3;
+  const int begin = slice * chunks / kSplit;
+  const int end = (slice + 1) * chunks / kSplit;
+  const int items = item_count<kKind>(a);
   const T* w = static_cast<const T*>(a.w);
-  const T* bias_half = static_cast<const T*>(a.bias_half);
-  for (int item = blockIdx.x * kGemvWarps + warp; item < items; item += gridDim.x * kGemvWarps) {
-    const int head = item / per_head;
-    const int j = item - head * per_head;
-    const bool rotate = head < rotated;
-    int row[4];
-    if (rotate) {
-      row[0] = head * D + 2 * j;
-      row[1] = row[0] + 1;
-      row[2] = row[0] + half;
-      row[3] = row[2] + 1;
-    } else {
-#pragma unroll
-      for (int r = 0; r < 4; ++r) row[r] = head * D + 4 * j + r;
+
+  {  // the weights do not depend on the producer: start this warp's first slice towards L2
+    const int item = blockIdx.x * kItems + local;
+    if (item < items && lane < kRows && end > begin) {
+      int row[kRows];
+      item_rows<kKind>(a, item, row);
+      prefetch_l2(w + static_cast<size_t>(row[lane]) * a.k + 8 * static_cast<size_t>(begin),
+                  static_cast<uint32_t>(end - begin) * 16u);
     }
-    const T* row_ptr[4];
-#pragma unroll
-    for (int r = 0; r < 4; ++r) row_ptr[r] = w + static_cast<size_t>(row[r]) * a.hidden;
-    float acc[4];
-    warp_dot<T, 4>(row_ptr, xs, chunks, acc);
-    if (lane != 0 || !valid) continue;
-    float v[4];
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      float value = acc[r];
-      if (bias_half != nullptr) value += Scalar<T>::to(bias_half[row[r]]);
-      value = round16<T>(value);
-      if (a.bias != nullptr) value += a.bias[row[r]];
-      v[r] = value;
+  }
+  wait_for_producer();
+  release_dependents();
+  const int position = kKind == kDecodeQkv ? a.state[1] : 0;
+  if constexpr (kKind == kDecodeQkv) {
+    if ((position < 0 || position >= a.table_positions || position >= a.context) && blockIdx.x == 0 &&
+        threadIdx.x == 0) {
+      report_status(a.status, kStatusPositionOutOfRange);
     }
-    if (rotate) {
-      const size_t at = static_cast<size_t>(position) * half + 2 * j;
-      const float c0 = a.cos_table[at], c1 = a.cos_table[at + 1];
-      const float s0 = a.sin_table[at], s1 = a.sin_table[at + 1];
-      const float lo0 = v[0] * c0 - v[2] * s0;
-      const float hi0 = v[2] * c0 + v[0] * s0;
-      const float lo1 = v[1] * c1 - v[3] * s1;
-      const float hi1 = v[3] * c1 + v[1] * s1;
-      T* dst = head < a.query_heads
-                   ? static_cast<T*>(a.q_out) + static_cast<size_t>(head) * D
-                   : static_cast<T*>(a.k_cache) +
-                         (static_cast<size_t>(head - a.query_heads) * a.context + position) * D;
-      *reinterpret_cast<uint32_t*>(dst + 2 * j) = pack2<T>(lo0, lo1);
-      *reinterpret_cast<uint32_t*>(dst + half + 2 * j) = pack2<T>(hi0, hi1);
-    } else {
-      T* dst = static_cast<T*>(a.v_cache) + (static_cast<size_t>(head - rotated) * a.context + position) * D + 4 * j;
-      uint2 packed;
-      packed.x = pack2<T>(v[0], v[1]);
-      packed.y = pack2<T>(v[2], v[3]);
-      *reinterpret_cast<uint2*>(dst) = packed;
+  }
+  stage_x<T>(a, xs, scratch);
+
+  float best = -INFINITY;
+  int best_at = INT_MAX;
+  if constexpr (kSplit == 1) {
+    // every warp walks its own items: no block-wide step between them, loads stay in flight
+    for (int item = blockIdx.x * kGemvWarps + warp; item < items; item += gridDim.x * kGemvWarps) {
+      int row[kRows];
+      item_rows<kKind>(a, item, row);
+      const T* row_ptr[kRows];
+#pragma unroll
+      for (int r = 0; r < kRows; ++r) row_ptr[r] = w + static_cast<size_t>(row[r]) * a.k;
+      float acc[kRows];
+      warp_dot_range<T, kRows, kInFlight>(row_ptr, xs, 0, chunks, acc);
+      if (lane == 0) finish_item<T, kKind>(a, item, acc, best, best_at);
     }
+  } else {
+    for (int group = blockIdx.x; group * kItems < items; group += gridDim.x) {
+      const int item = group * kItems + local;
+      float acc[kRows];
+      [[maybe_unused]] QkvOperands operands;
+      if constexpr (kKind == kDecodeQkv) {
+        if (slice == 0 && lane == 0 && item < items) load_qkv_operands<T>(a, item, position, operands);
+      }
+      if (item < items) {
+        int row[kRows];
+        item_rows<kKind>(a, item, row);
+        const T* row_ptr[kRows];
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) row_ptr[r] = w + static_cast<size_t>(row[r]) * a.k;
+        warp_dot_range<T, kRows, kInFlight>(row_ptr, xs, begin, end, acc);
+      } else {
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) acc[r] = 0.0f;
+      }
+      if (lane == 0) {
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) partial[warp][r] = acc[r];
+      }
+      __syncthreads();
+      if (slice == 0 && lane == 0 && item < items) {
+        float sum[kRows];
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) {
+          float s = 0.0f;
+#pragma unroll
+          for (int q = 0; q < kSplit; ++q) s += partial[warp + q][r];
+          sum[r] = s;
+        }
+        if constexpr (kKind == kDecodeQkv) {
+          finish_qkv<T>(a, item, position, sum, operands);
+        } else {
+          finish_item<T, kKind>(a, item, sum, best, best_at);
+        }
+      }
+      __syncthreads();
+    }
+  }
+  if constexpr (kKind == kDecodeLogits) {
+    if (a.pick) finish_pick(a, best, best_at);
   }
 }
 
@@ -241,22 +507,30 @@ __device__ __forceinline__ float warp_max(float value) {
   return value;
 }
 
-// One CTA per (key-range split, KV head). Warp w owns query heads w, w + 4, ... of the group:
+// One CTA per (key-range split, KV head). Warp w owns query heads w, w + 8 of the group:
 // lane l scores keys l and l + 32 of each 64-key pass (scores scaled into log2 units), keeps the
-// online-softmax max and sum, and accumulates output dims 4l .. 4l + 3 in fp32.
+// online-softmax max and sum, and accumulates output dims 4l .. 4l + 3 in fp32. The last CTA of
+// a KV head (ticket) merges the splits of the group's heads:
+//   out[h, d] = sum_s 2^(m_s - M) O_s[d] / sum_s 2^(m_s - M) l_s.
 template <typename T>
-__global__ void __launch_bounds__(kDecodeThreads) decode_attention_kernel(DecodeAttentionArgs a, float scale_log2) {
+__global__ void __launch_bounds__(kDecodeThreads) decode_attention_kernel(const DecodeAttentionArgs a,
+                                                                          float scale_log2) {
   __shared__ float q_s[kDecodeMaxGroup][kDecodeDim];
   __shared__ __align__(16) T k_s[kDecodeKeys][kKeyStride];
   __shared__ __align__(16) T v_s[kDecodeKeys][kDecodeDim];
   __shared__ float p_s[kDecodeMaxGroup][kDecodeKeys];
-  constexpr int kHeadsPerWarp = kDecodeMaxGroup / (kDecodeThreads / 32);
+  __shared__ bool last;
+  constexpr int kWarps = kDecodeThreads / 32;
+  constexpr int kHeadsPerWarp = kDecodeMaxGroup / kWarps;
   const int split = blockIdx.x;
   const int kv_head = blockIdx.y;
   const int group = a.query_heads / a.kv_heads;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int position = a.state[1];
+  // The step's position was fixed before this step's first kernel ran, and cache rows below it
+  // come from earlier steps: both are read before waiting for the q|k|v kernel, whose output
+  // (q and the cache row at `position`) is read after.
+  const int position = __ldcg(a.state + 1);
   const bool valid = position >= 0 && position < a.context;
   const int length = valid ? position + 1 : 0;
   const int first = a.sliding_window > 0 && length > a.sliding_window ? length - a.sliding_window : 0;
@@ -264,12 +538,39 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_attention_kernel(Decode
   const int per_split = (span + kDecodeSplits - 1) / kDecodeSplits;
   const int begin = first + split * per_split;
   const int end = min(begin + per_split, length);
-
-  for (int i = threadIdx.x; i < group * kDecodeDim; i += kDecodeThreads) {
-    const int g = i / kDecodeDim;
-    const int d = i - g * kDecodeDim;
-    q_s[g][d] = Scalar<T>::to(static_cast<const T*>(a.q)[static_cast<size_t>(kv_head * group + g) * kDecodeDim + d]) *
-                scale_log2;
+  const T* k_head = static_cast<const T*>(a.k_cache) + static_cast<size_t>(kv_head) * a.context * kDecodeDim;
+  const T* v_head = static_cast<const T*>(a.v_cache) + static_cast<size_t>(kv_head) * a.context * kDecodeDim;
+  // K and V rows [base, base + keys) into shared memory, except row `skip`
+  auto stage_keys = [&](int base, int keys, int skip) {
+    for (int i = threadIdx.x; i < keys * (kDecodeDim / 8); i += kDecodeThreads) {
+      const int key = i / (kDecodeDim / 8);
+      if (base + key == skip) continue;
+      const int c = i - key * (kDecodeDim / 8);
+      const size_t at = static_cast<size_t>(base + key) * kDecodeDim + 8 * c;
+      *reinterpret_cast<uint4*>(&k_s[key][8 * c]) = __ldcg(reinterpret_cast<const uint4*>(k_head + at));
+      *reinterpret_cast<uint4*>(&v_s[key][8 * c]) = __ldcg(reinterpret_cast<const uint4*>(v_head + at));
+    }
+  };
+  if (begin < end) stage_keys(begin, min(kDecodeKeys, end - begin), position);  // the first pass's history rows
+  wait_for_producer();
+  release_dependents();
+  if (position >= begin && position < end && position < begin + kDecodeKeys) {
+    // the newest row, written by the q|k|v kernel of this step
+    for (int i = threadIdx.x; i < kDecodeDim / 8; i += kDecodeThreads) {
+      const size_t at = static_cast<size_t>(position) * kDecodeDim + 8 * i;
+      *reinterpret_cast<uint4*>(&k_s[position - begin][8 * i]) = __ldcg(reinterpret_cast<const uint4*>(k_head + at));
+      *reinterpret_cast<uint4*>(&v_s[position - begin][8 * i]) = __ldcg(reinterpret_cast<const uint4*>(v_head + at));
+    }
+  }
+  for (int i = threadIdx.x; i < group * (kDecodeDim / 8); i += kDecodeThreads) {
+    const int g = i / (kDecodeDim / 8);
+    const int c = i - g * (kDecodeDim / 8);
+    float qv[8];
+    unpack8<T>(__ldcg(reinterpret_cast<const uint4*>(static_cast<const T*>(a.q) +
+                                                      static_cast<size_t>(kv_head * group + g) * kDecodeDim + 8 * c)),
+               qv);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) q_s[g][8 * c + e] = qv[e] * scale_log2;
   }
   float m[kHeadsPerWarp];
   float l[kHeadsPerWarp];
@@ -281,28 +582,22 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_attention_kernel(Decode
 #pragma unroll
     for (int i = 0; i < 4; ++i) o[h][i] = 0.0f;
   }
-  const T* k_head = static_cast<const T*>(a.k_cache) + static_cast<size_t>(kv_head) * a.context * kDecodeDim;
-  const T* v_head = static_cast<const T*>(a.v_cache) + static_cast<size_t>(kv_head) * a.context * kDecodeDim;
   for (int base = begin; base < end; base += kDecodeKeys) {
     const int keys = min(kDecodeKeys, end - base);
-    __syncthreads();  // q_s written / the previous pass's K, V and P consumed
-    for (int i = threadIdx.x; i < keys * (kDecodeDim / 8); i += kDecodeThreads) {
-      const int key = i / (kDecodeDim / 8);
-      const int c = i - key * (kDecodeDim / 8);
-      const size_t at = static_cast<size_t>(base + key) * kDecodeDim + 8 * c;
-      *reinterpret_cast<uint4*>(&k_s[key][8 * c]) = load_nc(k_head + at);
-      *reinterpret_cast<uint4*>(&v_s[key][8 * c]) = load_nc(v_head + at);
+    if (base != begin) {
+      __syncthreads();  // the previous pass's K, V and P are consumed
+      stage_keys(base, keys, -1);
     }
     __syncthreads();
 #pragma unroll
     for (int h = 0; h < kHeadsPerWarp; ++h) {
-      const int g = warp + 4 * h;
+      const int g = warp + kWarps * h;
       if (g >= group) break;
       float s[2];
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const int key = lane + 32 * half;
-        s[half] = -INFINITY;
+      for (int which = 0; which < 2; ++which) {
+        const int key = lane + 32 * which;
+        s[which] = -INFINITY;
         if (key < keys) {
           float dot = 0.0f;
 #pragma unroll 4
@@ -320,7 +615,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_attention_kernel(Decode
             dot = fmaf(q1.z, kv[6], dot);
             dot = fmaf(q1.w, kv[7], dot);
           }
-          s[half] = dot;
+          s[which] = dot;
         }
       }
       const float m_new = fmaxf(m[h], warp_max(fmaxf(s[0], s[1])));  // finite: keys >= 1
@@ -349,7 +644,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_attention_kernel(Decode
   }
 #pragma unroll
   for (int h = 0; h < kHeadsPerWarp; ++h) {
-    const int g = warp + 4 * h;
+    const int g = warp + kWarps * h;
     if (g >= group) break;
     const int head = kv_head * group + g;
     const size_t slot = static_cast<size_t>(head) * kDecodeSplits + split;
@@ -359,27 +654,41 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_attention_kernel(Decode
       a.stats[2 * slot + 1] = l[h];
     }
   }
-}
-
-// out[h, d] = sum_s 2^(m_s - M) O_s[d] / sum_s 2^(m_s - M) l_s over the splits of head h.
-template <typename T>
-__global__ void __launch_bounds__(kDecodeDim) decode_combine_kernel(const float* __restrict__ partials,
-                                                                    const float* __restrict__ stats, T* __restrict__ out) {
-  const int head = blockIdx.x;
-  const int d = threadIdx.x;
-  const float* st = stats + static_cast<size_t>(head) * kDecodeSplits * 2;
-  float top = -INFINITY;
-  for (int s = 0; s < kDecodeSplits; ++s) top = fmaxf(top, st[2 * s]);
-  float sum = 0.0f;
-  float acc = 0.0f;
-  for (int s = 0; s < kDecodeSplits; ++s) {
-    const float m = st[2 * s];
-    if (m == -INFINITY) continue;
-    const float weight = exp2f(m - top);
-    sum = fmaf(weight, st[2 * s + 1], sum);
-    acc = fmaf(weight, partials[(static_cast<size_t>(head) * kDecodeSplits + s) * kDecodeDim + d], acc);
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(a.tickets + kv_head, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  // warp w merges heads w, w + 8: lane s holds split s's (m, l); lane l combines dims 4l..4l+3
+  static_assert(kDecodeSplits == 32, "one split per lane");
+  for (int g = warp; g < group; g += kWarps) {
+    const int head = kv_head * group + g;
+    const float* st = a.stats + static_cast<size_t>(head) * kDecodeSplits * 2;
+    const float* part = a.partials + static_cast<size_t>(head) * kDecodeSplits * kDecodeDim;
+    const float ms = __ldcg(st + 2 * lane);
+    const float ls = __ldcg(st + 2 * lane + 1);
+    const float top = warp_max(ms);
+    const float weight = ms == -INFINITY ? 0.0f : exp2f(ms - top);
+    const float total = warp_sum(weight * ls);
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 8
+    for (int split = 0; split < kDecodeSplits; ++split) {
+      const float ws = __shfl_sync(0xffffffffu, weight, split);
+      if (ws == 0.0f) continue;  // an empty split (uniform over the warp)
+      const float4 p = __ldcg(reinterpret_cast<const float4*>(part + static_cast<size_t>(split) * kDecodeDim + 4 * lane));
+      acc[0] = fmaf(ws, p.x, acc[0]);
+      acc[1] = fmaf(ws, p.y, acc[1]);
+      acc[2] = fmaf(ws, p.z, acc[2]);
+      acc[3] = fmaf(ws, p.w, acc[3]);
+    }
+    const float inverse = total > 0.0f ? 1.0f / total : 0.0f;
+    uint2 packed;
+    packed.x = pack2<T>(acc[0] * inverse, acc[1] * inverse);
+    packed.y = pack2<T>(acc[2] * inverse, acc[3] * inverse);
+    *reinterpret_cast<uint2*>(static_cast<T*>(a.out) + static_cast<size_t>(head) * kDecodeDim + 4 * lane) = packed;
   }
-  out[static_cast<size_t>(head) * kDecodeDim + d] = Scalar<T>::from(sum > 0.0f ? acc / sum : 0.0f);
+  if (threadIdx.x == 0) a.tickets[kv_head] = 0u;
 }
 
 template <typename T>
@@ -424,12 +733,11 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __r
       index = i;
     }
   }
-  // larger value wins; equal values: the smaller index (the first maximum overall)
 #pragma unroll
   for (int offset = 16; offset > 0; offset >>= 1) {
     const float other = __shfl_xor_sync(0xffffffffu, best, offset);
     const int other_index = __shfl_xor_sync(0xffffffffu, index, offset);
-    if (other > best || (other == best && other_index < index)) {
+    if (better(other, other_index, best, index)) {
       best = other;
       index = other_index;
     }
@@ -447,7 +755,7 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __r
     for (int offset = 16; offset > 0; offset >>= 1) {
       const float other = __shfl_xor_sync(0xffffffffu, best, offset);
       const int other_index = __shfl_xor_sync(0xffffffffu, index, offset);
-      if (other > best || (other == best && other_index < index)) {
+      if (better(other, other_index, best, index)) {
         best = other;
         index = other_index;
       }
@@ -459,111 +767,113 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const float* __r
   }
 }
 
-template <typename Kernel>
-int gemv_grid(Kernel kernel, long long items, size_t smem) {
+template <typename Kernel, typename... Args>
+cudaError_t launch(Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool programmatic,
+                   Args... args) {
+  cudaLaunchConfig_t config = {};
+  config.gridDim = grid;
+  config.blockDim = block;
+  config.dynamicSmemBytes = smem;
+  config.stream = stream;
+  cudaLaunchAttribute attribute[1];
+  attribute[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attribute[0].val.programmaticStreamSerializationAllowed = 1;
+  config.attrs = programmatic ? attribute : nullptr;
+  config.numAttrs = programmatic ? 1 : 0;
+  return cudaLaunchKernelEx(&config, kernel, args...);
+}
+
+// CTAs per SM a decode GEMV may fill; ATTNRANK_DECODE_CTAS_PER_SM caps it (0 or unset: as many
+// as fit), leaving room for the next kernel's CTAs to start early under programmatic launch.
+int decode_ctas_per_sm_cap() {
+  static const int cap = [] {
+    const char* text = std::getenv("ATTNRANK_DECODE_CTAS_PER_SM");
+    return text != nullptr ? std::atoi(text) : 0;
+  }();
+  return cap;
+}
+
+template <typename T, int kKind, int kSplit, int kInFlight>
+cudaError_t gemv_typed(const DecodeGemvArgs& args, bool programmatic, cudaStream_t stream) {
+  auto kernel = decode_gemv_kernel<T, kKind, kSplit, kInFlight>;
+  const size_t smem = static_cast<size_t>(args.k) * 2;
+  if (smem > 48 * 1024) {
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    const cudaError_t status =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (status != cudaSuccess) return status;
+  }
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kGemvThreads, smem) != cudaSuccess || per_sm <= 0) {
     per_sm = 1;
   }
-  const long long needed = (items + kGemvWarps - 1) / kGemvWarps;
+  const int cap_per_sm = decode_ctas_per_sm_cap();
+  if (cap_per_sm > 0 && per_sm > cap_per_sm) per_sm = cap_per_sm;
+  constexpr int kItems = kGemvWarps / kSplit;
+  const int items = kKind == kDecodeQkv ? args.rows / 4 : (args.rows + 1) / 2;
+  long long grid = (items + kItems - 1) / kItems;
   const long long cap = static_cast<long long>(sm_count()) * per_sm;
-  return static_cast<int>(needed < cap ? (needed > 0 ? needed : 1) : cap);
-}
-
-// x staged in dynamic shared memory: opt in above the 48 KB default once per kernel
-template <typename Kernel>
-cudaError_t prepare_smem(Kernel kernel, size_t smem) {
-  if (smem <= 48 * 1024) return cudaSuccess;
-  if (smem > 227 * 1024) return cudaErrorInvalidValue;
-  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (grid > cap) grid = cap;
+  if (kKind == kDecodeLogits && grid > kDecodePickSlots) grid = kDecodePickSlots;
+  if (grid < 1) grid = 1;
+  return launch(kernel, dim3(static_cast<unsigned>(grid)), dim3(kGemvThreads), smem, stream, programmatic, args);
 }
 
 template <typename T>
-cudaError_t gemv_typed(const void* w, const void* x, int rows, int k, void* y, bool f32_out, cudaStream_t stream) {
-  const size_t smem = static_cast<size_t>(k) * 2;
-  const long long items = (rows + 1) / 2;
-  if (f32_out) {
-    auto kernel = gemv_kernel<T, true>;
-    cudaError_t status = prepare_smem(kernel, smem);
-    if (status != cudaSuccess) return status;
-    kernel<<<gemv_grid(kernel, items, smem), kGemvThreads, smem, stream>>>(static_cast<const T*>(w),
-                                                                          static_cast<const T*>(x), rows, k, y);
-  } else {
-    auto kernel = gemv_kernel<T, false>;
-    cudaError_t status = prepare_smem(kernel, smem);
-    if (status != cudaSuccess) return status;
-    kernel<<<gemv_grid(kernel, items, smem), kGemvThreads, smem, stream>>>(static_cast<const T*>(w),
-                                                                          static_cast<const T*>(x), rows, k, y);
+cudaError_t gemv_dispatch(const DecodeGemvArgs& args, bool programmatic, cudaStream_t stream) {
+  switch (args.kind) {
+    case kDecodePlain:
+      return args.k >= 8192 ? gemv_typed<T, kDecodePlain, 8, 16>(args, programmatic, stream)
+                            : gemv_typed<T, kDecodePlain, 4, 8>(args, programmatic, stream);
+    case kDecodeLogits:
+      return gemv_typed<T, kDecodeLogits, 1, 16>(args, programmatic, stream);
+    case kDecodeGateUp:
+      return gemv_typed<T, kDecodeGateUp, 1, 16>(args, programmatic, stream);
+    case kDecodeQkv:
+      return gemv_typed<T, kDecodeQkv, 4, 8>(args, programmatic, stream);
+    default:
+      return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
-}
-
-template <typename T>
-cudaError_t gate_up_typed(const void* w, const void* x, int inter, int k, void* act, cudaStream_t stream) {
-  const size_t smem = static_cast<size_t>(k) * 2;
-  auto kernel = gate_up_kernel<T>;
-  cudaError_t status = prepare_smem(kernel, smem);
-  if (status != cudaSuccess) return status;
-  kernel<<<gemv_grid(kernel, (inter + 1) / 2, smem), kGemvThreads, smem, stream>>>(
-      static_cast<const T*>(w), static_cast<const T*>(x), inter, k, static_cast<T*>(act));
-  return cudaGetLastError();
-}
-
-template <typename T>
-cudaError_t qkv_typed(const DecodeQkvArgs& args, cudaStream_t stream) {
-  const size_t smem = static_cast<size_t>(args.hidden) * 2;
-  auto kernel = qkv_rope_kernel<T>;
-  cudaError_t status = prepare_smem(kernel, smem);
-  if (status != cudaSuccess) return status;
-  const long long items = static_cast<long long>(args.query_heads + 2 * args.kv_heads) * (args.head_dim / 4);
-  kernel<<<gemv_grid(kernel, items, smem), kGemvThreads, smem, stream>>>(args);
-  return cudaGetLastError();
-}
-
-template <typename T>
-cudaError_t attention_typed(const DecodeAttentionArgs& args, cudaStream_t stream) {
-  const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(args.head_dim));
-  decode_attention_kernel<T><<<dim3(kDecodeSplits, args.kv_heads), kDecodeThreads, 0, stream>>>(args, scale_log2);
-  cudaError_t status = cudaGetLastError();
-  if (status != cudaSuccess) return status;
-  decode_combine_kernel<T><<<args.query_heads, kDecodeDim, 0, stream>>>(args.partials, args.stats,
-                                                                        static_cast<T*>(args.out));
-  return cudaGetLastError();
 }
 
 bool valid_dtype(int dtype) { return dtype == kActFp16 || dtype == kActBf16; }
 
 }  // namespace
 
-cudaError_t launch_decode_gemv(const void* w, const void* x, int rows, int k, void* y, bool f32_out, int dtype,
-                               cudaStream_t stream) {
-  if (rows <= 0 || k <= 0 || k % 8 != 0 || !valid_dtype(dtype)) return cudaErrorInvalidValue;
-  return dtype == kActFp16 ? gemv_typed<__half>(w, x, rows, k, y, f32_out, stream)
-                           : gemv_typed<__nv_bfloat16>(w, x, rows, k, y, f32_out, stream);
-}
-
-cudaError_t launch_decode_gate_up(const void* w, const void* x, int inter, int k, void* act, int dtype,
-                                  cudaStream_t stream) {
-  if (inter <= 0 || k <= 0 || k % 8 != 0 || !valid_dtype(dtype)) return cudaErrorInvalidValue;
-  return dtype == kActFp16 ? gate_up_typed<__half>(w, x, inter, k, act, stream)
-                           : gate_up_typed<__nv_bfloat16>(w, x, inter, k, act, stream);
-}
-
-cudaError_t launch_decode_qkv(const DecodeQkvArgs& args, cudaStream_t stream) {
-  if (args.hidden <= 0 || args.hidden % 8 != 0 || args.head_dim % 4 != 0 || args.query_heads <= 0 ||
-      args.kv_heads <= 0 || args.context <= 0 || !valid_dtype(args.dtype)) {
+cudaError_t launch_decode_gemv(const DecodeGemvArgs& args, bool programmatic, cudaStream_t stream) {
+  if (args.rows <= 0 || args.k <= 0 || args.k % 8 != 0 || !valid_dtype(args.dtype) || args.w == nullptr ||
+      (args.x == nullptr && args.residual_in == nullptr)) {
     return cudaErrorInvalidValue;
   }
-  return args.dtype == kActFp16 ? qkv_typed<__half>(args, stream) : qkv_typed<__nv_bfloat16>(args, stream);
+  if (args.residual_in != nullptr && (args.k > kDecodeMaxNormHidden || args.gamma == nullptr)) {
+    return cudaErrorInvalidValue;
+  }
+  if (args.kind == kDecodeQkv &&
+      (args.head_dim % 4 != 0 || args.query_heads <= 0 || args.kv_heads <= 0 || args.context <= 0 ||
+       args.state == nullptr || args.rows != (args.query_heads + 2 * args.kv_heads) * args.head_dim)) {
+    return cudaErrorInvalidValue;
+  }
+  if (args.pick && (args.kind != kDecodeLogits || args.state == nullptr || args.ticket == nullptr ||
+                    args.pick_values == nullptr || args.pick_indices == nullptr)) {
+    return cudaErrorInvalidValue;
+  }
+  return args.dtype == kActFp16 ? gemv_dispatch<__half>(args, programmatic, stream)
+                                : gemv_dispatch<__nv_bfloat16>(args, programmatic, stream);
 }
 
-cudaError_t launch_decode_attention(const DecodeAttentionArgs& args, cudaStream_t stream) {
+cudaError_t launch_decode_attention(const DecodeAttentionArgs& args, bool programmatic, cudaStream_t stream) {
   if (args.head_dim != kDecodeDim || args.kv_heads <= 0 || args.query_heads % args.kv_heads != 0 ||
-      args.query_heads / args.kv_heads > kDecodeMaxGroup || args.context <= 0 || !valid_dtype(args.dtype)) {
+      args.query_heads / args.kv_heads > kDecodeMaxGroup || args.context <= 0 || !valid_dtype(args.dtype) ||
+      args.tickets == nullptr) {
     return cudaErrorInvalidValue;
   }
-  return args.dtype == kActFp16 ? attention_typed<__half>(args, stream)
-                                : attention_typed<__nv_bfloat16>(args, stream);
+  const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(args.head_dim));
+  const dim3 grid(kDecodeSplits, args.kv_heads);
+  return args.dtype == kActFp16
+             ? launch(decode_attention_kernel<__half>, grid, dim3(kDecodeThreads), 0, stream, programmatic, args,
+                      scale_log2)
+             : launch(decode_attention_kernel<__nv_bfloat16>, grid, dim3(kDecodeThreads), 0, stream, programmatic,
+                      args, scale_log2);
 }
 
 cudaError_t launch_store_kv(const void* qkv, int tokens, int query_heads, int kv_heads, int head_dim, void* k_cache,

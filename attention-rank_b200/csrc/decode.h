@@ -4,15 +4,19 @@
 // One token runs through every layer per step, so each projection is a matrix-vector product
 // that streams its 16-bit weight matrix from HBM exactly once. The reference runs these steps
 // through cuBLAS at m = 1 plus its elementwise kernels (model.cu:324-350); here each projection
-// is one bandwidth-bound kernel with its elementwise successor fused into the epilogue:
-//   q|k|v   + bias + RoPE + KV-cache append  (model.cu:367-392, scatter_kv_cache :426-440)
-//   gate|up + SiLU * up                      (model.cu:410-415)
-//   o_proj, down_proj                        plain, 16-bit out (the engine's RMSNorm kernel follows)
-//   lm_head                                  fp32 logits (model.cu:341-350)
-// Attention of the one query row over the cache is split over key ranges and combined (one CTA
-// per (split, KV head) serves every query head of the GQA group from one load of K and V).
+// is one bandwidth-bound kernel that also does the elementwise work around it:
+//   q|k|v   RMSNorm(residual + delta) prologue; bias + RoPE + KV-cache append epilogue
+//           (model.cu:367-392, scatter_kv_cache :426-440)
+//   o_proj  plain, 16-bit out
+//   gate|up RMSNorm(residual + delta) prologue; SiLU * up epilogue (model.cu:398-415)
+//   down    plain, 16-bit out
+//   lm_head final RMSNorm prologue; fp32 logits (model.cu:341-350), optionally the greedy pick
+// Attention of the one query row over the cache is split over key ranges; the last CTA of each
+// KV head merges the splits (one CTA per (split, KV head) serves every query head of the group).
 // Every launch reads the step's token and position from device memory (`state` = {token,
-// position}), so a captured CUDA graph of the whole step replays without host arguments.
+// position}), so a captured CUDA graph of the whole step replays without host arguments, and
+// every kernel waits for its producer with griddepcontrol.wait after issuing the loads that do
+// not depend on it (programmatic dependent launch).
 #pragma once
 
 #include <cuda_runtime.h>
@@ -21,25 +25,38 @@
 
 namespace arb {
 
-// Key-range splits of the decode attention per KV head (the combine step merges them).
+// Key-range splits of the decode attention per KV head.
 constexpr int kDecodeSplits = 32;
 // Largest GQA group (query heads per KV head) the decode attention handles.
 constexpr int kDecodeMaxGroup = 16;
+// Largest hidden size of the fused RMSNorm prologue (256 threads x 4 x 8 values).
+constexpr int kDecodeMaxNormHidden = 8192;
+// Per-CTA slots of the greedy pick (>= the largest logits grid).
+constexpr int kDecodePickSlots = 8192;
 
-// y[n] = w[n, :] . x for n < rows; w 16-bit [rows, k] row-major, x 16-bit [k], k % 8 == 0.
-// y is 16-bit (rounded once) or fp32 when f32_out.
-cudaError_t launch_decode_gemv(const void* w, const void* x, int rows, int k, void* y, bool f32_out, int dtype,
-                               cudaStream_t stream);
+enum DecodeGemvKind : int {
+  kDecodePlain = 0,   // y[n] = w[n] . x, 16-bit
+  kDecodeLogits = 1,  // y[n] = w[n] . x, fp32
+  kDecodeGateUp = 2,  // y[j] = silu(w[j] . x) * (w[inter + j] . x), 16-bit; rows = inter
+  kDecodeQkv = 3,     // q|k|v with bias, RoPE and the cache append; rows = (Hq + 2 Hkv) D
+};
 
-// act[j] = silu(g_j) * u_j, g_j = w[j] . x, u_j = w[inter + j] . x (the fused gate|up matrix
-// [2 inter, k]); g and u are rounded to 16 bits first, as the prefill's GEMM output is.
-cudaError_t launch_decode_gate_up(const void* w, const void* x, int inter, int k, void* act, int dtype,
-                                  cudaStream_t stream);
-
-struct DecodeQkvArgs {
-  const void* w = nullptr;          // 16-bit [(Hq + 2 Hkv) D, hidden]
-  const void* x = nullptr;          // 16-bit [hidden]
-  int hidden = 0;
+struct DecodeGemvArgs {
+  int kind = kDecodePlain;
+  const void* w = nullptr;  // 16-bit [rows (2 x inter for gate|up), k] row-major
+  int rows = 0;
+  int k = 0;                // % 8 == 0
+  // input: x (16-bit [k]), or -- when residual_in is set -- x = 16-bit(v * rsqrt(mean(v^2) + eps)
+  // * gamma) with v = residual_in + delta (delta nullable), the engine's RMSNorm with residual;
+  // CTA 0 then stores v into residual_out (nullable; must not alias residual_in)
+  const void* x = nullptr;
+  const float* residual_in = nullptr;
+  const void* delta = nullptr;
+  const float* gamma = nullptr;
+  float eps = 0.0f;
+  float* residual_out = nullptr;
+  void* y = nullptr;  // plain / logits / gate|up output
+  // kDecodeQkv
   const void* bias_half = nullptr;  // 16-bit bias added before rounding (the fp16 GEMM epilogue), or null
   const float* bias = nullptr;      // fp32 bias added after rounding (the bf16 path), or null
   int query_heads = 0;
@@ -48,15 +65,23 @@ struct DecodeQkvArgs {
   const float* cos_table = nullptr;  // [table_positions, D / 2]
   const float* sin_table = nullptr;
   int table_positions = 0;
-  const int32_t* state = nullptr;   // {token, position}
-  void* q_out = nullptr;            // 16-bit [Hq D], rotated
-  void* k_cache = nullptr;          // this layer's 16-bit [Hkv, context, D]; row `position` is written
+  void* q_out = nullptr;    // 16-bit [Hq D], rotated
+  void* k_cache = nullptr;  // this layer's 16-bit [Hkv, context, D]; row `position` is written
   void* v_cache = nullptr;
   int context = 0;
   int* status = nullptr;
+  // state = {token, position}: read by kDecodeQkv; with `pick` (kDecodeLogits), the first maximum
+  // of the logits (GreedySampler::select, model.cpp:70-73) is written as {index, position + 1}
+  int32_t* state = nullptr;
+  bool pick = false;
+  float* pick_values = nullptr;   // [kDecodePickSlots] scratch
+  int32_t* pick_indices = nullptr;
+  unsigned* ticket = nullptr;     // zero between launches
   int dtype = 1;
 };
-cudaError_t launch_decode_qkv(const DecodeQkvArgs& args, cudaStream_t stream);
+// `programmatic`: launched with programmatic stream serialization (it may start before its
+// predecessor on the stream ends; it waits for it before reading its outputs).
+cudaError_t launch_decode_gemv(const DecodeGemvArgs& args, bool programmatic, cudaStream_t stream);
 
 struct DecodeAttentionArgs {
   const void* q = nullptr;          // 16-bit [Hq D]
@@ -70,19 +95,18 @@ struct DecodeAttentionArgs {
   int sliding_window = 0;
   float* partials = nullptr;        // fp32 [Hq, kDecodeSplits, D]
   float* stats = nullptr;           // fp32 [Hq, kDecodeSplits, 2] (running max in log2 units, sum)
+  unsigned* tickets = nullptr;      // [Hkv], zero between launches
   void* out = nullptr;              // 16-bit [Hq D]
   int dtype = 1;
 };
-// Split attention followed by the combine step (two launches).
-cudaError_t launch_decode_attention(const DecodeAttentionArgs& args, cudaStream_t stream);
+cudaError_t launch_decode_attention(const DecodeAttentionArgs& args, bool programmatic, cudaStream_t stream);
 
 // K and V of a prefilled prompt (rows 0 .. tokens-1 of the q|k|v buffer, after RoPE) into the
 // cache at positions 0 .. tokens-1.
 cudaError_t launch_store_kv(const void* qkv, int tokens, int query_heads, int kv_heads, int head_dim, void* k_cache,
                             void* v_cache, int context, int dtype, cudaStream_t stream);
 
-// Greedy selection: the index of the first maximum of logits[0, count) (std::max_element
-// order, as GreedySampler::select, model.cpp:70-73). Writes state = {index, state[1] + 1}.
+// Greedy selection over logits[0, count) alone (std::max_element order): state = {index, state[1] + 1}.
 cudaError_t launch_argmax_token(const float* logits, int count, int32_t* state, cudaStream_t stream);
 
 }  // namespace arb

@@ -135,6 +135,9 @@ struct GenerationState {
   float* partials = nullptr;      // fp32 [Hq][kDecodeSplits][D]
   float* stats = nullptr;         // fp32 [Hq][kDecodeSplits][2]
   float* logits = nullptr;        // fp32 [vocab]
+  float* pick_values = nullptr;   // greedy pick: per-CTA candidates [kDecodePickSlots]
+  int32_t* pick_indices = nullptr;
+  unsigned* tickets = nullptr;    // [1 + Hkv]: the pick's and the attention's last-CTA counters
   int32_t* state = nullptr;       // device {token, position}
   int32_t* meta = nullptr;        // device: prompt tokens | offsets [2] | attention tiles
   size_t meta_capacity = 0;       // int32 elements of meta (and of the staging area behind the slots)
@@ -143,6 +146,7 @@ struct GenerationState {
   cudaEvent_t slot_ready[2] = {nullptr, nullptr};
   cudaGraphExec_t graphs[2] = {nullptr, nullptr};  // decode step: [0] logits only, [1] + greedy pick
   bool warmed[2] = {false, false};  // the first step of each kind runs eagerly, later ones replay
+  bool programmatic = true;       // decode kernels use programmatic dependent launch
   int position = -1;              // position of the next token fed; -1: no prompt
   ~GenerationState();
 };
@@ -216,6 +220,9 @@ class Engine {
   // Position the next decoded token takes (prompt length + tokens fed so far); -1 before a prompt.
   int generation_position() const;
   int generation_context() const { return options_.max_sequence_length; }
+  // Whether decode steps use programmatic dependent launch (after the first captured step: false
+  // when the graph could not be captured with it).
+  bool decode_programmatic() const;
 
   // Raw access for the kernel-level tests: the device buffers of the last batch.
   const void* qkv_buffer() const { return qkv_; }

@@ -15,6 +15,7 @@
 //     next step's token, so consecutive steps chain on the device; the host only reads each token
 //     back to test for eos, with the next step already queued behind it.
 #include <algorithm>
+#include <cstdlib>
 #include <string>
 
 #include "common.cuh"
@@ -78,6 +79,9 @@ void Engine::ensure_generation() {
   g->partials = static_cast<float*>(device_alloc(Hq * kDecodeSplits * D * 4));
   g->stats = static_cast<float*>(device_alloc(Hq * kDecodeSplits * 2 * 4));
   g->logits = static_cast<float*>(device_alloc(V * 4));
+  g->pick_values = static_cast<float*>(device_alloc(kDecodePickSlots * sizeof(float)));
+  g->pick_indices = static_cast<int32_t*>(device_alloc(kDecodePickSlots * sizeof(int32_t)));
+  g->tickets = static_cast<unsigned*>(device_alloc((1 + c.num_key_value_heads) * sizeof(unsigned)));
   g->state = static_cast<int32_t*>(device_alloc(4 * sizeof(int32_t)));
   g->meta_capacity = static_cast<size_t>(capacity_tokens_) + 2 + 2 * (capacity_tokens_ / kAttentionQueryTile + 1);
   g->meta = static_cast<int32_t*>(device_alloc(g->meta_capacity * 4));
@@ -87,8 +91,13 @@ void Engine::ensure_generation() {
   for (auto& event : g->slot_ready) {
     check_cuda(cudaEventCreateWithFlags(&event, cudaEventDisableTiming), "cudaEventCreate");
   }
+  // ATTNRANK_DECODE_PDL=0 launches the decode kernels without programmatic dependent launch
+  const char* pdl = std::getenv("ATTNRANK_DECODE_PDL");
+  g->programmatic = !(pdl != nullptr && pdl[0] == '0');
   generation_ = std::move(g);
 }
+
+bool Engine::decode_programmatic() const { return generation_ && generation_->programmatic; }
 
 void Engine::prefill_generation(int M) {
   const ModelConfig& c = config_;
@@ -146,8 +155,15 @@ void Engine::prefill_generation(int M) {
                "norm");
   }
   // normed_ holds final_norm(hidden); the logits of the last row (read_logits, model.cu:341-350)
-  const auto* last_row = static_cast<const uint16_t*>(normed_) + static_cast<size_t>(M - 1) * H;
-  check_cuda(launch_decode_gemv(output_head(), last_row, c.vocab_size, H, g.logits, true, dtype, stream_), "lm_head");
+  DecodeGemvArgs head;
+  head.kind = kDecodeLogits;
+  head.w = output_head();
+  head.rows = c.vocab_size;
+  head.k = H;
+  head.x = static_cast<const uint16_t*>(normed_) + static_cast<size_t>(M - 1) * H;
+  head.y = g.logits;
+  head.dtype = dtype;
+  check_cuda(launch_decode_gemv(head, false, stream_), "lm_head");
 }
 
 void Engine::launch_decode_step(bool greedy) {
@@ -156,12 +172,21 @@ void Engine::launch_decode_step(bool greedy) {
   const int H = c.hidden_size, I = c.intermediate_size, Hq = c.num_attention_heads, Hkv = c.num_key_value_heads;
   const int D = c.head_dim();
   const int dtype = options_.activation_dtype;
+  const bool pdl = g.programmatic;
+  // residual stream: two fp32 rows used in turn (a fused norm reads one and its CTA 0 writes the
+  // sum into the other); the two deltas are the o_proj and down_proj outputs
+  float* residual[2] = {residual_, residual_ + H};
+  int current = 0;
+  void* delta_attention = delta_;
+  void* delta_mlp = static_cast<uint16_t*>(delta_) + H;
   check_cuda(launch_embed_rms_norm(g.state, 1, embedding_, c.vocab_size, H, layers_[0].input_norm, c.rms_norm_eps,
-                                   residual_, normed_, status_, dtype, stream_),
+                                   residual[0], normed_, status_, dtype, stream_),
              "decode embedding");
-  DecodeQkvArgs qkv;
-  qkv.x = normed_;
-  qkv.hidden = H;
+  DecodeGemvArgs qkv;
+  qkv.kind = kDecodeQkv;
+  qkv.rows = c.qkv_width();
+  qkv.k = H;
+  qkv.eps = c.rms_norm_eps;
   qkv.query_heads = Hq;
   qkv.kv_heads = Hkv;
   qkv.head_dim = D;
@@ -183,13 +208,42 @@ void Engine::launch_decode_step(bool greedy) {
   attention.sliding_window = c.sliding_window;
   attention.partials = g.partials;
   attention.stats = g.stats;
+  attention.tickets = g.tickets + 1;
   attention.out = attn_;
   attention.dtype = dtype;
+  DecodeGemvArgs out_proj;
+  out_proj.kind = kDecodePlain;
+  out_proj.rows = H;
+  out_proj.k = Hq * D;
+  out_proj.x = attn_;
+  out_proj.y = delta_attention;
+  out_proj.dtype = dtype;
+  DecodeGemvArgs gate_up;
+  gate_up.kind = kDecodeGateUp;
+  gate_up.rows = I;
+  gate_up.k = H;
+  gate_up.eps = c.rms_norm_eps;
+  gate_up.delta = delta_attention;
+  gate_up.y = act_;
+  gate_up.dtype = dtype;
+  DecodeGemvArgs down;
+  down.kind = kDecodePlain;
+  down.rows = H;
+  down.k = I;
+  down.x = act_;
+  down.y = delta_mlp;
+  down.dtype = dtype;
   for (int l = 0; l < c.num_hidden_layers; ++l) {
     const LayerWeights& w = layers_[l];
     auto* k_layer = static_cast<uint16_t*>(g.k_cache) + static_cast<size_t>(l) * g.layer_elements;
     auto* v_layer = static_cast<uint16_t*>(g.v_cache) + static_cast<size_t>(l) * g.layer_elements;
+    // pre-attention norm fused into q|k|v (layer 0: the embedding row itself, no delta)
     qkv.w = w.qkv;
+    qkv.residual_in = residual[current];
+    qkv.delta = l == 0 ? nullptr : delta_mlp;
+    qkv.residual_out = l == 0 ? nullptr : residual[current ^ 1];
+    if (l > 0) current ^= 1;
+    qkv.gamma = w.input_norm;
     // the prefill's bias placement: fp16 adds its fp16 copy before rounding (GEMM epilogue),
     // bf16 adds the fp32 bias after rounding (RoPE kernel)
     const bool half_bias = dtype == kActFp16 && w.qkv_bias_half != nullptr;
@@ -197,22 +251,40 @@ void Engine::launch_decode_step(bool greedy) {
     qkv.bias = half_bias ? nullptr : w.qkv_bias;
     qkv.k_cache = k_layer;
     qkv.v_cache = v_layer;
-    check_cuda(launch_decode_qkv(qkv, stream_), "decode q|k|v");
+    check_cuda(launch_decode_gemv(qkv, pdl, stream_), "decode q|k|v");
     attention.k_cache = k_layer;
     attention.v_cache = v_layer;
-    check_cuda(launch_decode_attention(attention, stream_), "decode attention");
-    check_cuda(launch_decode_gemv(w.out, attn_, H, Hq * D, delta_, false, dtype, stream_), "decode o_proj");
-    check_cuda(launch_rms_norm_residual(residual_, delta_, w.post_norm, 1, H, c.rms_norm_eps, normed_, dtype, stream_),
-               "decode post-attention norm");
-    check_cuda(launch_decode_gate_up(w.gate_up, normed_, I, H, act_, dtype, stream_), "decode gate|up");
-    check_cuda(launch_decode_gemv(w.down, act_, H, I, delta_, false, dtype, stream_), "decode down_proj");
-    const float* next_norm = l + 1 < c.num_hidden_layers ? layers_[l + 1].input_norm : final_norm_;
-    check_cuda(launch_rms_norm_residual(residual_, delta_, next_norm, 1, H, c.rms_norm_eps, normed_, dtype, stream_),
-               "decode norm");
+    check_cuda(launch_decode_attention(attention, pdl, stream_), "decode attention");
+    out_proj.w = w.out;
+    check_cuda(launch_decode_gemv(out_proj, pdl, stream_), "decode o_proj");
+    // post-attention norm fused into gate|up
+    gate_up.w = w.gate_up;
+    gate_up.residual_in = residual[current];
+    gate_up.residual_out = residual[current ^ 1];
+    current ^= 1;
+    gate_up.gamma = w.post_norm;
+    check_cuda(launch_decode_gemv(gate_up, pdl, stream_), "decode gate|up");
+    down.w = w.down;
+    check_cuda(launch_decode_gemv(down, pdl, stream_), "decode down_proj");
   }
-  check_cuda(launch_decode_gemv(output_head(), normed_, c.vocab_size, H, g.logits, true, dtype, stream_),
-             "decode lm_head");
-  if (greedy) check_cuda(launch_argmax_token(g.logits, c.vocab_size, g.state, stream_), "greedy pick");
+  // final norm fused into lm_head; greedy: the first maximum becomes the next step's token
+  DecodeGemvArgs head;
+  head.kind = kDecodeLogits;
+  head.w = output_head();
+  head.rows = c.vocab_size;
+  head.k = H;
+  head.residual_in = residual[current];
+  head.delta = delta_mlp;
+  head.gamma = final_norm_;
+  head.eps = c.rms_norm_eps;
+  head.y = g.logits;
+  head.state = g.state;
+  head.pick = greedy;
+  head.pick_values = g.pick_values;
+  head.pick_indices = g.pick_indices;
+  head.ticket = g.tickets;
+  head.dtype = dtype;
+  check_cuda(launch_decode_gemv(head, pdl, stream_), "decode lm_head");
 }
 
 void Engine::run_decode_step(bool greedy) {
@@ -225,19 +297,28 @@ void Engine::run_decode_step(bool greedy) {
     g.warmed[kind] = true;
   } else {
     if (g.graphs[kind] == nullptr) {
-      cudaGraph_t graph = nullptr;
-      check_cuda(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeRelaxed), "decode capture");
-      try {
-        launch_decode_step(greedy);
-      } catch (...) {
-        cudaStreamEndCapture(stream_, &graph);
+      // programmatic edges in a captured graph need driver support: without it the capture is
+      // repeated with ordinary launches
+      for (int attempt = 0; attempt < 2 && g.graphs[kind] == nullptr; ++attempt) {
+        cudaGraph_t graph = nullptr;
+        check_cuda(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeRelaxed), "decode capture");
+        try {
+          launch_decode_step(greedy);
+        } catch (...) {
+          cudaStreamEndCapture(stream_, &graph);
+          if (graph != nullptr) cudaGraphDestroy(graph);
+          throw;
+        }
+        cudaError_t status = cudaStreamEndCapture(stream_, &graph);
+        if (status == cudaSuccess) status = cudaGraphInstantiate(&g.graphs[kind], graph, 0);
         if (graph != nullptr) cudaGraphDestroy(graph);
-        throw;
+        if (status != cudaSuccess) {
+          cudaGetLastError();
+          g.graphs[kind] = nullptr;
+          if (!g.programmatic || attempt == 1) check_cuda(status, "decode graph");
+          g.programmatic = false;
+        }
       }
-      check_cuda(cudaStreamEndCapture(stream_, &graph), "decode capture");
-      const cudaError_t status = cudaGraphInstantiate(&g.graphs[kind], graph, 0);
-      cudaGraphDestroy(graph);
-      check_cuda(status, "decode graph instantiate");
     }
     check_cuda(cudaGraphLaunch(g.graphs[kind], stream_), "decode graph launch");
   }
@@ -271,6 +352,8 @@ void Engine::begin_generation(const int32_t* prompt, int count) {
   }
   g.staging[kStateUpload] = 0;
   g.staging[kStateUpload + 1] = count - 1;  // the last prompt token's position
+  check_cuda(cudaMemsetAsync(g.tickets, 0, (1 + config_.num_key_value_heads) * sizeof(unsigned), stream_),
+             "ticket reset");
   check_cuda(cudaMemcpyAsync(g.meta, meta, static_cast<size_t>(count + 2 + 2 * tiles) * 4, cudaMemcpyHostToDevice,
                              stream_),
              "prompt upload");

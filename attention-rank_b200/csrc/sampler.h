@@ -2,10 +2,11 @@
 // (GreedySampler, NucleusSampler, make_sampler; attnrank/src/model.cpp:70-127).
 //
 // Selection runs on the host over fp32 logits, as in the reference, so that the same logits and
-// seed give the same token ids: the nucleus sampler orders candidates with std::partial_sort
-// under the same "larger logit first" predicate, weighs them in double precision, and draws from
-// std::mt19937_64 through std::uniform_real_distribution<double>. (The engine's greedy path does
-// not come through here: it takes the first maximum on the device.)
+// seed give the same token ids: the nucleus sampler weighs candidates in double precision in the
+// reference's order, draws from std::mt19937_64 through std::uniform_real_distribution<double>,
+// and where equal logits make the order matter, takes it from std::partial_sort under the
+// reference's "larger logit first" predicate. (The engine's greedy path does not come through
+// here: it takes the first maximum on the device.)
 #pragma once
 
 #include <cstdint>
@@ -43,9 +44,16 @@ class NucleusTokenSampler final : public TokenSampler {
   bool greedy() const override { return false; }
 
  private:
+  void sort_descending(const float* logits, int count);
+
   SamplerConfig config_;
   std::mt19937_64 random_;
-  std::vector<int> order_;       // candidate ids, reused between calls
+  // buffers reused between calls
+  std::vector<int> order_;            // ids by descending logit (ties: ascending id)
+  std::vector<uint32_t> keys_;        // their order keys
+  std::vector<int> spare_order_;
+  std::vector<uint32_t> spare_keys_;
+  std::vector<int> exact_;            // the reference's partial_sort order, built only on ties
   std::vector<double> weights_;
 };
 

@@ -267,12 +267,22 @@ def test_generation_stops(cuda):
     assert len(tokens) == 20
     assert engine.generate(prompt, max_new_tokens=0).generated_tokens == []
     assert engine.generate(prompt, max_new_tokens=1).generated_tokens == tokens[:1]
-    # eos ends generation without being returned
-    stop = next(i for i in range(1, 20) if tokens[i] not in tokens[:i])
-    engine.config.eos_token_id = tokens[stop]
-    assert engine.generate(prompt, max_new_tokens=50).generated_tokens == tokens[:stop]
+    # eos ends generation without being returned (greedy: on the device; sampled: on the host).
+    # Random weights often make greedy decoding repeat one token, so the sampled run supplies a
+    # token whose first appearance is not the first step.
     engine.config.eos_token_id = tokens[0]
     assert engine.generate(prompt, max_new_tokens=50).generated_tokens == []
+    sample = dict(temperature=1.5, top_p=1.0, top_k=0, seed=5)
+    engine.config.eos_token_id = -1
+    sampled = engine.generate(prompt, max_new_tokens=50, **sample).generated_tokens
+    assert len(sampled) == 20
+    stop = next(i for i in range(1, 20) if sampled[i] not in sampled[:i])
+    engine.config.eos_token_id = sampled[stop]
+    assert engine.generate(prompt, max_new_tokens=50, **sample).generated_tokens == sampled[:stop]
+    greedy_stop = next((i for i in range(1, 20) if tokens[i] not in tokens[:i]), None)
+    if greedy_stop is not None:
+        engine.config.eos_token_id = tokens[greedy_stop]
+        assert engine.generate(prompt, max_new_tokens=50).generated_tokens == tokens[:greedy_stop]
     engine.close()
 
 

@@ -88,3 +88,22 @@ def test_generate_needs_decode_for_stop_strings():
     settings = ar.GenerationSettings()
     assert (settings.max_new_tokens, settings.temperature, settings.top_p, settings.top_k, settings.seed) == \
         (128, 0.0, 0.9, 0, 1234)
+
+
+@pytest.mark.parametrize("temperature,top_p,top_k,quantum", [(0.7, 0.9, 0, 0.0), (1.0, 0.95, 0, 0.25),
+                                                              (0.5, 0.9, 50, 0.0), (1.3, 0.5, 0, 1.0)])
+def test_library_sampler_matches_reference_at_full_vocabulary(reference_lib, temperature, top_p, top_k, quantum):
+    """152064-wide logits (the Qwen vocabulary) against the reference's own sampler: the library's
+    radix-sorted fast path must give the same ids, with and without tied logits."""
+    if reference_lib is None:
+        pytest.skip("oracle/_ref is not built")
+    import attnrank as ar
+    from oracle import reference
+    rng = np.random.default_rng(int(temperature * 100) + top_k)
+    rows = rng.normal(0.0, 2.0, size=(6, 152064))
+    if quantum > 0.0:
+        rows = np.round(rows / quantum) * quantum
+    rows = rows.astype(np.float32)
+    want = reference.sample(rows, temperature, top_p, top_k, 2024)
+    sampler = ar.make_sampler(temperature, top_p, top_k, 2024)
+    assert [sampler.select(row) for row in rows] == want
