@@ -81,6 +81,9 @@ def parse_args():
     parser.add_argument("--dtype", choices=["fp16", "bf16"], default="fp16",
                         help="16-bit type of weights, GEMM operands and activations")
     parser.add_argument("--attention", choices=["tcgen05", "mma"], default="tcgen05")
+    parser.add_argument("--decode", action="store_true",
+                        help="decode tokens/s of greedy generation after one config-3 prompt (a separate line)")
+    parser.add_argument("--decode-tokens", type=int, default=256)
     parser.add_argument("--sweep", action="store_true",
                         help="only the fused-kernel bandwidth sweep of BASELINE config 5 (one GPU)")
     return parser.parse_args()
@@ -623,6 +626,190 @@ def run_reference(args, rank, world, local_rank):
     }
 
 
+# ---------------------------------------------------------------------------------------------
+# Decode (generation after reranking, the answering step of CudaLlamaModel::generate): one
+# prompt of the config-3 shape, greedy, a fixed number of new tokens (eos disabled). Decode does
+# not shard: with N GPUs every rank runs its own replica and `value` is the sum over replicas.
+DECODE_METRIC = "decode tokens/s (Qwen2.5-7B arch, greedy, one prompt)"
+
+
+def decode_bytes_per_token(config, context: int) -> float:
+    """Algorithmic HBM bytes of one decode step: every 16-bit weight matrix once (q|k|v, o, gate|up,
+    down per layer; the tied output head) plus the K and V rows of `context` cached positions."""
+    H, I, V = config.hidden_size, config.intermediate_size, config.vocab_size
+    D = H // config.num_attention_heads
+    qkv = (config.num_attention_heads + 2 * config.num_key_value_heads) * D
+    per_layer = (qkv * H + H * config.num_attention_heads * D + 2 * I * H + H * I) * 2
+    cache = 2 * config.num_key_value_heads * D * 2 * context
+    return config.num_hidden_layers * (per_layer + cache) + V * H * 2
+
+
+def decode_setup(args):
+    from attnrank import synthetic
+    config = synthetic.qwen2_7b()
+    config.tie_word_embeddings = True  # the reference harness ties the head to the embedding
+    prompt = list(synthetic.prompts(1, config.vocab_size, synthetic.QWEN_PROMPTS)[0].tokens)
+    return config, prompt
+
+
+def cpu_decode_baseline(config, context: int, layers: int = 2) -> dict:
+    """The decode step restated in fp32 torch on the host cores (q|k|v, RoPE-free attention over
+    `context` cached keys, o_proj, SwiGLU MLP per layer; the output head), timed on `layers`
+    layers plus the head and scaled to the full depth. Random weights: the time does not depend
+    on their values."""
+    import torch
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    H, I, V = config.hidden_size, config.intermediate_size, config.vocab_size
+    Hq, Hkv = config.num_attention_heads, config.num_key_value_heads
+    D = H // Hq
+    g = torch.Generator().manual_seed(0)
+    w_qkv = torch.randn((Hq + 2 * Hkv) * D, H, generator=g) * 0.02
+    w_o = torch.randn(H, Hq * D, generator=g) * 0.02
+    w_gu = torch.randn(2 * I, H, generator=g) * 0.02
+    w_d = torch.randn(H, I, generator=g) * 0.02
+    head = torch.randn(V, H, generator=g) * 0.02
+    keys = torch.randn(Hkv, context, D, generator=g)
+    values = torch.randn(Hkv, context, D, generator=g)
+    x = torch.randn(H, generator=g)
+
+    def layer(h):
+        n = h * torch.rsqrt(h.pow(2).mean() + 1e-6)
+        qkv = w_qkv @ n
+        q = qkv[:Hq * D].view(Hq, D)
+        scores = torch.einsum("hd,hkd->hk", q, keys.repeat_interleave(Hq // Hkv, dim=0)) / math.sqrt(D)
+        attn = torch.einsum("hk,hkd->hd", torch.softmax(scores, dim=-1), values.repeat_interleave(Hq // Hkv, dim=0))
+        h = h + w_o @ attn.reshape(-1)
+        n = h * torch.rsqrt(h.pow(2).mean() + 1e-6)
+        gu = w_gu @ n
+        return h + w_d @ (torch.nn.functional.silu(gu[:I]) * gu[I:])
+
+    layer(x)
+    start = time.perf_counter()
+    h = x
+    for _ in range(layers):
+        h = layer(h)
+    logits = head @ h
+    seconds_layers = time.perf_counter() - start
+    start = time.perf_counter()
+    head @ h
+    seconds_head = time.perf_counter() - start
+    per_token = (seconds_layers - seconds_head) * config.num_hidden_layers / layers + seconds_head
+    del logits
+    return {"value": round(1.0 / per_token, 4), "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{layers} of {config.num_hidden_layers} layers + the output head of one decode step over "
+                      f"{context} cached keys, fp32 torch on the host, scaled to all layers"}
+
+
+def run_decode(args, rank, world, local_rank):
+    import torch
+    import attnrank as ar
+    config, prompt = decode_setup(args)
+    new = args.decode_tokens
+    engine = ar.Engine.synthetic(config, seed=0, options=ar.RuntimeOptions(device_index=local_rank,
+                                                                            max_sequence_length=4096))
+    engine.config.eos_token_id = -1  # a fixed number of new tokens
+    stream = torch.cuda.ExternalStream(engine.stream, device=torch.device("cuda", local_rank))
+    for _ in range(max(args.warmup, 1)):
+        engine.generate(prompt, max_new_tokens=new)
+    torch.cuda.synchronize(local_rank)
+    barrier(world)
+
+    def timed(tokens):
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        wall = time.perf_counter()
+        result = engine.generate(prompt, max_new_tokens=tokens)
+        stop.record(stream)
+        stop.synchronize()
+        return start.elapsed_time(stop) / 1000.0, time.perf_counter() - wall, result
+
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    full, first, walls, results = [], [], [], None
+    for _ in range(args.steps):
+        seconds, wall, results = timed(new)
+        full.append(seconds)
+        walls.append(wall)
+        first.append(timed(1)[0])
+    clocks = sampler.stop()
+    full_s = max_over_ranks(statistics.median(full), world)
+    first_s = max_over_ranks(statistics.median(first), world)
+    wall_s = max_over_ranks(statistics.median(walls), world)
+    per_token = (full_s - first_s) / (new - 1)
+    peak, kind = peaks()
+    hbm = peak.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+    context = len(prompt) + new // 2
+    traffic = decode_bytes_per_token(config, context)
+    achieved = traffic / per_token / 1e9
+    result = {
+        "metric": DECODE_METRIC, "value": round(world / per_token, 2), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_token": round(per_token * 1000, 4),
+        "ms_per_step": round(full_s * 1000, 3), "higher_is_better": True,
+        "scaling": "weak (replicas only: one prompt's decode does not shard)", "vs_baseline": None, "dtype": "fp16",
+        "data": "synthetic (seeded random-init weights, seeded random token-id prompt)",
+        "config": {"workload": f"greedy generate of {new} new tokens after one {len(prompt)}-token prompt "
+                               "(config-3 shape), Qwen2.5-7B architecture, tied output head, eos disabled; "
+                               "value = decode steps only: (T(generate N) - T(generate 1)) / (N - 1)",
+                   "global_batch": 1, "seq_len": len(prompt) + new, "parallelism": f"{world} replica(s)",
+                   "l2": "weights (14 GB) exceed L2 on every step: no flush needed"},
+        "prefill_and_first_token_ms": round(first_s * 1000, 3),
+        "e2e": {"value": round(world * new / wall_s, 2), "unit": "tokens/s (generate call, prefill included)",
+                "h2d_bytes_per_step": 4 * len(prompt) + 8, "d2h_bytes_per_step": 8 * new},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "traffic": None,
+                     "per_token_bytes": traffic,
+                     "note": f"whole decode step (all kernels) against the {kind} copy bandwidth"},
+        "clocks": clocks,
+        "gpu_launches": args.steps * (2 + 5 * config.num_hidden_layers) * (new - 1),
+        "programmatic_launch": engine.decode_programmatic,
+        "tokens_head": results.generated_tokens[:8] if results else None,
+    }
+    engine.close()
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_decode_baseline(config, context)
+    return result
+
+
+def run_decode_reference(args, rank, world, local_rank):
+    from oracle import reference
+    if reference.load_or_none() is None:
+        return {"impl": "reference", "unavailable": "oracle/_ref/libattnrank_ref.so was not built (make -C oracle reference)"}
+    config, prompt = decode_setup(args)
+    new = args.decode_tokens
+    model = reference.ReferenceModel(config, seed=0, max_sequence_length=4096, device=local_rank)
+    for _ in range(max(args.warmup, 1)):
+        model.generate(prompt, max_new_tokens=min(new, 16))
+    full, first = [], []
+    tokens = None
+    for _ in range(args.steps):
+        tokens, seconds = model.generate(prompt, max_new_tokens=new)
+        full.append(seconds)
+        first.append(model.generate(prompt, max_new_tokens=1)[1])
+    model.close()
+    full_s = max_over_ranks(statistics.median(full), world)
+    first_s = max_over_ranks(statistics.median(first), world)
+    per_token = (full_s - first_s) / (new - 1)
+    value = world / per_token
+    return {
+        "metric": DECODE_METRIC, "impl": "reference", "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_token": round(per_token * 1000, 4),
+        "ms_per_step": round(full_s * 1000, 3), "higher_is_better": True, "scaling": "weak (replicas only)",
+        "vs_baseline": None, "dtype": "fp16/fp32",
+        "data": "synthetic (seeded random-init weights, seeded random token-id prompt)",
+        "config": {"workload": f"reference CudaLlamaModel::generate, greedy, {new} new tokens after the same "
+                               f"{len(prompt)}-token prompt (eos 2 never met in this run: "
+                               f"{len(tokens) if tokens is not None else 0} tokens)",
+                   "global_batch": 1, "parallelism": f"{world} replica(s)"},
+        "prefill_and_first_token_ms": round(first_s * 1000, 3),
+        "tokens_head": tokens[:8] if tokens else None,
+        "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": os.cpu_count() or 1,
+                         "kind": "reference", "sample": "the reference's path is CUDA: wall clock around its "
+                                                        "synchronous generate"},
+        "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
 def main():
     args = parse_args()
     rank, world, local_rank = init_distributed(args)
@@ -639,6 +826,8 @@ def main():
                                               peak.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]),
                                               tokens=args.kernel_tokens, dtype=args.dtype),
                   "kernels_peak_source": f"{kind} hbm_gbs / bf16_tflops (burst)", "tokens": args.kernel_tokens}
+    elif args.decode:
+        result = (run_decode_reference if args.impl == "reference" else run_decode)(args, rank, world, local_rank)
     elif args.impl == "reference":
         result = run_reference(args, rank, world, local_rank)
     else:

@@ -15,6 +15,7 @@
 //   * its generate (model.cu:532-565), the answering step, with the reference's samplers;
 //   * the reference's host functions (profile, basin statistics, position order, the samplers of
 //     model.cpp:70-127), which run without a GPU and produce the golden fixtures under tests/golden/.
+#include <algorithm>
 #include <chrono>
 #include <cstdint>
 #include <cstring>
@@ -332,6 +333,35 @@ int ref_generate(void* handle, const int32_t* prompt, int prompt_count, int max_
     for (size_t i = 0; i < result.generated_tokens.size(); ++i) tokens_out[i] = result.generated_tokens[i];
     *token_count_out = static_cast<int>(result.generated_tokens.size());
     if (seconds_out) *seconds_out = std::chrono::duration<double>(stop - start).count();
+    return 0;
+  } catch (const std::exception& error) {
+    g_error = error.what();
+    return 1;
+  }
+}
+
+// The logits the reference's generate hands its sampler after the prefill (model.cu:541-542,
+// read_logits :341-350): a sampler that records them, run for one new token.
+namespace {
+class RecordingSampler : public ISampler {
+ public:
+  int select(const std::vector<float>& logits) override {
+    recorded = logits;
+    return GreedySampler().select(logits);
+  }
+  std::vector<float> recorded;
+};
+}  // namespace
+
+int ref_prefill_logits(void* handle, const int32_t* prompt, int prompt_count, float* logits_out) {
+  try {
+    auto* holder = static_cast<Holder*>(handle);
+    GenerationRequest request;
+    request.prompt_tokens.assign(prompt, prompt + prompt_count);
+    request.max_new_tokens = 1;
+    RecordingSampler sampler;
+    holder->shared->generate(request, sampler);
+    std::copy(sampler.recorded.begin(), sampler.recorded.end(), logits_out);
     return 0;
   } catch (const std::exception& error) {
     g_error = error.what();

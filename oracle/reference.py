@@ -54,6 +54,7 @@ def load_or_none():
     lib.ref_resolve_position_order.argtypes = [P, I, I, P]
     lib.ref_generate.argtypes = [P, P, I, I, ctypes.c_float, ctypes.c_float, I, ctypes.c_uint64, P, P, P]
     lib.ref_sample.argtypes = [ctypes.c_float, ctypes.c_float, I, ctypes.c_uint64, P, I, I, P]
+    lib.ref_prefill_logits.argtypes = [P, P, I, P]
     _lib = lib
     return lib
 
@@ -148,6 +149,16 @@ class ReferenceModel:
                             seed, out.ctypes.data, ctypes.byref(count), ctypes.byref(seconds)) != 0:
             raise RuntimeError(lib.ref_last_error().decode())
         return [int(t) for t in out[:count.value]], seconds.value
+
+
+    def prefill_logits(self, prompt_tokens, vocab_size: int) -> np.ndarray:
+        """The fp32 logits the reference's generate gives its sampler after prefilling the prompt."""
+        lib = _require()
+        tokens = np.ascontiguousarray(np.asarray(prompt_tokens, dtype=np.int32))
+        out = np.zeros(vocab_size, dtype=np.float32)
+        if lib.ref_prefill_logits(self.handle, tokens.ctypes.data, tokens.size, out.ctypes.data) != 0:
+            raise RuntimeError(lib.ref_last_error().decode())
+        return out
 
 
 @dataclass
