@@ -84,6 +84,8 @@ def parse_args():
     parser.add_argument("--decode", action="store_true",
                         help="decode tokens/s of greedy generation after one config-3 prompt (a separate line)")
     parser.add_argument("--decode-tokens", type=int, default=256)
+    parser.add_argument("--decode-layers", type=int, default=None,
+                        help="decode on the first N layers only (a small case for ncu captures; not a bench line)")
     parser.add_argument("--sweep", action="store_true",
                         help="only the fused-kernel bandwidth sweep of BASELINE config 5 (one GPU)")
     return parser.parse_args()
@@ -648,6 +650,8 @@ def decode_setup(args):
     from attnrank import synthetic
     config = synthetic.qwen2_7b()
     config.tie_word_embeddings = True  # the reference harness ties the head to the embedding
+    if getattr(args, "decode_layers", None):
+        config.num_hidden_layers = args.decode_layers
     prompt = list(synthetic.prompts(1, config.vocab_size, synthetic.QWEN_PROMPTS)[0].tokens)
     return config, prompt
 
