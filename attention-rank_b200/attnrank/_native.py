@@ -152,7 +152,19 @@ _RESTYPES = {
 }
 
 
+def _load_cublas_once() -> None:
+    """One process must hold one cuBLAS. When PyTorch is installed, its bundled cuBLAS and cuBLASLt
+    are loaded first, so that this library's libcublasLt.so.12 resolves to that same copy: the
+    dynamic linker reuses a loaded soname, and a CUDA-toolkit cuBLASLt of another version loaded
+    first under the same name makes torch's own cuBLAS calls fail (CUBLAS_STATUS_INVALID_VALUE)."""
+    try:
+        import torch  # noqa: F401
+    except ImportError:
+        pass
+
+
 def _load() -> ctypes.CDLL:
+    _load_cublas_once()
     if not LIBRARY_PATH.exists():
         raise ImportError(
             f"{LIBRARY_PATH.name} is not built; run `make -C attention-rank_b200/csrc` "

@@ -20,6 +20,7 @@ namespace {
 
 constexpr int kRowThreadsCap = 256;
 constexpr int kRopeUnroll = 4;       // heads loaded per rotary step (loads in flight per thread)
+constexpr int kRopeGroupHeads = 8;   // heads of one rotary work item
 constexpr int kSiluUnroll = 2;   // 8-value chunks in flight per SwiGLU thread
 
 // ---------------------------------------------------------------------------------------------
@@ -130,9 +131,11 @@ __global__ void __launch_bounds__(kRowThreadsCap) rms_norm_residual_kernel(
 
 // ---------------------------------------------------------------------------------------------
 // Bias + rotary embedding, in place on the fused [tokens, (Hq + 2 Hkv) * D] projection output.
-// One thread owns 8 rotation pairs (x_i, x_{i + D/2}) at one offset of one token and walks all of
-// that token's heads, so its cos/sin values are loaded once (not once per head, which made the
-// kernel L1-bound); kRopeUnroll heads are loaded before any is stored. Query and key heads get
+// A work item is 8 rotation pairs (x_i, x_{i + D/2}) at one offset of one token over a group of
+// kRopeGroupHeads heads, so its cos/sin values are loaded once per group (not once per head, which
+// made the kernel L1-bound), and there are enough items for one resident wave of threads to share
+// them evenly (all heads in one item left most threads with one item and some with two);
+// kRopeUnroll heads are loaded before any is stored. Query and key heads get
 // bias + rotation; value heads get the bias only (and are skipped without bias). The engine
 // applies the bias in the q|k|v GEMM epilogue and passes none.
 // ---------------------------------------------------------------------------------------------
@@ -147,16 +150,21 @@ __global__ void __launch_bounds__(256, kBias ? 2 : 3) rotary_bias_kernel(T* __re
   const int rotated_heads = query_heads + kv_heads;
   const int heads = kBias ? rotated_heads + kv_heads : rotated_heads;
   const int row_width = (query_heads + 2 * kv_heads) * head_dim;
-  const int total = tokens * chunks_per_head;  // < 2^31: the launcher bounds tokens
+  const int groups = (heads + kRopeGroupHeads - 1) / kRopeGroupHeads;
+  const int total = tokens * groups * chunks_per_head;  // < 2^31: the launcher bounds tokens
   for (int item = blockIdx.x * blockDim.x + threadIdx.x; item < total; item += gridDim.x * blockDim.x) {
-    const int token = item / chunks_per_head;
-    const int chunk = item - token * chunks_per_head;
+    const int chunk = item % chunks_per_head;
+    const int rest = item / chunks_per_head;
+    const int group = rest % groups;
+    const int token = rest / groups;
+    const int group_first = group * kRopeGroupHeads;
+    const int group_end = min(group_first + kRopeGroupHeads, heads);
     const int position = positions[token];
     const bool in_table = position >= 0 && position < table_positions;
     if (!in_table) report_status(status, kStatusPositionOutOfRange);
     float c[8];
     float s[8];
-    if (in_table) {
+    if (in_table && group_first < rotated_heads) {
       const float* cos_row = cos_table + static_cast<size_t>(position) * half + chunk * 8;
       const float* sin_row = sin_table + static_cast<size_t>(position) * half + chunk * 8;
       const float4 c0 = __ldg(reinterpret_cast<const float4*>(cos_row));
@@ -167,14 +175,14 @@ __global__ void __launch_bounds__(256, kBias ? 2 : 3) rotary_bias_kernel(T* __re
       s[0] = s0.x; s[1] = s0.y; s[2] = s0.z; s[3] = s0.w; s[4] = s1.x; s[5] = s1.y; s[6] = s1.z; s[7] = s1.w;
     }
     // without a valid position only the bias-only value heads are written
-    const int first_head = in_table ? 0 : rotated_heads;
+    const int first_head = in_table ? group_first : max(group_first, rotated_heads);
     T* row = qkv + static_cast<size_t>(token) * row_width + chunk * 8;
-    for (int h0 = first_head; h0 < heads; h0 += kRopeUnroll) {
+    for (int h0 = first_head; h0 < group_end; h0 += kRopeUnroll) {
       uint4 low_raw[kRopeUnroll];
       uint4 high_raw[kRopeUnroll];
 #pragma unroll
       for (int u = 0; u < kRopeUnroll; ++u) {
-        if (h0 + u < heads) {
+        if (h0 + u < group_end) {
           low_raw[u] = *reinterpret_cast<const uint4*>(row + (h0 + u) * head_dim);
           high_raw[u] = *reinterpret_cast<const uint4*>(row + (h0 + u) * head_dim + half);
         }
@@ -182,7 +190,7 @@ __global__ void __launch_bounds__(256, kBias ? 2 : 3) rotary_bias_kernel(T* __re
 #pragma unroll
       for (int u = 0; u < kRopeUnroll; ++u) {
         const int head = h0 + u;
-        if (head >= heads) break;
+        if (head >= group_end) break;
         float low[8];
         float high[8];
         unpack8<T>(low_raw[u], low);
@@ -397,11 +405,12 @@ cudaError_t launch_rotary_bias(void* qkv, const float* bias, const int32_t* posi
                                cudaStream_t stream) {
   if (tokens <= 0) return cudaSuccess;
   if (head_dim % 16 != 0 || head_dim > 1024 || tokens > (1 << 24)) return cudaErrorInvalidValue;
-  const int items = tokens * (head_dim / 16);
+  const int heads = query_heads + kv_heads + (bias != nullptr ? kv_heads : 0);
+  const int items = tokens * ((heads + kRopeGroupHeads - 1) / kRopeGroupHeads) * (head_dim / 16);
   const int threads = 256;
   if (dtype != kActFp16 && dtype != kActBf16) return cudaErrorInvalidValue;
   auto launch = [&](auto kernel, auto* data) {
-    // one wave of resident CTAs walks all (token, chunk) items (no tail wave)
+    // one wave of resident CTAs walks all (token, head group, chunk) items (no tail wave)
     const int per_sm = resident_per_sm(kernel, threads);
     const int grid = std::max(1, std::min((items + threads - 1) / threads, sm_count() * per_sm));
     kernel<<<grid, threads, 0, stream>>>(data, bias, positions, tokens, query_heads, kv_heads, head_dim, cos_table,

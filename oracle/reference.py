@@ -38,6 +38,10 @@ def load_or_none():
         return _lib
     if not LIBRARY.exists():
         return None
+    try:  # one cuBLAS per process: PyTorch's copy first, which the reference's libcublas.so.12 then reuses
+        import torch  # noqa: F401
+    except ImportError:
+        pass
     lib = ctypes.CDLL(str(LIBRARY))
     P, I, I64, D = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_double
     lib.ref_last_error.restype = ctypes.c_char_p
