@@ -658,22 +658,36 @@ bool Engine::gemm(const void* x, const void* w, void* y, int m, int n, int k, co
   return plan.bias;
 }
 
+// Consecutive prompts into batches of at most capacity_tokens_ tokens and max_batch_prompts
+// prompts. The batch count is the smallest those limits allow (the greedy fill's), and each batch
+// closes near an equal share of the tokens, so a scan shard does not end on a sliver of a batch
+// that runs its GEMMs at a fraction of their rate.
 std::vector<Engine::Batch> Engine::plan_batches(const std::vector<PromptView>& prompts) const {
-  std::vector<Batch> batches;
-  Batch current;
-  for (int i = 0; i < static_cast<int>(prompts.size()); ++i) {
-    const int tokens = prompts[i].token_count;
-    if (current.count > 0 &&
-        (current.tokens + tokens > capacity_tokens_ || current.count + 1 > options_.max_batch_prompts)) {
-      batches.push_back(current);
-      current = Batch{};
+  auto greedy = [&](double target) {
+    std::vector<Batch> batches;
+    Batch current;
+    for (int i = 0; i < static_cast<int>(prompts.size()); ++i) {
+      const int tokens = prompts[i].token_count;
+      const bool full = current.tokens + tokens > capacity_tokens_ || current.count + 1 > options_.max_batch_prompts;
+      // past the share: close here if that leaves the batch nearer to it than taking the prompt
+      const bool past_share = current.tokens + 0.5 * tokens > target;
+      if (current.count > 0 && (full || past_share)) {
+        batches.push_back(current);
+        current = Batch{};
+      }
+      if (current.count == 0) current.first = i;
+      current.count += 1;
+      current.tokens += tokens;
     }
-    if (current.count == 0) current.first = i;
-    current.count += 1;
-    current.tokens += tokens;
-  }
-  if (current.count > 0) batches.push_back(current);
-  return batches;
+    if (current.count > 0) batches.push_back(current);
+    return batches;
+  };
+  std::vector<Batch> batches = greedy(static_cast<double>(capacity_tokens_) + 1.0);
+  if (batches.size() < 2) return batches;
+  double total = 0.0;
+  for (const PromptView& p : prompts) total += p.token_count;
+  std::vector<Batch> balanced = greedy(total / static_cast<double>(batches.size()));
+  return balanced.size() <= batches.size() ? balanced : batches;
 }
 
 void Engine::ensure_partials(size_t items, int span_count, int layers) {

@@ -618,8 +618,8 @@ def run_reference(args, rank, world, local_rank):
         "data": "synthetic (seeded random-init weights, seeded random token-id prompts)",
         "config": {"workload": spec["text"].format(n=sample) + "; reference CudaLlamaModel + "
                                "AttentionLayerScanner (stock path)",
-                   "global_batch": sample, "parallelism": f"{world} independent processes on "
-                   "prompt shards (the reference's multi-GPU practice)"},
+                   "global_batch": sample, "parallelism": "one GPU (rank 0 under torchrun): the reference has "
+                   "no multi-GPU path"},
         "selected_layer": result.selected_layer if result else None,
         "cpu_baseline": {"value": round(value, 3), "unit": "prompts/s", "cores": cores, "kind": "reference",
                          "sample": f"first {sample} of the {spec['prompts']} prompts per step; the reference's "
@@ -816,6 +816,20 @@ def run_decode_reference(args, rank, world, local_rank):
 
 def main():
     args = parse_args()
+    if args.impl == "reference":
+        # The reference has no multi-GPU path (README.md:17, :149): under torchrun rank 0 alone runs
+        # it on its GPU and prints the line; the other ranks exit 0 without work.
+        rank = int(os.environ.get("RANK", "0"))
+        if rank != 0:
+            return
+        local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        import torch
+        torch.cuda.set_device(local_rank)
+        result = (run_decode_reference if args.decode else run_reference)(args, 0, 1, local_rank)
+        result["n_gpus"] = int(os.environ.get("WORLD_SIZE", "1"))
+        result["reference_gpus_used"] = 1
+        print(json.dumps(result), flush=True)
+        return
     rank, world, local_rank = init_distributed(args)
     if args.sweep:
         peak, kind = peaks()
@@ -831,9 +845,7 @@ def main():
                                               tokens=args.kernel_tokens, dtype=args.dtype),
                   "kernels_peak_source": f"{kind} hbm_gbs / bf16_tflops (burst)", "tokens": args.kernel_tokens}
     elif args.decode:
-        result = (run_decode_reference if args.impl == "reference" else run_decode)(args, rank, world, local_rank)
-    elif args.impl == "reference":
-        result = run_reference(args, rank, world, local_rank)
+        result = run_decode(args, rank, world, local_rank)
     else:
         result = run_b200(args, rank, world, local_rank)
     if rank == 0:
