@@ -814,8 +814,19 @@ def run_decode_reference(args, rank, world, local_rank):
     }
 
 
+def emit(line: dict, out) -> None:
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
 def main():
     args = parse_args()
+    # stdout carries exactly one JSON line. Whatever a library prints there (NCCL's version
+    # banner, for one) goes to stderr: file descriptor 1 points at stderr for the whole run, and
+    # the JSON line is written through a saved copy of the original stdout.
+    sys.stdout.flush()
+    out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     if args.impl == "reference":
         # The reference has no multi-GPU path (README.md:17, :149): under torchrun rank 0 alone runs
         # it on its GPU and prints the line; the other ranks exit 0 without work.
@@ -828,7 +839,7 @@ def main():
         result = (run_decode_reference if args.decode else run_reference)(args, 0, 1, local_rank)
         result["n_gpus"] = int(os.environ.get("WORLD_SIZE", "1"))
         result["reference_gpus_used"] = 1
-        print(json.dumps(result), flush=True)
+        emit(result, out)
         return
     rank, world, local_rank = init_distributed(args)
     if args.sweep:
@@ -849,7 +860,7 @@ def main():
     else:
         result = run_b200(args, rank, world, local_rank)
     if rank == 0:
-        print(json.dumps(result), flush=True)
+        emit(result, out)
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
