@@ -126,7 +126,7 @@ SIGNATURES: dict[str, list] = {
     "ar_engine_generation_begin": [_P, _P, _I, _P],
     "ar_engine_generation_step": [_P, ctypes.c_int32, _P],
     "ar_engine_generation_position": [_P],
-    "ar_engine_decode_programmatic": [_P],
+    "ar_engine_decode_mode": [_P],
     "ar_sampler_create": [ctypes.POINTER(SamplerConfigStruct), ctypes.POINTER(_P)],
     "ar_sampler_select": [_P, _P, _I, _P],
     "ar_sampler_destroy": [_P],

@@ -687,9 +687,10 @@ class Engine:
         return int(lib.ar_engine_generation_position(self._handle))
 
     @property
-    def decode_programmatic(self) -> bool:
-        """Additive: whether decode steps use programmatic dependent launch."""
-        return bool(lib.ar_engine_decode_programmatic(self._handle))
+    def decode_mode(self) -> str:
+        """Additive: how decode steps run ("persistent", "programmatic", "serialised", or "" before
+        the first generation)."""
+        return {2: "persistent", 1: "programmatic", 0: "serialised"}.get(int(lib.ar_engine_decode_mode(self._handle)), "")
 
     def prepare_scan(self, prompts: Sequence[StructuredPrompt], layer_begin: int = 0, layer_end: int = -1,
                      normalize_by_length: bool = False) -> "PreparedScan":

@@ -563,9 +563,7 @@ int ar_engine_generation_position(ar_engine* engine) {
   return engine ? engine->engine->generation_position() : -1;
 }
 
-int ar_engine_decode_programmatic(ar_engine* engine) {
-  return engine != nullptr && engine->engine->decode_programmatic() ? 1 : 0;
-}
+int ar_engine_decode_mode(ar_engine* engine) { return engine != nullptr ? engine->engine->decode_mode() : -1; }
 
 int ar_sampler_create(const ar_sampler_config* config, ar_sampler** sampler) {
   return guarded([&] {

@@ -110,11 +110,13 @@ __device__ __forceinline__ void item_rows(const DecodeGemvArgs& a, int item, int
 }
 
 // x into shared memory: copied, or built by the RMSNorm prologue (the formula of the engine's
-// rms_norm_residual_kernel: v = residual + delta, y = v * rsqrt(sum(v^2) / k + eps) * gamma).
+// rms_norm_residual_kernel: v = residual + delta, y = v * rsqrt(sum(v^2) / k + eps) * gamma), where
+// v may also be the embedding row of the step's token (embed_rms_norm_kernel's formula; an id out
+// of range gives a zero row and a status, as there). Block 0 keeps v in residual_out.
 template <typename T>
-__device__ __forceinline__ void stage_x(const DecodeGemvArgs& a, uint4* xs, float* scratch) {
+__device__ __forceinline__ void stage_x(const DecodeGemvArgs& a, uint4* xs, float* scratch, int block) {
   const int chunks = a.k >> 3;
-  if (a.residual_in == nullptr) {
+  if (a.residual_in == nullptr && a.embed_table == nullptr) {
     const T* x = static_cast<const T*>(a.x);
     for (int i = threadIdx.x; i < chunks; i += kGemvThreads) {
       xs[i] = __ldcg(reinterpret_cast<const uint4*>(x + 8 * static_cast<size_t>(i)));
@@ -123,12 +125,28 @@ __device__ __forceinline__ void stage_x(const DecodeGemvArgs& a, uint4* xs, floa
     return;
   }
   const T* delta = static_cast<const T*>(a.delta);
+  const T* embedded = nullptr;
+  if (a.embed_table != nullptr) {
+    const int token = __ldcg(a.state);
+    if (token >= 0 && token < a.vocab) {
+      embedded = static_cast<const T*>(a.embed_table) + static_cast<size_t>(token) * a.k;
+    } else if (block == 0 && threadIdx.x == 0) {
+      report_status(a.status, kStatusTokenOutOfRange);
+    }
+  }
   float values[kNormVpt][8];
   float squares = 0.0f;
 #pragma unroll
   for (int v = 0; v < kNormVpt; ++v) {
     const int chunk = threadIdx.x + v * kGemvThreads;
-    if (chunk < chunks) {
+    if (chunk < chunks && a.embed_table != nullptr) {
+      if (embedded != nullptr) {
+        unpack8<T>(load_nc(embedded + 8 * chunk), values[v]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) values[v][i] = 0.0f;
+      }
+    } else if (chunk < chunks) {
       const float4 r0 = __ldcg(reinterpret_cast<const float4*>(a.residual_in + 8 * chunk));
       const float4 r1 = __ldcg(reinterpret_cast<const float4*>(a.residual_in + 8 * chunk + 4));
       float d[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
@@ -150,7 +168,7 @@ __device__ __forceinline__ void stage_x(const DecodeGemvArgs& a, uint4* xs, floa
   }
   const float total = block_sum(squares, scratch);
   const float scale = rsqrtf(total / static_cast<float>(a.k) + a.eps);
-  const bool keep = a.residual_out != nullptr && blockIdx.x == 0;
+  const bool keep = a.residual_out != nullptr && block == 0;
 #pragma unroll
   for (int v = 0; v < kNormVpt; ++v) {
     const int chunk = threadIdx.x + v * kGemvThreads;
@@ -335,15 +353,12 @@ __device__ __forceinline__ void finish_qkv(const DecodeGemvArgs& a, int item, in
   }
 }
 
-// The CTA's best (value, index) into its slot; the last CTA to finish reduces the slots into
-// state = {index, position + 1}. No CTA waits for another: the last one is found by a ticket.
-__device__ void finish_pick(const DecodeGemvArgs& a, float best, int best_at) {
+// The CTA's first maximum (lane 0 of every warp holds a candidate) into pick slot `block`.
+__device__ void pick_slot(const DecodeGemvArgs& a, float best, int best_at, int block) {
   __shared__ float values[kGemvWarps];
   __shared__ int indices[kGemvWarps];
-  __shared__ bool last;
   const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  if (lane == 0) {
+  if ((threadIdx.x & 31) == 0) {
     values[warp] = best;
     indices[warp] = best_at;
   }
@@ -357,17 +372,21 @@ __device__ void finish_pick(const DecodeGemvArgs& a, float best, int best_at) {
         at = indices[w];
       }
     }
-    a.pick_values[blockIdx.x] = v;
-    a.pick_indices[blockIdx.x] = at;
-    __threadfence();
-    last = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
+    a.pick_values[block] = v;
+    a.pick_indices[block] = at;
   }
   __syncthreads();
-  if (!last) return;
-  __threadfence();
+}
+
+// One CTA reduces pick slots [0, slots) into state = {first maximum, position + 1}.
+__device__ void reduce_pick(const DecodeGemvArgs& a, int slots) {
+  __shared__ float values[kGemvWarps];
+  __shared__ int indices[kGemvWarps];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
   float v = -INFINITY;
   int at = INT_MAX;
-  for (int s = threadIdx.x; s < static_cast<int>(gridDim.x); s += kGemvThreads) {
+  for (int s = threadIdx.x; s < slots; s += kGemvThreads) {
     const float sv = __ldcg(a.pick_values + s);
     const int si = __ldcg(a.pick_indices + s);
     if (better(sv, si, v, at)) {
@@ -384,7 +403,6 @@ __device__ void finish_pick(const DecodeGemvArgs& a, float best, int best_at) {
       at = oi;
     }
   }
-  __syncthreads();  // values / indices reused
   if (lane == 0) {
     values[warp] = v;
     indices[warp] = at;
@@ -399,12 +417,52 @@ __device__ void finish_pick(const DecodeGemvArgs& a, float best, int best_at) {
     }
     a.state[0] = indices[0] == INT_MAX ? 0 : indices[0];
     a.state[1] = a.state[1] + 1;
-    *a.ticket = 0u;
+  }
+  __syncthreads();
+}
+
+// Standalone kernels: the last CTA to finish (an atomic ticket; no CTA waits for another) reduces.
+__device__ void finish_pick(const DecodeGemvArgs& a, float best, int best_at, int block, int blocks) {
+  __shared__ bool last;
+  pick_slot(a, best, best_at, block);
+  if (threadIdx.x == 0) {
+    __threadfence();
+    last = atomicAdd(a.ticket, 1u) == static_cast<unsigned>(blocks) - 1u;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  reduce_pick(a, blocks);
+  if (threadIdx.x == 0) *a.ticket = 0u;
+}
+
+// First slice of this block's first work item towards L2 (weights never depend on the producer).
+template <int kKind, int kSplit>
+__device__ __forceinline__ void gemv_prefetch(const DecodeGemvArgs& a, int block) {
+  constexpr int kRows = GemvShape<kKind>::kRows;
+  constexpr int kItems = kGemvWarps / kSplit;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int local = warp / kSplit;
+  const int slice = warp - local * kSplit;
+  const int chunks = a.k >> 3;
+  const int begin = slice * chunks / kSplit;
+  const int end = (slice + 1) * chunks / kSplit;
+  const int item = block * kItems + local;
+  if (item < item_count<kKind>(a) && lane < kRows && end > begin) {
+    int row[kRows];
+    item_rows<kKind>(a, item, row);
+    const uint16_t* w = static_cast<const uint16_t*>(a.w);
+    prefetch_l2(w + static_cast<size_t>(row[lane]) * a.k + 8 * static_cast<size_t>(begin),
+                static_cast<uint32_t>(end - begin) * 16u);
   }
 }
 
+// One projection over the work items of blocks block, block + blocks, ... (a grid-stride loop);
+// `slot_pick`: the greedy pick leaves this block's candidate in its slot (the caller reduces),
+// else the last block reduces by ticket.
 template <typename T, int kKind, int kSplit, int kInFlight>
-__global__ void __launch_bounds__(kGemvThreads) decode_gemv_kernel(const DecodeGemvArgs a) {
+__device__ void gemv_body(const DecodeGemvArgs& a, int block, int blocks, bool slot_pick) {
   constexpr int kRows = GemvShape<kKind>::kRows;
   constexpr int kItems = kGemvWarps / kSplit;
   extern __shared__ uint4 xs[];
@@ -419,32 +477,20 @@ __global__ void __launch_bounds__(kGemvThreads) decode_gemv_kernel(const DecodeG
   const int end = (slice + 1) * chunks / kSplit;
   const int items = item_count<kKind>(a);
   const T* w = static_cast<const T*>(a.w);
-
-  {  // the weights do not depend on the producer: start this warp's first slice towards L2
-    const int item = blockIdx.x * kItems + local;
-    if (item < items && lane < kRows && end > begin) {
-      int row[kRows];
-      item_rows<kKind>(a, item, row);
-      prefetch_l2(w + static_cast<size_t>(row[lane]) * a.k + 8 * static_cast<size_t>(begin),
-                  static_cast<uint32_t>(end - begin) * 16u);
-    }
-  }
-  wait_for_producer();
-  release_dependents();
-  const int position = kKind == kDecodeQkv ? a.state[1] : 0;
+  const int position = kKind == kDecodeQkv ? __ldcg(a.state + 1) : 0;
   if constexpr (kKind == kDecodeQkv) {
-    if ((position < 0 || position >= a.table_positions || position >= a.context) && blockIdx.x == 0 &&
+    if ((position < 0 || position >= a.table_positions || position >= a.context) && block == 0 &&
         threadIdx.x == 0) {
       report_status(a.status, kStatusPositionOutOfRange);
     }
   }
-  stage_x<T>(a, xs, scratch);
+  stage_x<T>(a, xs, scratch, block);
 
   float best = -INFINITY;
   int best_at = INT_MAX;
   if constexpr (kSplit == 1) {
     // every warp walks its own items: no block-wide step between them, loads stay in flight
-    for (int item = blockIdx.x * kGemvWarps + warp; item < items; item += gridDim.x * kGemvWarps) {
+    for (int item = block * kGemvWarps + warp; item < items; item += blocks * kGemvWarps) {
       int row[kRows];
       item_rows<kKind>(a, item, row);
       const T* row_ptr[kRows];
@@ -455,7 +501,7 @@ __global__ void __launch_bounds__(kGemvThreads) decode_gemv_kernel(const DecodeG
       if (lane == 0) finish_item<T, kKind>(a, item, acc, best, best_at);
     }
   } else {
-    for (int group = blockIdx.x; group * kItems < items; group += gridDim.x) {
+    for (int group = block; group * kItems < items; group += blocks) {
       const int item = group * kItems + local;
       float acc[kRows];
       [[maybe_unused]] QkvOperands operands;
@@ -497,8 +543,23 @@ __global__ void __launch_bounds__(kGemvThreads) decode_gemv_kernel(const DecodeG
     }
   }
   if constexpr (kKind == kDecodeLogits) {
-    if (a.pick) finish_pick(a, best, best_at);
+    if (a.pick) {
+      if (slot_pick) {
+        pick_slot(a, best, best_at, block);
+      } else {
+        finish_pick(a, best, best_at, block, blocks);
+      }
+    }
   }
+  __syncthreads();  // shared memory is reused by the caller's next body
+}
+
+template <typename T, int kKind, int kSplit, int kInFlight>
+__global__ void __launch_bounds__(kGemvThreads) decode_gemv_kernel(const DecodeGemvArgs a) {
+  gemv_prefetch<kKind, kSplit>(a, blockIdx.x);
+  wait_for_producer();
+  release_dependents();
+  gemv_body<T, kKind, kSplit, kInFlight>(a, blockIdx.x, gridDim.x, false);
 }
 
 __device__ __forceinline__ float warp_max(float value) {
@@ -513,18 +574,16 @@ __device__ __forceinline__ float warp_max(float value) {
 // a KV head (ticket) merges the splits of the group's heads:
 //   out[h, d] = sum_s 2^(m_s - M) O_s[d] / sum_s 2^(m_s - M) l_s.
 template <typename T>
-__global__ void __launch_bounds__(kDecodeThreads) decode_attention_kernel(const DecodeAttentionArgs a,
-                                                                          float scale_log2) {
-  __shared__ float q_s[kDecodeMaxGroup][kDecodeDim];
+__device__ void attention_body(const DecodeAttentionArgs& a, int split, int kv_head, int splits, float scale_log2) {
+  __shared__ __align__(16) float q_s[kDecodeMaxGroup][kDecodeDim];  // read as float4
   __shared__ __align__(16) T k_s[kDecodeKeys][kKeyStride];
   __shared__ __align__(16) T v_s[kDecodeKeys][kDecodeDim];
   __shared__ float p_s[kDecodeMaxGroup][kDecodeKeys];
   __shared__ bool last;
   constexpr int kWarps = kDecodeThreads / 32;
   constexpr int kHeadsPerWarp = kDecodeMaxGroup / kWarps;
-  const int split = blockIdx.x;
-  const int kv_head = blockIdx.y;
   const int group = a.query_heads / a.kv_heads;
+  __syncthreads();  // shared memory may still hold the caller's previous body
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   // The step's position was fixed before this step's first kernel ran, and cache rows below it
@@ -656,7 +715,7 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_attention_kernel(const 
   }
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) last = atomicAdd(a.tickets + kv_head, 1u) == gridDim.x - 1;
+  if (threadIdx.x == 0) last = atomicAdd(a.tickets + kv_head, 1u) == static_cast<unsigned>(splits) - 1u;
   __syncthreads();
   if (!last) return;
   __threadfence();
@@ -689,6 +748,124 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_attention_kernel(const 
     *reinterpret_cast<uint2*>(static_cast<T*>(a.out) + static_cast<size_t>(head) * kDecodeDim + 4 * lane) = packed;
   }
   if (threadIdx.x == 0) a.tickets[kv_head] = 0u;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kDecodeThreads) decode_attention_kernel(const DecodeAttentionArgs a,
+                                                                          float scale_log2) {
+  attention_body<T>(a, blockIdx.x, blockIdx.y, gridDim.x, scale_log2);
+}
+
+// ---- the persistent decode step --------------------------------------------------------------
+constexpr unsigned kBarrierSpinLimit = 1u << 22;  // polls of 64 ns or more: over 0.25 s
+
+// Grid-wide barrier of a cooperative launch. Thread 0 of each CTA publishes the CTA's writes
+// (fence), arrives on the counter and polls it until every CTA of this generation has arrived.
+// The poll is bounded; false after a timeout or when the status word already reports an error,
+// and then every CTA returns.
+__device__ bool grid_barrier(unsigned* counter, unsigned& target, int* status) {
+  __shared__ int proceed;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    target += gridDim.x;
+    __threadfence();
+    atomicAdd(counter, 1u);
+    int ok = 1;
+    for (unsigned spins = 0;; ++spins) {
+      unsigned arrived;
+      asm volatile("ld.acquire.gpu.u32 %0, [%1];" : "=r"(arrived) : "l"(counter) : "memory");
+      if (arrived >= target) break;
+      if (*reinterpret_cast<volatile int*>(status) != 0) {
+        ok = 0;
+        break;
+      }
+      if (spins >= kBarrierSpinLimit) {
+        report_status(status, kStatusWaitTimeout);
+        ok = 0;
+        break;
+      }
+      __nanosleep(64);
+    }
+    __threadfence();
+    proceed = ok;
+  }
+  __syncthreads();
+  return proceed != 0;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kGemvThreads, 2) decode_step_kernel(const DecodeStepArgs s) {
+  unsigned target = 0;
+  int current = 0;
+  const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(s.attention.head_dim));
+  const int attention_blocks = kDecodeSplits * s.attention.kv_heads;
+  for (int l = 0; l < s.layer_count; ++l) {
+    const DecodeLayerWeights p = s.layers[l];
+    // pre-attention RMSNorm + q|k|v + bias + RoPE + cache append (layer 0: the embedding row)
+    DecodeGemvArgs qkv = s.qkv;
+    qkv.w = p.qkv;
+    qkv.bias_half = p.qkv_bias_half;
+    qkv.bias = p.qkv_bias;
+    qkv.gamma = p.input_norm;
+    qkv.k_cache = p.k_cache;
+    qkv.v_cache = p.v_cache;
+    if (l == 0) {
+      qkv.residual_in = nullptr;
+      qkv.delta = nullptr;
+      qkv.residual_out = s.residual[0];
+    } else {
+      qkv.embed_table = nullptr;
+      qkv.residual_in = s.residual[current];
+      qkv.residual_out = s.residual[current ^ 1];
+      current ^= 1;
+    }
+    if (l == 0) gemv_prefetch<kDecodeQkv, 4>(qkv, blockIdx.x);
+    gemv_body<T, kDecodeQkv, 4, 8>(qkv, blockIdx.x, gridDim.x, true);
+    DecodeAttentionArgs attention = s.attention;
+    attention.k_cache = p.k_cache;
+    attention.v_cache = p.v_cache;
+    if (!grid_barrier(s.barrier, target, s.status)) return;
+    // split attention over the cache; the last CTA of each KV head merges its splits
+    for (int b = blockIdx.x; b < attention_blocks; b += gridDim.x) {
+      attention_body<T>(attention, b % kDecodeSplits, b / kDecodeSplits, kDecodeSplits, scale_log2);
+    }
+    DecodeGemvArgs out_proj = s.out_proj;
+    out_proj.w = p.out;
+    gemv_prefetch<kDecodePlain, 4>(out_proj, blockIdx.x);
+    if (!grid_barrier(s.barrier, target, s.status)) return;
+    gemv_body<T, kDecodePlain, 4, 8>(out_proj, blockIdx.x, gridDim.x, true);
+    // post-attention RMSNorm + gate|up + SwiGLU
+    DecodeGemvArgs gate_up = s.gate_up;
+    gate_up.w = p.gate_up;
+    gate_up.gamma = p.post_norm;
+    gate_up.residual_in = s.residual[current];
+    gate_up.residual_out = s.residual[current ^ 1];
+    current ^= 1;
+    gemv_prefetch<kDecodeGateUp, 1>(gate_up, blockIdx.x);
+    if (!grid_barrier(s.barrier, target, s.status)) return;
+    gemv_body<T, kDecodeGateUp, 1, 16>(gate_up, blockIdx.x, gridDim.x, true);
+    DecodeGemvArgs down = s.down;
+    down.w = p.down;
+    gemv_prefetch<kDecodePlain, 8>(down, blockIdx.x);
+    if (!grid_barrier(s.barrier, target, s.status)) return;
+    gemv_body<T, kDecodePlain, 8, 16>(down, blockIdx.x, gridDim.x, true);
+    if (l + 1 < s.layer_count) {
+      DecodeGemvArgs next = s.qkv;
+      next.w = s.layers[l + 1].qkv;
+      gemv_prefetch<kDecodeQkv, 4>(next, blockIdx.x);
+    } else {
+      gemv_prefetch<kDecodeLogits, 1>(s.head, blockIdx.x);
+    }
+    if (!grid_barrier(s.barrier, target, s.status)) return;
+  }
+  // final RMSNorm + output head; greedy: every CTA's candidate, then block 0 picks
+  DecodeGemvArgs head = s.head;
+  head.residual_in = s.residual[current];
+  gemv_body<T, kDecodeLogits, 1, 16>(head, blockIdx.x, gridDim.x, true);
+  if (head.pick) {
+    if (!grid_barrier(s.barrier, target, s.status)) return;
+    if (blockIdx.x == 0) reduce_pick(head, gridDim.x);
+  }
 }
 
 template <typename T>
@@ -838,7 +1015,42 @@ cudaError_t gemv_dispatch(const DecodeGemvArgs& args, bool programmatic, cudaStr
 
 bool valid_dtype(int dtype) { return dtype == kActFp16 || dtype == kActBf16; }
 
+template <typename T>
+cudaError_t step_typed(const DecodeStepArgs& args, cudaStream_t stream) {
+  auto kernel = decode_step_kernel<T>;
+  const size_t smem = static_cast<size_t>(args.max_k) * 2;
+  cudaError_t status = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (status != cudaSuccess) return status;
+  int per_sm = 0;
+  status = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kGemvThreads, smem);
+  if (status != cudaSuccess) return status;
+  if (per_sm <= 0) return cudaErrorCooperativeLaunchTooLarge;
+  const int grid = per_sm * sm_count();
+  if (grid > kDecodePickSlots) return cudaErrorCooperativeLaunchTooLarge;
+  cudaLaunchConfig_t config = {};
+  config.gridDim = dim3(grid);
+  config.blockDim = dim3(kGemvThreads);
+  config.dynamicSmemBytes = smem;
+  config.stream = stream;
+  cudaLaunchAttribute attribute[1];
+  attribute[0].id = cudaLaunchAttributeCooperative;
+  attribute[0].val.cooperative = 1;
+  config.attrs = attribute;
+  config.numAttrs = 1;
+  return cudaLaunchKernelEx(&config, kernel, args);
+}
+
 }  // namespace
+
+cudaError_t launch_decode_step(const DecodeStepArgs& args, cudaStream_t stream) {
+  if (args.layers == nullptr || args.layer_count <= 0 || args.barrier == nullptr || args.status == nullptr ||
+      !valid_dtype(args.dtype) || args.max_k <= 0 || args.max_k % 8 != 0 ||
+      args.qkv.k > kDecodeMaxNormHidden || args.attention.head_dim != kDecodeDim ||
+      args.attention.query_heads / args.attention.kv_heads > kDecodeMaxGroup) {
+    return cudaErrorInvalidValue;
+  }
+  return args.dtype == kActFp16 ? step_typed<__half>(args, stream) : step_typed<__nv_bfloat16>(args, stream);
+}
 
 cudaError_t launch_decode_gemv(const DecodeGemvArgs& args, bool programmatic, cudaStream_t stream) {
   if (args.rows <= 0 || args.k <= 0 || args.k % 8 != 0 || !valid_dtype(args.dtype) || args.w == nullptr ||

@@ -51,6 +51,9 @@ struct DecodeGemvArgs {
   // CTA 0 then stores v into residual_out (nullable; must not alias residual_in)
   const void* x = nullptr;
   const float* residual_in = nullptr;
+  // or v = the embedding row of token state[0] (16-bit [vocab, k]); residual_in then unused
+  const void* embed_table = nullptr;
+  int vocab = 0;
   const void* delta = nullptr;
   const float* gamma = nullptr;
   float eps = 0.0f;
@@ -100,6 +103,46 @@ struct DecodeAttentionArgs {
   int dtype = 1;
 };
 cudaError_t launch_decode_attention(const DecodeAttentionArgs& args, bool programmatic, cudaStream_t stream);
+
+// One decode step as ONE persistent kernel (a cooperative launch of as many CTAs as fit): the
+// phases q|k|v, attention, o_proj, gate|up, down of every layer and the output head run in turn,
+// separated by a grid-wide barrier, so the step pays no launch, ramp-up or drain between phases.
+// Before arriving at a barrier every CTA sends its share of the next phase's weights towards L2,
+// which keeps HBM busy across the phase boundary. The barrier's wait is bounded: on a timeout it
+// reports kStatusWaitTimeout and every CTA returns. Layer 0's q|k|v prologue reads the embedding
+// row of the step's token itself. The phase bodies are those of the per-phase kernels.
+struct DecodeLayerWeights {
+  const void* qkv = nullptr;
+  const void* qkv_bias_half = nullptr;
+  const float* qkv_bias = nullptr;
+  const void* out = nullptr;
+  const void* gate_up = nullptr;
+  const void* down = nullptr;
+  const float* input_norm = nullptr;
+  const float* post_norm = nullptr;
+  void* k_cache = nullptr;
+  void* v_cache = nullptr;
+};
+
+struct DecodeStepArgs {
+  const DecodeLayerWeights* layers = nullptr;  // device array [layer_count]
+  int layer_count = 0;
+  // phase templates; the kernel fills in each layer's weights, norms, caches and residual rows
+  DecodeGemvArgs qkv;       // embed_table, vocab, state, RoPE tables, q_out, context, status set
+  DecodeGemvArgs out_proj;  // x = attention output, y = delta of the attention block
+  DecodeGemvArgs gate_up;   // delta = delta of the attention block, y = SwiGLU output
+  DecodeGemvArgs down;      // x = SwiGLU output, y = delta of the MLP block
+  DecodeGemvArgs head;      // delta = delta of the MLP block, gamma = final norm, y = logits, pick
+  DecodeAttentionArgs attention;
+  float* residual[2] = {nullptr, nullptr};  // two fp32 rows used in turn
+  unsigned* barrier = nullptr;              // zero before every launch
+  int* status = nullptr;
+  int dtype = 1;
+  int max_k = 0;                            // largest row length staged (shared memory: 2 max_k bytes)
+};
+// Cooperative launch of the step; cudaErrorCooperativeLaunchTooLarge (or another error) when the
+// device cannot hold the grid, in which case the per-phase kernels are the way.
+cudaError_t launch_decode_step(const DecodeStepArgs& args, cudaStream_t stream);
 
 // K and V of a prefilled prompt (rows 0 .. tokens-1 of the q|k|v buffer, after RoPE) into the
 // cache at positions 0 .. tokens-1.

@@ -137,7 +137,8 @@ struct GenerationState {
   float* logits = nullptr;        // fp32 [vocab]
   float* pick_values = nullptr;   // greedy pick: per-CTA candidates [kDecodePickSlots]
   int32_t* pick_indices = nullptr;
-  unsigned* tickets = nullptr;    // [1 + Hkv]: the pick's and the attention's last-CTA counters
+  unsigned* tickets = nullptr;    // [2 + Hkv]: the pick's and the attention's last-CTA tickets, the step barrier
+  void* layer_table = nullptr;    // DecodeLayerWeights [layers] for the persistent step kernel
   int32_t* state = nullptr;       // device {token, position}
   int32_t* meta = nullptr;        // device: prompt tokens | offsets [2] | attention tiles
   size_t meta_capacity = 0;       // int32 elements of meta (and of the staging area behind the slots)
@@ -146,7 +147,8 @@ struct GenerationState {
   cudaEvent_t slot_ready[2] = {nullptr, nullptr};
   cudaGraphExec_t graphs[2] = {nullptr, nullptr};  // decode step: [0] logits only, [1] + greedy pick
   bool warmed[2] = {false, false};  // the first step of each kind runs eagerly, later ones replay
-  bool programmatic = true;       // decode kernels use programmatic dependent launch
+  bool programmatic = true;       // per-phase kernels use programmatic dependent launch
+  bool persistent = true;         // one persistent kernel per step (falls back to per-phase kernels)
   int position = -1;              // position of the next token fed; -1: no prompt
   ~GenerationState();
 };
@@ -220,9 +222,10 @@ class Engine {
   // Position the next decoded token takes (prompt length + tokens fed so far); -1 before a prompt.
   int generation_position() const;
   int generation_context() const { return options_.max_sequence_length; }
-  // Whether decode steps use programmatic dependent launch (after the first captured step: false
-  // when the graph could not be captured with it).
-  bool decode_programmatic() const;
+  // How decode steps run: 2 = one persistent kernel per step, 1 = per-phase kernels with
+  // programmatic dependent launch, 0 = per-phase kernels serialised (set by the environment, or
+  // by a launch or graph capture the device refused).
+  int decode_mode() const;
 
   // Raw access for the kernel-level tests: the device buffers of the last batch.
   const void* qkv_buffer() const { return qkv_; }
@@ -234,6 +237,7 @@ class Engine {
   void ensure_generation();
   void prefill_generation(int tokens);  // metadata already uploaded
   void launch_decode_step(bool greedy);  // the step's kernels, in order, on stream_
+  bool launch_persistent_step(bool greedy);  // false: the device refused the cooperative launch
   void run_decode_step(bool greedy);     // eager on first use, then a CUDA graph replay
   void release_decode_graphs();
   const void* output_head() const;

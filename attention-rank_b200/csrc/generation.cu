@@ -81,7 +81,7 @@ void Engine::ensure_generation() {
   g->logits = static_cast<float*>(device_alloc(V * 4));
   g->pick_values = static_cast<float*>(device_alloc(kDecodePickSlots * sizeof(float)));
   g->pick_indices = static_cast<int32_t*>(device_alloc(kDecodePickSlots * sizeof(int32_t)));
-  g->tickets = static_cast<unsigned*>(device_alloc((1 + c.num_key_value_heads) * sizeof(unsigned)));
+  g->tickets = static_cast<unsigned*>(device_alloc((2 + c.num_key_value_heads) * sizeof(unsigned)));
   g->state = static_cast<int32_t*>(device_alloc(4 * sizeof(int32_t)));
   g->meta_capacity = static_cast<size_t>(capacity_tokens_) + 2 + 2 * (capacity_tokens_ / kAttentionQueryTile + 1);
   g->meta = static_cast<int32_t*>(device_alloc(g->meta_capacity * 4));
@@ -91,13 +91,41 @@ void Engine::ensure_generation() {
   for (auto& event : g->slot_ready) {
     check_cuda(cudaEventCreateWithFlags(&event, cudaEventDisableTiming), "cudaEventCreate");
   }
-  // ATTNRANK_DECODE_PDL=0 launches the decode kernels without programmatic dependent launch
+  // the persistent step kernel's table of per-layer weights and cache rows (stable addresses)
+  std::vector<DecodeLayerWeights> table(L);
+  for (size_t l = 0; l < L; ++l) {
+    const LayerWeights& w = layers_[l];
+    const bool half_bias = options_.activation_dtype == kActFp16 && w.qkv_bias_half != nullptr;
+    table[l].qkv = w.qkv;
+    table[l].qkv_bias_half = half_bias ? w.qkv_bias_half : nullptr;
+    table[l].qkv_bias = half_bias ? nullptr : w.qkv_bias;
+    table[l].out = w.out;
+    table[l].gate_up = w.gate_up;
+    table[l].down = w.down;
+    table[l].input_norm = w.input_norm;
+    table[l].post_norm = w.post_norm;
+    table[l].k_cache = static_cast<uint16_t*>(g->k_cache) + l * g->layer_elements;
+    table[l].v_cache = static_cast<uint16_t*>(g->v_cache) + l * g->layer_elements;
+  }
+  g->layer_table = device_alloc(L * sizeof(DecodeLayerWeights));
+  check_cuda(cudaMemcpyAsync(g->layer_table, table.data(), L * sizeof(DecodeLayerWeights), cudaMemcpyHostToDevice,
+                             stream_),
+             "decode layer table");
+  synchronize();  // the host table goes out of scope
+  // ATTNRANK_DECODE_PERSISTENT=1: one persistent kernel per step (measured slower than the
+  // per-phase kernels on B200: 3.48 against 3.11 ms per Qwen-7B token); ATTNRANK_DECODE_PDL=0:
+  // per-phase kernels without programmatic launch
+  const char* persistent = std::getenv("ATTNRANK_DECODE_PERSISTENT");
+  g->persistent = persistent != nullptr && persistent[0] == '1';
   const char* pdl = std::getenv("ATTNRANK_DECODE_PDL");
   g->programmatic = !(pdl != nullptr && pdl[0] == '0');
   generation_ = std::move(g);
 }
 
-bool Engine::decode_programmatic() const { return generation_ && generation_->programmatic; }
+int Engine::decode_mode() const {
+  if (!generation_) return -1;
+  return generation_->persistent ? 2 : generation_->programmatic ? 1 : 0;
+}
 
 void Engine::prefill_generation(int M) {
   const ModelConfig& c = config_;
@@ -166,9 +194,99 @@ void Engine::prefill_generation(int M) {
   check_cuda(launch_decode_gemv(head, false, stream_), "lm_head");
 }
 
+bool Engine::launch_persistent_step(bool greedy) {
+  const ModelConfig& c = config_;
+  GenerationState& g = *generation_;
+  const int H = c.hidden_size, I = c.intermediate_size, Hq = c.num_attention_heads, Hkv = c.num_key_value_heads;
+  const int D = c.head_dim();
+  const int dtype = options_.activation_dtype;
+  DecodeStepArgs s;
+  s.layers = static_cast<const DecodeLayerWeights*>(g.layer_table);
+  s.layer_count = c.num_hidden_layers;
+  s.qkv.kind = kDecodeQkv;
+  s.qkv.rows = c.qkv_width();
+  s.qkv.k = H;
+  s.qkv.eps = c.rms_norm_eps;
+  s.qkv.embed_table = embedding_;
+  s.qkv.vocab = c.vocab_size;
+  s.qkv.query_heads = Hq;
+  s.qkv.kv_heads = Hkv;
+  s.qkv.head_dim = D;
+  s.qkv.cos_table = cos_table_;
+  s.qkv.sin_table = sin_table_;
+  s.qkv.table_positions = options_.max_sequence_length;
+  s.qkv.state = g.state;
+  s.qkv.q_out = g.q;
+  s.qkv.context = g.context;
+  s.qkv.status = status_;
+  s.qkv.dtype = dtype;
+  void* delta_attention = delta_;
+  void* delta_mlp = static_cast<uint16_t*>(delta_) + H;
+  s.qkv.delta = delta_mlp;
+  s.out_proj.kind = kDecodePlain;
+  s.out_proj.rows = H;
+  s.out_proj.k = Hq * D;
+  s.out_proj.x = attn_;
+  s.out_proj.y = delta_attention;
+  s.out_proj.dtype = dtype;
+  s.gate_up.kind = kDecodeGateUp;
+  s.gate_up.rows = I;
+  s.gate_up.k = H;
+  s.gate_up.eps = c.rms_norm_eps;
+  s.gate_up.delta = delta_attention;
+  s.gate_up.y = act_;
+  s.gate_up.dtype = dtype;
+  s.down.kind = kDecodePlain;
+  s.down.rows = H;
+  s.down.k = I;
+  s.down.x = act_;
+  s.down.y = delta_mlp;
+  s.down.dtype = dtype;
+  s.head.kind = kDecodeLogits;
+  s.head.w = output_head();
+  s.head.rows = c.vocab_size;
+  s.head.k = H;
+  s.head.delta = delta_mlp;
+  s.head.gamma = final_norm_;
+  s.head.eps = c.rms_norm_eps;
+  s.head.y = g.logits;
+  s.head.state = g.state;
+  s.head.pick = greedy;
+  s.head.pick_values = g.pick_values;
+  s.head.pick_indices = g.pick_indices;
+  s.head.dtype = dtype;
+  s.attention.q = g.q;
+  s.attention.context = g.context;
+  s.attention.state = g.state;
+  s.attention.query_heads = Hq;
+  s.attention.kv_heads = Hkv;
+  s.attention.head_dim = D;
+  s.attention.sliding_window = c.sliding_window;
+  s.attention.partials = g.partials;
+  s.attention.stats = g.stats;
+  s.attention.tickets = g.tickets + 1;
+  s.attention.out = attn_;
+  s.attention.dtype = dtype;
+  s.residual[0] = residual_;
+  s.residual[1] = residual_ + H;
+  s.barrier = g.tickets + 1 + Hkv;
+  s.status = status_;
+  s.dtype = dtype;
+  s.max_k = std::max(std::max(H, I), Hq * D);
+  check_cuda(cudaMemsetAsync(g.tickets, 0, (2 + Hkv) * sizeof(unsigned), stream_), "decode tickets");
+  const cudaError_t status = ::arb::launch_decode_step(s, stream_);
+  if (status == cudaSuccess) return true;
+  cudaGetLastError();  // a refused cooperative launch ran nothing: the per-phase kernels take over
+  return false;
+}
+
 void Engine::launch_decode_step(bool greedy) {
   const ModelConfig& c = config_;
   GenerationState& g = *generation_;
+  if (g.persistent) {
+    if (launch_persistent_step(greedy)) return;
+    g.persistent = false;
+  }
   const int H = c.hidden_size, I = c.intermediate_size, Hq = c.num_attention_heads, Hkv = c.num_key_value_heads;
   const int D = c.head_dim();
   const int dtype = options_.activation_dtype;
@@ -297,9 +415,9 @@ void Engine::run_decode_step(bool greedy) {
     g.warmed[kind] = true;
   } else {
     if (g.graphs[kind] == nullptr) {
-      // programmatic edges in a captured graph need driver support: without it the capture is
-      // repeated with ordinary launches
-      for (int attempt = 0; attempt < 2 && g.graphs[kind] == nullptr; ++attempt) {
+      // a cooperative launch or programmatic edges in a captured graph need driver support:
+      // without it the capture is repeated with per-phase kernels, then with ordinary launches
+      for (int attempt = 0; attempt < 3 && g.graphs[kind] == nullptr; ++attempt) {
         cudaGraph_t graph = nullptr;
         check_cuda(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeRelaxed), "decode capture");
         try {
@@ -315,8 +433,12 @@ void Engine::run_decode_step(bool greedy) {
         if (status != cudaSuccess) {
           cudaGetLastError();
           g.graphs[kind] = nullptr;
-          if (!g.programmatic || attempt == 1) check_cuda(status, "decode graph");
-          g.programmatic = false;
+          if (attempt == 2 || (!g.persistent && !g.programmatic)) check_cuda(status, "decode graph");
+          if (g.persistent) {
+            g.persistent = false;
+          } else {
+            g.programmatic = false;
+          }
         }
       }
     }
@@ -352,7 +474,7 @@ void Engine::begin_generation(const int32_t* prompt, int count) {
   }
   g.staging[kStateUpload] = 0;
   g.staging[kStateUpload + 1] = count - 1;  // the last prompt token's position
-  check_cuda(cudaMemsetAsync(g.tickets, 0, (1 + config_.num_key_value_heads) * sizeof(unsigned), stream_),
+  check_cuda(cudaMemsetAsync(g.tickets, 0, (2 + config_.num_key_value_heads) * sizeof(unsigned), stream_),
              "ticket reset");
   check_cuda(cudaMemcpyAsync(g.meta, meta, static_cast<size_t>(count + 2 + 2 * tiles) * 4, cudaMemcpyHostToDevice,
                              stream_),

@@ -765,8 +765,9 @@ def run_decode(args, rank, world, local_rank):
                      "per_token_bytes": traffic,
                      "note": f"whole decode step (all kernels) against the {kind} copy bandwidth"},
         "clocks": clocks,
-        "gpu_launches": args.steps * (2 + 5 * config.num_hidden_layers) * (new - 1),
-        "programmatic_launch": engine.decode_programmatic,
+        "gpu_launches": args.steps * (new - 1) * (1 if engine.decode_mode == "persistent"
+                                                   else 2 + 5 * config.num_hidden_layers),
+        "decode_mode": engine.decode_mode,
         "tokens_head": results.generated_tokens[:8] if results else None,
     }
     engine.close()

@@ -267,10 +267,12 @@ int ar_engine_generation_begin(ar_engine* engine, const int32_t* prompt, int pro
 int ar_engine_generation_step(ar_engine* engine, int32_t token, float* logits_out);
 /* Position of the next token fed (prompt length + steps), -1 before a prompt. */
 int ar_engine_generation_position(ar_engine* engine);
-/* 1 when decode steps run with programmatic dependent launch (each kernel may start before its
- * predecessor ends and waits for it before reading its output), 0 when they are serialised
- * (ATTNRANK_DECODE_PDL=0 in the environment, or a graph that could not be captured with it). */
-int ar_engine_decode_programmatic(ar_engine* engine);
+/* How decode steps run (-1 before the first generation): 2 = one persistent kernel per step (a
+ * cooperative launch whose phases meet at a grid barrier), 1 = one kernel per phase with
+ * programmatic dependent launch (the default), 0 = one kernel per phase, serialised.
+ * ATTNRANK_DECODE_PERSISTENT=1 and ATTNRANK_DECODE_PDL=0 in the environment select modes 2 and 0;
+ * a launch or graph capture that the device refuses falls back to the next mode down. */
+int ar_engine_decode_mode(ar_engine* engine);
 
 /* Host samplers: GreedySampler / NucleusSampler (model.cpp:70-127). The same logits and
  * config give the reference's token ids; a nucleus sampler's draws advance its own

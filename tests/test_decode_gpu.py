@@ -377,3 +377,28 @@ def test_qwen7b_prefill_logits_match_the_reference(cuda, reference_lib):
     top = np.sort(want)[-2:]
     if top[1] - top[0] > 2 * error:
         assert int(np.argmax(got)) == int(np.argmax(want))
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+def test_persistent_step_matches_the_per_phase_kernels(cuda, monkeypatch, dtype):
+    """ATTNRANK_DECODE_PERSISTENT=1: one cooperative kernel per step (the same phase bodies, a
+    grid barrier between phases, layer 0 reading its embedding row itself). Its logits equal the
+    per-phase kernels' up to the norms' summation order (rel 1e-3 of max |logit|), and greedy ids
+    agree."""
+    config = small_config(layers=3)
+    prompt = prompt_tokens(180, config.vocab_size, seed=12)
+    runs = {}
+    for mode in ("0", "1"):
+        monkeypatch.setenv("ATTNRANK_DECODE_PERSISTENT", mode)
+        engine = make_engine(config, dtype)
+        engine.config.eos_token_id = -1
+        logits = [engine.generation_begin(prompt)]
+        for token in (5, 77, 1999):
+            logits.append(engine.generation_step(token))
+        tokens = engine.generate(prompt, max_new_tokens=12).generated_tokens
+        runs[mode] = (logits, tokens, engine.decode_mode)
+        engine.close()
+    assert runs["1"][2] == "persistent" and runs["0"][2] == "programmatic"
+    for got, want in zip(runs["1"][0], runs["0"][0]):
+        assert np.abs(got - want).max() <= 1e-3 * np.abs(want).max()
+    assert runs["1"][1] == runs["0"][1]
