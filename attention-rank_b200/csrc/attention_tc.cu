@@ -202,6 +202,34 @@ __device__ __forceinline__ void tmem_st32(uint32_t address, const uint32_t (&r)[
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void softmax_barrier() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Packed fp32 pairs (sm_100a f32x2 arithmetic): one instruction does two lanes' worth of FMA or
+// add, which frees issue slots in the softmax loop for the exponentials.
+__device__ __forceinline__ unsigned long long pack_f32x2(float a, float b) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void unpack_f32x2(unsigned long long v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long fma_f32x2(unsigned long long a, unsigned long long b,
+                                                        unsigned long long c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ unsigned long long add_f32x2(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// max(a, b, c) in one instruction
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // 2^x with the SFU's ex2 instruction, results below 2^-126 flushed to zero: a row's largest
 // probability relative to its reference is at least 1, so those vanish in O, l and the span sums
 __device__ __forceinline__ float ex2_ftz(float x) {
@@ -468,7 +496,9 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
       for (int c = 0; c < kChains; ++c) m_part[c] = x[c];
 #pragma unroll
-      for (int i = kChains; i < kKeys; ++i) m_part[i % kChains] = fmaxf(m_part[i % kChains], x[i]);
+      for (int i = kChains; i < kKeys; i += 2) {
+        m_part[(i / 2) % kChains] = max3(m_part[(i / 2) % kChains], x[i], x[i + 1]);
+      }
 #pragma unroll
       for (int c = 1; c < kChains; ++c) m_part[0] = fmaxf(m_part[0], m_part[c]);
       const float m_tile = m_part[0] * scale_log2;  // the tile max in log2 units (the scale is positive)
@@ -506,19 +536,31 @@ __global__ void __launch_bounds__(kThreads, 2)
       float sum = 0.0f;
       {
         uint32_t packed[kKeys / 2];  // 64 probabilities -> 32 TMEM columns of 16-bit pairs
-        float s_part[kChains] = {};
+        // p = 2^(s * log2(e) / sqrt(D) - m_ref): one packed FFMA per pair of scores, one ex2 each;
+        // the row sum runs in kChains / 2 packed accumulators (kChains partial sums)
+        unsigned long long s_pair[kChains / 2];
 #pragma unroll
-        for (int i = 0; i < kKeys / 2; ++i) {  // p = 2^(s * log2(e) / sqrt(D) - m_ref): one FFMA + one ex2
-          const float p0 = ex2_ftz(fmaf(x[2 * i], scale_log2, neg_reference));
-          const float p1 = ex2_ftz(fmaf(x[2 * i + 1], scale_log2, neg_reference));
-          s_part[i % kChains] += p0 + p1;
+        for (int c = 0; c < kChains / 2; ++c) s_pair[c] = 0ull;
+        const unsigned long long scale2 = pack_f32x2(scale_log2, scale_log2);
+        const unsigned long long reference2 = pack_f32x2(neg_reference, neg_reference);
+#pragma unroll
+        for (int i = 0; i < kKeys / 2; ++i) {
+          float t0, t1;
+          unpack_f32x2(fma_f32x2(pack_f32x2(x[2 * i], x[2 * i + 1]), scale2, reference2), t0, t1);
+          const float p0 = ex2_ftz(t0);
+          const float p1 = ex2_ftz(t1);
+          s_pair[i % (kChains / 2)] = add_f32x2(s_pair[i % (kChains / 2)], pack_f32x2(p0, p1));
           packed[i] = pack2<T>(p0, p1);
           x[2 * i] = p0;
           x[2 * i + 1] = p1;
         }
         tmem_st32(tmem + lane_base + stage * kKeys, packed);
 #pragma unroll
-        for (int c = 0; c < kChains; ++c) sum += s_part[c];
+        for (int c = 0; c < kChains / 2; ++c) {
+          float a, b;
+          unpack_f32x2(s_pair[c], a, b);
+          sum += a + b;
+        }
       }
       // fused mass: span sums of this tile's fp32 probabilities, by the warps that hold probe rows
       // (spans and k0 are CTA-uniform); a span that covers the whole tile takes the tile's sum
