@@ -7,10 +7,11 @@
 //   * the prefill is one packed forward of the whole prompt through the probe's batched kernels
 //     (cuBLASLt GEMMs, tcgen05 attention), with K and V of every layer copied into a 16-bit
 //     cache after RoPE; only the last row goes through lm_head;
-//   * a decode step is the chain of single-token kernels of decode.cu (fused q|k|v + RoPE + cache
-//     append, split attention, o_proj, RMSNorm, fused gate|up + SwiGLU, down_proj, RMSNorm,
-//     lm_head), captured once into a CUDA graph that reads the token and its position from device
-//     memory, so every later step is one graph launch;
+//   * a decode step is the chain of single-token kernels of decode.cu: per layer RMSNorm + q|k|v
+//     + RoPE + cache append, split attention, o_proj, RMSNorm + gate|up + SwiGLU, down_proj (each
+//     norm fused into the projection that consumes it), then final RMSNorm + lm_head. The chain is
+//     captured once into a CUDA graph that reads the token and its position from device memory, so
+//     every later step is one graph launch (or, opt-in, one persistent kernel per step);
 //   * greedy selection (the reference's default, temperature 0) is a device argmax that writes the
 //     next step's token, so consecutive steps chain on the device; the host only reads each token
 //     back to test for eos, with the next step already queued behind it.
