@@ -13,7 +13,10 @@ from attnrank.core import (AttentionProfile, AttnRankError, BasinCriterion, Basi
 from attnrank.data.classes import EngineSettings, GenerationSettings, LayerScanSettings, ProfileSettings
 from attnrank.engine import (LayerScan, attention_slot_order, basin_statistics, extract_attention_profile,
                              find_shallowest_attention_layer, from_pretrained, generate_from_prompt,
-                             is_model_directory,
+                             is_model_directory, set_log_level, model_config, resolve_model_directory,
+                             download_model, load_model_and_profile, chat_format_names, detect_chat_format,
+                             make_document, make_documents, make_probe_sample, make_probe_samples,
+                             load_probe_samples, synthetic_probe_samples, build_prompt, generate_answer,
                              load_attention_profile, load_model, make_prompt, make_reranker,
                              measure_attention_by_layer, measure_document_attention, profile_to_dict,
                              rerank_baseline, rerank_documents, rerank_with_profile, reranker_names,
@@ -31,5 +34,8 @@ __all__ = [
     "load_attention_profile", "load_model", "make_prompt", "make_reranker", "measure_attention_by_layer",
     "measure_document_attention", "profile_to_dict", "rerank_baseline", "rerank_documents", "rerank_with_profile",
     "reranker_names", "save_attention_profile", "scan_attention_layers", "select_shallowest_basin_layer",
-    "synthetic_engine",
+    "synthetic_engine", "set_log_level", "model_config", "resolve_model_directory", "download_model",
+    "load_model_and_profile", "chat_format_names", "detect_chat_format", "make_document", "make_documents",
+    "make_probe_sample", "make_probe_samples", "load_probe_samples", "synthetic_probe_samples", "build_prompt",
+    "generate_answer",
 ]

@@ -9,7 +9,10 @@ Same function names, arguments and return types as the reference for:
   rerank_documents (:440-445), rerank_with_profile (:448-449), make_reranker (:452-471),
   rerank_baseline (:474-490).
 Probe samples are token-id prompts (core.StructuredPrompt); the reference's text samples need its
-tokenizer and prompt builder, which are outside this build.
+tokenizer and prompt builder, which are outside this build: the text-only names (make_document,
+build_prompt, generate_answer, ...) exist and raise AttnRankError saying so. Also here:
+set_log_level, model_config, resolve_model_directory (local directories), load_model_and_profile,
+generate_from_prompt (:504-514).
 """
 from __future__ import annotations
 
@@ -56,6 +59,94 @@ def from_pretrained(*, model: str | Path, settings: EngineSettings = EngineSetti
     if candidate.exists():
         raise FileNotFoundError(f"{model} exists but holds no {MODEL_CONFIG_FILE} and weight shards")
     raise FileNotFoundError(f"{model} is not a local checkpoint directory (hub downloads are outside this build)")
+
+
+def set_log_level(*, level: str = "info") -> None:
+    """set_log_level (reference engine.py:75-76): the level of this package's logger."""
+    import logging
+    logging.getLogger("attnrank").setLevel(level.upper())
+
+
+def model_config(*, model_dir: Path) -> dict[str, Any]:
+    """model_config (reference engine.py:131-133): the checkpoint's config.json."""
+    return json.loads((Path(model_dir) / MODEL_CONFIG_FILE).read_text())
+
+
+def resolve_model_directory(*, model: str | Path, cache_dir: Path | None = None, revision: str | None = None,
+                            token: str | None = None) -> Path:
+    """resolve_model_directory (reference engine.py:108-128) for local checkpoint directories; hub
+    downloads are outside this build."""
+    candidate = Path(model)
+    if is_model_directory(path=candidate):
+        return candidate.resolve()
+    raise FileNotFoundError(f"{model} is not a local checkpoint directory (hub downloads are outside this build)")
+
+
+def download_model(*, repo_id: str, out_dir: Path | None = None, revision: str | None = None,
+                   token: str | None = None, max_workers: int = 8) -> Path:
+    """download_model (reference engine.py:85-105): hub downloads are outside this build."""
+    raise AttnRankError(f"cannot download {repo_id}: hub downloads are outside this build; pass a local "
+                        "checkpoint directory to from_pretrained")
+
+
+def load_model_and_profile(*, model: str | Path, profile: Path,
+                           settings: EngineSettings = EngineSettings()) -> tuple[Engine, AttentionProfile]:
+    """load_model_and_profile (reference engine.py:185-193)."""
+    return from_pretrained(model=model, settings=settings), load_attention_profile(path=profile)
+
+
+def chat_format_names() -> list[str]:
+    """chat_format_names (reference engine.py:140-141): chat formats belong to the reference's
+    prompt builder, which this build does not carry."""
+    return []
+
+
+def detect_chat_format(*, model_dir: Path) -> str:
+    """detect_chat_format (reference engine.py:136-137): no chat formats in this build."""
+    return ""
+
+
+def _needs_text(name: str) -> AttnRankError:
+    return AttnRankError(f"{name} works on text, which needs the reference's tokenizer and prompt builder; this "
+                         "build takes token-id prompts (attnrank.make_prompt / StructuredPrompt)")
+
+
+def make_document(*, item: Any, fallback_id: str = "") -> Any:
+    """make_document (reference engine.py:196-207): text documents are outside this build."""
+    raise _needs_text("make_document")
+
+
+def make_documents(*, items: Any, prefix: str = "doc") -> list[Any]:
+    raise _needs_text("make_documents")
+
+
+def make_probe_sample(*, question: str, documents: Any, sample_id: str = "sample") -> Any:
+    raise _needs_text("make_probe_sample")
+
+
+def make_probe_samples(*, items: Any) -> list[Any]:
+    raise _needs_text("make_probe_samples")
+
+
+def load_probe_samples(*, path: Path, limit: int = 0) -> list[Any]:
+    raise _needs_text("load_probe_samples")
+
+
+def synthetic_probe_samples(*, settings: Any = None) -> list[Any]:
+    """synthetic_probe_samples (reference engine.py:249-255) builds text samples; the token-id
+    equivalent is attnrank.synthetic.prompts."""
+    raise _needs_text("synthetic_probe_samples")
+
+
+def build_prompt(*, engine: Engine, question: str, documents: Any) -> Any:
+    raise _needs_text("build_prompt")
+
+
+def generate_answer(*, engine: Engine, question: str, documents: Any,
+                    settings: GenerationSettings = GenerationSettings()) -> Any:
+    """generate_answer (reference engine.py:493-501) formats text; generate_from_prompt or
+    Engine.generate take the token ids."""
+    raise _needs_text("generate_answer")
 
 
 def synthetic_engine(*, config: LlamaConfig, seed: int = 0, std: float = 0.02,
