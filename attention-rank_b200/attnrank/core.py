@@ -795,6 +795,87 @@ class PreparedScan:
             self._handle = None
 
 
+# ---- text-side records of the reference's _core (bindings.cpp:136-244), kept for API compatibility.
+# This build probes token-id prompts; these records carry text, which needs the reference's
+# tokenizer and prompt builder, so scans given them raise AttnRankError (see _as_prompts).
+@dataclass
+class Document:
+    """Document (core.hpp:43-47; bindings.cpp:136-149)."""
+
+    id: str = ""
+    title: str = ""
+    text: str = ""
+
+
+@dataclass
+class ProbeSample:
+    """ProbeSample (bindings.cpp:151-162): a question with its documents."""
+
+    question: str = ""
+    documents: list[Document] = field(default_factory=list)
+
+
+@dataclass
+class PromptTemplate:
+    """DocumentPromptTemplate (prompt.hpp:78-92; bindings.cpp:207-219), the reference prompt
+    builder's layout and defaults."""
+
+    instruction: str = ("Write a high-quality answer for the given question using only the provided search "
+                        "results (some of which might be irrelevant).")
+    example: str = ""
+    documents_header: str = ""
+    document_label: str = "Document [{index}] "
+    document_index_placeholder: str = "{index}"
+    document_separator: str = "\n"
+    question_prefix: str = "Question: "
+    answer_prefix: str = "Answer:"
+    max_document_tokens: int = 0
+    include_titles: bool = False
+    extra_stop_sequences: list[str] = field(default_factory=list)
+
+
+@dataclass
+class SyntheticProbeConfig:
+    """SyntheticProbeConfig (attnrank.hpp:43-48): the reference's synthetic TEXT samples. The
+    token-id workloads of this build come from attnrank.synthetic.prompts."""
+
+    document_slots: int = 10
+    sample_count: int = 400
+    words_per_document: int = 60
+    seed: int = 20250807
+
+
+def _text_unavailable(name: str) -> AttnRankError:
+    return AttnRankError(f"{name} builds text samples, which need the reference's tokenizer and prompt "
+                         "builder; this build takes token-id prompts (StructuredPrompt)")
+
+
+def load_probe_samples(jsonl_path) -> list[ProbeSample]:
+    """load_probe_samples (bindings.cpp:331): text samples are outside this build."""
+    raise _text_unavailable("load_probe_samples")
+
+
+def synthetic_probe_samples(config: SyntheticProbeConfig) -> list[ProbeSample]:
+    """synthetic_probe_samples (bindings.cpp:332): text samples are outside this build."""
+    raise _text_unavailable("synthetic_probe_samples")
+
+
+def chat_format_names() -> list[str]:
+    """chat_format_names (bindings.cpp:333): no chat formats in this build."""
+    return []
+
+
+def detect_chat_format(model_directory) -> str:
+    """detect_chat_format (bindings.cpp:334): no chat formats in this build."""
+    return ""
+
+
+def set_log_level(level: str) -> None:
+    """set_log_level (bindings.cpp:335): the level of this package's logger."""
+    import logging
+    logging.getLogger("attnrank").setLevel(str(level).upper())
+
+
 def _as_prompts(samples: Sequence) -> list[StructuredPrompt]:
     prompts = []
     for index, sample in enumerate(samples):

@@ -97,3 +97,23 @@ def test_text_only_helpers_say_why_they_are_unavailable(tmp_path):
     with pytest.raises(FileNotFoundError):
         ar.resolve_model_directory(model=tmp_path)  # a config.json alone is not a checkpoint directory
     ar.set_log_level(level="debug")
+
+
+# classes and functions the reference's pybind module registers (bindings.cpp:131-369)
+REFERENCE_CORE = ["AttentionProfile", "AttnRankError", "BasinCriterion", "BasinStatistics", "Document",
+                  "GenerationResult", "LayerProbeResult", "LayerScanConfig", "LlamaConfig", "ProbeSample",
+                  "ProfilerConfig", "PromptTemplate", "RuntimeOptions", "ScoredDocument", "StructuredPrompt",
+                  "SyntheticProbeConfig", "TokenSpan", "basin_statistics", "build_attention_profile",
+                  "chat_format_names", "detect_chat_format", "load_probe_samples", "make_reranker", "reranker_names",
+                  "resolve_position_order", "scan_attention_layers", "select_shallowest_basin_layer", "set_log_level",
+                  "synthetic_probe_samples", "Engine"]
+
+
+def test_core_module_names_match_the_reference_bindings():
+    from attnrank import core
+    missing = [name for name in REFERENCE_CORE if not hasattr(core, name)]
+    assert not missing, missing
+    template = core.PromptTemplate()
+    assert template.document_index_placeholder == "{index}" and not template.include_titles
+    with pytest.raises(core.AttnRankError, match="tokenizer"):
+        core.synthetic_probe_samples(core.SyntheticProbeConfig())
