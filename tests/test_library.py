@@ -50,3 +50,56 @@ def test_engine_creation_without_gpu_fails_loudly():
                             num_key_value_heads=2, vocab_size=100)
     with pytest.raises(ar.AttnRankError):
         ar.Engine.synthetic(config)
+
+
+def _c_declarations(text: str) -> str:
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return re.sub(r"//[^\n]*", "", text)
+
+
+def _ctype_of(declaration: str):
+    """ctypes class of one C parameter or field declaration (the name dropped)."""
+    if "*" in declaration:
+        return "pointer"
+    kind = declaration.replace("const", " ").split()[0]
+    return {"int": ctypes.c_int, "int32_t": ctypes.c_int32, "int64_t": ctypes.c_int64, "uint64_t": ctypes.c_uint64,
+            "float": ctypes.c_float, "double": ctypes.c_double}[kind]
+
+
+def _same(expected, actual) -> bool:
+    if expected == "pointer":
+        return actual in (ctypes.c_void_p, ctypes.c_char_p) or hasattr(actual, "_type_") and actual.__name__.startswith("LP_")
+    return ctypes.sizeof(actual) == ctypes.sizeof(expected) and actual._type_ == expected._type_
+
+
+def test_python_binding_argument_types_match_the_header():
+    """Every ctypes argtypes list has the header's arity and, position by position, its C types
+    (a float passed where the library takes a double, or an int where it takes int64_t, would
+    read garbage without any error)."""
+    from attnrank import _native
+    text = _c_declarations(HEADER.read_text())
+    prototypes = re.findall(r"\b(ar_[a-z0-9_]+)\s*\(([^;{)]*)\)\s*;", text)
+    assert len(prototypes) == len(declared_functions())
+    for name, parameters in prototypes:
+        parameters = parameters.strip()
+        declared = [] if parameters in ("", "void") else [p.strip() for p in parameters.split(",")]
+        bound = _native.SIGNATURES[name]
+        assert len(bound) == len(declared), f"{name}: {len(bound)} ctypes arguments, {len(declared)} in the header"
+        for index, (c_declaration, ctype) in enumerate(zip(declared, bound)):
+            assert _same(_ctype_of(c_declaration), ctype), f"{name} argument {index}: `{c_declaration}` vs {ctype}"
+
+
+def test_python_structures_match_the_header_layout():
+    """Field order, types and size of each ctypes Structure against its typedef struct."""
+    from attnrank import _native
+    text = _c_declarations(HEADER.read_text())
+    structures = {"ar_llama_config": _native.LlamaConfigStruct, "ar_runtime_options": _native.RuntimeOptionsStruct,
+                  "ar_prompt": _native.PromptStruct, "ar_sampler_config": _native.SamplerConfigStruct,
+                  "ar_basin_stats": _native.BasinStatsStruct}
+    for c_name, structure in structures.items():
+        body = re.search(r"typedef struct\s*\{([^}]*)\}\s*" + c_name + r"\s*;", text)
+        assert body, c_name
+        fields = [f.strip() for f in body.group(1).split(";") if f.strip()]
+        assert [f.split()[-1].lstrip("*") for f in fields] == [n for n, _ in structure._fields_], c_name
+        for c_field, (field_name, ctype) in zip(fields, structure._fields_):
+            assert _same(_ctype_of(c_field), ctype), f"{c_name}.{field_name}: `{c_field}` vs {ctype}"
