@@ -37,6 +37,16 @@ def shard_by_length(lengths: Sequence[int], world_size: int) -> list[list[int]]:
     return [sorted(shard) for shard in shards]
 
 
+def layer_range(settings: LayerScanSettings, num_layers: int) -> tuple[int, int]:
+    """The scanned layers [begin, end): a negative begin means 0 and a negative (or absent) end
+    means every layer, as AttentionLayerProbeRequest::resolve_layers (attnrank/src/model.cpp:66-68)."""
+    begin = 0 if settings.layer_begin < 0 else settings.layer_begin
+    end = num_layers if settings.layer_end is None or settings.layer_end < 0 else settings.layer_end
+    if begin >= end or end > num_layers:
+        raise core.AttnRankError(f"layer range [{begin}, {end}) is outside the model's {num_layers} layers")
+    return begin, end
+
+
 def _dist():
     import torch.distributed as dist
     return dist if dist.is_available() and dist.is_initialized() else None
@@ -65,16 +75,14 @@ class ProbeScheduler:
 
         if len(samples) == 0:
             raise core.AttnRankError("probe needs at least one sample")
-        begin = settings.layer_begin
-        end = self.engine.num_layers if settings.layer_end is None else settings.layer_end
+        begin, end = layer_range(settings, self.engine.num_layers)
         slots = len(samples[0].document_spans)
         accumulator = torch.zeros((end - begin) * slots, dtype=torch.float32, device=self.accumulator_device())
         if accumulator.is_cuda:
             torch.cuda.synchronize(accumulator.device)
         mine = [samples[i] for i in self.shard(samples)]
         if mine:
-            self.engine.scan(mine, begin, -1 if settings.layer_end is None else settings.layer_end,
-                             settings.normalize_by_length, accumulator=accumulator)
+            self.engine.scan(mine, begin, end, settings.normalize_by_length, accumulator=accumulator)
         dist = _dist()
         if dist is not None and self.world_size > 1:
             dist.all_reduce(accumulator, op=dist.ReduceOp.SUM, group=self.group)
@@ -89,7 +97,8 @@ class ProbeScheduler:
             raise ValueError(f"attention-basin detection needs at least {MINIMUM_BASIN_SLOTS} documents per sample")
         accumulated = self.accumulate(samples, settings)
         model_id = settings.model_id or getattr(self.engine, "model_directory", "")
-        profiles = [core.AttentionProfile.from_accumulated(model_id, settings.layer_begin + layer, len(samples),
+        begin, _ = layer_range(settings, self.engine.num_layers)
+        profiles = [core.AttentionProfile.from_accumulated(model_id, begin + layer, len(samples),
                                                            accumulated[layer])
                     for layer in range(accumulated.shape[0])]
         selected = core.select_shallowest_basin_layer(profiles, core.BasinCriterion(settings.min_edge_ratio))

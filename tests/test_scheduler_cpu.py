@@ -40,8 +40,9 @@ class FakeEngine:
     def scan(self, prompts, layer_begin, layer_end, normalize_by_length, accumulator=None):
         if self.fail:
             raise RuntimeError("injected rank failure")
+        begin = 0 if layer_begin < 0 else layer_begin  # the engine's own range resolution
         end = self.num_layers if layer_end < 0 else layer_end
-        total = sum(self.rows(p, self.num_layers)[layer_begin:end] for p in prompts)
+        total = sum(self.rows(p, self.num_layers)[begin:end] for p in prompts)
         accumulator += __import__("torch").from_numpy(total.reshape(-1).astype(np.float32))
         return total
 
@@ -124,3 +125,25 @@ def test_rank_failure_propagates_without_hanging():
     results = _run(2, fail_rank=1)
     assert results[1][1] == "error" and "injected" in results[1][3]
     assert results[0][1] == "error"  # the surviving rank's all-reduce fails instead of hanging
+
+
+def test_layer_range_follows_the_reference_resolution():
+    """A negative begin means layer 0 and a negative or absent end means every layer
+    (model.cpp:66-68); the profiles carry the resolved layer indices."""
+    import attnrank as ar
+    from attnrank.scheduler import layer_range
+    prompts = _prompts()
+    everything = ProbeScheduler(FakeEngine()).find_shallowest_attention_layer(prompts, ar.LayerScanSettings())
+    for begin, end in [(-1, None), (0, -1), (-5, -2)]:
+        scan = ProbeScheduler(FakeEngine()).find_shallowest_attention_layer(
+            prompts, ar.LayerScanSettings(layer_begin=begin, layer_end=end))
+        assert [p.layer_index for p in scan.profiles] == [0, 1, 2, 3]
+        for mine, full in zip(scan.profiles, everything.profiles):
+            np.testing.assert_allclose(mine.attention, full.attention, rtol=1e-6)
+    window = ProbeScheduler(FakeEngine()).find_shallowest_attention_layer(
+        prompts, ar.LayerScanSettings(layer_begin=1, layer_end=3))
+    assert [p.layer_index for p in window.profiles] == [1, 2]
+    np.testing.assert_allclose(window.profiles[0].attention, everything.profiles[1].attention, rtol=1e-6)
+    for bad in [(2, 2), (0, 9), (3, 1)]:
+        with pytest.raises(ar.AttnRankError):
+            layer_range(ar.LayerScanSettings(layer_begin=bad[0], layer_end=bad[1]), 4)
