@@ -77,6 +77,10 @@ class ProbeScheduler:
             raise core.AttnRankError("probe needs at least one sample")
         begin, end = layer_range(settings, self.engine.num_layers)
         slots = len(samples[0].document_spans)
+        for index, sample in enumerate(samples):  # every rank checks every sample, before any collective
+            if len(sample.document_spans) != slots:
+                raise core.AttnRankError(f"probe sample {index} produced {len(sample.document_spans)} spans, "
+                                         f"expected {slots}")
         accumulator = torch.zeros((end - begin) * slots, dtype=torch.float32, device=self.accumulator_device())
         if accumulator.is_cuda:
             torch.cuda.synchronize(accumulator.device)

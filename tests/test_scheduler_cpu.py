@@ -147,3 +147,17 @@ def test_layer_range_follows_the_reference_resolution():
     for bad in [(2, 2), (0, 9), (3, 1)]:
         with pytest.raises(ar.AttnRankError):
             layer_range(ar.LayerScanSettings(layer_begin=bad[0], layer_end=bad[1]), 4)
+
+
+def test_mixed_span_counts_fail_on_every_rank_before_the_all_reduce():
+    """AttentionProbeRun::run (attnrank.cpp:283-307) rejects a sample whose span count differs from
+    the first one; the sharded scan checks all samples on every rank, so no rank reaches the
+    collective with a mismatched accumulator."""
+    import attnrank as ar
+    from attnrank import core
+    prompts = list(_prompts())
+    odd = prompts[5]
+    prompts[5] = core.StructuredPrompt(tokens=odd.tokens, document_spans=list(odd.document_spans)[:4],
+                                       query_span=odd.query_span)
+    with pytest.raises(ar.AttnRankError, match="probe sample 5 produced 4 spans, expected 5"):
+        ProbeScheduler(FakeEngine()).find_shallowest_attention_layer(prompts, ar.LayerScanSettings())
