@@ -766,12 +766,14 @@ void Engine::validate(const std::vector<PromptView>& prompts, int span_count, La
     if (p.token_count > options_.max_sequence_length) {
       throw Error("probe input of " + std::to_string(p.token_count) + " tokens exceeds the context window");
     }
-    if (p.query_begin < 0 || p.query_end < p.query_begin) {
-      throw Error("probe prompt " + std::to_string(i) + " has an invalid query span");
-    }
+    // Degenerate spans are accepted as the reference accepts them (DocumentAttentionProbe and
+    // reduce_document_attention_kernel, attnrank/src/model.cu:248-251, kernels.cu:211-219): the
+    // query span is clipped to [0, tokens), so an empty or reversed one gives all-zero rows, and a
+    // document span with end <= begin holds no keys (zero mass). A negative document begin is
+    // rejected: there the reference reads before the score row.
     for (int s = 0; s < span_count; ++s) {
-      if (p.spans[2 * s] < 0 || p.spans[2 * s + 1] < p.spans[2 * s]) {
-        throw Error("probe prompt " + std::to_string(i) + " has an invalid document span");
+      if (p.spans[2 * s] < 0) {
+        throw Error("probe prompt " + std::to_string(i) + " has a document span that begins before token 0");
       }
     }
   }

@@ -94,6 +94,7 @@ def document_mass(probs: torch.Tensor, prompt: Prompt, chunk: int, normalize_by_
     """
     T = probs.shape[-1]
     qb, qe = prompt.query_span
+    qb = max(qb, 0)  # rows before token 0 do not exist (kernels.cu:218 keeps every row >= begin)
     qe = min(qe, T)
     out = np.zeros(len(prompt.spans), dtype=np.float64)
     if qe <= qb:

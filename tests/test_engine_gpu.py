@@ -136,6 +136,48 @@ def test_engine_rejects_bad_requests(cuda):
     assert engine.measure_attention_by_layer(good).layer_begin == 0
 
 
+@pytest.mark.parametrize("kernel", ["tcgen05", "mma"])
+def test_degenerate_spans_follow_the_reference(cuda, kernel):
+    """Spans the reference accepts without an error (DocumentAttentionProbe, model.cu:248-251;
+    reduce_document_attention_kernel, kernels.cu:211-219): a query span starting before token 0
+    covers every row from 0, an empty or reversed query span gives all-zero rows, and an empty or
+    reversed document span holds no keys. A document span beginning before token 0 is rejected
+    (the reference would read before the score row)."""
+    import attnrank as ar
+    from oracle import forward as F
+    config = small_config(True, layers=2)
+    engine = ar.Engine.synthetic(config, seed=4, options=ar.RuntimeOptions(attention_kernel=kernel))
+    oracle = F.OracleModel(oracle_shape(config), seed=4)
+    base = small_prompts(1, config.vocab_size, seed=11)[0]
+    q0, q1 = base.query_span.begin, base.query_span.end
+    spans = [(s.begin, s.end) for s in base.document_spans]
+    reversed_doc = list(spans)
+    reversed_doc[2] = (spans[2][1], spans[2][0])
+    empty_doc = list(spans)
+    empty_doc[2] = (spans[2][1], spans[2][1])
+
+    def probe(query, document_spans):
+        prompt = ar.StructuredPrompt(tokens=base.tokens, document_spans=document_spans, query_span=query)
+        return np.asarray(engine.measure_attention_by_layer(prompt).attention_by_layer)
+
+    def expected(query, document_spans):
+        prompt = F.Prompt(tokens=np.asarray(base.tokens), query_span=query, spans=document_spans)
+        return oracle.probe([prompt])[0][0]
+
+    for query in [(-7, q1), (0, q1)]:
+        assert_rows_close(probe(query, spans), expected(query, spans))
+    np.testing.assert_array_equal(probe((-7, q1), spans), probe((0, q1), spans))
+    for query in [(q1, q0), (q0, q0)]:
+        assert not np.any(probe(query, spans))
+    got = probe((q0, q1), reversed_doc)
+    np.testing.assert_array_equal(got, probe((q0, q1), empty_doc))
+    assert not np.any(got[:, 2])
+    assert_rows_close(got, expected((q0, q1), reversed_doc))
+    with pytest.raises(ar.AttnRankError, match="before token 0"):
+        probe((q0, q1), [(-1, 5)] + spans[1:])
+    assert engine.measure_attention_by_layer(base).layer_begin == 0  # still usable
+
+
 # ---- 7B architecture against the reference's CUDA build ------------------------------------
 @pytest.fixture(scope="module")
 def qwen_pair(cuda, reference_lib):

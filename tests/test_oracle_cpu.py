@@ -59,17 +59,22 @@ def _loop_reduction(probs, heads, T, qb, qe, spans, chunk, normalize):
 
 
 @pytest.mark.parametrize("normalize", [False, True])
-def test_document_mass_matches_literal_reference_loop(normalize):
+@pytest.mark.parametrize("query", [(13, 21), (-4, 21), (5, 40), (21, 13), (13, 13)])
+def test_document_mass_matches_literal_reference_loop(normalize, query):
+    """Ordinary and degenerate spans the reference accepts without an error: a query span that
+    starts before token 0 or ends past the prompt, an empty or reversed query span, and empty or
+    reversed document spans (their key loops run zero times)."""
     rng = np.random.default_rng(5)
     heads, T, chunk = 3, 23, 8
     scores = torch.from_numpy(rng.standard_normal((heads, T, T)).astype(np.float32))
     mask = torch.arange(T)[None, :] <= torch.arange(T)[:, None]
     probs = torch.softmax(scores.masked_fill(~mask[None], float("-inf")), dim=-1)
-    spans = [(0, 5), (5, 11), (11, 16), (3, 9), (14, 40)]
-    prompt = F.Prompt(tokens=np.zeros(T, np.int32), query_span=(13, 21), spans=spans)
+    spans = [(0, 5), (5, 11), (11, 16), (3, 9), (14, 40), (9, 3), (7, 7)]
+    prompt = F.Prompt(tokens=np.zeros(T, np.int32), query_span=query, spans=spans)
     got = F.document_mass(probs, prompt, chunk, normalize)
-    want = _loop_reduction(probs.numpy(), heads, T, 13, 21, spans, chunk, normalize)
+    want = _loop_reduction(probs.numpy(), heads, T, query[0], query[1], spans, chunk, normalize)
     np.testing.assert_allclose(got, want, rtol=1e-12)
+    assert got[5] == 0.0 and got[6] == 0.0
 
 
 def _fixture(name):
