@@ -554,6 +554,9 @@ class Engine:
             if model_directory is None:
                 raise AttnRankError("Engine needs a model directory or a config")
             config = LlamaConfig.from_file(Path(model_directory) / "config.json")
+            # q/k/v biases are used when the checkpoint holds them (model.cu:160-162)
+            from attnrank.checkpoint import has_attention_bias
+            config.attention_bias = has_attention_bias(Path(model_directory))
         self.config = config
         handle = ctypes.c_void_p()
         options_struct = self.options.to_struct()

@@ -28,7 +28,7 @@ from attnrank.data.classes import (DEFAULT_MIN_EDGE_RATIO, DEFAULT_SEED, EngineS
                                    LayerScanSettings, ProfileSettings)
 
 MODEL_CONFIG_FILE = "config.json"
-WEIGHT_FILE_PATTERNS = ("*.safetensors",)
+WEIGHT_FILE_PATTERNS = ("*.safetensors", "pytorch_model*.bin")
 MINIMUM_BASIN_SLOTS = 3
 
 ProgressCallback = Callable[[int, int], None]

@@ -88,6 +88,41 @@ def test_from_pretrained_equals_synthetic_engine(cuda, tmp_path, matrix_dtype):
     reference.close()
 
 
+def test_from_pretrained_reads_a_torch_archive_and_finds_its_biases(cuda, tmp_path):
+    """The same weights as a pytorch_model.bin archive (the reference's fallback when a directory
+    has no safetensors, checkpoint.cpp:157-172), with a config.json that names no attention bias
+    (model_type "llama"): the biases are used because the checkpoint holds them, as the
+    reference's optional bias upload does (model.cu:160-162)."""
+    import torch
+
+    import attnrank as ar
+    from attnrank import synthetic
+    from attnrank.checkpoint import iter_tensors
+    config = _config()
+    _write_checkpoint(tmp_path, config, "BF16")
+    shard = tmp_path / "model.safetensors"
+    state = {}
+    for name, array, code in iter_tensors(shard):
+        values = torch.from_numpy(np.array(array))
+        state[name] = values.view(torch.bfloat16) if code == 2 else values
+    shard.unlink()
+    torch.save(state, tmp_path / "pytorch_model.bin")
+    settings = json.loads((tmp_path / "config.json").read_text())
+    settings["model_type"] = "llama"
+    (tmp_path / "config.json").write_text(json.dumps(settings))
+    assert not ar.LlamaConfig.from_file(tmp_path / "config.json").attention_bias
+    loaded = ar.from_pretrained(model=tmp_path)
+    assert loaded.config.attention_bias
+    reference = ar.Engine.synthetic(config, seed=0)
+    shape = synthetic.PromptShape(documents=5, document_min=20, document_max=90, question=12)
+    prompts = synthetic.prompts(3, config.vocab_size, shape, seed=8)
+    got, _ = loaded.probe_rows(prompts)
+    want, _ = reference.probe_rows(prompts)
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-9)
+    loaded.close()
+    reference.close()
+
+
 def test_from_pretrained_reports_a_missing_tensor(cuda, tmp_path):
     import attnrank as ar
     from attnrank import synthetic
