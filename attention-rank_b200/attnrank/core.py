@@ -96,8 +96,12 @@ class LlamaConfig:
     @classmethod
     def from_dict(cls, root: dict) -> "LlamaConfig":
         def read(key, fallback):
+            # Json::as_int64 / as_double (core.cpp:418-428): a number, a bool as 0 / 1, anything
+            # else (absent, null, a list such as Llama-3's eos_token_id, a string) the fallback
             value = root.get(key)
-            return fallback if value is None else value
+            if isinstance(value, bool):
+                return int(value)
+            return value if isinstance(value, (int, float)) else fallback
 
         config = cls()
         config.hidden_size = int(read("hidden_size", config.hidden_size))
@@ -114,7 +118,8 @@ class LlamaConfig:
         window = root.get("sliding_window")
         if isinstance(window, (int, float)) and not isinstance(window, bool):
             config.sliding_window = int(window)
-        config.tie_word_embeddings = bool(root.get("tie_word_embeddings", False))
+        tied = root.get("tie_word_embeddings")  # Json::as_bool(false), core.cpp:412-416
+        config.tie_word_embeddings = bool(tied) if isinstance(tied, (bool, int, float)) else False
         model_type = str(root.get("model_type", ""))
         config.attention_bias = bool(root.get("attention_bias", model_type.startswith("qwen2")))
         if config.num_attention_heads <= 0 or config.hidden_size % config.num_attention_heads != 0:

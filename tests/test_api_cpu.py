@@ -117,3 +117,27 @@ def test_core_module_names_match_the_reference_bindings():
     assert template.document_index_placeholder == "{index}" and not template.include_titles
     with pytest.raises(core.AttnRankError, match="tokenizer"):
         core.synthetic_probe_samples(core.SyntheticProbeConfig())
+
+
+def test_config_json_values_are_read_like_the_reference(tmp_path):
+    """LlamaConfig::from_json (model.cpp:24-51) through Json::as_int64 / as_double / as_bool
+    (core.cpp:412-428): numbers are used, bools count as 0 / 1, and anything else (null, a list
+    such as Llama-3-Instruct's eos_token_id, a string) keeps the default."""
+    import json
+
+    import attnrank as ar
+    (tmp_path / "config.json").write_text(json.dumps({
+        "hidden_size": 4096, "intermediate_size": 14336, "num_hidden_layers": 32, "num_attention_heads": 32,
+        "num_key_value_heads": 8, "vocab_size": 128256, "rms_norm_eps": 1e-5, "rope_theta": 500000.0,
+        "bos_token_id": 128000, "eos_token_id": [128001, 128008, 128009], "max_position_embeddings": None,
+        "tie_word_embeddings": False, "sliding_window": None, "model_type": "llama"}))
+    config = ar.LlamaConfig.from_file(tmp_path / "config.json")
+    assert (config.num_key_value_heads, config.vocab_size, config.bos_token_id) == (8, 128256, 128000)
+    assert config.eos_token_id == 2 and config.max_position_embeddings == 4096  # the defaults
+    assert config.rope_theta == 500000.0 and config.sliding_window == 0 and not config.tie_word_embeddings
+    quirky = ar.LlamaConfig.from_dict({"hidden_size": 512, "num_attention_heads": 4, "vocab_size": "2000",
+                                       "tie_word_embeddings": 1, "sliding_window": True})
+    assert quirky.vocab_size == 32000 and quirky.tie_word_embeddings and quirky.sliding_window == 0
+    assert quirky.num_key_value_heads == 4  # defaults to the attention heads
+    with pytest.raises(ar.AttnRankError, match="key/value head"):
+        ar.LlamaConfig.from_dict({"hidden_size": 512, "num_attention_heads": 4, "num_key_value_heads": 3})
