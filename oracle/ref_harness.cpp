@@ -13,8 +13,9 @@
 //     (attnrank.cpp:257-265), fed token-id prompts through an IPromptBuilder (prompt.hpp:25-30)
 //     that returns the given StructuredPrompt for each sample;
 //   * its generate (model.cu:532-565), the answering step, with the reference's samplers;
-//   * the reference's host functions (profile, basin statistics, position order, the samplers of
-//     model.cpp:70-127), which run without a GPU and produce the golden fixtures under tests/golden/.
+//   * the reference's host functions (profile, basin statistics, position order, the rerankers of
+//     attnrank.cpp:394-456, the samplers of model.cpp:70-127), which run without a GPU and produce
+//     the golden fixtures under tests/golden/.
 #include <algorithm>
 #include <chrono>
 #include <cstdint>
@@ -433,6 +434,35 @@ int ref_resolve_position_order(const int* preferred, int preferred_count, int co
                                                         static_cast<size_t>(count));
   for (int i = 0; i < count; ++i) order_out[i] = order[i];
   return 0;
+}
+
+// One reranker of RerankerFactory::create (attnrank.cpp:445-456) applied `calls` times to the
+// ranking 0 .. count-1 (score count - i, as engine.py's rerank_baseline builds it): out[c][i] is
+// the index at position i after call c. The random reranker's state carries across calls.
+int ref_rerank(const char* strategy, uint64_t seed, int lim_start_first, const int* position_order, int order_count,
+               int count, int calls, int* out) {
+  try {
+    AttentionProfile profile;
+    profile.position_order.assign(position_order, position_order + order_count);
+    RerankerOptions options;
+    options.profile = &profile;
+    options.seed = seed;
+    options.lim_start_first = lim_start_first != 0;
+    const std::shared_ptr<IReranker> reranker = RerankerFactory::create(strategy, options);
+    std::vector<ScoredDocument> ranked(static_cast<size_t>(count));
+    for (int i = 0; i < count; ++i) {
+      ranked[i].index = static_cast<size_t>(i);
+      ranked[i].score = static_cast<double>(count - i);
+    }
+    for (int c = 0; c < calls; ++c) {
+      const std::vector<ScoredDocument> result = reranker->rerank(ranked);
+      for (int i = 0; i < count; ++i) out[static_cast<size_t>(c) * count + i] = static_cast<int>(result[i].index);
+    }
+    return 0;
+  } catch (const std::exception& error) {
+    g_error = error.what();
+    return 1;
+  }
 }
 
 }  // extern "C"

@@ -56,6 +56,7 @@ def load_or_none():
     lib.ref_basin_statistics.argtypes = [P, I, D, P]
     lib.ref_select_shallowest.argtypes = [P, P, I, I, D]
     lib.ref_resolve_position_order.argtypes = [P, I, I, P]
+    lib.ref_rerank.argtypes = [ctypes.c_char_p, ctypes.c_uint64, I, P, I, I, I, P]
     lib.ref_generate.argtypes = [P, P, I, I, ctypes.c_float, ctypes.c_float, I, ctypes.c_uint64, P, P, P]
     lib.ref_sample.argtypes = [ctypes.c_float, ctypes.c_float, I, ctypes.c_uint64, P, I, I, P]
     lib.ref_prefill_logits.argtypes = [P, P, I, P]
@@ -206,6 +207,19 @@ def resolve_position_order(preferred: Sequence[int], count: int) -> list[int]:
     out = np.zeros(count, dtype=np.int32)
     lib.ref_resolve_position_order(pref.ctypes.data if pref.size else None, pref.size, count, out.ctypes.data)
     return [int(v) for v in out]
+
+
+def rerank(strategy: str, count: int, calls: int = 1, seed: int = 1234, lim_start_first: bool = False,
+           position_order: Sequence[int] = ()) -> list[list[int]]:
+    """The reference's RerankerFactory reranker applied `calls` times to the ranking 0..count-1:
+    the document index at each position after every call (the random reranker's state carries)."""
+    lib = _require()
+    order = np.ascontiguousarray(np.asarray(position_order, dtype=np.int32))
+    out = np.zeros((max(calls, 1), max(count, 1)), dtype=np.int32)
+    if lib.ref_rerank(strategy.encode(), seed, int(lim_start_first), order.ctypes.data if order.size else None,
+                      order.size, count, calls, out.ctypes.data) != 0:
+        raise RuntimeError(lib.ref_last_error().decode())
+    return [[int(v) for v in row[:count]] for row in out[:calls]]
 
 
 def sample(logits_rows: np.ndarray, temperature: float, top_p: float, top_k: int, seed: int) -> list[int]:
