@@ -7,10 +7,11 @@ token-id prompts (``StructuredPrompt``). All probing runs in libattnrank_b200.so
 package without the built library raises ImportError.
 """
 from attnrank import core
-from attnrank.core import (AttentionProfile, AttnRankError, BasinCriterion, BasinStatistics, Engine, GenerationResult,
-                           LayerProbeResult, LayerScanConfig, LlamaConfig, ProfilerConfig, RuntimeOptions,
-                           StructuredPrompt, TokenSampler, TokenSpan, make_sampler)
-from attnrank.data.classes import EngineSettings, GenerationSettings, LayerScanSettings, ProfileSettings
+from attnrank.core import (AttentionProfile, AttnRankError, BasinCriterion, BasinStatistics, Document, Engine,
+                           GenerationResult, LayerProbeResult, LayerScanConfig, LlamaConfig, ProbeSample,
+                           ProfilerConfig, RuntimeOptions, StructuredPrompt, TokenSampler, TokenSpan, make_sampler)
+from attnrank.data.classes import (EngineSettings, GenerationSettings, LayerScanSettings, ProfileSettings,
+                                   SyntheticProbeSettings)
 from attnrank.engine import (LayerScan, attention_slot_order, basin_statistics, extract_attention_profile,
                              find_shallowest_attention_layer, from_pretrained, generate_from_prompt,
                              is_model_directory, set_log_level, model_config, resolve_model_directory,
@@ -26,7 +27,8 @@ from attnrank.engine import (LayerScan, attention_slot_order, basin_statistics, 
 __version__ = "0.1.0"
 
 __all__ = [
-    "AttentionProfile", "AttnRankError", "BasinCriterion", "BasinStatistics", "Engine", "EngineSettings",
+    "AttentionProfile", "AttnRankError", "BasinCriterion", "BasinStatistics", "Document", "Engine", "EngineSettings",
+    "ProbeSample", "SyntheticProbeSettings",
     "GenerationResult", "GenerationSettings", "TokenSampler", "generate_from_prompt", "make_sampler",
     "LayerProbeResult", "LayerScan", "LayerScanConfig", "LayerScanSettings", "LlamaConfig", "ProfileSettings",
     "ProfilerConfig", "RuntimeOptions", "StructuredPrompt", "TokenSpan", "attention_slot_order", "basin_statistics",

@@ -141,3 +141,39 @@ def test_config_json_values_are_read_like_the_reference(tmp_path):
     assert quirky.num_key_value_heads == 4  # defaults to the attention heads
     with pytest.raises(ar.AttnRankError, match="key/value head"):
         ar.LlamaConfig.from_dict({"hidden_size": 512, "num_attention_heads": 4, "num_key_value_heads": 3})
+
+
+# attnrank/__init__.py of the reference, less the text facade (AttnRank, PromptTemplate), the dataset
+# sources (DatasetSpec, FieldMapping, load_rows) and the answer services (rerank_top_k,
+# answer_with_top_k): those need a tokenizer or a dataset service, outside the profiling path
+REFERENCE_TOP_LEVEL = [
+    "AttentionProfile", "AttnRankError", "Document", "Engine", "EngineSettings", "GenerationSettings", "LayerScan",
+    "LayerScanSettings", "ProbeSample", "ProfileSettings", "SyntheticProbeSettings", "attention_slot_order",
+    "basin_statistics", "build_prompt", "chat_format_names", "core", "detect_chat_format", "download_model",
+    "extract_attention_profile", "find_shallowest_attention_layer", "from_pretrained", "generate_answer",
+    "generate_from_prompt", "is_model_directory", "load_attention_profile", "load_model", "load_model_and_profile",
+    "load_probe_samples", "make_document", "make_documents", "make_probe_sample", "make_probe_samples",
+    "make_reranker", "measure_attention_by_layer", "measure_document_attention", "model_config", "profile_to_dict",
+    "rerank_baseline", "rerank_documents", "rerank_with_profile", "reranker_names", "resolve_model_directory",
+    "save_attention_profile", "scan_attention_layers", "select_shallowest_basin_layer", "set_log_level",
+    "synthetic_probe_samples"]
+
+
+def test_package_exports_and_settings_keep_the_reference_fields():
+    import dataclasses
+
+    import attnrank as ar
+    from attnrank.data import classes
+    assert [name for name in REFERENCE_TOP_LEVEL if not hasattr(ar, name)] == []
+    # data/classes.py:19-31 of the reference, in its order (positional construction agrees)
+    engine_fields = ["device", "max_sequence", "chunk", "chat_format", "system_prompt", "instruction", "example",
+                     "max_document_tokens", "include_titles", "document_separator", "document_label",
+                     "extra_stop_sequences"]
+    assert [f.name for f in dataclasses.fields(ar.EngineSettings)][:len(engine_fields)] == engine_fields
+    settings = ar.EngineSettings(instruction="Answer briefly.", document_separator="\n\n")
+    assert (settings.max_sequence, settings.chunk, settings.document_label) == (4096, 512, None)
+    synthetic = ar.SyntheticProbeSettings()
+    assert (synthetic.document_slots, synthetic.sample_count, synthetic.words_per_document, synthetic.seed) == \
+        (5, 32, 60, 20250807)
+    assert classes.STRATEGIES == ("random", "descending", "ascending", "lim", "attnrank")
+    assert (classes.DEFAULT_MIN_EDGE_RATIO, classes.DEFAULT_PROBE_SAMPLES, classes.DEFAULT_SEED) == (1.3, 400, 1234)
