@@ -10,11 +10,10 @@ from __future__ import annotations
 
 import ctypes
 import json
-import math
 import threading
 from dataclasses import dataclass, field
 from pathlib import Path
-from typing import Callable, Iterable, Sequence
+from typing import Callable, Sequence
 
 import numpy as np
 

@@ -17,8 +17,6 @@ from __future__ import annotations
 import heapq
 from typing import Sequence
 
-import numpy as np
-
 from attnrank import core
 from attnrank.data.classes import LayerScanSettings
 
