@@ -856,9 +856,11 @@ BatchLayout Engine::build_metadata(const std::vector<PromptView>& prompts, const
       pairs = W * (W + 1) / 2 + (L - W) * W;
     }
     layout.attention_flops += 4 * D * Hq * pairs;
+    // work of the rows and keys that exist: spans clipped to the prompt as the kernels clip them
     double span_keys = 0;
-    for (int s = 0; s < S; ++s) span_keys += p.spans[2 * s + 1] - p.spans[2 * s];
-    layout.mass_flops += 2 * D * Hq * (p.query_end - p.query_begin) * span_keys;
+    for (int s = 0; s < S; ++s) span_keys += std::max(0, std::min(p.spans[2 * s + 1], p.token_count) - p.spans[2 * s]);
+    const int query_rows = std::max(0, std::min(p.query_end, p.token_count) - std::max(p.query_begin, 0));
+    layout.mass_flops += 2 * D * Hq * static_cast<double>(query_rows) * span_keys;
   }
   layout.tokens_at = tokens_at;
   layout.offsets_at = offsets_at;
