@@ -204,10 +204,10 @@ class TokenSampler:
         check(lib.ar_sampler_select(self._handle, values.ctypes.data, values.size, ctypes.byref(token)))
         return int(token.value)
 
-    def __del__(self):
+    def __del__(self, _destroy=lib.ar_sampler_destroy):  # bound now: module globals may be gone at exit
         handle = getattr(self, "_handle", None)
         if handle is not None and handle.value:
-            lib.ar_sampler_destroy(handle)
+            _destroy(handle)
             self._handle = None
 
 
@@ -580,10 +580,10 @@ class Engine:
         check(lib.ar_engine_init_synthetic(engine._handle, int(seed), float(std)))
         return engine
 
-    def __del__(self):
+    def __del__(self, _destroy=lib.ar_engine_destroy):  # bound now: module globals may be gone at exit
         handle = getattr(self, "_handle", None)
         if handle is not None and handle.value:
-            lib.ar_engine_destroy(handle)
+            _destroy(handle)
             self._handle = None
 
     def close(self) -> None:
@@ -795,10 +795,10 @@ class PreparedScan:
         check(lib.ar_engine_run_prepared_scan(self.engine._handle, self._handle, accumulator.data_ptr(),
                                               1 if synchronize else 0))
 
-    def __del__(self):
+    def __del__(self, _destroy=lib.ar_prepared_scan_destroy):  # bound now: module globals may be gone at exit
         handle = getattr(self, "_handle", None)
         if handle is not None and handle.value:
-            lib.ar_prepared_scan_destroy(handle)
+            _destroy(handle)
             self._handle = None
 
 
