@@ -6,6 +6,8 @@
 #include <cstring>
 #include <numeric>
 
+#include <omp.h>
+
 #include "engine.h"
 
 namespace arb {
@@ -22,6 +24,15 @@ inline uint32_t descending_key(float value) {
   return ~ascending;
 }
 
+// the logit of a key (+0.0 for the zero key, which -0.0 shares)
+inline double key_value(uint32_t key) {
+  const uint32_t ascending = ~key;
+  const uint32_t bits = (ascending & 0x80000000u) ? (ascending & 0x7FFFFFFFu) : ~ascending;
+  float value;
+  std::memcpy(&value, &bits, sizeof(value));
+  return value;
+}
+
 }  // namespace
 
 // GreedySampler::select (model.cpp:70-73): the first index holding the largest logit.
@@ -34,30 +45,82 @@ NucleusTokenSampler::NucleusTokenSampler(const SamplerConfig& config) : config_(
   if (!(config_.temperature > 0.0f)) throw Error("nucleus sampling needs a positive temperature");
 }
 
-// Stable sort of all logits by descending value (radix sort of 32-bit keys, 8 bits a pass):
-// order_ holds the ids, keys_ their keys.
-void NucleusTokenSampler::sort_descending(const float* logits, int count) {
+// The order keys of the `keep` largest logits, ascending (so the logits descend), in keys_; keys
+// of equal logits are equal. One parallel most-significant-digit pass puts every key into one of
+// 4096 buckets by its top 12 bits (sign, exponent, three mantissa bits). Only the buckets that
+// hold the first `keep` keys are filled, and each is then sorted on its own. id_keys_ keeps every
+// id's key, so an id can be found again from its key.
+void NucleusTokenSampler::sort_keys(const float* logits, int count, size_t keep) {
+  constexpr int kBits = 12;
+  constexpr int kBuckets = 1 << kBits;
+  constexpr int kShift = 32 - kBits;
+  static_assert(kShift % 10 == 0 && (kShift / 10) % 2 == 0, "an even number of 10-bit passes per bucket");
   const size_t n = static_cast<size_t>(count);
-  keys_.resize(n);
-  order_.resize(n);
-  spare_keys_.resize(n);
-  spare_order_.resize(n);
-  for (size_t i = 0; i < n; ++i) {
-    keys_[i] = descending_key(logits[i]);
-    order_[i] = static_cast<int>(i);
-  }
-  for (int shift = 0; shift < 32; shift += 8) {
-    size_t counts[257] = {0};
-    for (size_t i = 0; i < n; ++i) ++counts[((keys_[i] >> shift) & 0xFFu) + 1];
-    if (counts[1] == n || counts[256] == n) continue;  // one bucket: this pass keeps the order
-    for (int b = 0; b < 256; ++b) counts[b + 1] += counts[b];
-    for (size_t i = 0; i < n; ++i) {
-      const size_t at = counts[(keys_[i] >> shift) & 0xFFu]++;
-      spare_keys_[at] = keys_[i];
-      spare_order_[at] = order_[i];
+  const int threads = n >= 32768 ? std::max(1, std::min(omp_get_max_threads(), 16)) : 1;
+  id_keys_.resize(n);
+  counts_.assign(static_cast<size_t>(threads) * kBuckets, 0u);
+  starts_.resize(kBuckets + 1);
+#pragma omp parallel num_threads(threads)
+  {
+    const int t = omp_get_thread_num();
+    uint32_t* histogram = counts_.data() + static_cast<size_t>(t) * kBuckets;
+    for (size_t i = n * t / threads, end = n * (t + 1) / threads; i < end; ++i) {
+      const uint32_t key = descending_key(logits[i]);
+      id_keys_[i] = key;
+      ++histogram[key >> kShift];
     }
-    keys_.swap(spare_keys_);
-    order_.swap(spare_order_);
+  }
+  // bucket starts; `needed` buckets hold at least `keep` keys
+  int needed = kBuckets;
+  uint32_t total = 0;
+  for (int b = 0; b < kBuckets; ++b) {
+    starts_[b] = total;
+    for (int t = 0; t < threads; ++t) {
+      uint32_t& slot = counts_[static_cast<size_t>(t) * kBuckets + b];
+      const uint32_t here = slot;
+      slot = total;  // this thread's first position in bucket b
+      total += here;
+    }
+    if (total >= keep && needed == kBuckets) needed = b + 1;
+  }
+  starts_[kBuckets] = total;
+  keys_.resize(starts_[needed]);
+#pragma omp parallel num_threads(threads)
+  {
+    const int t = omp_get_thread_num();
+    uint32_t* offset = counts_.data() + static_cast<size_t>(t) * kBuckets;
+    for (size_t i = n * t / threads, end = n * (t + 1) / threads; i < end; ++i) {
+      const uint32_t key = id_keys_[i];
+      const uint32_t bucket = key >> kShift;
+      if (bucket < static_cast<uint32_t>(needed)) keys_[offset[bucket]++] = key;
+    }
+  }
+  // each bucket: its keys share the top 12 bits; large buckets take two counting passes over the
+  // low 20 bits (10 bits a pass, through a per-thread scratch buffer), small ones std::sort
+  if (scratch_.size() < static_cast<size_t>(threads)) scratch_.resize(threads);
+#pragma omp parallel num_threads(threads)
+  {
+    std::vector<uint32_t>& scratch = scratch_[omp_get_thread_num()];
+#pragma omp for schedule(dynamic, 1)
+    for (int b = 0; b < needed; ++b) {
+      uint32_t* first = keys_.data() + starts_[b];
+      const uint32_t size = starts_[b + 1] - starts_[b];
+      if (size <= 256) {
+        std::sort(first, first + size);
+        continue;
+      }
+      if (scratch.size() < size) scratch.resize(size);
+      uint32_t* from = first;
+      uint32_t* to = scratch.data();
+      for (int shift = 0; shift < kShift; shift += 10) {
+        uint32_t digits[1025] = {0};
+        for (uint32_t i = 0; i < size; ++i) ++digits[((from[i] >> shift) & 0x3FFu) + 1];
+        for (int d = 0; d < 1024; ++d) digits[d + 1] += digits[d];
+        for (uint32_t i = 0; i < size; ++i) to[digits[(from[i] >> shift) & 0x3FFu]++] = from[i];
+        std::swap(from, to);
+      }
+      // an even number of passes: the sorted keys are back in the bucket
+    }
   }
 }
 
@@ -68,23 +131,23 @@ void NucleusTokenSampler::sort_descending(const float* logits, int count) {
 //   4. a uniform draw in [0, nucleus weight) walks the prefix; the candidate where it reaches 0
 //      is returned (the last nucleus candidate if rounding leaves it above 0).
 // Steps 2-4 depend only on the sequence of candidate VALUES, which every correct descending sort
-// yields (equal logits have equal weights). So the values come from a radix sort here, the weights
-// are computed in parallel (each exp is independent), and the sums, the cut and the walk run in
-// the reference's order. Only the id at the chosen position can depend on how std::partial_sort
-// orders equal logits: when the chosen value occurs more than once, the id is taken from the
-// reference's own partial_sort order; otherwise it is unique and identical by construction.
+// yields (equal logits have equal weights). So the values come from a sort of order keys
+// (sort_keys), the weights are computed in parallel (each exp is independent), and the sums, the
+// cut and the walk run in the reference's order. Only the id at the chosen position can depend on
+// how std::partial_sort orders equal logits: when the chosen value occurs more than once, the id
+// is taken from the reference's own partial_sort order; otherwise exactly one id has its key.
 int NucleusTokenSampler::select(const float* logits, int count) {
   if (logits == nullptr || count <= 0) throw Error("cannot sample from empty logits");
-  sort_descending(logits, count);
   const size_t n = static_cast<size_t>(count);
   const size_t keep = config_.top_k > 0 ? std::min<size_t>(static_cast<size_t>(config_.top_k), n) : n;
-  const double top = logits[order_[0]];
+  sort_keys(logits, count, keep);
+  const double top = key_value(keys_[0]);
   const double temperature = static_cast<double>(config_.temperature);
   weights_.resize(keep);
   const long long parallel_keep = static_cast<long long>(keep);
 #pragma omp parallel for schedule(static) if (parallel_keep > 32768)
   for (long long i = 0; i < parallel_keep; ++i) {
-    weights_[i] = std::exp((static_cast<double>(logits[order_[i]]) - top) / temperature);
+    weights_[i] = std::exp((key_value(keys_[i]) - top) / temperature);
   }
   double total = 0.0;
   for (size_t i = 0; i < keep; ++i) total += weights_[i];
@@ -109,9 +172,11 @@ int NucleusTokenSampler::select(const float* logits, int count) {
       break;
     }
   }
+  // equal keys share a bucket, and every filled bucket lies whole in keys_: the neighbours there
+  // tell whether the chosen logit occurs more than once among all ids
   const uint32_t key = keys_[chosen];
-  const bool tied = (chosen > 0 && keys_[chosen - 1] == key) || (chosen + 1 < n && keys_[chosen + 1] == key);
-  if (!tied) return order_[chosen];
+  const bool tied = (chosen > 0 && keys_[chosen - 1] == key) || (chosen + 1 < keys_.size() && keys_[chosen + 1] == key);
+  if (!tied) return static_cast<int>(std::find(id_keys_.begin(), id_keys_.end(), key) - id_keys_.begin());
   // equal logits around the chosen position: the reference's order decides which id it is
   exact_.resize(n);
   std::iota(exact_.begin(), exact_.end(), 0);

@@ -44,15 +44,16 @@ class NucleusTokenSampler final : public TokenSampler {
   bool greedy() const override { return false; }
 
  private:
-  void sort_descending(const float* logits, int count);
+  void sort_keys(const float* logits, int count, size_t keep);
 
   SamplerConfig config_;
   std::mt19937_64 random_;
   // buffers reused between calls
-  std::vector<int> order_;            // ids by descending logit (ties: ascending id)
-  std::vector<uint32_t> keys_;        // their order keys
-  std::vector<int> spare_order_;
-  std::vector<uint32_t> spare_keys_;
+  std::vector<uint32_t> id_keys_;     // order key of every id
+  std::vector<uint32_t> keys_;        // ascending keys (descending logits), at least the first keep
+  std::vector<uint32_t> counts_;      // per-thread bucket counts, then per-thread scatter offsets
+  std::vector<uint32_t> starts_;      // bucket starts in keys_
+  std::vector<std::vector<uint32_t>> scratch_;  // one buffer per sorting thread
   std::vector<int> exact_;            // the reference's partial_sort order, built only on ties
   std::vector<double> weights_;
 };
