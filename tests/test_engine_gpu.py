@@ -242,3 +242,23 @@ def test_llama3_long_context_rows_match_reference(cuda, reference_lib):
             assert_rows_close(rows[p], reference.measure_attention_by_layer(prompt))
     finally:
         reference.close()
+
+
+def test_scheduler_scan_on_one_process_equals_the_api_scan(cuda):
+    """ProbeScheduler (the multi-GPU scan, here with no process group) against
+    find_shallowest_attention_layer on the same engine: same profiles and pick; negative layer
+    bounds resolve like the reference (model.cpp:66-68)."""
+    import attnrank as ar
+    from attnrank.scheduler import ProbeScheduler
+    config = small_config(True, layers=3)
+    engine = ar.Engine.synthetic(config, seed=6)
+    prompts = small_prompts(9, config.vocab_size, seed=17)
+    settings = ar.LayerScanSettings(min_edge_ratio=1.0)
+    want = ar.find_shallowest_attention_layer(engine=engine, samples=prompts, settings=settings)
+    for scan_settings in [settings, ar.LayerScanSettings(layer_begin=-1, layer_end=-1, min_edge_ratio=1.0)]:
+        got = ProbeScheduler(engine).find_shallowest_attention_layer(prompts, scan_settings)
+        assert got.selected_layer == want.selected_layer
+        assert [p.layer_index for p in got.profiles] == [p.layer_index for p in want.profiles]
+        for mine, theirs in zip(got.profiles, want.profiles):
+            np.testing.assert_allclose(mine.attention, theirs.attention, rtol=1e-6)
+            assert mine.position_order == theirs.position_order
