@@ -59,7 +59,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, fail_rank, queue):
+def _worker(rank, world, port, fail_rank, queue, bad_spans=False):
     import datetime
     import sys
     from pathlib import Path
@@ -73,7 +73,12 @@ def _worker(rank, world, port, fail_rank, queue):
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
     try:
         engine = FakeEngine(fail=(rank == fail_rank))
-        scan = ProbeScheduler(engine).find_shallowest_attention_layer(_prompts(), ar.LayerScanSettings(min_edge_ratio=0.9))
+        prompts = list(_prompts())
+        if bad_spans:  # one sample with a span fewer than the rest
+            odd = prompts[-1]
+            prompts[-1] = ar.StructuredPrompt(tokens=odd.tokens, document_spans=list(odd.document_spans)[:4],
+                                              query_span=odd.query_span)
+        scan = ProbeScheduler(engine).find_shallowest_attention_layer(prompts, ar.LayerScanSettings(min_edge_ratio=0.9))
         queue.put((rank, "ok", scan.selected_layer, [p.attention for p in scan.profiles],
                    [p.position_order for p in scan.profiles]))
     except Exception as error:  # noqa: BLE001 - reported to the parent
@@ -85,11 +90,11 @@ def _worker(rank, world, port, fail_rank, queue):
             pass
 
 
-def _run(world, fail_rank=-1):
+def _run(world, fail_rank=-1, bad_spans=False):
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, fail_rank, queue)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, fail_rank, queue, bad_spans)) for r in range(world)]
     for p in procs:
         p.start()
     results = [queue.get(timeout=120) for _ in procs]
@@ -161,3 +166,12 @@ def test_mixed_span_counts_fail_on_every_rank_before_the_all_reduce():
                                        query_span=odd.query_span)
     with pytest.raises(ar.AttnRankError, match="probe sample 5 produced 4 spans, expected 5"):
         ProbeScheduler(FakeEngine()).find_shallowest_attention_layer(prompts, ar.LayerScanSettings())
+
+
+def test_bad_input_fails_on_every_rank_before_the_collective():
+    """Two gloo ranks, one sample with a missing span: both ranks raise the reference's error
+    themselves (none is left waiting in the all-reduce for its peer's timeout)."""
+    results = _run(2, bad_spans=True)
+    for _, status, kind, message, _ in results:
+        assert status == "error" and kind == "AttnRankError", results
+        assert "produced 4 spans, expected 5" in message
