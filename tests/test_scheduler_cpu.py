@@ -59,7 +59,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, fail_rank, queue, bad_spans=False):
+def _worker(rank, world, port, fail_rank, queue, bad_spans=False, prompt_count=None):
     import datetime
     import sys
     from pathlib import Path
@@ -73,7 +73,7 @@ def _worker(rank, world, port, fail_rank, queue, bad_spans=False):
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
     try:
         engine = FakeEngine(fail=(rank == fail_rank))
-        prompts = list(_prompts())
+        prompts = list(_prompts())[:prompt_count]
         if bad_spans:  # one sample with a span fewer than the rest
             odd = prompts[-1]
             prompts[-1] = ar.StructuredPrompt(tokens=odd.tokens, document_spans=list(odd.document_spans)[:4],
@@ -90,11 +90,12 @@ def _worker(rank, world, port, fail_rank, queue, bad_spans=False):
             pass
 
 
-def _run(world, fail_rank=-1, bad_spans=False):
+def _run(world, fail_rank=-1, bad_spans=False, prompt_count=None):
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, fail_rank, queue, bad_spans)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, fail_rank, queue, bad_spans, prompt_count))
+             for r in range(world)]
     for p in procs:
         p.start()
     results = [queue.get(timeout=120) for _ in procs]
@@ -175,3 +176,18 @@ def test_bad_input_fails_on_every_rank_before_the_collective():
     for _, status, kind, message, _ in results:
         assert status == "error" and kind == "AttnRankError", results
         assert "produced 4 spans, expected 5" in message
+
+
+def test_a_rank_with_no_prompts_still_joins_the_all_reduce():
+    """One prompt over two ranks: rank 1's shard is empty, it adds nothing and still takes part in
+    the all-reduce, so both ranks return the single-process result."""
+    import attnrank as ar
+    prompts = list(_prompts())[:1]
+    single = ProbeScheduler(FakeEngine()).find_shallowest_attention_layer(prompts, ar.LayerScanSettings(min_edge_ratio=0.9))
+    results = _run(2, prompt_count=1)
+    assert all(r[1] == "ok" for r in results), results
+    for _, _, selected, attention, order in results:
+        assert selected == single.selected_layer
+        for layer, profile in enumerate(single.profiles):
+            np.testing.assert_allclose(attention[layer], profile.attention, rtol=1e-6)
+            assert order[layer] == profile.position_order
