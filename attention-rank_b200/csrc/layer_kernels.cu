@@ -137,10 +137,11 @@ __global__ void __launch_bounds__(kRowThreadsCap) rms_norm_residual_kernel(
 // them evenly (all heads in one item left most threads with one item and some with two);
 // kRopeUnroll heads are loaded before any is stored. Query and key heads get
 // bias + rotation; value heads get the bias only (and are skipped without bias). The engine
-// applies the bias in the q|k|v GEMM epilogue and passes none.
+// applies the bias in the q|k|v GEMM epilogue and passes none. Two 256-thread CTAs per SM leave
+// 128 registers a thread: with three (85 registers) the kernel spilled and ran 4% slower.
 // ---------------------------------------------------------------------------------------------
 template <typename T, bool kBias>
-__global__ void __launch_bounds__(256, kBias ? 2 : 3) rotary_bias_kernel(T* __restrict__ qkv, const float* __restrict__ bias,
+__global__ void __launch_bounds__(256, 2) rotary_bias_kernel(T* __restrict__ qkv, const float* __restrict__ bias,
                                    const int32_t* __restrict__ positions, int tokens, int query_heads,
                                    int kv_heads, int head_dim, const float* __restrict__ cos_table,
                                    const float* __restrict__ sin_table, int table_positions,
