@@ -611,14 +611,28 @@ bool Engine::gemm(const void* x, const void* w, void* y, int m, int n, int k, co
     }
     cublasLtMatmulPreferenceDestroy(preference);
     if (status != CUBLAS_STATUS_SUCCESS || returned == 0) {
+      cublasLtMatmulDescDestroy(plan.op);
+      cublasLtMatrixLayoutDestroy(plan.a);
+      cublasLtMatrixLayoutDestroy(plan.b);
+      cublasLtMatrixLayoutDestroy(plan.c);
       throw Error("cuBLASLt found no algorithm for a " + std::to_string(m) + "x" + std::to_string(n) + "x" +
                   std::to_string(k) + " 16-bit GEMM");
     }
-    // Time each candidate once on this call's own buffers (y is overwritten by the real launch
-    // below) and keep the fastest; the first call of a shape happens in warm-up, not in a timed scan.
+    // From here the cache owns the plan's descriptors, with the heuristic's first choice. Each
+    // candidate is then timed once on this call's own buffers (y is overwritten by the real launch
+    // below) and the fastest kept; the first call of a shape happens in warm-up, not in a timed scan.
     plan.algo = results[0].algo;
+    found = cache.emplace(key, plan).first;
     if (returned > 1) {
-      cudaEvent_t start = nullptr, stop = nullptr;
+      struct Events {  // released on every path out, the throwing ones included
+        cudaEvent_t start = nullptr, stop = nullptr;
+        ~Events() {
+          if (start != nullptr) cudaEventDestroy(start);
+          if (stop != nullptr) cudaEventDestroy(stop);
+        }
+      } events;
+      cudaEvent_t& start = events.start;
+      cudaEvent_t& stop = events.stop;
       check_cuda(cudaEventCreate(&start), "autotune event");
       check_cuda(cudaEventCreate(&stop), "autotune event");
       const float one = 1.0f, zero = 0.0f;
@@ -638,13 +652,10 @@ bool Engine::gemm(const void* x, const void* w, void* y, int m, int n, int k, co
         check_cuda(cudaEventElapsedTime(&ms, start, stop), "autotune event");
         if (ok && (best == 0.0f || ms < best)) {
           best = ms;
-          plan.algo = results[i].algo;
+          found->second.algo = results[i].algo;
         }
       }
-      cudaEventDestroy(start);
-      cudaEventDestroy(stop);
     }
-    found = cache.emplace(key, plan).first;
   }
   const float alpha = 1.0f, beta = 0.0f;
   const GemmPlan& plan = found->second;
@@ -696,7 +707,8 @@ void Engine::ensure_partials(size_t items, int span_count, int layers) {
   synchronize();
   if (partials_ != nullptr) cudaFree(partials_);
   partials_ = nullptr;
-  size_t capacity = std::max(needed, partials_capacity_ * 2);
+  const size_t capacity = std::max(needed, partials_capacity_ * 2);
+  partials_capacity_ = 0;  // a failed allocation leaves no buffer to be mistaken for a large one
   check_cuda(cudaMalloc(reinterpret_cast<void**>(&partials_), capacity * sizeof(float)), "partials allocation");
   partials_capacity_ = capacity;
 }
@@ -711,6 +723,7 @@ void Engine::probe(const std::vector<PromptView>& prompts, int span_count, Layer
     synchronize();
     if (rows_device_ != nullptr) cudaFree(rows_device_);
     rows_device_ = nullptr;
+    rows_capacity_ = 0;  // as for the partials: no stale capacity after a failed allocation
     check_cuda(cudaMalloc(reinterpret_cast<void**>(&rows_device_), row_values * 2 * sizeof(double)), "rows allocation");
     rows_capacity_ = row_values * 2;
   }
