@@ -7,13 +7,16 @@
 #include <cstring>
 #include <limits>
 #include <numeric>
+#include <utility>
 #include <string>
 #include <vector>
 
 #include "../../include/attnrank_b200.h"
+#include "capi_guard.h"
 #include "decode.h"
 #include "engine.h"
 #include "layer_kernels.h"
+#include "mass_call.h"
 #include "mass_plan.h"
 #include "profile.h"
 #include "synthetic.h"
@@ -41,19 +44,7 @@ int fail(int code, const std::string& message) {
 
 template <typename F>
 int guarded(F&& body) {
-  try {
-    g_last_error.clear();
-    return body();
-  } catch (const arb::Error& error) {
-    const std::string what = error.what();
-    const bool device = what.find("device reported") != std::string::npos;
-    const bool cuda = what.find("CUDA error") != std::string::npos || what.find("cuBLASLt") != std::string::npos;
-    return fail(device ? AR_ERR_DEVICE : cuda ? AR_ERR_CUDA : AR_ERR_INVALID, what);
-  } catch (const std::bad_alloc&) {
-    return fail(AR_ERR_INTERNAL, "host allocation failed");
-  } catch (const std::exception& error) {
-    return fail(AR_ERR_INTERNAL, error.what());
-  }
+  return arb::guarded_call(std::forward<F>(body));
 }
 
 int cuda_result(cudaError_t status, const char* what) {
@@ -240,87 +231,15 @@ int ar_document_attention_mass(const void* qkv, int qkv_rows, const float* lse, 
                                int prefill_chunk_tokens, int normalize_by_length, double* mass_out, int dtype,
                                void* stream) {
   return guarded([&] {
-    if (prompt_count <= 0 || span_count <= 0 || span_count > arb::kMassMaxSpans) {
-      throw arb::Error("document_attention_mass: 1..32 spans and at least one prompt are required");
-    }
-    if (head_dim != 128 || kv_heads <= 0 || query_heads % kv_heads != 0) {
-      throw arb::Error("document_attention_mass: head_dim must be 128 and query_heads a multiple of kv_heads");
-    }
-    if (prompt_offsets_host[prompt_count] > qkv_rows) throw arb::Error("document_attention_mass: prompts exceed qkv rows");
-    const int group = query_heads / kv_heads;
-    // metadata: offsets | query spans | spans | item offsets
-    std::vector<int32_t> meta;
-    meta.insert(meta.end(), prompt_offsets_host, prompt_offsets_host + prompt_count + 1);
-    const size_t queries_at = meta.size();
-    meta.insert(meta.end(), query_spans_host, query_spans_host + 2 * prompt_count);
-    const size_t spans_at = meta.size();
-    meta.insert(meta.end(), spans_host, spans_host + 2 * static_cast<size_t>(prompt_count) * span_count);
-    const size_t items_at = meta.size();
-    meta.push_back(0);
-    for (int p = 0; p < prompt_count; ++p) {
-      const int length = prompt_offsets_host[p + 1] - prompt_offsets_host[p];
-      if (query_spans_host[2 * p] < 0 || query_spans_host[2 * p + 1] < query_spans_host[2 * p]) {
-        throw arb::Error("document_attention_mass: invalid query span");
-      }
-      for (int s = 0; s < span_count; ++s) {
-        const int32_t* span = spans_host + 2 * (static_cast<size_t>(p) * span_count + s);
-        if (span[0] < 0 || span[1] < span[0]) throw arb::Error("document_attention_mass: invalid document span");
-      }
-      const arb::MassItemShape shape = arb::mass_item_shape(query_spans_host + 2 * p,
-                                                            spans_host + 2 * static_cast<size_t>(p) * span_count,
-                                                            span_count, length, group);
-      meta.push_back(meta.back() + arb::mass_items_for_prompt(shape, kv_heads));
-    }
-    const int item_count = meta.back();
+    const char* who = "document_attention_mass";
+    arb::MassCallArgs call{qkv, qkv_rows, lse, prompt_offsets_host, prompt_count, query_spans_host, spans_host,
+                           span_count, query_heads, kv_heads, head_dim, sliding_window, prefill_chunk_tokens,
+                           normalize_by_length, mass_out, dtype};
+    const arb::MassBatch batch = arb::plan_mass_batch(who, call);
+    const arb::MassScratchLayout layout = arb::mass_scratch_layout(batch);
     cudaStream_t s = as_stream(stream);
     StreamScratch scratch(s);
-    auto* meta_device = static_cast<int32_t*>(scratch.get(meta.size() * sizeof(int32_t)));
-    auto* partials = static_cast<float*>(scratch.get(static_cast<size_t>(item_count) * span_count * sizeof(float)));
-    auto* rows = static_cast<double*>(scratch.get(static_cast<size_t>(prompt_count) * span_count * sizeof(double)));
-    auto* status = static_cast<int*>(scratch.get(sizeof(int)));
-    arb::check_cuda(cudaMemsetAsync(status, 0, sizeof(int), s), "status reset");
-    arb::check_cuda(cudaMemcpyAsync(meta_device, meta.data(), meta.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s),
-                    "metadata upload");
-    arb::MassArgs args;
-    args.qkv = qkv;
-    args.dtype = dtype;
-    args.qkv_rows_capacity = qkv_rows;
-    args.lse = lse;
-    args.prompt_offsets = meta_device;
-    args.query_spans = meta_device + queries_at;
-    args.spans = meta_device + spans_at;
-    args.item_offsets = meta_device + items_at;
-    args.prompt_count = prompt_count;
-    args.span_count = span_count;
-    args.item_count = item_count;
-    args.query_heads = query_heads;
-    args.kv_heads = kv_heads;
-    args.head_dim = head_dim;
-    args.sliding_window = sliding_window;
-    args.reference_chunk = prefill_chunk_tokens;
-    args.normalize_by_length = normalize_by_length;
-    args.partials = partials;
-    args.status = status;
-    arb::check_cuda(arb::launch_document_mass(args, s), "document_attention_mass");
-    arb::FinalizeArgs finalize;
-    finalize.partials = partials;
-    finalize.item_offsets = args.item_offsets;
-    finalize.query_spans = args.query_spans;
-    finalize.prompt_offsets = meta_device;
-    finalize.prompt_count = prompt_count;
-    finalize.span_count = span_count;
-    finalize.item_count = item_count;
-    finalize.layers = 1;
-    finalize.query_heads = query_heads;
-    finalize.raw_rows = rows;
-    arb::check_cuda(arb::launch_finalize_mass(finalize, s), "finalize");
-    int status_host = 0;
-    arb::check_cuda(cudaMemcpyAsync(mass_out, rows, static_cast<size_t>(prompt_count) * span_count * sizeof(double),
-                                    cudaMemcpyDeviceToHost, s),
-                    "mass download");
-    arb::check_cuda(cudaMemcpyAsync(&status_host, status, sizeof(int), cudaMemcpyDeviceToHost, s), "status download");
-    arb::check_cuda(cudaStreamSynchronize(s), "document_attention_mass");
-    if (status_host != 0) throw arb::Error("device reported an error in document_attention_mass (code " + std::to_string(status_host) + ")");
+    arb::run_mass_batch(who, call, batch, layout, scratch.get(layout.total), s);
     return AR_OK;
   });
 }

@@ -109,10 +109,13 @@ int ar_document_attention_mass(const void* qkv, int qkv_rows, const float* lse, 
  * (metadata, per-CTA partials, rows, status) comes from one fixed 8 MiB device array that every
  * GPU loading the library keeps until the process exits; it calls no cudaMalloc, cudaFree or
  * other allocating routine. Batches that need more than 8 MiB of scratch are rejected with
- * AR_ERR_INVALID. The array's device address is looked up once per device by the first call
- * made on that device (make that call before any stream capture). Calls share the array: calls
- * whose work overlaps on the GPU race, so issue them on one stream or wait in between. The
- * stream is synchronised before return. */
+ * AR_ERR_INVALID, as are the bad arguments ar_document_attention_mass rejects (same checks).
+ * The array's device address is looked up once per device by the first call made on that device
+ * (make that call before any stream capture) and cached; the cache is not refreshed after a
+ * cudaDeviceReset, so do not call this entry point on a device after resetting it. Every call
+ * shares the array, and calls whose work overlapped on the GPU would race on it: the library
+ * holds a per-device lock from the first copy until `stream` has drained, so calls from several
+ * host threads of one process run one after another. The stream is synchronised before return. */
 int ar_document_attention_mass_noalloc(const void* qkv, int qkv_rows, const float* lse,
                                        const int32_t* prompt_offsets_host, int prompt_count,
                                        const int32_t* query_spans_host, const int32_t* spans_host, int span_count,

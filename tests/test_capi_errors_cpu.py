@@ -84,3 +84,65 @@ def test_last_error_is_cleared_by_a_successful_call():
     order = (ctypes.c_int * 3)()
     assert lib.ar_resolve_position_order((ctypes.c_int * 1)(1), 1, 3, order) == _native.AR_OK
     assert lib.ar_last_error() == b"" and list(order) == [1, 0, 2]
+
+
+# --- the two kernel-level mass entry points: every argument check runs on the host before any
+# CUDA call, so both reject the same bad inputs here, without a GPU
+_MASS_FUNCTIONS = ("ar_document_attention_mass", "ar_document_attention_mass_noalloc")
+_FAKE_DEVICE_POINTER = ctypes.c_void_p(256)  # never dereferenced: each call below fails its checks first
+
+
+def _mass_call(name, offsets, query_spans, spans, span_count, qkv_rows=None, heads=28, kv_heads=4, head_dim=128,
+               qkv=_FAKE_DEVICE_POINTER):
+    import numpy as np
+    offsets = np.ascontiguousarray(offsets, dtype=np.int32)
+    query_spans = np.ascontiguousarray(query_spans, dtype=np.int32)
+    spans = np.ascontiguousarray(spans, dtype=np.int32)
+    prompt_count = len(offsets) - 1
+    out = np.zeros(max(prompt_count, 1) * max(span_count, 1), dtype=np.float64)
+    rows = int(offsets[-1]) if qkv_rows is None else qkv_rows
+    return getattr(lib, name)(qkv, rows, _FAKE_DEVICE_POINTER, offsets.ctypes.data, prompt_count,
+                              query_spans.ctypes.data, spans.ctypes.data, span_count, heads, kv_heads, head_dim, 0,
+                              512, 0, out.ctypes.data, F16, None)
+
+
+_ONE_PROMPT = dict(offsets=[0, 300], query_spans=[260, 300], spans=[0, 50, 50, 100, 100, 150, 150, 200, 200, 260],
+                   span_count=5)
+
+MASS_CASES = {
+    "no spans": (dict(_ONE_PROMPT, span_count=0), "1..32 spans"),
+    "33 spans": (dict(_ONE_PROMPT, spans=[0, 1] * 33, span_count=33), "1..32 spans"),
+    "head dim 64": (dict(_ONE_PROMPT, head_dim=64), "head_dim must be 128"),
+    "heads not a multiple": (dict(_ONE_PROMPT, heads=6, kv_heads=4), "multiple of kv_heads"),
+    "null qkv": (dict(_ONE_PROMPT, qkv=None), "null argument"),
+    "offsets past qkv rows": (dict(_ONE_PROMPT, qkv_rows=299), "exceed qkv rows"),
+    "negative first offset": (dict(_ONE_PROMPT, offsets=[-100, 50], qkv_rows=50), "start at 0"),
+    "decreasing offsets": (dict(offsets=[0, 300, 200], query_spans=[260, 300, 0, 10], spans=[0, 10] * 10,
+                                span_count=5, qkv_rows=300), "non-decreasing"),
+    "reversed query span": (dict(_ONE_PROMPT, query_spans=[300, 260]), "invalid query span"),
+    "negative query span": (dict(_ONE_PROMPT, query_spans=[-1, 300]), "invalid query span"),
+    "negative document span": (dict(_ONE_PROMPT, spans=[-5, 50] + _ONE_PROMPT["spans"][2:]), "invalid document span"),
+    "reversed document span": (dict(_ONE_PROMPT, spans=[50, 0] + _ONE_PROMPT["spans"][2:]), "invalid document span"),
+}
+
+
+@pytest.mark.parametrize("function", _MASS_FUNCTIONS)
+@pytest.mark.parametrize("case", sorted(MASS_CASES))
+def test_mass_entry_points_reject_bad_arguments_alike(function, case):
+    kwargs, message = MASS_CASES[case]
+    assert _mass_call(function, **kwargs) == _native.AR_ERR_INVALID
+    text = lib.ar_last_error().decode()
+    assert message in text and function[3:] in text, text
+
+
+def test_noalloc_rejects_a_batch_beyond_its_fixed_scratch_before_any_device_work():
+    """One 32K-token prompt probed on every row with 32 spans partitioning it needs 4 KV heads x
+    1792 row tiles x 64 key runs = 458752 work items, ~59 MB of per-CTA partial sums: more than
+    the fixed 8 MiB array, so the call is refused on the host."""
+    T, S = 32768, 32
+    edges = [T * i // S for i in range(S + 1)]
+    spans = [v for i in range(S) for v in (edges[i], edges[i + 1])]
+    status = _mass_call("ar_document_attention_mass_noalloc", [0, T], [0, T], spans, S)
+    assert status == _native.AR_ERR_INVALID
+    text = lib.ar_last_error().decode()
+    assert "fixed array holds 8388608" in text and "ar_document_attention_mass" in text, text

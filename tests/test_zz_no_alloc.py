@@ -6,9 +6,11 @@ scratch is a fixed device array reserved when the library loads. This file is co
 that a run stopping at the first failure has already run every other test; it must also pass on
 its own in a fresh process (its first call on the device looks up the array's address).
 
-Checks: two calls in a row give the same result as the allocating entry point
-(ar_document_attention_mass) on the same inputs, within the mass tolerance of the other GPU tests
-(rel 1e-3); and a batch whose scratch exceeds the fixed array is rejected with a clear error.
+Checks: two calls in a row give bit-for-bit the result of the allocating entry point
+(ar_document_attention_mass) on the same inputs -- the same kernels run on the same data, only the
+scratch differs -- and the span masses agree with the fp32 CPU oracle's softmax rows within the
+mass tolerance of the other GPU tests (rel 1e-3); a batch whose scratch exceeds the fixed array
+is rejected with a clear error.
 """
 from __future__ import annotations
 
@@ -75,7 +77,27 @@ def test_noalloc_matches_allocating_entry_point_twice(cuda, normalize):
     for _ in range(2):  # the fixed array keeps the previous call's contents; results must not depend on them
         status, got = _call(_native.lib.ar_document_attention_mass_noalloc, data, normalize)
         _native.check(status)
-        np.testing.assert_allclose(got, want, rtol=MASS_REL, atol=0)
+        np.testing.assert_array_equal(got, want)
+
+
+def test_noalloc_matches_the_oracle_span_mass(cuda):
+    """Span sums of the oracle's exact softmax rows (fp32 CPU, the same fp16 qkv values), divided
+    by query rows x heads as the reference does before its unit-sum step (model.cu:602-615)."""
+    import torch
+    from attnrank import _native
+    from oracle import forward as F
+    lengths = [940, 300, 64]
+    data = _inputs(cuda, lengths, seed=8)
+    status, got = _call(_native.lib.ar_document_attention_mass_noalloc, data)
+    _native.check(status)
+    qkv = data["qkv"].to(torch.float32).cpu().numpy()
+    _, _, probs = F.op_attention(qkv, data["offsets"], data["heads"], data["kv_heads"], 128, 0)
+    for p, T in enumerate(lengths):
+        query = tuple(int(v) for v in data["query_spans"][2 * p:2 * p + 2])
+        spans = data["spans"].reshape(len(lengths), data["span_count"], 2)[p]
+        prompt = F.Prompt(tokens=np.zeros(T, np.int32), query_span=query, spans=[(int(a), int(b)) for a, b in spans])
+        want = F.document_mass(probs[p], prompt, 512, False) / ((query[1] - query[0]) * data["heads"])
+        np.testing.assert_allclose(got[p], want, rtol=MASS_REL, atol=1e-9)
 
 
 def test_noalloc_rejects_batches_beyond_its_fixed_scratch(cuda):
