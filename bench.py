@@ -15,6 +15,12 @@ resident in HBM; `e2e` is the same scan through the public Python API with host 
 tokens and batch metadata and D2H of the accumulator inside the timed region, wall clock, max over
 ranks). Inputs are larger than L2 (15 GB of weights stream through every batch), so no L2 flush
 is needed between steps.
+
+`--impl reference` times the reference's own scan (its unmodified sources compiled into
+oracle/_ref: CudaLlamaModel + AttentionLayerScanner + select_shallowest_basin_layer) on the same
+prompts, one GPU, and leaves its per-layer profiles in a result file; the B200 arm, run after it on
+the same box, compares its own profiles, slot orders and pick against that file
+(`reference_parity`). The reference arm imports nothing from this build's package.
 """
 from __future__ import annotations
 
@@ -40,25 +46,49 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 
 # The scan workloads: BASELINE config 3 (the default bench line) and config 4.
 WORKLOADS = {
-    "qwen-scan": {"model": "qwen2_7b", "shape": "QWEN_PROMPTS", "prompts": 400, "max_sequence": 4096,
-                  "reference_sample": 128,
+    "qwen-scan": {"model": "QWEN2_7B", "shape": "QWEN_PROMPTS", "prompts": 400, "max_sequence": 4096,
                   "text": "layer scan, Qwen2.5-7B architecture, {n} prompts x (5 docs U[120,240] + 40-token question), "
                           "min_edge_ratio 1.3"},
-    "llama3-long": {"model": "llama3_8b", "shape": "LLAMA3_LONG_PROMPTS", "prompts": 256, "max_sequence": 8192,
-                    "reference_sample": 16,
+    "llama3-long": {"model": "LLAMA3_8B", "shape": "LLAMA3_LONG_PROMPTS", "prompts": 256, "max_sequence": 8192,
                     "text": "long-context layer scan, Llama-3-8B architecture, {n} prompts x (20 docs U[150,250] + "
                             "64-token question), min_edge_ratio 1.3"},
 }
 
 
 def workload(args):
-    """(LlamaConfig, prompts, spec) of the chosen workload."""
+    """(LlamaConfig, prompts, spec) of the chosen workload, as the library's API types."""
     from attnrank import synthetic
     spec = WORKLOADS[args.config]
-    config = getattr(synthetic, spec["model"])()
+    config = synthetic.config_of(getattr(synthetic, spec["model"]))
     count = args.prompts if args.prompts is not None else spec["prompts"]
     prompts = synthetic.prompts(count, config.vocab_size, getattr(synthetic, spec["shape"]))
     return config, prompts, spec
+
+
+def plain_workload(args):
+    """The same workload from the numpy-only generator (loads no library of this build)."""
+    import probe_workloads as PW
+    spec = WORKLOADS[args.config]
+    shape = getattr(PW, spec["model"])
+    count = args.prompts if args.prompts is not None else spec["prompts"]
+    return shape, PW.token_prompts(count, shape.vocab_size, getattr(PW, spec["shape"])), spec
+
+
+def reference_result_path(config_name: str, prompt_count: int) -> Path:
+    """Where the reference arm leaves its scan result for the B200 arm run after it on the same box."""
+    import tempfile
+    return Path(tempfile.gettempdir()) / f"attnrank_bench_reference_{config_name}_{prompt_count}.json"
+
+
+def slot_gap(attention_rows) -> float:
+    """Smallest relative gap between adjacent masses of any layer's sorted row: a mass error below
+    half of it cannot reorder the slots."""
+    gaps = []
+    for row in attention_rows:
+        ordered = sorted(row, reverse=True)
+        for a, b in zip(ordered, ordered[1:]):
+            gaps.append((a - b) / a if a > 0 else 0.0)
+    return min(gaps) if gaps else 0.0
 
 
 def parse_args():
@@ -70,8 +100,6 @@ def parse_args():
     parser.add_argument("--config", choices=sorted(WORKLOADS), default="qwen-scan",
                         help="qwen-scan: BASELINE config 3 (the bench line); llama3-long: config 4")
     parser.add_argument("--prompts", type=int, default=None, help="prompts per scan (default: the workload's)")
-    parser.add_argument("--reference-sample", type=int, default=None,
-                        help="prompts per reference step (a bounded sample of the scan; default: the workload's)")
     parser.add_argument("--batch-tokens", type=int, default=16384)
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-kernels", action="store_true", help="skip the per-kernel roofline timing")
@@ -408,6 +436,7 @@ def cpu_baseline(config, prompt, layers: int = 4) -> dict:
     model = F.OracleModel(shape, seed=0)
     sample = F.Prompt(tokens=prompt.tokens, query_span=(prompt.query_span.begin, prompt.query_span.end),
                       spans=[(s.begin, s.end) for s in prompt.document_spans])
+    model.prepare([sample])  # weights and embedding rows are generated before the clock starts
     start = time.perf_counter()
     model.probe([sample])
     seconds = (time.perf_counter() - start) * config.num_hidden_layers / layers
@@ -418,15 +447,18 @@ def cpu_baseline(config, prompt, layers: int = 4) -> dict:
     import numpy as np
     tokens = np.random.default_rng(0).integers(0, 32000, 256).astype(np.int32)
     c1 = F.Prompt(tokens=tokens, query_span=(240, 256), spans=[(48 * i, 48 * i + 48) for i in range(5)])
+    tiny_model = F.OracleModel(tiny, seed=0)
+    tiny_model.prepare([c1])
     start = time.perf_counter()
-    F.OracleModel(tiny, seed=0).probe([c1])
+    tiny_model.probe([c1])
     c1_seconds = time.perf_counter() - start
     return {"value": round(1.0 / seconds, 5), "unit": "prompts/s", "cores": cores, "kind": "port",
             "sample": f"1 prompt ({len(prompt.tokens)} tokens) x {layers} of {config.num_hidden_layers} layers, "
-                      f"fp32 torch-CPU oracle incl. weight generation, scaled to all layers",
+                      f"fp32 torch-CPU oracle, forward pass only (weights generated before the clock), "
+                      f"scaled to all layers",
             "config1_seconds": round(c1_seconds, 4),
             "config1": "TinyLlama-1.1B-shaped single layer, 256 tokens, mass of 16 query tokens over 5 spans "
-                       "of 48 (weight generation included)"}
+                       "of 48 (forward pass only)"}
 
 
 # ---------------------------------------------------------------------------------------------
@@ -491,6 +523,13 @@ def run_b200(args, rank, world, local_rank):
     accumulated = accumulator.double().cpu().numpy().reshape(L, slots)
     profiles = [ar.AttentionProfile.from_accumulated("synthetic", l, prompt_count, accumulated[l]) for l in range(L)]
     selected = ar.select_shallowest_basin_layer(profiles=profiles, min_edge_ratio=MIN_EDGE_RATIO)
+    ratios = [ar.basin_statistics(attention=p.attention, min_edge_ratio=MIN_EDGE_RATIO).edge_ratio for p in profiles]
+    highest = profiles[max(range(L), key=lambda i: ratios[i])].layer_index
+    profile_record = {"layer_index": [p.layer_index for p in profiles],
+                      "attention": [[float(v) for v in p.attention] for p in profiles],
+                      "position_order": [[int(v) for v in p.position_order] for p in profiles],
+                      "edge_ratio": [float(r) for r in ratios]}
+    parity = reference_parity(args.config, prompt_count, profile_record, selected, highest)
 
     # end to end through the public API (host prompts in, H2D + D2H inside the timed region)
     scheduler = ProbeScheduler(engine)
@@ -557,6 +596,9 @@ def run_b200(args, rank, world, local_rank):
                    "l2": "inputs larger than L2 (15-16 GB of weights streamed per batch); no flush"},
         "selected_layer": selected,
         "slot_order_selected": profiles[selected].position_order if selected >= 0 else None,
+        "highest_ratio_layer": highest,
+        "profiles": profile_record,
+        "reference_parity": parity,
         "e2e": {"value": round(prompt_count / e2e_step, 3), "unit": "prompts/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h), "selected_layer": scan.selected_layer,
                 "api": "attnrank.scheduler.ProbeScheduler.find_shallowest_attention_layer"},
@@ -585,47 +627,88 @@ def run_b200(args, rank, world, local_rank):
     return result
 
 
+def reference_parity(config_name: str, prompt_count: int, profiles: dict, selected: int, highest: int) -> dict:
+    """This arm's scan result against the reference arm's, when the reference arm ran before this one
+    on the same box with the same workload (its result file): the largest relative mass error, slot
+    orders of every layer, the basin pick, the highest-ratio layer, and the smallest relative gap
+    between adjacent masses (an error below half of it cannot flip an order)."""
+    path = reference_result_path(config_name, prompt_count)
+    if not path.exists():
+        return {"available": False, "reason": f"no reference result for this workload ({path.name}); run "
+                                              "bench.py --impl reference first on this box"}
+    want = json.loads(path.read_text())
+    theirs = want["profiles"]
+    if want.get("prompts") != prompt_count or theirs["layer_index"] != profiles["layer_index"]:
+        return {"available": False, "reason": "the reference result covers another workload"}
+    worst = 0.0
+    for mine, ref in zip(profiles["attention"], theirs["attention"]):
+        for a, b in zip(mine, ref):
+            worst = max(worst, abs(a - b) / max(abs(b), 1e-12))
+    orders_equal = [a == b for a, b in zip(profiles["position_order"], theirs["position_order"])]
+    return {"available": True, "prompts": prompt_count, "layers": len(orders_equal),
+            "max_rel_err_vs_reference": worst, "mass_tolerance": 1e-3,
+            "slot_orders_equal": all(orders_equal), "layers_with_equal_order": sum(orders_equal),
+            "selected_layer_equal": selected == want["selected_layer"], "reference_selected_layer":
+                want["selected_layer"],
+            "highest_ratio_layer_equal": highest == want["highest_ratio_layer"],
+            "min_adjacent_slot_gap_rel": slot_gap(theirs["attention"])}
+
+
 def run_reference(args, rank, world, local_rank):
-    from attnrank import synthetic
-    from attnrank.scheduler import shard_by_length
+    """The reference's own scan (CudaLlamaModel + AttentionLayerScanner + select_shallowest_basin_layer,
+    compiled from its unmodified sources into oracle/_ref) on the same prompts as the B200 arm. It
+    imports nothing from this build's package: the prompts come from the numpy-only generator."""
     from oracle import reference
 
     if reference.load_or_none() is None:
         return {"impl": "reference", "unavailable": "oracle/_ref/libattnrank_ref.so was not built (make -C oracle reference)"}
-    spec = WORKLOADS[args.config]
-    sample = args.reference_sample if args.reference_sample is not None else spec["reference_sample"]
-    config, prompts, spec = workload(argparse.Namespace(config=args.config, prompts=sample))
-    shard = shard_by_length([len(p.tokens) for p in prompts], world)[rank]
-    mine = [prompts[i] for i in shard]
+    shape, prompts, spec = plain_workload(args)
+    count = len(prompts)
     longest = max(len(p.tokens) for p in prompts)
-    model = reference.ReferenceModel(config, seed=0, max_sequence_length=max(2048, longest), device=local_rank)
-    for _ in range(args.warmup):
-        model.scan(mine[: max(1, len(mine) // 8)], min_edge_ratio=MIN_EDGE_RATIO)
-    barrier(world)
+    model = reference.ReferenceModel(shape, seed=0, max_sequence_length=max(2048, longest), device=local_rank)
+    for _ in range(args.warmup):  # warm-up on a slice: the reference's first calls set up cuBLAS
+        model.scan(prompts[:8], min_edge_ratio=MIN_EDGE_RATIO)
     seconds = []
     result = None
+    sampler = ClockSampler(local_rank)
+    sampler.start()
     for _ in range(args.steps):
-        result = model.scan(mine, min_edge_ratio=MIN_EDGE_RATIO)
+        result = model.scan(prompts, min_edge_ratio=MIN_EDGE_RATIO)
         seconds.append(result.seconds)
-    step_seconds = max_over_ranks(sum(seconds) / len(seconds), world)
-    value = sample / step_seconds
-    cores = os.cpu_count() or 1
+    clocks = sampler.stop()
     model.close()
-    return {
+    step_seconds = sum(seconds) / len(seconds)
+    value = count / step_seconds
+    attention = [[float(v) for v in row] for row in result.attention]
+    ratios = [float(reference.basin_statistics(row, MIN_EDGE_RATIO)[3]) for row in result.attention]
+    highest = int(result.layer_index[max(range(len(ratios)), key=lambda i: ratios[i])])
+    profiles = {"layer_index": [int(v) for v in result.layer_index], "attention": attention,
+                "position_order": [[int(v) for v in row] for row in result.position_order],
+                "edge_ratio": ratios}
+    reference_result_path(args.config, count).write_text(json.dumps({
+        "config": args.config, "prompts": count, "min_edge_ratio": MIN_EDGE_RATIO,
+        "selected_layer": int(result.selected_layer), "highest_ratio_layer": highest, "profiles": profiles}))
+    line = {
         "metric": METRIC, "impl": "reference", "value": round(value, 3), "unit": "prompts/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_seconds * 1000, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16/fp32",
         "data": "synthetic (seeded random-init weights, seeded random token-id prompts)",
-        "config": {"workload": spec["text"].format(n=sample) + "; reference CudaLlamaModel + "
+        "config": {"workload": spec["text"].format(n=count) + "; reference CudaLlamaModel + "
                                "AttentionLayerScanner (stock path)",
-                   "global_batch": sample, "parallelism": "one GPU (rank 0 under torchrun): the reference has "
-                   "no multi-GPU path"},
-        "selected_layer": result.selected_layer if result else None,
-        "cpu_baseline": {"value": round(value, 3), "unit": "prompts/s", "cores": cores, "kind": "reference",
-                         "sample": f"first {sample} of the {spec['prompts']} prompts per step; the reference's "
-                                   "path is CUDA, so it runs on the GPU (wall clock around its synchronous scan)"},
+                   "global_batch": count, "seq_len": round(sum(len(p.tokens) for p in prompts) / count, 1),
+                   "parallelism": "one GPU (rank 0 under torchrun): the reference has no multi-GPU path"},
+        "reference_device": "gpu",
+        "reference_note": "the reference's path is CUDA (model.cu, kernels.cu): value is its stock scan on one "
+                          "B200, wall clock around the synchronous AttentionLayerScanner::scan",
+        "clocks": clocks,
+        "selected_layer": int(result.selected_layer),
+        "highest_ratio_layer": highest,
+        "profiles": profiles,
         "e2e": {"value": round(value, 3), "unit": "prompts/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(shape, prompts[0])
+    return line
 
 
 # ---------------------------------------------------------------------------------------------
@@ -646,13 +729,21 @@ def decode_bytes_per_token(config, context: int) -> float:
     return config.num_hidden_layers * (per_layer + cache) + V * H * 2
 
 
-def decode_setup(args):
-    from attnrank import synthetic
-    config = synthetic.qwen2_7b()
-    config.tie_word_embeddings = True  # the reference harness ties the head to the embedding
+def decode_setup(args, plain: bool = False):
+    """(config, prompt tokens) of the decode workload; `plain` gives the architecture as the
+    numpy-only ModelShape (for the reference arm, which loads no library of this build)."""
+    import dataclasses
+
+    import probe_workloads as PW
+    shape = PW.QWEN2_7B
     if getattr(args, "decode_layers", None):
-        config.num_hidden_layers = args.decode_layers
-    prompt = list(synthetic.prompts(1, config.vocab_size, synthetic.QWEN_PROMPTS)[0].tokens)
+        shape = dataclasses.replace(shape, num_hidden_layers=args.decode_layers)
+    prompt = [int(t) for t in PW.token_prompts(1, shape.vocab_size, PW.QWEN_PROMPTS)[0].tokens]
+    if plain:
+        return shape, prompt
+    from attnrank import synthetic
+    config = synthetic.config_of(shape)
+    config.tie_word_embeddings = True  # the reference harness ties the head to the embedding
     return config, prompt
 
 
@@ -780,7 +871,7 @@ def run_decode_reference(args, rank, world, local_rank):
     from oracle import reference
     if reference.load_or_none() is None:
         return {"impl": "reference", "unavailable": "oracle/_ref/libattnrank_ref.so was not built (make -C oracle reference)"}
-    config, prompt = decode_setup(args)
+    config, prompt = decode_setup(args, plain=True)
     new = args.decode_tokens
     model = reference.ReferenceModel(config, seed=0, max_sequence_length=4096, device=local_rank)
     for _ in range(max(args.warmup, 1)):
@@ -808,9 +899,9 @@ def run_decode_reference(args, rank, world, local_rank):
                    "global_batch": 1, "parallelism": f"{world} replica(s)"},
         "prefill_and_first_token_ms": round(first_s * 1000, 3),
         "tokens_head": tokens[:8] if tokens else None,
-        "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": os.cpu_count() or 1,
-                         "kind": "reference", "sample": "the reference's path is CUDA: wall clock around its "
-                                                        "synchronous generate"},
+        "reference_device": "gpu",
+        "reference_note": "the reference's path is CUDA: wall clock around its synchronous generate on one B200",
+        "cpu_baseline": cpu_decode_baseline(config, len(prompt) + new // 2),
         "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 

@@ -205,20 +205,53 @@ def test_qwen7b_rows_match_reference(qwen_pair):
         assert_rows_close(rows[p], want)
 
 
+def _slot_gap(rows):
+    """Smallest relative gap between adjacent masses of any sorted row (an error below half of it
+    cannot reorder the slots)."""
+    gaps = [(a - b) / a for row in rows for a, b in zip(sorted(row)[::-1], sorted(row)[::-1][1:]) if a > 0]
+    return min(gaps)
+
+
 @pytest.mark.slow
 def test_qwen7b_scan_matches_reference(qwen_pair):
+    """BASELINE config 3 in full: the 400-prompt scan through find_shallowest_attention_layer
+    against the reference's stock AttentionLayerScanner::scan (attnrank.cpp:364-375) on the same
+    prompts: every layer's mass row (rel 1e-3) and slot order (exact), the pick at min_edge_ratio
+    1.3, LayerScan.highest_ratio_layer (engine.py:304-306), and select_shallowest_basin_layer
+    (attnrank.cpp:257-265) at thresholds that pick a layer, each halfway between two adjacent
+    edge ratios of the reference's profiles and at least 1% from every ratio, so that no
+    threshold sits inside the mass tolerance of a ratio."""
     import attnrank as ar
     from attnrank import synthetic
+    from oracle import reference as R
     config, engine, reference = qwen_pair
-    prompts = synthetic.prompts(48, config.vocab_size)
+    prompts = synthetic.prompts(400, config.vocab_size)
     scan = ar.find_shallowest_attention_layer(engine=engine, samples=prompts,
                                               settings=ar.LayerScanSettings(min_edge_ratio=1.3))
     want = reference.scan(prompts, min_edge_ratio=1.3)
+    gap = _slot_gap(want.attention)
+    worst = max(float(np.max(np.abs(np.asarray(p.attention) - want.attention[i]) / np.abs(want.attention[i])))
+                for i, p in enumerate(scan.profiles))
     assert scan.selected_layer == want.selected_layer
     for layer, profile in enumerate(scan.profiles):
         assert profile.layer_index == int(want.layer_index[layer])
         assert_rows_close(profile.attention, want.attention[layer])
-        assert list(profile.position_order) == [int(v) for v in want.position_order[layer]]
+        assert list(profile.position_order) == [int(v) for v in want.position_order[layer]], (
+            f"layer {layer}: max rel mass error {worst:.2e}, smallest adjacent slot gap {gap:.2e}")
+    ratios = [float(R.basin_statistics(row, 1.3)[3]) for row in want.attention]
+    highest = int(want.layer_index[max(range(len(ratios)), key=lambda i: ratios[i])])
+    assert scan.highest_ratio_layer() == highest
+    distinct = sorted(set(ratios))
+    thresholds = [0.5 * (a + b) for a, b in zip(distinct, distinct[1:])
+                  if all(abs(0.5 * (a + b) - r) > 0.01 * r for r in ratios)]
+    assert len(thresholds) >= 3, ratios
+    picked = set()
+    for threshold in thresholds:
+        mine = ar.select_shallowest_basin_layer(profiles=scan.profiles, min_edge_ratio=threshold)
+        theirs = R.select_shallowest(want.attention, want.layer_index, threshold)
+        assert mine == theirs, (threshold, mine, theirs)
+        picked.add(mine)
+    assert any(layer >= 0 for layer in picked), (ratios, thresholds)
 
 
 # ---- Llama-3-8B long-context probe (4K-token prompts, 20 document spans) against the reference build
