@@ -68,6 +68,13 @@ class StructuredPrompt:
         self.document_spans = [_span(s) for s in self.document_spans]
         self.query_span = _span(self.query_span)
 
+    @property
+    def documents(self) -> list[TokenSpan]:
+        """The document spans, under the name a ProbeSample gives its documents: the reference's
+        Python layer checks `len(samples[0].documents)` before a scan (engine.py:343-346), so
+        token-id prompts pass through it unchanged."""
+        return self.document_spans
+
 
 @dataclass
 class LlamaConfig:

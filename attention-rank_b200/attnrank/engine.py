@@ -21,6 +21,8 @@ from dataclasses import dataclass, field
 from pathlib import Path
 from typing import Any, Callable, Sequence
 
+import numpy as np
+
 from attnrank import core
 from attnrank.core import (AttentionProfile, AttnRankError, Engine, LlamaConfig, RuntimeOptions, StructuredPrompt,
                            TokenSpan)
@@ -163,79 +165,106 @@ def make_prompt(*, tokens: Sequence[int], document_spans: Sequence[tuple[int, in
 
 
 def basin_statistics(*, attention: Sequence[float], min_edge_ratio: float = DEFAULT_MIN_EDGE_RATIO) -> Any:
-    return core.basin_statistics(list(attention), core.BasinCriterion(min_edge_ratio))
+    """The basin test of one profile row (reference: engine.py:258-259, attnrank.cpp:236-255)."""
+    return core.basin_statistics(attention, core.BasinCriterion(min_edge_ratio))
+
+
+def _scan_config(settings: LayerScanSettings, engine: Engine) -> core.LayerScanConfig:
+    """LayerScanSettings -> the core's LayerScanConfig (a missing layer_end means every layer)."""
+    config = core.LayerScanConfig()
+    config.model_id = settings.model_id if settings.model_id else engine.model_directory
+    config.layer_begin = settings.layer_begin
+    config.layer_end = settings.layer_end if settings.layer_end is not None else -1
+    config.normalize_by_document_length = settings.normalize_by_length
+    config.progress_interval = 0
+    return config
 
 
 def scan_attention_layers(*, engine: Engine, samples: Sequence[StructuredPrompt],
                           settings: LayerScanSettings = LayerScanSettings(),
                           progress: ProgressCallback | None = None) -> list[AttentionProfile]:
-    config = core.LayerScanConfig()
-    config.model_id = settings.model_id or engine.model_directory
-    config.layer_begin = settings.layer_begin
-    config.layer_end = -1 if settings.layer_end is None else settings.layer_end
-    config.normalize_by_document_length = settings.normalize_by_length
-    config.progress_interval = 0
-    return core.scan_attention_layers(engine, list(samples), config, progress)
+    """Profiles of every probed layer over the samples (reference: engine.py:262-275)."""
+    return core.scan_attention_layers(engine, list(samples), _scan_config(settings, engine), progress)
 
 
 def select_shallowest_basin_layer(*, profiles: Sequence[AttentionProfile],
                                   min_edge_ratio: float = DEFAULT_MIN_EDGE_RATIO) -> int:
-    return core.select_shallowest_basin_layer(list(profiles), core.BasinCriterion(min_edge_ratio))
+    """The shallowest basin layer, -1 if none (reference: engine.py:278-283)."""
+    return core.select_shallowest_basin_layer(profiles, core.BasinCriterion(min_edge_ratio))
+
+
+# Columns of LayerScan.table(): header, width, and the row value (profile, statistics) -> text.
+_SCAN_COLUMNS = (
+    ("layer", 5, lambda profile, stats: f"{profile.layer_index:>5}"),
+    ("first", 8, lambda profile, stats: f"{stats.first:>8.4f}"),
+    ("interior", 9, lambda profile, stats: f"{stats.interior_mean:>9.4f}"),
+    ("last", 8, lambda profile, stats: f"{stats.last:>8.4f}"),
+    ("ratio", 7, lambda profile, stats: f"{stats.edge_ratio:>7.2f}"),
+)
 
 
 @dataclass
 class LayerScan:
+    """What find_shallowest_attention_layer returns: the pick and the profile of every probed
+    layer. Fields, methods and the table / dict layouts are the reference's LayerScan
+    (engine.py:286-334); its callers (the profile service, the facade) log table(), look a layer
+    up with profile_for() and fall back to highest_ratio_layer() when no layer is a basin."""
+
     selected_layer: int
     min_edge_ratio: float
     profiles: list[AttentionProfile] = field(default_factory=list)
 
     def statistics(self) -> list[Any]:
-        return [basin_statistics(attention=profile.attention, min_edge_ratio=self.min_edge_ratio)
-                for profile in self.profiles]
+        """Basin statistics of each profile, in scan order, at this scan's min_edge_ratio."""
+        criterion = core.BasinCriterion(self.min_edge_ratio)
+        return [core.basin_statistics(profile.attention, criterion) for profile in self.profiles]
 
     def profile_for(self, *, layer_index: int) -> AttentionProfile:
-        for profile in self.profiles:
-            if profile.layer_index == layer_index:
-                return profile
-        raise KeyError(f"layer {layer_index} is not part of this scan")
+        found = next((profile for profile in self.profiles if profile.layer_index == layer_index), None)
+        if found is None:
+            raise KeyError(f"layer {layer_index} is not part of this scan")
+        return found
 
     def highest_ratio_layer(self) -> int:
-        ratios = [statistics.edge_ratio for statistics in self.statistics()]
-        return self.profiles[max(range(len(ratios)), key=lambda index: ratios[index])].layer_index
+        """Layer with the largest edge ratio (the first of equal ones); ValueError on an empty scan."""
+        ratios = np.array([stats.edge_ratio for stats in self.statistics()], dtype=np.float64)
+        if ratios.size == 0:
+            raise ValueError("highest_ratio_layer of a scan without profiles")
+        return self.profiles[int(np.argmax(ratios))].layer_index
 
     def table(self) -> str:
-        lines = [f"{'layer':>5} {'first':>8} {'interior':>9} {'last':>8} {'ratio':>7}  basin"]
+        header = " ".join(f"{name:>{width}}" for name, width, _ in _SCAN_COLUMNS) + "  basin"
+        rows = [header]
         for profile, stats in zip(self.profiles, self.statistics()):
-            mark = "yes" if stats.is_basin else "-"
-            if profile.layer_index == self.selected_layer:
-                mark += "  <- selected"
-            lines.append(f"{profile.layer_index:>5} {stats.first:>8.4f} {stats.interior_mean:>9.4f} "
-                         f"{stats.last:>8.4f} {stats.edge_ratio:>7.2f}  {mark}")
-        return "\n".join(lines)
+            cells = " ".join(render(profile, stats) for _, _, render in _SCAN_COLUMNS)
+            mark = ("yes" if stats.is_basin else "-") + ("  <- selected" if profile.layer_index == self.selected_layer
+                                                        else "")
+            rows.append(f"{cells}  {mark}")
+        return "\n".join(rows)
 
     def to_dict(self) -> dict[str, Any]:
-        return {
-            "selected_layer": self.selected_layer,
-            "min_edge_ratio": self.min_edge_ratio,
-            "profiles": [
-                {"layer_index": profile.layer_index, "attention": list(profile.attention),
-                 "position_order": list(profile.position_order), "edge_ratio": stats.edge_ratio,
-                 "is_basin": stats.is_basin}
-                for profile, stats in zip(self.profiles, self.statistics())
-            ],
-        }
+        layers = []
+        for profile, stats in zip(self.profiles, self.statistics()):
+            layers.append(dict(layer_index=profile.layer_index, attention=list(profile.attention),
+                               position_order=list(profile.position_order), edge_ratio=stats.edge_ratio,
+                               is_basin=stats.is_basin))
+        return dict(selected_layer=self.selected_layer, min_edge_ratio=self.min_edge_ratio, profiles=layers)
 
 
 def find_shallowest_attention_layer(*, engine: Engine, samples: Sequence[StructuredPrompt],
                                     settings: LayerScanSettings = LayerScanSettings(),
                                     progress: ProgressCallback | None = None) -> LayerScan:
-    if len(samples) == 0:
+    """Scan every probed layer and pick the shallowest attention basin (reference: engine.py:337-355;
+    the same ValueErrors for an empty sample list and for fewer than three documents)."""
+    if not samples:
         raise ValueError("at least one probe sample is required")
-    if len(samples[0].document_spans) < MINIMUM_BASIN_SLOTS:
+    slots = len(samples[0].document_spans)
+    if slots < MINIMUM_BASIN_SLOTS:
         raise ValueError(f"attention-basin detection needs at least {MINIMUM_BASIN_SLOTS} documents per sample")
     profiles = scan_attention_layers(engine=engine, samples=samples, settings=settings, progress=progress)
-    selected = select_shallowest_basin_layer(profiles=profiles, min_edge_ratio=settings.min_edge_ratio)
-    return LayerScan(selected_layer=selected, min_edge_ratio=settings.min_edge_ratio, profiles=profiles)
+    return LayerScan(selected_layer=select_shallowest_basin_layer(profiles=profiles,
+                                                                  min_edge_ratio=settings.min_edge_ratio),
+                     min_edge_ratio=settings.min_edge_ratio, profiles=profiles)
 
 
 def extract_attention_profile(*, engine: Engine, samples: Sequence[StructuredPrompt], settings: ProfileSettings,
@@ -284,18 +313,20 @@ def measure_document_attention(*, engine: Engine, prompt: StructuredPrompt, laye
 
 
 def attention_slot_order(*, position_order: Sequence[int], count: int) -> list[int]:
-    return list(core.resolve_position_order(list(position_order), count))
+    """The slot of every rank: the profile's order deduplicated and completed to 0..count-1
+    (reference: engine.py:436-437, attnrank.cpp:377-392)."""
+    return core.resolve_position_order(position_order, count)
 
 
 def rerank_documents(*, documents_by_relevance: Sequence[Any], position_order: Sequence[int]) -> list[Any]:
+    """Place the document of rank r at slot order[r] (reference: engine.py:440-445)."""
     slots = attention_slot_order(position_order=position_order, count=len(documents_by_relevance))
-    placed: list[Any] = [None] * len(documents_by_relevance)
-    for rank, document in enumerate(documents_by_relevance):
-        placed[slots[rank]] = document
-    return placed
+    at_slot = dict(zip(slots, documents_by_relevance))  # slots is a permutation of 0..n-1
+    return [at_slot[slot] for slot in range(len(documents_by_relevance))]
 
 
 def rerank_with_profile(*, documents_by_relevance: Sequence[Any], profile: AttentionProfile) -> list[Any]:
+    """rerank_documents with the profile's position order (reference: engine.py:448-449)."""
     return rerank_documents(documents_by_relevance=documents_by_relevance, position_order=profile.position_order)
 
 

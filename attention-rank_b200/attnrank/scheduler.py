@@ -8,12 +8,21 @@ and a single all-reduce (NCCL over NVLink on GPUs; gloo in the CPU tests) joins 
 per-prompt rows is order independent, so the profile equals the single-GPU scan up to fp32
 rounding; profiles, the basin pick and the slot order are then computed identically on every rank.
 
-Failure handling: the process group is created with a timeout by the caller; a rank that raises
-before the all-reduce makes the others' all-reduce fail with an error instead of hanging (NCCL
-async error handling / gloo timeout), and the exception propagates to every caller.
+Failure handling. Every failure surfaces on every rank as AttnRankError, the error type of the
+reference's bindings (attnrank/src/bindings.cpp:134):
+  * input errors (span counts, layer range) are checked on every rank before any collective, so
+    all ranks reject the same input themselves;
+  * before the all-reduce the ranks exchange a small header (accumulator length, layer range,
+    slots, prompt count); a rank whose accumulator does not match the others' makes every rank
+    raise instead of reducing buffers of different lengths;
+  * each collective runs asynchronously under a host deadline (`deadline_s`): a rank that raised
+    before the collective, stalls past the deadline or died leaves the others waiting at most
+    that long; they then abort the process group's communicators where the backend supports it
+    (NCCL) and raise.
 """
 from __future__ import annotations
 
+import datetime
 import heapq
 from typing import Sequence
 
@@ -50,15 +59,51 @@ def _dist():
     return dist if dist.is_available() and dist.is_initialized() else None
 
 
+DEFAULT_DEADLINE_S = 120.0  # host deadline of one collective of a scan
+
+
 class ProbeScheduler:
     """Runs one layer scan over all ranks of the default (or given) process group."""
 
-    def __init__(self, engine, group=None):
+    def __init__(self, engine, group=None, deadline_s: float = DEFAULT_DEADLINE_S):
         self.engine = engine
         self.group = group
+        self.deadline_s = float(deadline_s)
         dist = _dist()
         self.rank = dist.get_rank(group) if dist else 0
         self.world_size = dist.get_world_size(group) if dist else 1
+
+    def _bounded(self, dist, work, what: str) -> None:
+        """Wait for an asynchronous collective until the deadline; on expiry or error abort the
+        group's communicators (where the backend can) and raise AttnRankError."""
+        try:
+            work.wait(datetime.timedelta(seconds=self.deadline_s))
+            if not work.is_completed():
+                raise TimeoutError("not completed")
+        except Exception as error:  # noqa: BLE001 - every backend failure becomes AttnRankError
+            group = self.group if self.group is not None else dist.group.WORLD
+            try:
+                group.abort()
+            except Exception:  # noqa: BLE001 - a backend without abort (gloo) just drops the collective
+                pass
+            raise core.AttnRankError(f"rank {self.rank}: {what} failed or missed its {self.deadline_s:g} s "
+                                     f"deadline ({type(error).__name__}: {str(error)[:200]})") from error
+
+    def _reduce(self, accumulator, header: list[int]) -> None:
+        """Header check, then the one all-reduce of the accumulator, both under the deadline."""
+        import torch
+        dist = _dist()
+        if dist is None or self.world_size <= 1:
+            return
+        mine = torch.tensor(header, dtype=torch.int64, device=accumulator.device)
+        gathered = [torch.empty_like(mine) for _ in range(self.world_size)]
+        self._bounded(dist, dist.all_gather(gathered, mine, group=self.group, async_op=True), "the scan header exchange")
+        rows = [[int(v) for v in g.cpu()] for g in gathered]
+        if any(row != rows[0] for row in rows):
+            raise core.AttnRankError("ranks disagree on the scan (accumulator length, layer begin, layer end, slots, "
+                                     f"prompts): {rows}")
+        self._bounded(dist, dist.all_reduce(accumulator, op=dist.ReduceOp.SUM, group=self.group, async_op=True),
+                      "the accumulator all-reduce")
 
     def accumulator_device(self) -> str:
         device = getattr(self.engine, "accumulator_device", None)
@@ -85,9 +130,7 @@ class ProbeScheduler:
         mine = [samples[i] for i in self.shard(samples)]
         if mine:
             self.engine.scan(mine, begin, end, settings.normalize_by_length, accumulator=accumulator)
-        dist = _dist()
-        if dist is not None and self.world_size > 1:
-            dist.all_reduce(accumulator, op=dist.ReduceOp.SUM, group=self.group)
+        self._reduce(accumulator, [accumulator.numel(), begin, end, slots, len(samples)])
         return accumulator.double().cpu().numpy().reshape(end - begin, slots)
 
     def find_shallowest_attention_layer(self, samples: Sequence[core.StructuredPrompt],
@@ -108,6 +151,7 @@ class ProbeScheduler:
 
 
 def find_shallowest_attention_layer_sharded(*, engine, samples: Sequence[core.StructuredPrompt],
-                                            settings: LayerScanSettings = LayerScanSettings(), group=None):
+                                            settings: LayerScanSettings = LayerScanSettings(), group=None,
+                                            deadline_s: float = DEFAULT_DEADLINE_S):
     """find_shallowest_attention_layer over every rank of the process group (same result on all)."""
-    return ProbeScheduler(engine, group).find_shallowest_attention_layer(samples, settings)
+    return ProbeScheduler(engine, group, deadline_s).find_shallowest_attention_layer(samples, settings)

@@ -855,7 +855,7 @@ BatchLayout Engine::build_metadata(const std::vector<PromptView>& prompts, const
   host[cursor++] = 0;
   for (int i = 0; i < P; ++i) {
     const int tiles = fused_mass_tiles(host + queries_at + 2 * i, prompts[batch.first + i].token_count);
-    host[cursor] = host[cursor - 1] + c.num_attention_heads * tiles;
+    host[cursor] = host[cursor - 1] + c.num_attention_heads * tiles * kFusedMassSlotsPerTile;
     ++cursor;
   }
   BatchLayout layout;

@@ -21,43 +21,53 @@ namespace {
 constexpr int kRowThreadsCap = 256;
 constexpr int kRopeUnroll = 4;       // heads loaded per rotary step (loads in flight per thread)
 constexpr int kRopeGroupHeads = 8;   // heads of one rotary work item
-constexpr int kSiluUnroll = 2;   // 8-value chunks in flight per SwiGLU thread
+constexpr int kSiluUnroll = 4;   // 8-value chunks in flight per SwiGLU thread
 
 // ---------------------------------------------------------------------------------------------
-// Row kernels: one CTA per token row, each thread holds VPT vectors of 8 channels in registers,
-// so the row is read once, reduced, and written once.
+// Row kernels: a resident grid walks the token rows (row = blockIdx.x, += gridDim.x). Each thread
+// holds VPT vectors of 8 channels of a row in registers, so a row is read once, reduced, and
+// written once; the loads of the CTA's next row are issued before the current row's block-wide
+// reduction, so they are in flight while the CTA waits at its barrier and stores.
 // ---------------------------------------------------------------------------------------------
+// Sum over the whole block through one of two scratch buffers (alternate them between calls:
+// one barrier per call then suffices, since a warp can only reuse a buffer after every warp has
+// passed the barrier of the call in between).
+__device__ __forceinline__ float block_sum_buffered(float value, float* scratch) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int warps = (blockDim.x + 31) >> 5;
+  value = warp_sum(value);
+  if (lane == 0) scratch[warp] = value;
+  __syncthreads();
+  float total = lane < warps ? scratch[lane] : 0.0f;
+  return warp_sum(total);
+}
+
 template <typename T, int VPT>
-__global__ void __launch_bounds__(kRowThreadsCap) embed_rms_norm_kernel(
-    const int32_t* __restrict__ token_ids, const T* __restrict__ table, int vocab, int hidden,
-    const float* __restrict__ gamma, float eps, float* __restrict__ residual, T* __restrict__ normed,
-    int* status) {
-  __shared__ float scratch[32];
-  const int row = blockIdx.x;
-  int token = token_ids[row];
-  if (token < 0 || token >= vocab) {
-    if (threadIdx.x == 0) report_status(status, kStatusTokenOutOfRange);
-    token = -1;
-  }
-  const int chunks = hidden >> 3;
-  float values[VPT][8];
-  float squares = 0.0f;
+struct NormRowLoads {
+  float4 residual[VPT][2];
+  uint4 delta[VPT];
+};
+
+template <typename T, int VPT>
+__device__ __forceinline__ void load_norm_row(NormRowLoads<T, VPT>& loads, const float* residual, const T* delta,
+                                              int row, int hidden, int chunks) {
+  const float* residual_row = residual + static_cast<size_t>(row) * hidden;
+  const T* delta_row = delta + static_cast<size_t>(row) * hidden;
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
     const int chunk = threadIdx.x + k * blockDim.x;
-    if (chunk < chunks && token >= 0) {
-      unpack8<T>(load_nc(table + static_cast<size_t>(token) * hidden + chunk * 8), values[k]);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) values[k][i] = 0.0f;
+    if (chunk < chunks) {
+      loads.residual[k][0] = load_stream_f4(residual_row + chunk * 8);
+      loads.residual[k][1] = load_stream_f4(residual_row + chunk * 8 + 4);
+      loads.delta[k] = load_stream(delta_row + chunk * 8);
     }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) squares += values[k][i] * values[k][i];
   }
-  const float total = block_sum(squares, scratch);
-  const float scale = rsqrtf(total / static_cast<float>(hidden) + eps);
-  float* residual_row = residual + static_cast<size_t>(row) * hidden;
-  T* normed_row = normed + static_cast<size_t>(row) * hidden;
+}
+
+template <typename T, int VPT>
+__device__ __forceinline__ void store_normed_row(const float (&values)[VPT][8], float scale, const float* gamma,
+                                                 T* normed_row, int chunks) {
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
     const int chunk = threadIdx.x + k * blockDim.x;
@@ -65,67 +75,112 @@ __global__ void __launch_bounds__(kRowThreadsCap) embed_rms_norm_kernel(
     const float4 g0 = __ldg(reinterpret_cast<const float4*>(gamma + chunk * 8));
     const float4 g1 = __ldg(reinterpret_cast<const float4*>(gamma + chunk * 8 + 4));
     const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-    float4* out = reinterpret_cast<float4*>(residual_row + chunk * 8);
-    __stcs(out, make_float4(values[k][0], values[k][1], values[k][2], values[k][3]));
-    __stcs(out + 1, make_float4(values[k][4], values[k][5], values[k][6], values[k][7]));
     float y[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) y[i] = values[k][i] * scale * g[i];
-    *reinterpret_cast<uint4*>(normed_row + chunk * 8) = pack8<T>(y);
+    __stcs(reinterpret_cast<uint4*>(normed_row + chunk * 8), pack8<T>(y));
+  }
+}
+
+template <typename T, int VPT>
+__global__ void __launch_bounds__(kRowThreadsCap) embed_rms_norm_kernel(
+    const int32_t* __restrict__ token_ids, const T* __restrict__ table, int tokens, int vocab, int hidden,
+    const float* __restrict__ gamma, float eps, float* __restrict__ residual, T* __restrict__ normed,
+    int* status) {
+  __shared__ float scratch[2][32];
+  const int chunks = hidden >> 3;
+  // the table row of a token id outside [0, vocab) is never read: that row becomes zeros
+  auto checked_token = [&](int row) {
+    const int token = __ldg(token_ids + row);
+    if (token < 0 || token >= vocab) {
+      if (threadIdx.x == 0) report_status(status, kStatusTokenOutOfRange);
+      return -1;
+    }
+    return token;
+  };
+  auto load_row = [&](uint4 (&raw)[VPT], int token) {
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int chunk = threadIdx.x + k * blockDim.x;
+      raw[k] = make_uint4(0u, 0u, 0u, 0u);
+      if (chunk < chunks && token >= 0) raw[k] = load_nc(table + static_cast<size_t>(token) * hidden + chunk * 8);
+    }
+  };
+  int row = blockIdx.x;
+  uint4 next[VPT];
+  if (row < tokens) load_row(next, checked_token(row));
+  for (int parity = 0; row < tokens; row += gridDim.x, parity ^= 1) {
+    uint4 current[VPT];
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) current[k] = next[k];
+    if (row + static_cast<int>(gridDim.x) < tokens) load_row(next, checked_token(row + gridDim.x));
+    float values[VPT][8];
+    float squares = 0.0f;
+    float* residual_row = residual + static_cast<size_t>(row) * hidden;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      unpack8<T>(current[k], values[k]);
+      const int chunk = threadIdx.x + k * blockDim.x;
+      if (chunk < chunks) {
+        float4* out = reinterpret_cast<float4*>(residual_row + chunk * 8);
+        __stcs(out, make_float4(values[k][0], values[k][1], values[k][2], values[k][3]));
+        __stcs(out + 1, make_float4(values[k][4], values[k][5], values[k][6], values[k][7]));
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) squares += values[k][i] * values[k][i];
+    }
+    const float total = block_sum_buffered(squares, scratch[parity]);
+    const float scale = rsqrtf(total / static_cast<float>(hidden) + eps);
+    store_normed_row<T, VPT>(values, scale, gamma, normed + static_cast<size_t>(row) * hidden, chunks);
   }
 }
 
 template <typename T, int VPT>
 __global__ void __launch_bounds__(kRowThreadsCap) rms_norm_residual_kernel(
-    float* __restrict__ residual, const T* __restrict__ delta, const float* __restrict__ gamma,
+    float* __restrict__ residual, const T* __restrict__ delta, const float* __restrict__ gamma, int tokens,
     int hidden, float eps, T* __restrict__ normed) {
-  __shared__ float scratch[32];
-  const int row = blockIdx.x;
+  __shared__ float scratch[2][32];
   const int chunks = hidden >> 3;
-  float* residual_row = residual + static_cast<size_t>(row) * hidden;
-  const T* delta_row = delta + static_cast<size_t>(row) * hidden;
-  float values[VPT][8];
-  float squares = 0.0f;
-#pragma unroll
-  for (int k = 0; k < VPT; ++k) {
-    const int chunk = threadIdx.x + k * blockDim.x;
-    if (chunk < chunks) {
-      const float4 r0 = load_stream_f4(residual_row + chunk * 8);
-      const float4 r1 = load_stream_f4(residual_row + chunk * 8 + 4);
-      float d[8];
-      unpack8<T>(load_stream(delta_row + chunk * 8), d);
-      values[k][0] = r0.x + d[0];
-      values[k][1] = r0.y + d[1];
-      values[k][2] = r0.z + d[2];
-      values[k][3] = r0.w + d[3];
-      values[k][4] = r1.x + d[4];
-      values[k][5] = r1.y + d[5];
-      values[k][6] = r1.z + d[6];
-      values[k][7] = r1.w + d[7];
-      float4* out = reinterpret_cast<float4*>(residual_row + chunk * 8);
-      __stcs(out, make_float4(values[k][0], values[k][1], values[k][2], values[k][3]));
-      __stcs(out + 1, make_float4(values[k][4], values[k][5], values[k][6], values[k][7]));
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) values[k][i] = 0.0f;
+  int row = blockIdx.x;
+  NormRowLoads<T, VPT> next;
+  if (row < tokens) load_norm_row<T, VPT>(next, residual, delta, row, hidden, chunks);
+  for (int parity = 0; row < tokens; row += gridDim.x, parity ^= 1) {
+    const NormRowLoads<T, VPT> current = next;
+    if (row + static_cast<int>(gridDim.x) < tokens) {
+      load_norm_row<T, VPT>(next, residual, delta, row + gridDim.x, hidden, chunks);
     }
+    float* residual_row = residual + static_cast<size_t>(row) * hidden;
+    float values[VPT][8];
+    float squares = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) squares += values[k][i] * values[k][i];
-  }
-  const float total = block_sum(squares, scratch);
-  const float scale = rsqrtf(total / static_cast<float>(hidden) + eps);
-  T* normed_row = normed + static_cast<size_t>(row) * hidden;
+    for (int k = 0; k < VPT; ++k) {
+      const int chunk = threadIdx.x + k * blockDim.x;
+      if (chunk < chunks) {
+        float d[8];
+        unpack8<T>(current.delta[k], d);
+        const float4 r0 = current.residual[k][0];
+        const float4 r1 = current.residual[k][1];
+        values[k][0] = r0.x + d[0];
+        values[k][1] = r0.y + d[1];
+        values[k][2] = r0.z + d[2];
+        values[k][3] = r0.w + d[3];
+        values[k][4] = r1.x + d[4];
+        values[k][5] = r1.y + d[5];
+        values[k][6] = r1.z + d[6];
+        values[k][7] = r1.w + d[7];
+        float4* out = reinterpret_cast<float4*>(residual_row + chunk * 8);
+        __stcs(out, make_float4(values[k][0], values[k][1], values[k][2], values[k][3]));
+        __stcs(out + 1, make_float4(values[k][4], values[k][5], values[k][6], values[k][7]));
+      } else {
 #pragma unroll
-  for (int k = 0; k < VPT; ++k) {
-    const int chunk = threadIdx.x + k * blockDim.x;
-    if (chunk >= chunks) continue;
-    const float4 g0 = __ldg(reinterpret_cast<const float4*>(gamma + chunk * 8));
-    const float4 g1 = __ldg(reinterpret_cast<const float4*>(gamma + chunk * 8 + 4));
-    const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-    float y[8];
+        for (int i = 0; i < 8; ++i) values[k][i] = 0.0f;
+      }
 #pragma unroll
-    for (int i = 0; i < 8; ++i) y[i] = values[k][i] * scale * g[i];
-    *reinterpret_cast<uint4*>(normed_row + chunk * 8) = pack8<T>(y);
+      for (int i = 0; i < 8; ++i) squares += values[k][i] * values[k][i];
+    }
+    const float total = block_sum_buffered(squares, scratch[parity]);
+    const float scale = rsqrtf(total / static_cast<float>(hidden) + eps);
+    store_normed_row<T, VPT>(values, scale, gamma, normed + static_cast<size_t>(row) * hidden, chunks);
   }
 }
 
@@ -248,43 +303,46 @@ __global__ void rope_table_kernel(float* __restrict__ cos_out, float* __restrict
 // output has g in columns [0, I) and u in [I, 2I) of each row).
 // ---------------------------------------------------------------------------------------------
 template <typename T>
-__global__ void __launch_bounds__(256, 6) silu_multiply_kernel(const T* __restrict__ gate, const T* __restrict__ up, long long in_stride,
-                                     T* __restrict__ out, long long out_stride, int tokens, int width) {
-  // CTAs walk rows; a thread handles chunks c, c + blockDim, ... of the row, kSiluUnroll of them
-  // loaded before any is computed (no integer division on the index path)
-  const int chunks = width >> 3;
-  const int span = blockDim.x * kSiluUnroll;
-  for (int token = blockIdx.x; token < tokens; token += gridDim.x) {
-    const T* gate_row = gate + token * in_stride;
-    const T* up_row = up + token * in_stride;
-    T* out_row = out + token * out_stride;
-    for (int first = threadIdx.x; first < chunks; first += span) {
-      uint4 g_raw[kSiluUnroll];
-      uint4 u_raw[kSiluUnroll];
+__global__ void __launch_bounds__(256) silu_multiply_kernel(const T* __restrict__ gate, const T* __restrict__ up,
+                                                            long long in_stride, T* __restrict__ out,
+                                                            long long out_stride, int tokens, int width) {
+  // The (row, 8-value chunk) pairs of the whole batch form one index space that a resident grid
+  // walks; a thread loads kSiluUnroll chunks (grid-stride apart) before it computes any, so the
+  // whole wave has the same number of loads in flight and no row leaves a partial tail.
+  const unsigned chunks = static_cast<unsigned>(width) >> 3;
+  const unsigned total = static_cast<unsigned>(tokens) * chunks;  // < 2^31: the launcher checks
+  const unsigned stride = gridDim.x * blockDim.x;
+  for (unsigned first = blockIdx.x * blockDim.x + threadIdx.x; first < total; first += stride * kSiluUnroll) {
+    uint4 g_raw[kSiluUnroll];
+    uint4 u_raw[kSiluUnroll];
+    long long out_at[kSiluUnroll];
 #pragma unroll
-      for (int k = 0; k < kSiluUnroll; ++k) {
-        const int chunk = first + k * blockDim.x;
-        if (chunk < chunks) {
-          g_raw[k] = load_stream(gate_row + chunk * 8);
-          u_raw[k] = load_stream(up_row + chunk * 8);
-        }
+    for (int k = 0; k < kSiluUnroll; ++k) {
+      const unsigned item = first + k * stride;
+      out_at[k] = -1;
+      if (item < total) {
+        const unsigned token = item / chunks;
+        const unsigned chunk = item - token * chunks;
+        const long long in_at = static_cast<long long>(token) * in_stride + chunk * 8;
+        g_raw[k] = load_stream(gate + in_at);
+        u_raw[k] = load_stream(up + in_at);
+        out_at[k] = static_cast<long long>(token) * out_stride + chunk * 8;
       }
+    }
 #pragma unroll
-      for (int k = 0; k < kSiluUnroll; ++k) {
-        const int chunk = first + k * blockDim.x;
-        if (chunk >= chunks) break;
-        float g[8];
-        float u[8];
-        unpack8<T>(g_raw[k], g);
-        unpack8<T>(u_raw[k], u);
-        // silu(g) * u = g / (1 + e^-g) * u, the reference formula (kernels.cu:169) with a fast
-        // fp32 divide: its few-ulp fp32 error vanishes in the 16-bit rounding of the result
-        // (for e^-g = inf the quotient is 0, the limit of silu)
-        float a[8];
+    for (int k = 0; k < kSiluUnroll; ++k) {
+      if (out_at[k] < 0) break;
+      float g[8];
+      float u[8];
+      unpack8<T>(g_raw[k], g);
+      unpack8<T>(u_raw[k], u);
+      // silu(g) * u = g / (1 + e^-g) * u, the reference formula (kernels.cu:169) with a fast
+      // fp32 divide: its few-ulp fp32 error vanishes in the 16-bit rounding of the result
+      // (for e^-g = inf the quotient is 0, the limit of silu)
+      float a[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) a[i] = __fdividef(g[i], 1.0f + __expf(-g[i])) * u[i];
-        __stcs(reinterpret_cast<uint4*>(out_row + chunk * 8), pack8<T>(a));
-      }
+      for (int i = 0; i < 8; ++i) a[i] = __fdividef(g[i], 1.0f + __expf(-g[i])) * u[i];
+      __stcs(reinterpret_cast<uint4*>(out + out_at[k]), pack8<T>(a));
     }
   }
 }
@@ -343,6 +401,12 @@ static int stride_grid(long long items, int threads, int ctas_per_sm) {
   return static_cast<int>(needed < cap ? (needed > 0 ? needed : 1) : cap);
 }
 
+// A resident grid (every CTA slot of every SM, one wave) walks the rows.
+template <typename Kernel>
+static int row_grid(Kernel kernel, int threads, int tokens) {
+  return std::max(1, std::min(tokens, sm_count() * resident_per_sm(kernel, threads)));
+}
+
 template <typename T>
 cudaError_t embed_typed(const int32_t* token_ids, int tokens, const void* table, int vocab, int hidden,
                         const float* gamma, float eps, float* residual, void* normed, int* status,
@@ -351,11 +415,15 @@ cudaError_t embed_typed(const int32_t* token_ids, int tokens, const void* table,
   const int threads = row_threads(hidden, &vpt);
   const auto* t = static_cast<const T*>(table);
   auto* n = static_cast<T*>(normed);
+  auto launch = [&](auto kernel) {
+    kernel<<<row_grid(kernel, threads, tokens), threads, 0, stream>>>(token_ids, t, tokens, vocab, hidden, gamma, eps,
+                                                                      residual, n, status);
+  };
   switch (vpt) {
-    case 1: embed_rms_norm_kernel<T, 1><<<tokens, threads, 0, stream>>>(token_ids, t, vocab, hidden, gamma, eps, residual, n, status); break;
-    case 2: embed_rms_norm_kernel<T, 2><<<tokens, threads, 0, stream>>>(token_ids, t, vocab, hidden, gamma, eps, residual, n, status); break;
-    case 3: embed_rms_norm_kernel<T, 3><<<tokens, threads, 0, stream>>>(token_ids, t, vocab, hidden, gamma, eps, residual, n, status); break;
-    case 4: embed_rms_norm_kernel<T, 4><<<tokens, threads, 0, stream>>>(token_ids, t, vocab, hidden, gamma, eps, residual, n, status); break;
+    case 1: launch(embed_rms_norm_kernel<T, 1>); break;
+    case 2: launch(embed_rms_norm_kernel<T, 2>); break;
+    case 3: launch(embed_rms_norm_kernel<T, 3>); break;
+    case 4: launch(embed_rms_norm_kernel<T, 4>); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
@@ -368,11 +436,14 @@ cudaError_t norm_typed(float* residual, const void* delta, const float* gamma, i
   const int threads = row_threads(hidden, &vpt);
   const auto* d = static_cast<const T*>(delta);
   auto* n = static_cast<T*>(normed);
+  auto launch = [&](auto kernel) {
+    kernel<<<row_grid(kernel, threads, tokens), threads, 0, stream>>>(residual, d, gamma, tokens, hidden, eps, n);
+  };
   switch (vpt) {
-    case 1: rms_norm_residual_kernel<T, 1><<<tokens, threads, 0, stream>>>(residual, d, gamma, hidden, eps, n); break;
-    case 2: rms_norm_residual_kernel<T, 2><<<tokens, threads, 0, stream>>>(residual, d, gamma, hidden, eps, n); break;
-    case 3: rms_norm_residual_kernel<T, 3><<<tokens, threads, 0, stream>>>(residual, d, gamma, hidden, eps, n); break;
-    case 4: rms_norm_residual_kernel<T, 4><<<tokens, threads, 0, stream>>>(residual, d, gamma, hidden, eps, n); break;
+    case 1: launch(rms_norm_residual_kernel<T, 1>); break;
+    case 2: launch(rms_norm_residual_kernel<T, 2>); break;
+    case 3: launch(rms_norm_residual_kernel<T, 3>); break;
+    case 4: launch(rms_norm_residual_kernel<T, 4>); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
@@ -440,10 +511,13 @@ cudaError_t launch_rope_table(float* cos_out, float* sin_out, int positions, int
 cudaError_t launch_silu_multiply(const void* gate, const void* up, long long in_stride, void* out,
                                  long long out_stride, int tokens, int width, int dtype, cudaStream_t stream) {
   if (tokens <= 0 || width <= 0) return cudaSuccess;
+  const long long items = static_cast<long long>(tokens) * (width / 8);
+  if (items >= (1LL << 31)) return cudaErrorInvalidValue;
   const int threads = 256;
   const int per_sm = dtype == kActFp16 ? resident_per_sm(silu_multiply_kernel<__half>, threads)
                                        : resident_per_sm(silu_multiply_kernel<__nv_bfloat16>, threads);
-  const int grid = std::min(tokens, sm_count() * per_sm);  // one wave of resident CTAs walks all rows
+  const long long needed = (items + threads * kSiluUnroll - 1) / (threads * kSiluUnroll);
+  const int grid = static_cast<int>(std::max(1LL, std::min<long long>(needed, sm_count() * per_sm)));
   if (dtype == kActFp16) {
     silu_multiply_kernel<__half><<<grid, threads, 0, stream>>>(static_cast<const __half*>(gate),
                                                                static_cast<const __half*>(up), in_stride,

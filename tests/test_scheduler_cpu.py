@@ -24,9 +24,10 @@ class FakeEngine:
     accumulator_device = "cpu"
     model_directory = "fake"
 
-    def __init__(self, layers=4, fail=False):
+    def __init__(self, layers=4, fail=False, stall_s=0.0):
         self.num_layers = layers
         self.fail = fail
+        self.stall_s = stall_s
 
     @staticmethod
     def rows(prompt, layers):
@@ -40,6 +41,8 @@ class FakeEngine:
     def scan(self, prompts, layer_begin, layer_end, normalize_by_length, accumulator=None):
         if self.fail:
             raise RuntimeError("injected rank failure")
+        if self.stall_s:
+            __import__("time").sleep(self.stall_s)
         begin = 0 if layer_begin < 0 else layer_begin  # the engine's own range resolution
         end = self.num_layers if layer_end < 0 else layer_end
         total = sum(self.rows(p, self.num_layers)[begin:end] for p in prompts)
@@ -59,7 +62,8 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, fail_rank, queue, bad_spans=False, prompt_count=None):
+def _worker(rank, world, port, fail_rank, queue, bad_spans=False, prompt_count=None, stall_rank=-1, stall_s=0.0,
+            deadline_s=60.0, short_rank=-1):
     import datetime
     import sys
     from pathlib import Path
@@ -72,17 +76,25 @@ def _worker(rank, world, port, fail_rank, queue, bad_spans=False, prompt_count=N
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
     try:
-        engine = FakeEngine(fail=(rank == fail_rank))
+        engine = FakeEngine(layers=3 if rank == short_rank else 4, fail=(rank == fail_rank),
+                            stall_s=stall_s if rank == stall_rank else 0.0)
         prompts = list(_prompts())[:prompt_count]
         if bad_spans:  # one sample with a span fewer than the rest
             odd = prompts[-1]
             prompts[-1] = ar.StructuredPrompt(tokens=odd.tokens, document_spans=list(odd.document_spans)[:4],
                                               query_span=odd.query_span)
-        scan = ProbeScheduler(engine).find_shallowest_attention_layer(prompts, ar.LayerScanSettings(min_edge_ratio=0.9))
+        import time
+        start = time.monotonic()
+        try:
+            scan = ProbeScheduler(engine, deadline_s=deadline_s).find_shallowest_attention_layer(
+                prompts, ar.LayerScanSettings(min_edge_ratio=0.9))
+        except Exception as error:  # noqa: BLE001 - reported to the parent with the time it took
+            queue.put((rank, "error", type(error).__name__, str(error)[:300], time.monotonic() - start))
+            return
         queue.put((rank, "ok", scan.selected_layer, [p.attention for p in scan.profiles],
                    [p.position_order for p in scan.profiles]))
     except Exception as error:  # noqa: BLE001 - reported to the parent
-        queue.put((rank, "error", type(error).__name__, str(error)[:200], None))
+        queue.put((rank, "error", type(error).__name__, str(error)[:300], None))
     finally:
         try:
             dist.destroy_process_group()
@@ -90,11 +102,12 @@ def _worker(rank, world, port, fail_rank, queue, bad_spans=False, prompt_count=N
             pass
 
 
-def _run(world, fail_rank=-1, bad_spans=False, prompt_count=None):
+def _run(world, fail_rank=-1, bad_spans=False, prompt_count=None, **options):
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, fail_rank, queue, bad_spans, prompt_count))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, fail_rank, queue, bad_spans, prompt_count),
+                         kwargs=options)
              for r in range(world)]
     for p in procs:
         p.start()
@@ -191,3 +204,25 @@ def test_a_rank_with_no_prompts_still_joins_the_all_reduce():
         for layer, profile in enumerate(single.profiles):
             np.testing.assert_allclose(attention[layer], profile.attention, rtol=1e-6)
             assert order[layer] == profile.position_order
+
+
+def test_a_stalled_rank_makes_the_others_raise_at_the_deadline():
+    """Rank 1 stalls 12 s inside its scan; rank 0 waits for it in the header exchange for its 2 s
+    deadline only, then raises AttnRankError (the reference's error type, bindings.cpp:134)
+    instead of waiting for the process group's 20 s timeout. Rank 1, arriving late to a group
+    its peer has left, fails with an error too."""
+    results = _run(2, stall_rank=1, stall_s=12.0, deadline_s=2.0)
+    rank0 = results[0]
+    assert rank0[1] == "error" and rank0[2] == "AttnRankError", results
+    assert "deadline" in rank0[3] and rank0[4] < 10.0, rank0
+    assert results[1][1] == "error", results
+
+
+def test_a_rank_with_a_wrong_length_accumulator_fails_every_rank():
+    """Rank 1's engine reports 3 layers instead of 4, so its accumulator is shorter: the header
+    exchange before the all-reduce shows the mismatch and both ranks raise AttnRankError instead
+    of reducing buffers of different lengths."""
+    results = _run(2, short_rank=1)
+    for _, status, kind, message, _ in results:
+        assert status == "error" and kind == "AttnRankError", results
+        assert "ranks disagree" in message and "[20, 0, 4, 5, 37]" in message and "[15, 0, 3, 5, 37]" in message
