@@ -133,6 +133,7 @@ SIGNATURES: dict[str, list] = {
     "ar_decode_gemv": [_P, _P, _I, _I, _P, _I, _I, _P],
     "ar_decode_gate_up": [_P, _P, _I, _I, _P, _I, _P],
     "ar_decode_attention": [_P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _I, _P],
+    "ar_bounded_wait_selftest": [_I, ctypes.c_uint32, _P],
     "ar_profile_from_accumulated": [_P, _I, _I64, _P, _P],
     "ar_position_order": [_P, _I, _P],
     "ar_basin_statistics": [_P, _I, _D, ctypes.POINTER(BasinStatsStruct)],

@@ -157,7 +157,10 @@ class RuntimeOptions:
     max_batch_tokens: int = 16384
     max_batch_prompts: int = 256
     # Additive: the 16-bit type of weights, GEMM operands and activations ("fp16", the reference's
-    # GEMM operand type, or "bf16"), and the attention kernel ("tcgen05" or "mma").
+    # GEMM operand type, or "bf16"), and the attention kernel ("tcgen05" or "mma"). Only "fp16"
+    # is held to the rel 1e-3 attention-mass bar against the reference at the 7B shape: rounding
+    # the GEMM inputs to bf16 alone moves the mass rows by up to 1.0e-3 from fp32, and a bf16
+    # engine measured rel 1.7e-3 against the reference's build. "bf16" is outside that budget.
     activation_dtype: str = "fp16"
     attention_kernel: str = "tcgen05"
 

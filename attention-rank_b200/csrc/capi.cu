@@ -568,6 +568,30 @@ int ar_decode_attention(const void* q, const void* k_cache, const void* v_cache,
   });
 }
 
+int ar_bounded_wait_selftest(int ctas, uint32_t spin_limit, void* stream) {
+  return guarded([&] {
+    if (ctas <= 0 || ctas > 1024 || spin_limit == 0 || spin_limit > (1u << 22)) {
+      throw arb::Error("bounded_wait_selftest: ctas must be 1..1024 and spin_limit 1..4194304");
+    }
+    cudaStream_t s = as_stream(stream);
+    StreamScratch scratch(s);
+    auto* words = static_cast<unsigned*>(scratch.get(2 * sizeof(unsigned)));  // counter | status
+    arb::check_cuda(cudaMemsetAsync(words, 0, 2 * sizeof(unsigned), s), "selftest reset");
+    arb::check_cuda(arb::launch_bounded_wait_selftest(words, reinterpret_cast<int*>(words + 1), ctas, spin_limit, s),
+                    "bounded_wait_selftest");
+    unsigned status = 0;
+    arb::check_cuda(cudaMemcpyAsync(&status, words + 1, sizeof(unsigned), cudaMemcpyDeviceToHost, s), "status read");
+    arb::check_cuda(cudaStreamSynchronize(s), "bounded_wait_selftest");
+    if (status != static_cast<unsigned>(arb::kStatusWaitTimeout)) {
+      throw arb::Error("bounded_wait_selftest: the unreachable wait ended with status " + std::to_string(status) +
+                       " instead of a wait timeout");
+    }
+    throw arb::Error("device reported a wait timeout (status " + std::to_string(status) +
+                     "): the bounded wait gave up as designed");
+    return AR_OK;
+  });
+}
+
 int ar_profile_from_accumulated(const double* accumulated, int slots, int64_t sample_count, double* attention_out,
                                 int* position_order_out) {
   return guarded([&] {

@@ -763,7 +763,8 @@ constexpr unsigned kBarrierSpinLimit = 1u << 22;  // polls of 64 ns or more: ove
 // (fence), arrives on the counter and polls it until every CTA of this generation has arrived.
 // The poll is bounded; false after a timeout or when the status word already reports an error,
 // and then every CTA returns.
-__device__ bool grid_barrier(unsigned* counter, unsigned& target, int* status) {
+__device__ bool grid_barrier(unsigned* counter, unsigned& target, int* status,
+                             unsigned spin_limit = kBarrierSpinLimit) {
   __shared__ int proceed;
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -779,7 +780,7 @@ __device__ bool grid_barrier(unsigned* counter, unsigned& target, int* status) {
         ok = 0;
         break;
       }
-      if (spins >= kBarrierSpinLimit) {
+      if (spins >= spin_limit) {
         report_status(status, kStatusWaitTimeout);
         ok = 0;
         break;
@@ -866,6 +867,14 @@ __global__ void __launch_bounds__(kGemvThreads, 2) decode_step_kernel(const Deco
     if (!grid_barrier(s.barrier, target, s.status)) return;
     if (blockIdx.x == 0) reduce_pick(head, gridDim.x);
   }
+}
+
+// Self-test of the bounded grid barrier: every CTA waits for one arrival more than the grid makes,
+// a counter value nothing will ever write, so the wait must run out after `spin_limit` polls,
+// record kStatusWaitTimeout and let every CTA return (the others see the status word and stop).
+__global__ void bounded_wait_selftest_kernel(unsigned* counter, int* status, unsigned spin_limit) {
+  unsigned target = 1;  // grid_barrier adds gridDim.x: one more than the CTAs that arrive
+  grid_barrier(counter, target, status, spin_limit);
 }
 
 template <typename T>
@@ -1086,6 +1095,13 @@ cudaError_t launch_decode_attention(const DecodeAttentionArgs& args, bool progra
                       scale_log2)
              : launch(decode_attention_kernel<__nv_bfloat16>, grid, dim3(kDecodeThreads), 0, stream, programmatic,
                       args, scale_log2);
+}
+
+cudaError_t launch_bounded_wait_selftest(unsigned* counter, int* status, int ctas, unsigned spin_limit,
+                                         cudaStream_t stream) {
+  if (ctas <= 0 || ctas > 1024 || spin_limit == 0 || spin_limit > kBarrierSpinLimit) return cudaErrorInvalidValue;
+  bounded_wait_selftest_kernel<<<ctas, 32, 0, stream>>>(counter, status, spin_limit);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_store_kv(const void* qkv, int tokens, int query_heads, int kv_heads, int head_dim, void* k_cache,

@@ -144,6 +144,13 @@ struct DecodeStepArgs {
 // device cannot hold the grid, in which case the per-phase kernels are the way.
 cudaError_t launch_decode_step(const DecodeStepArgs& args, cudaStream_t stream);
 
+// The bounded grid barrier of the persistent decode step, made to run out on purpose: `ctas` CTAs
+// (at most 1024) wait on a counter value nothing writes, for `spin_limit` polls (at most the
+// production limit), then record kStatusWaitTimeout in *status and return. counter and status
+// start at zero.
+cudaError_t launch_bounded_wait_selftest(unsigned* counter, int* status, int ctas, unsigned spin_limit,
+                                         cudaStream_t stream);
+
 // K and V of a prefilled prompt (rows 0 .. tokens-1 of the q|k|v buffer, after RoPE) into the
 // cache at positions 0 .. tokens-1.
 cudaError_t launch_store_kv(const void* qkv, int tokens, int query_heads, int kv_heads, int head_dim, void* k_cache,

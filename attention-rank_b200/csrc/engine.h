@@ -107,7 +107,7 @@ struct BatchLayout {
   int tokens = 0;
   int tile_count = 0;  // attention query tiles
   int item_count = 0;  // mass CTAs (separate mass kernel)
-  int fused_item_count = 0;  // mass partial slots of the fused attention (Hq x query tiles in the span x 4)
+  int fused_item_count = 0;  // mass partial slots of the fused attention (Hq x query tiles in the span)
   double attention_flops = 0;  // 4 D Hq x visible causal (query, key) pairs
   double mass_flops = 0;       // 2 D Hq x sum over prompts of query rows x document-span keys
 };

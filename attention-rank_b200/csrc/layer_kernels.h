@@ -49,14 +49,13 @@ struct AttentionArgs {
   int dtype = kActFp16;             // ActivationType of qkv and out
   int rows = 0;                     // rows of qkv (tensor-map extent; tcgen05 kernel)
   int* status = nullptr;            // device status word (tcgen05 kernel: wait timeouts)
-  // Fused attention mass (tcgen05 kernel only; mass_partials == nullptr: none). Partial slots of
-  // (prompt p, query head h, query tile t): mass_items[p] + (h * tiles_p + (t - first_p)) *
-  // kFusedMassSlotsPerTile + w for the tile's softmax warps w, where first_p.. are the query
-  // tiles that hold rows of p's query span (fused_mass_tiles).
+  // Fused attention mass (tcgen05 kernel only; mass_partials == nullptr: none). Partial slot of
+  // (prompt p, query head h, query tile t): mass_items[p] + h * tiles_p + (t - first_p), where
+  // first_p.. are the query tiles that hold rows of p's query span (fused_mass_tiles).
   const int32_t* query_spans = nullptr;   // [prompts * 2], prompt-relative
   const int32_t* spans = nullptr;         // [prompts * span_count * 2], prompt-relative
   const int32_t* mass_items = nullptr;    // [prompts + 1]
-  float* mass_partials = nullptr;         // [slots * span_count], each the sum over 32 rows of a tile
+  float* mass_partials = nullptr;         // [items * span_count], each the sum over the tile's rows
   int span_count = 0;
   int normalize_by_length = 0;
   int reference_chunk = 0;
@@ -65,9 +64,9 @@ struct AttentionArgs {
 cudaError_t launch_causal_attention(const AttentionArgs& args, cudaStream_t stream);
 cudaError_t launch_causal_attention_tc(const AttentionArgs& args, cudaStream_t stream);
 constexpr int kAttentionQueryTile = 128;
-// Fused mass partial slots per (query head, query tile): one per softmax warp of the tile (each
-// the fixed-order sum over its 32 rows), summed in a fixed order by the finalize kernel.
-constexpr int kFusedMassSlotsPerTile = 4;
+// Fused mass partial slots per (query head, query tile): one, the fixed-order sum over the tile's
+// rows, summed in a fixed order by the finalize kernel.
+constexpr int kFusedMassSlotsPerTile = 1;
 
 // Query tiles (kAttentionQueryTile rows) that hold rows of a prompt's query span: the fused mass
 // writes one partial per (query head, such tile).

@@ -116,6 +116,8 @@ def parse_args():
                         help="decode on the first N layers only (a small case for ncu captures; not a bench line)")
     parser.add_argument("--sweep", action="store_true",
                         help="only the fused-kernel bandwidth sweep of BASELINE config 5 (one GPU)")
+    parser.add_argument("--no-sweep", action="store_true",
+                        help="leave the config-5 sweep out of the N=1 bench line")
     return parser.parse_args()
 
 
@@ -226,6 +228,18 @@ def max_over_ranks(value: float, world: int) -> float:
     t = torch.tensor([value], dtype=torch.float64, device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def gather_over_ranks(values: list[float], world: int) -> list[list[float]]:
+    """Every rank's list of floats, in rank order (one all-gather)."""
+    if world == 1:
+        return [list(values)]
+    import torch
+    import torch.distributed as dist
+    mine = torch.tensor(values, dtype=torch.float64, device="cuda")
+    gathered = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(gathered, mine)
+    return [[float(v) for v in g.cpu()] for g in gathered]
 
 
 def barrier(world: int):
@@ -485,13 +499,23 @@ def run_b200(args, rank, world, local_rank):
     torch.cuda.synchronize()
     engine_stream = torch.cuda.ExternalStream(engine.stream, device=f"cuda:{local_rank}")
 
-    def step():
+    marks = []  # per timed step: events before the scan, after it and after the all-reduce
+
+    def step(record=False):
         with torch.cuda.stream(engine_stream):
+            events = [torch.cuda.Event(enable_timing=True) for _ in range(3)] if record else None
             accumulator.zero_()
+            if record:
+                events[0].record(engine_stream)
             prepared.run(accumulator, synchronize=False)
+            if record:
+                events[1].record(engine_stream)
             if world > 1:
                 import torch.distributed as dist
                 dist.all_reduce(accumulator)
+            if record:
+                events[2].record(engine_stream)
+                marks.append(events)
 
     for _ in range(args.warmup):
         step()
@@ -503,7 +527,7 @@ def run_b200(args, rank, world, local_rank):
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(engine_stream)
     for _ in range(args.steps):
-        step()
+        step(record=True)
     stop.record(engine_stream)
     stop.synchronize()
     clocks = sampler.stop()
@@ -511,6 +535,11 @@ def run_b200(args, rank, world, local_rank):
     elapsed_ms = max_over_ranks(start.elapsed_time(stop), world)
     ms_per_step = elapsed_ms / args.steps
     value = prompt_count / (ms_per_step / 1000.0)
+    # per rank: mean scan time and all-reduce time of the timed steps; min / max over ranks
+    scan_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in marks)
+    reduce_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in marks)
+    per_rank = gather_over_ranks([scan_ms, reduce_ms, float(sum(len(p.tokens) for p in mine)), float(len(mine))],
+                                 world)
 
     # one more (untimed) step with every engine launch bracketed by CUDA events: per-kernel
     # device time and algorithmic work inside the real scan, and the count of our own launches
@@ -609,6 +638,12 @@ def run_b200(args, rank, world, local_rank):
                      "peak_source": f"{peak_kind} bf16_tflops_sustained x {world} GPU(s)",
                      "algorithmic_flops_per_step": flops},
         "clocks": clocks,
+        "ranks": {"scan_ms": {"min": round(min(r[0] for r in per_rank), 3), "max": round(max(r[0] for r in per_rank), 3)},
+                  "allreduce_ms": {"min": round(min(r[1] for r in per_rank), 4),
+                                   "max": round(max(r[1] for r in per_rank), 4)},
+                  "tokens": [int(r[2]) for r in per_rank], "prompts": [int(r[3]) for r in per_rank],
+                  "note": "per rank: mean over the timed steps of the scan and of the all-reduce (CUDA events "
+                          "on the engine stream)"},
         "gpu_launches": gpu_launches,
         "attention_kernel": args.attention,
         "kernels": kernels,
@@ -624,6 +659,12 @@ def run_b200(args, rank, world, local_rank):
         result["cpu_baseline"] = cpu_baseline(config, prompts[0])
     del prepared
     engine.close()
+    if rank == 0 and world == 1 and not args.no_sweep:
+        torch.cuda.empty_cache()
+        result["sweep"] = {"rows": bandwidth_sweep(hbm_peak, dtype=args.dtype), "peak_source": f"{peak_kind} hbm_gbs",
+                           "config": "BASELINE config 5: tokens {1,64,1024,8192,32768} x hidden {2048,3584,4096,8192}, "
+                                     "head_dim 128, intermediate 3.5 x hidden, vocab 152064; each kernel timed alone "
+                                     "(CUDA events, 3 warm-up + 20 launches)"}
     return result
 
 

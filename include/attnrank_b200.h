@@ -300,6 +300,15 @@ int ar_decode_attention(const void* q, const void* k_cache, const void* v_cache,
                         int query_heads, int kv_heads, int head_dim, int sliding_window, void* out, int dtype,
                         void* stream);
 
+/* Self-test of the library's bounded device waits. No counterpart in the reference: its kernels
+ * never wait on one another. `ctas` CTAs (1..1024) wait on the grid barrier of the persistent
+ * decode step for a counter value that nothing writes; the wait gives up after `spin_limit` polls
+ * (each at least 64 ns; 1..4194304, the production limit) and the call returns AR_ERR_DEVICE with a
+ * wait-timeout message. The device stays usable afterwards: a deployment can check that a stalled
+ * wait ends in an error, not a hang. Allocates 8 bytes with cudaMallocAsync on `stream` and
+ * synchronises the stream. */
+int ar_bounded_wait_selftest(int ctas, uint32_t spin_limit, void* stream);
+
 /* ------------------------------------------------------------------------------------------
  * Profile accumulator and basin pick (host functions of attnrank/src/attnrank.cpp).
  * ------------------------------------------------------------------------------------------ */

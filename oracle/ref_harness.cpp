@@ -31,6 +31,7 @@
 #include "attnrank/model.hpp"
 #include "attnrank/prompt.hpp"
 #include "attnrank/tokenizer.hpp"
+#include "ref_abi.h"
 
 extern "C" {
 void oracle_fill_bf16(uint16_t* out, int64_t first, int64_t count, uint64_t seed, int layer, int kind,
@@ -125,30 +126,39 @@ StructuredPrompt make_prompt(const int32_t* tokens, int token_count, int query_b
   return prompt;
 }
 
+// The seeded synthetic checkpoint of `config`, as the safetensors loader would hand it over.
+void add_synthetic_weights(WeightRegistry& registry, const LlamaConfig& config, bool attention_bias, uint64_t seed,
+                           double std) {
+  const int64_t H = config.hidden_size, I = config.intermediate_size, V = config.vocab_size;
+  const int64_t QD = static_cast<int64_t>(config.num_attention_heads) * config.head_dim();
+  const int64_t KV = config.kv_hidden_size();
+  auto source = std::make_unique<MemoryWeightSource>();
+  source->add("model.embed_tokens.weight", {V, H}, generate(V * H, seed, -1, kEmbedding, std));
+  source->add("model.norm.weight", {H}, ones(H));
+  for (int l = 0; l < config.num_hidden_layers; ++l) {
+    const std::string p = "model.layers." + std::to_string(l) + ".";
+    source->add(p + "self_attn.q_proj.weight", {QD, H}, generate(QD * H, seed, l, kQuery, std));
+    source->add(p + "self_attn.k_proj.weight", {KV, H}, generate(KV * H, seed, l, kKey, std));
+    source->add(p + "self_attn.v_proj.weight", {KV, H}, generate(KV * H, seed, l, kValue, std));
+    source->add(p + "self_attn.o_proj.weight", {H, QD}, generate(H * QD, seed, l, kOutput, std));
+    if (attention_bias) {
+      source->add(p + "self_attn.q_proj.bias", {QD}, generate(QD, seed, l, kQueryBias, std));
+      source->add(p + "self_attn.k_proj.bias", {KV}, generate(KV, seed, l, kKeyBias, std));
+      source->add(p + "self_attn.v_proj.bias", {KV}, generate(KV, seed, l, kValueBias, std));
+    }
+    source->add(p + "mlp.gate_proj.weight", {I, H}, generate(I * H, seed, l, kGate, std));
+    source->add(p + "mlp.up_proj.weight", {I, H}, generate(I * H, seed, l, kUp, std));
+    source->add(p + "mlp.down_proj.weight", {H, I}, generate(H * I, seed, l, kDown, std));
+    source->add(p + "input_layernorm.weight", {H}, ones(H));
+    source->add(p + "post_attention_layernorm.weight", {H}, ones(H));
+  }
+  registry.add_source(std::move(source));
+}
+
 }  // namespace
 
 extern "C" {
 
-struct ref_config {
-  int hidden_size;
-  int intermediate_size;
-  int num_hidden_layers;
-  int num_attention_heads;
-  int num_key_value_heads;
-  int vocab_size;
-  float rms_norm_eps;
-  float rope_theta;
-  int sliding_window;
-  int attention_bias;
-};
-
-struct ref_prompt {
-  const int32_t* tokens;
-  int token_count;
-  int query_begin;
-  int query_end;
-  const int32_t* spans;
-};
 
 const char* ref_last_error() { return g_error.c_str(); }
 
@@ -169,31 +179,8 @@ void* ref_create(const ref_config* c, uint64_t seed, double std, int max_sequenc
     config.sliding_window = c->sliding_window;
     config.tie_word_embeddings = true;  // the output head is never used by probing
 
-    const int64_t H = config.hidden_size, I = config.intermediate_size, V = config.vocab_size;
-    const int64_t QD = static_cast<int64_t>(config.num_attention_heads) * config.head_dim();
-    const int64_t KV = config.kv_hidden_size();
-    auto source = std::make_unique<MemoryWeightSource>();
-    source->add("model.embed_tokens.weight", {V, H}, generate(V * H, seed, -1, kEmbedding, std));
-    source->add("model.norm.weight", {H}, ones(H));
-    for (int l = 0; l < config.num_hidden_layers; ++l) {
-      const std::string p = "model.layers." + std::to_string(l) + ".";
-      source->add(p + "self_attn.q_proj.weight", {QD, H}, generate(QD * H, seed, l, kQuery, std));
-      source->add(p + "self_attn.k_proj.weight", {KV, H}, generate(KV * H, seed, l, kKey, std));
-      source->add(p + "self_attn.v_proj.weight", {KV, H}, generate(KV * H, seed, l, kValue, std));
-      source->add(p + "self_attn.o_proj.weight", {H, QD}, generate(H * QD, seed, l, kOutput, std));
-      if (c->attention_bias) {
-        source->add(p + "self_attn.q_proj.bias", {QD}, generate(QD, seed, l, kQueryBias, std));
-        source->add(p + "self_attn.k_proj.bias", {KV}, generate(KV, seed, l, kKeyBias, std));
-        source->add(p + "self_attn.v_proj.bias", {KV}, generate(KV, seed, l, kValueBias, std));
-      }
-      source->add(p + "mlp.gate_proj.weight", {I, H}, generate(I * H, seed, l, kGate, std));
-      source->add(p + "mlp.up_proj.weight", {I, H}, generate(I * H, seed, l, kUp, std));
-      source->add(p + "mlp.down_proj.weight", {H, I}, generate(H * I, seed, l, kDown, std));
-      source->add(p + "input_layernorm.weight", {H}, ones(H));
-      source->add(p + "post_attention_layernorm.weight", {H}, ones(H));
-    }
     WeightRegistry registry;
-    registry.add_source(std::move(source));
+    add_synthetic_weights(registry, config, c->attention_bias != 0, seed, std);
     LlamaRuntimeOptions options;
     options.device_index = device_index;
     options.max_sequence_length = max_sequence_length;
@@ -256,14 +243,16 @@ int ref_measure_attention(void* handle, const ref_prompt* prompt, int span_count
   }
 }
 
-// The stock scan: AttentionLayerScanner over a StaticProbeSampleSource, then the basin pick.
+// The stock scan: AttentionLayerScanner over a StaticProbeSampleSource, then the basin pick, with
+// any IAttentionProvider behind it (the reference's CudaLlamaModel, or a provider of another
+// library built against the reference's headers).
 // attention_out / order_out: [layers][span_count]; seconds_out: wall time of the scan call
 // (synchronous in the reference: every prompt ends with a device-to-host copy).
-int ref_scan(void* handle, const ref_prompt* prompts, int prompt_count, int span_count, int layer_begin,
-             int layer_end, int normalize_by_length, double min_edge_ratio, double* attention_out, int* order_out,
-             int* layer_index_out, int* layer_count_out, int* selected_out, double* seconds_out) {
+static int scan_with(std::shared_ptr<IAttentionProvider> provider, const ref_prompt* prompts, int prompt_count,
+                     int span_count, int layer_begin, int layer_end, int normalize_by_length, double min_edge_ratio,
+                     double* attention_out, int* order_out, int* layer_index_out, int* layer_count_out,
+                     int* selected_out, double* seconds_out) {
   try {
-    auto* holder = static_cast<Holder*>(handle);
     std::vector<StructuredPrompt> structured;
     std::vector<ProbeSample> samples;
     structured.reserve(prompt_count);
@@ -276,7 +265,7 @@ int ref_scan(void* handle, const ref_prompt* prompts, int prompt_count, int span
       samples.push_back(std::move(sample));
     }
     ProbeDependencies dependencies;
-    dependencies.attention_provider = holder->shared;
+    dependencies.attention_provider = std::move(provider);
     dependencies.prompt_builder = std::make_shared<TokenPromptBuilder>(&structured);
     dependencies.progress = std::make_shared<NullProgressObserver>();
     LayerScanConfig config;
@@ -309,6 +298,58 @@ int ref_scan(void* handle, const ref_prompt* prompts, int prompt_count, int span
     return 1;
   }
 }
+
+int ref_scan(void* handle, const ref_prompt* prompts, int prompt_count, int span_count, int layer_begin,
+             int layer_end, int normalize_by_length, double min_edge_ratio, double* attention_out, int* order_out,
+             int* layer_index_out, int* layer_count_out, int* selected_out, double* seconds_out) {
+  return scan_with(static_cast<Holder*>(handle)->shared, prompts, prompt_count, span_count, layer_begin, layer_end,
+                   normalize_by_length, min_edge_ratio, attention_out, order_out, layer_index_out, layer_count_out,
+                   selected_out, seconds_out);
+}
+
+// The same stock scan over a caller's provider: `provider` is a std::shared_ptr<IAttentionProvider>*.
+int ref_scan_provider(void* provider, const ref_prompt* prompts, int prompt_count, int span_count, int layer_begin,
+                      int layer_end, int normalize_by_length, double min_edge_ratio, double* attention_out,
+                      int* order_out, int* layer_index_out, int* layer_count_out, int* selected_out,
+                      double* seconds_out) {
+  return scan_with(*static_cast<std::shared_ptr<IAttentionProvider>*>(provider), prompts, prompt_count, span_count,
+                   layer_begin, layer_end, normalize_by_length, min_edge_ratio, attention_out, order_out,
+                   layer_index_out, layer_count_out, selected_out, seconds_out);
+}
+
+// The seeded synthetic checkpoint as a WeightRegistry with its LlamaConfig, for a caller that
+// builds its own provider from them (ref_weights_registry / ref_weights_config give the objects).
+struct SyntheticWeights {
+  LlamaConfig config;
+  WeightRegistry registry;
+};
+
+void* ref_weights_create(const ref_config* c, uint64_t seed, double std, int max_sequence_length) {
+  try {
+    auto weights = std::make_unique<SyntheticWeights>();
+    LlamaConfig& config = weights->config;
+    config.hidden_size = c->hidden_size;
+    config.intermediate_size = c->intermediate_size;
+    config.num_hidden_layers = c->num_hidden_layers;
+    config.num_attention_heads = c->num_attention_heads;
+    config.num_key_value_heads = c->num_key_value_heads;
+    config.vocab_size = c->vocab_size;
+    config.max_position_embeddings = max_sequence_length;
+    config.rms_norm_eps = c->rms_norm_eps;
+    config.rope_theta = c->rope_theta;
+    config.sliding_window = c->sliding_window;
+    config.tie_word_embeddings = true;
+    add_synthetic_weights(weights->registry, config, c->attention_bias != 0, seed, std);
+    return weights.release();
+  } catch (const std::exception& error) {
+    g_error = error.what();
+    return nullptr;
+  }
+}
+
+void ref_weights_destroy(void* weights) { delete static_cast<SyntheticWeights*>(weights); }
+const void* ref_weights_registry(void* weights) { return &static_cast<SyntheticWeights*>(weights)->registry; }
+const void* ref_weights_config(void* weights) { return &static_cast<SyntheticWeights*>(weights)->config; }
 
 // CudaLlamaModel::generate (model.cu:532-565) with the sampler of make_sampler (model.cpp:124-127).
 // tokens_out has room for max_new_tokens ids; seconds_out: wall time of the generate call.

@@ -35,10 +35,8 @@ int main(int argc, char**) {
 
 
 def _adapter_source() -> str:
-    blocks = re.findall(r"```cpp\n(.*?)```", DOC, re.S)
-    assert len(blocks) == 2, "INTEGRATION.md holds the provider and the language model blocks"
-    # the second block continues the first one's namespace
-    return blocks[0].replace("}  // namespace attnrank\n", "") + blocks[1] + "\n}  // namespace attnrank\n"
+    from oracle.extract_adapter import adapter_source
+    return adapter_source(DOC)
 
 
 def test_cpp_adapters_compile_and_link_against_the_reference(tmp_path):

@@ -63,6 +63,7 @@ def _ctype_of(declaration: str):
         return "pointer"
     kind = declaration.replace("const", " ").split()[0]
     return {"int": ctypes.c_int, "int32_t": ctypes.c_int32, "int64_t": ctypes.c_int64, "uint64_t": ctypes.c_uint64,
+            "uint32_t": ctypes.c_uint32,
             "float": ctypes.c_float, "double": ctypes.c_double}[kind]
 
 
