@@ -56,6 +56,8 @@ CASES = {
     "sampler select": (lambda: lib.ar_sampler_select(None, None, 4, None), "null argument"),
     "profile slots": (lambda: lib.ar_profile_from_accumulated(None, -1, 1, None, None), "invalid arguments"),
     "position order count": (lambda: lib.ar_resolve_position_order(None, 0, -1, (ctypes.c_int * 1)()), ""),
+    "wait selftest ctas": (lambda: lib.ar_bounded_wait_selftest(0, 16, None), "ctas must be 1..1024"),
+    "wait selftest limit": (lambda: lib.ar_bounded_wait_selftest(4, (1 << 22) + 1, None), "spin_limit 1..4194304"),
 }
 
 
