@@ -118,6 +118,8 @@ def parse_args():
                         help="only the fused-kernel bandwidth sweep of BASELINE config 5 (one GPU)")
     parser.add_argument("--no-sweep", action="store_true",
                         help="leave the config-5 sweep out of the N=1 bench line")
+    parser.add_argument("--attention-compare", action="store_true",
+                        help="only the tcgen05 attention beside torch's cuDNN and flash attention (one GPU)")
     return parser.parse_args()
 
 
@@ -354,6 +356,85 @@ def kernel_rooflines(config, hbm_peak, tensor_peak, tokens: int = 16384, repeats
         512, 0, mass.ctypes.data, code, s)), flops=mass_flops)
     torch.cuda.synchronize()
     return results
+
+
+def attention_comparison(tensor_peak: float, dtype: str = "fp16", repeats: int = 20) -> list[dict]:
+    """This build's tcgen05 attention beside the attention kernels shipped with torch (cuDNN's and
+    the flash backend of scaled_dot_product_attention) on equal-length causal batches of the scan's
+    two shapes: 17 prompts of 940 tokens with 28/4 heads (config 3) and 4 of 4096 with 32/8 heads
+    (config 4). Same inputs for all; FLOPs count the causal triangle, 2·Hq·D·T(T+1) per prompt. The
+    build's figure goes through the C ABI (host tile list and a sync inside every call); the
+    libraries' are back-to-back launches. Output difference against cuDNN is reported beside it."""
+    import ctypes
+
+    import numpy as np
+    import torch
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    from attnrank import _native
+
+    half = torch.float16 if dtype == "fp16" else torch.bfloat16
+    code = _native.DTYPE_F16 if dtype == "fp16" else _native.DTYPE_BF16
+    lib = _native.lib
+    dev = torch.device("cuda")
+    stream = torch.cuda.current_stream()
+    s = ctypes.c_void_p(stream.cuda_stream)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    gen = torch.Generator(device=dev).manual_seed(1)
+
+    def time_it(launch) -> float:
+        for _ in range(3):
+            launch()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(repeats):
+            launch()
+        stop.record(stream)
+        stop.synchronize()
+        return start.elapsed_time(stop) / 1000 / repeats
+
+    rows = []
+    for name, B, T, Hq, Hkv in [("config 3 shape", 17, 940, 28, 4), ("config 4 shape", 4, 4096, 32, 8)]:
+        D = 128
+        W = (Hq + 2 * Hkv) * D
+        flops = B * 2 * Hq * D * T * (T + 1)
+        qkv = torch.randn(B * T, W, device=dev, generator=gen).to(half)
+        out = torch.empty(B * T, Hq * D, device=dev, dtype=half)
+        lse = torch.empty(B * T, Hq, device=dev)
+        offsets = (np.arange(B + 1) * T).astype(np.int32)
+        offsets_d = torch.from_numpy(offsets).to(dev)
+        entry = {"case": name, "prompts": B, "tokens_per_prompt": T, "heads": f"{Hq}/{Hkv}",
+                 "gflop": round(flops / 1e9, 1)}
+
+        def ours():
+            _native.check(lib.ar_causal_attention(P(qkv), P(out), P(lse), offsets.ctypes.data, P(offsets_d), B, Hq,
+                                                  Hkv, D, 0, code, s))
+        seconds = time_it(ours)
+        entry["this_build_tcgen05"] = {"us": round(seconds * 1e6, 1), "tflops": round(flops / seconds / 1e12, 1),
+                                       "frac": round(flops / seconds / 1e12 / tensor_peak, 4)}
+        view = qkv.view(B, T, Hq + 2 * Hkv, D)
+        q = view[:, :, :Hq].transpose(1, 2)
+        k = view[:, :, Hq:Hq + Hkv].transpose(1, 2).repeat_interleave(Hq // Hkv, dim=1)
+        v = view[:, :, Hq + Hkv:].transpose(1, 2).repeat_interleave(Hq // Hkv, dim=1)
+        mine = out.view(B, T, Hq, D).transpose(1, 2).float()
+        for label, backend in [("torch_sdpa_cudnn", SDPBackend.CUDNN_ATTENTION),
+                               ("torch_sdpa_flash", SDPBackend.FLASH_ATTENTION)]:
+            try:
+                with sdpa_kernel([backend]):
+                    seconds = time_it(lambda: F.scaled_dot_product_attention(q, k, v, is_causal=True))
+                    reference = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+                torch.cuda.synchronize()
+                entry[label] = {"us": round(seconds * 1e6, 1), "tflops": round(flops / seconds / 1e12, 1),
+                                "frac": round(flops / seconds / 1e12 / tensor_peak, 4),
+                                "max_abs_diff_vs_this_build": float((reference.float() - mine).abs().max())}
+                del reference
+            except Exception as error:  # noqa: BLE001 - a backend this torch build lacks is reported
+                entry[label] = {"unavailable": repr(error)[:200]}
+        rows.append(entry)
+        del qkv, out, lse, q, k, v, view, mine
+        torch.cuda.empty_cache()
+    return rows
 
 
 SWEEP_TOKENS = (1, 64, 1024, 8192, 32768)
@@ -650,13 +731,22 @@ def run_b200(args, rank, world, local_rank):
         "kernels_peak_source": f"{peak_kind}: hbm_gbs for HBM-bound, bf16_tflops_sustained for tensor-bound; "
                                "CUDA events around every launch on the engine stream during one extra step",
     }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(config, prompts[0])
     if rank == 0 and not args.no_kernels:
+        # The scan holds the GPU at its power-capped clock (about 1.3 GHz) and the power limiter
+        # takes a while to release it; "alone" means at the clock these kernels set by themselves,
+        # so the GPU idles first (the CPU baseline above already gave it that time at N=1), and
+        # the SM clock seen during the timing is reported beside the figures.
+        torch.cuda.synchronize()
+        time.sleep(0 if "cpu_baseline" in result else 3)
+        isolated_clock = ClockSampler(local_rank)
+        isolated_clock.start()
         result["kernels_isolated"] = kernel_rooflines(config, hbm_peak, peak.get("bf16_tflops",
                                                                                  FALLBACK_PEAKS["bf16_tflops"]),
                                                       dtype=args.dtype)
         result["kernels_isolated_peak_source"] = f"{peak_kind} hbm_gbs / bf16_tflops (burst)"
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        result["cpu_baseline"] = cpu_baseline(config, prompts[0])
+        result["kernels_isolated_clocks"] = isolated_clock.stop()
     del prepared
     engine.close()
     if rank == 0 and world == 1 and not args.no_sweep:
@@ -981,6 +1071,11 @@ def main():
                   "peak_source": f"{kind} hbm_gbs", "dtype": args.dtype,
                   "config": "tokens {1,64,1024,8192,32768} x hidden {2048,3584,4096,8192}, head_dim 128, "
                             "intermediate 3.5 x hidden, vocab 152064"}
+    elif args.attention_compare:
+        peak, kind = peaks()
+        result = {"attention_comparison": attention_comparison(peak.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]),
+                                                               dtype=args.dtype),
+                  "peak_source": f"{kind} bf16_tflops (burst)", "dtype": args.dtype}
     elif args.kernels_only:
         from attnrank import synthetic
         peak, kind = peaks()
