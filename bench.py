@@ -100,7 +100,8 @@ def parse_args():
     parser.add_argument("--config", choices=sorted(WORKLOADS), default="qwen-scan",
                         help="qwen-scan: BASELINE config 3 (the bench line); llama3-long: config 4")
     parser.add_argument("--prompts", type=int, default=None, help="prompts per scan (default: the workload's)")
-    parser.add_argument("--batch-tokens", type=int, default=16384)
+    parser.add_argument("--batch-tokens", type=int, default=32768,
+                        help="packed tokens per batch (engine max_batch_tokens)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-kernels", action="store_true", help="skip the per-kernel roofline timing")
     parser.add_argument("--kernels-only", action="store_true",
