@@ -294,7 +294,21 @@ __global__ void __launch_bounds__(256) silu_multiply_kernel(const T* __restrict_
   const unsigned chunks = static_cast<unsigned>(width) >> 3;
   const unsigned total = static_cast<unsigned>(tokens) * chunks;  // < 2^31: the launcher checks
   const unsigned stride = gridDim.x * blockDim.x;
-  for (unsigned first = blockIdx.x * blockDim.x + threadIdx.x; first < total; first += stride * kSiluUnroll) {
+  // (token, chunk) of the current item, advanced by the grid stride without a division per item
+  const unsigned stride_rows = stride / chunks;
+  const unsigned stride_chunks = stride - stride_rows * chunks;
+  unsigned first = blockIdx.x * blockDim.x + threadIdx.x;
+  unsigned token = first / chunks;
+  unsigned chunk = first - token * chunks;
+  auto advance = [&]() {
+    token += stride_rows;
+    chunk += stride_chunks;
+    if (chunk >= chunks) {
+      chunk -= chunks;
+      ++token;
+    }
+  };
+  for (; first < total; first += stride * kSiluUnroll) {
     uint4 g_raw[kSiluUnroll];
     uint4 u_raw[kSiluUnroll];
     long long out_at[kSiluUnroll];
@@ -303,13 +317,12 @@ __global__ void __launch_bounds__(256) silu_multiply_kernel(const T* __restrict_
       const unsigned item = first + k * stride;
       out_at[k] = -1;
       if (item < total) {
-        const unsigned token = item / chunks;
-        const unsigned chunk = item - token * chunks;
         const long long in_at = static_cast<long long>(token) * in_stride + chunk * 8;
         g_raw[k] = load_stream(gate + in_at);
         u_raw[k] = load_stream(up + in_at);
         out_at[k] = static_cast<long long>(token) * out_stride + chunk * 8;
       }
+      advance();
     }
 #pragma unroll
     for (int k = 0; k < kSiluUnroll; ++k) {

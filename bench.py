@@ -121,6 +121,8 @@ def parse_args():
                         help="leave the config-5 sweep out of the N=1 bench line")
     parser.add_argument("--attention-compare", action="store_true",
                         help="only the tcgen05 attention beside torch's cuDNN and flash attention (one GPU)")
+    parser.add_argument("--copy-under-cap", action="store_true",
+                        help="only a plain device copy timed alone and between power-capping GEMMs (one GPU)")
     return parser.parse_args()
 
 
@@ -436,6 +438,50 @@ def attention_comparison(tensor_peak: float, dtype: str = "fp16", repeats: int =
         del qkv, out, lse, q, k, v, view, mine
         torch.cuda.empty_cache()
     return rows
+
+
+def copy_under_power_cap(local_rank: int) -> dict:
+    """A plain 1 GiB device copy (torch, CUDA events) timed alone, then between bursts of 8192^3
+    bf16 GEMMs that hold the GPU at its power-capped clock, as the scan's GEMMs do: how much of
+    the HBM-bound kernels' in-scan slowdown the memory path itself shows at that clock."""
+    import torch
+
+    stream = torch.cuda.current_stream()
+    a = torch.randn(1 << 29, device="cuda", dtype=torch.bfloat16)
+    b = torch.empty_like(a)
+    x = torch.randn(8192, 8192, device="cuda", dtype=torch.bfloat16)
+    y = torch.randn(8192, 8192, device="cuda", dtype=torch.bfloat16)
+    z = torch.empty_like(x)
+
+    def copy_gbs(repeats: int) -> float:
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(repeats):
+            b.copy_(a)
+        stop.record(stream)
+        stop.synchronize()
+        return 2 * a.numel() * a.element_size() * repeats / (start.elapsed_time(stop) / 1000) / 1e9
+
+    for _ in range(3):
+        copy_gbs(3)
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    alone = [copy_gbs(10) for _ in range(60)]  # about 0.2 s: long enough for a clock sample
+    clocks_alone = sampler.stop()
+    for _ in range(200):  # about 3 s of GEMMs: the power limiter settles
+        torch.matmul(x, y, out=z)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    capped = []
+    for _ in range(10):
+        for _ in range(20):
+            torch.matmul(x, y, out=z)
+        capped.append(copy_gbs(2))
+    clocks_capped = sampler.stop()
+    return {"copy_alone_gbs": round(statistics.median(alone), 1), "clocks_alone": clocks_alone,
+            "copy_between_gemms_gbs": round(statistics.median(capped), 1), "clocks_between_gemms": clocks_capped,
+            "ratio": round(statistics.median(capped) / statistics.median(alone), 3)}
 
 
 SWEEP_TOKENS = (1, 64, 1024, 8192, 32768)
@@ -1072,6 +1118,8 @@ def main():
                   "peak_source": f"{kind} hbm_gbs", "dtype": args.dtype,
                   "config": "tokens {1,64,1024,8192,32768} x hidden {2048,3584,4096,8192}, head_dim 128, "
                             "intermediate 3.5 x hidden, vocab 152064"}
+    elif args.copy_under_cap:
+        result = {"copy_under_power_cap": copy_under_power_cap(local_rank)}
     elif args.attention_compare:
         peak, kind = peaks()
         result = {"attention_comparison": attention_comparison(peak.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]),
