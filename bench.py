@@ -357,6 +357,10 @@ def kernel_rooflines(config, hbm_peak, tensor_peak, tokens: int = 16384, repeats
     timed("document_mass (incl. host planning + sync)", lambda: _native.check(lib.ar_document_attention_mass(
         P(qkv2), total, P(lse), offsets.ctypes.data, len(prompts), qs.ctypes.data, sp.ctypes.data, 5, Hq, Hkv, D, 0,
         512, 0, mass.ctypes.data, code, s)), flops=mass_flops)
+    # 4.6 GFLOP is a few µs of tensor work: this synchronous call (host planning, metadata upload,
+    # the mass kernel and its finaliser, read-back of the doubles) is latency, not a roofline
+    entry = results["document_mass (incl. host planning + sync)"]
+    entry.update({"bound": "latency: one synchronous C-ABI call", "frac": None})
     torch.cuda.synchronize()
     return results
 
