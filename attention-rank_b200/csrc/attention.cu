@@ -295,8 +295,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-}  // namespace
-
+// internal linkage: its per-device flag belongs to this copy of the library (a template with
+// external linkage would share one flag with any other copy loaded into the same process)
 template <typename T>
 cudaError_t launch_typed(const AttentionArgs& args, cudaStream_t stream) {
   int device = 0;
@@ -314,6 +314,8 @@ cudaError_t launch_typed(const AttentionArgs& args, cudaStream_t stream) {
       args.query_heads, args.kv_heads, args.sliding_window);
   return cudaGetLastError();
 }
+
+}  // namespace
 
 cudaError_t launch_causal_attention(const AttentionArgs& args, cudaStream_t stream) {
   if (args.tile_count <= 0) return cudaSuccess;

@@ -6,11 +6,11 @@
 //     qkv  += bias; RoPE(q, k)                rotary_bias_kernel (in place)
 //     attn, lse = causal_attention(qkv)       attention_tc.cu (tcgen05 flash, no score matrix)
 //     partials[layer] = document_mass(qkv, lse)   mass.cu (tcgen05), probed layers only
-//     delta = attn @ Wo^T
-//     residual += delta; normed = rms(residual) * post_norm
+//     residual += attn @ Wo^T                 cuBLASLt, fp32 accumulator added into the fp32 residual
+//     normed = rms(residual) * post_norm
 //     gate|up = normed @ Wgu^T; act = silu(gate) * up
-//     delta = act @ Wdown^T
-//     residual += delta; normed = rms(residual) * next input_norm
+//     residual += act @ Wdown^T
+//     normed = rms(residual) * next input_norm
 //   finalize(partials) -> per-prompt unit-sum rows, += device accumulator
 //
 // The order of operations per layer is the reference's LlamaForwardPass
@@ -129,7 +129,7 @@ struct GemmPlan {
   bool bias = false;  // the fp32 bias epilogue is part of the plan
 };
 
-using GemmKey = std::tuple<int, int, int, int>;  // m, n, k, bias requested
+using GemmKey = std::tuple<int, int, int, int>;  // m, n, k, epilogue (0 none, 1 bias, 2 accumulate fp32)
 
 void destroy_plans(std::map<GemmKey, GemmPlan>& plans) {
   for (auto& entry : plans) {
@@ -348,7 +348,8 @@ void Engine::allocate() {
   qkv_ = device_alloc(T * Wqkv * 2);
   attn_ = device_alloc(T * Hq * D * 2);
   delta_ = device_alloc(T * H * 2);
-  gate_up_ = device_alloc(T * 2 * I * 2);
+  gate_up_bytes_ = T * 2 * I * 2;
+  gate_up_ = device_alloc(gate_up_bytes_);
   act_ = device_alloc(T * I * 2);
   lse_ = static_cast<float*>(device_alloc(T * Hq * 4));
   positions_ = static_cast<int32_t*>(device_alloc(T * 4));
@@ -556,8 +557,21 @@ void Engine::refresh_half_bias(int layer) {
 }
 
 bool Engine::gemm(const void* x, const void* w, void* y, int m, int n, int k, const void* bias) {
+  return gemm_plan_and_run(x, w, y, m, n, k, bias, false);
+}
+
+// residual[m, n] (fp32) += x[m, k] w[n, k]^T: the projection's fp32 accumulator is added to the
+// fp32 residual in the GEMM epilogue (beta = 1), as the reference adds its fp32 GEMM output
+// (model.cu:360-364 writes CUDA_R_32F; add_in_place at :397 and :418), with no 16-bit rounding of
+// the projection in between.
+void Engine::gemm_residual(const void* x, const void* w, float* residual, int m, int n, int k) {
+  gemm_plan_and_run(x, w, residual, m, n, k, nullptr, true);
+}
+
+bool Engine::gemm_plan_and_run(const void* x, const void* w, void* y, int m, int n, int k, const void* bias,
+                               bool accumulate) {
   auto& cache = plans_->by_shape;
-  const auto key = std::make_tuple(m, n, k, bias != nullptr ? 1 : 0);
+  const auto key = std::make_tuple(m, n, k, bias != nullptr ? 1 : (accumulate ? 2 : 0));
   auto found = cache.find(key);
   if (found == cache.end()) {
     if (cache.size() > 512) {
@@ -578,7 +592,7 @@ bool Engine::gemm(const void* x, const void* w, void* y, int m, int n, int k, co
     const cudaDataType_t type = options_.activation_dtype == kActFp16 ? CUDA_R_16F : CUDA_R_16BF;
     check_lt(cublasLtMatrixLayoutCreate(&plan.a, type, k, n, k), "layout a");
     check_lt(cublasLtMatrixLayoutCreate(&plan.b, type, k, m, k), "layout b");
-    check_lt(cublasLtMatrixLayoutCreate(&plan.c, type, n, m, n), "layout c");
+    check_lt(cublasLtMatrixLayoutCreate(&plan.c, accumulate ? CUDA_R_32F : type, n, m, n), "layout c");
     cublasLtMatmulPreference_t preference = nullptr;
     check_lt(cublasLtMatmulPreferenceCreate(&preference), "preference");
     check_lt(cublasLtMatmulPreferenceSetAttribute(preference, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES,
@@ -621,9 +635,16 @@ bool Engine::gemm(const void* x, const void* w, void* y, int m, int n, int k, co
     // From here the cache owns the plan's descriptors, with the heuristic's first choice. Each
     // candidate is then timed once on this call's own buffers (y is overwritten by the real launch
     // below) and the fastest kept; the first call of a shape happens in warm-up, not in a timed scan.
+    // An accumulating GEMM must not add into y more than once: its candidates run on the gate|up
+    // buffer instead (as fp32 [m, n]; no live data there when the o_proj and down GEMMs run), and
+    // with too small a buffer the heuristic's first choice is kept untimed.
     plan.algo = results[0].algo;
     found = cache.emplace(key, plan).first;
-    if (returned > 1) {
+    void* trial = y;
+    if (accumulate) {
+      trial = static_cast<size_t>(m) * n * sizeof(float) <= gate_up_bytes_ ? gate_up_ : nullptr;
+    }
+    if (returned > 1 && trial != nullptr) {
       struct Events {  // released on every path out, the throwing ones included
         cudaEvent_t start = nullptr, stop = nullptr;
         ~Events() {
@@ -635,16 +656,18 @@ bool Engine::gemm(const void* x, const void* w, void* y, int m, int n, int k, co
       cudaEvent_t& stop = events.stop;
       check_cuda(cudaEventCreate(&start), "autotune event");
       check_cuda(cudaEventCreate(&stop), "autotune event");
-      const float one = 1.0f, zero = 0.0f;
+      const float one = 1.0f;
+      const float trial_beta = accumulate ? 1.0f : 0.0f;
       float best = 0.0f;
       for (int i = 0; i < returned; ++i) {
         if (results[i].state != CUBLAS_STATUS_SUCCESS) continue;
-        bool ok = cublasLtMatmul(lt_, plan.op, &one, w, plan.a, x, plan.b, &zero, y, plan.c, y, plan.c, &results[i].algo,
-                                 lt_workspace_, lt_workspace_bytes_, stream_) == CUBLAS_STATUS_SUCCESS;  // warm
+        bool ok = cublasLtMatmul(lt_, plan.op, &one, w, plan.a, x, plan.b, &trial_beta, trial, plan.c, trial, plan.c,
+                                 &results[i].algo, lt_workspace_, lt_workspace_bytes_, stream_) ==
+                  CUBLAS_STATUS_SUCCESS;  // warm
         check_cuda(cudaEventRecord(start, stream_), "autotune event");
         for (int r = 0; ok && r < 3; ++r) {
-          ok = cublasLtMatmul(lt_, plan.op, &one, w, plan.a, x, plan.b, &zero, y, plan.c, y, plan.c, &results[i].algo,
-                              lt_workspace_, lt_workspace_bytes_, stream_) == CUBLAS_STATUS_SUCCESS;
+          ok = cublasLtMatmul(lt_, plan.op, &one, w, plan.a, x, plan.b, &trial_beta, trial, plan.c, trial, plan.c,
+                              &results[i].algo, lt_workspace_, lt_workspace_bytes_, stream_) == CUBLAS_STATUS_SUCCESS;
         }
         check_cuda(cudaEventRecord(stop, stream_), "autotune event");
         check_cuda(cudaEventSynchronize(stop), "autotune event");
@@ -657,7 +680,7 @@ bool Engine::gemm(const void* x, const void* w, void* y, int m, int n, int k, co
       }
     }
   }
-  const float alpha = 1.0f, beta = 0.0f;
+  const float alpha = 1.0f, beta = accumulate ? 1.0f : 0.0f;
   const GemmPlan& plan = found->second;
   if (plan.bias) {
     check_lt(cublasLtMatmulDescSetAttribute(plan.op, CUBLASLT_MATMUL_DESC_BIAS_POINTER, &bias, sizeof(bias)),
@@ -1033,7 +1056,7 @@ void Engine::execute_batch(const BatchLayout& layout, const int32_t* dev, int sp
   mass.dtype = dtype;
 
   // algorithmic work of each launch: FLOPs for GEMMs / attention / mass, HBM bytes otherwise
-  const double norm_bytes = m * H * (4 + 2 + 4 + 2);
+  const double norm_bytes = m * H * (4 + 2);  // read the fp32 residual, write the 16-bit row
   const double silu_bytes = m * I * 2 * 3;
   const int last_layer = range.end - 1;
   for (int l = 0; l <= last_layer; ++l) {
@@ -1066,9 +1089,9 @@ void Engine::execute_batch(const BatchLayout& layout, const int32_t* dev, int sp
     // no probe output depends on them (the reference computes them, model.cu:334-337), so the
     // forward ends at the last mass capture.
     if (l == last_layer) break;
-    timed(kClassGemmOut, 2 * m * H * Hq * D, [&] { gemm(attn_, w.out, delta_, M, H, Hq * D); });
+    timed(kClassGemmOut, 2 * m * H * Hq * D, [&] { gemm_residual(attn_, w.out, residual_, M, H, Hq * D); });
     timed(kClassNorm, norm_bytes, [&] {
-      check_cuda(launch_rms_norm_residual(residual_, delta_, w.post_norm, M, H, c.rms_norm_eps, normed_, dtype, stream_),
+      check_cuda(launch_rms_norm_residual(residual_, nullptr, w.post_norm, M, H, c.rms_norm_eps, normed_, dtype, stream_),
                  "post-attention norm");
     });
     timed(kClassGemmGateUp, 2 * m * 2 * I * H, [&] { gemm(normed_, w.gate_up, gate_up_, M, 2 * I, H); });
@@ -1077,10 +1100,10 @@ void Engine::execute_batch(const BatchLayout& layout, const int32_t* dev, int sp
                                       dtype, stream_),
                  "swiglu");
     });
-    timed(kClassGemmDown, 2 * m * H * I, [&] { gemm(act_, w.down, delta_, M, H, I); });
+    timed(kClassGemmDown, 2 * m * H * I, [&] { gemm_residual(act_, w.down, residual_, M, H, I); });
     const float* next_norm = l + 1 < c.num_hidden_layers ? layers_[l + 1].input_norm : final_norm_;
     timed(kClassNorm, norm_bytes, [&] {
-      check_cuda(launch_rms_norm_residual(residual_, delta_, next_norm, M, H, c.rms_norm_eps, normed_, dtype, stream_),
+      check_cuda(launch_rms_norm_residual(residual_, nullptr, next_norm, M, H, c.rms_norm_eps, normed_, dtype, stream_),
                  "pre-attention norm");
     });
   }

@@ -264,6 +264,9 @@ class Engine {
   // y[m, n] = x[m, k] w[n, k]^T (+ bias[n], 16-bit like y, when given and cuBLASLt offers the
   // epilogue; returns whether the bias was applied)
   bool gemm(const void* x, const void* w, void* y, int m, int n, int k, const void* bias = nullptr);
+  void gemm_residual(const void* x, const void* w, float* residual, int m, int n, int k);
+  bool gemm_plan_and_run(const void* x, const void* w, void* y, int m, int n, int k, const void* bias,
+                         bool accumulate);
   void refresh_half_bias(int layer);
   void run_batch(const std::vector<PromptView>& prompts, const Batch& batch, int span_count, LayerRange range,
                  bool normalize_by_length, double* rows_device, double* raw_rows_device, float* device_accumulator,
@@ -307,6 +310,7 @@ class Engine {
   void* qkv_ = nullptr;
   void* attn_ = nullptr;
   void* delta_ = nullptr;
+  size_t gate_up_bytes_ = 0;
   void* gate_up_ = nullptr;
   void* act_ = nullptr;
   float* lse_ = nullptr;

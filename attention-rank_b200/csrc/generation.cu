@@ -171,16 +171,16 @@ void Engine::prefill_generation(int M) {
     check_cuda(options_.attention_kernel == 0 ? launch_causal_attention_tc(attention, stream_)
                                               : launch_causal_attention(attention, stream_),
                "attention");
-    gemm(attn_, w.out, delta_, M, H, Hq * D);
-    check_cuda(launch_rms_norm_residual(residual_, delta_, w.post_norm, M, H, c.rms_norm_eps, normed_, dtype, stream_),
+    gemm_residual(attn_, w.out, residual_, M, H, Hq * D);
+    check_cuda(launch_rms_norm_residual(residual_, nullptr, w.post_norm, M, H, c.rms_norm_eps, normed_, dtype, stream_),
                "post-attention norm");
     gemm(normed_, w.gate_up, gate_up_, M, 2 * I, H);
     check_cuda(launch_silu_multiply(gate_up_, static_cast<const uint16_t*>(gate_up_) + I, 2LL * I, act_, I, M, I, dtype,
                                     stream_),
                "swiglu");
-    gemm(act_, w.down, delta_, M, H, I);
+    gemm_residual(act_, w.down, residual_, M, H, I);
     const float* next_norm = l + 1 < c.num_hidden_layers ? layers_[l + 1].input_norm : final_norm_;
-    check_cuda(launch_rms_norm_residual(residual_, delta_, next_norm, M, H, c.rms_norm_eps, normed_, dtype, stream_),
+    check_cuda(launch_rms_norm_residual(residual_, nullptr, next_norm, M, H, c.rms_norm_eps, normed_, dtype, stream_),
                "norm");
   }
   // normed_ holds final_norm(hidden); the logits of the last row (read_logits, model.cu:341-350)

@@ -120,7 +120,9 @@ __global__ void __launch_bounds__(kRowThreadsCap) embed_rms_norm_kernel(
   }
 }
 
-template <typename T, int VPT>
+// kDelta false: the residual already holds the sum (the projection GEMM accumulated into it), so
+// the row is only read and normalised (6 bytes per element instead of 12).
+template <typename T, int VPT, bool kDelta>
 __global__ void __launch_bounds__(kRowThreadsCap) rms_norm_residual_kernel(
     float* __restrict__ residual, const T* __restrict__ delta, const float* __restrict__ gamma, int tokens,
     int hidden, float eps, T* __restrict__ normed) {
@@ -128,7 +130,7 @@ __global__ void __launch_bounds__(kRowThreadsCap) rms_norm_residual_kernel(
   const int row = blockIdx.x;
   const int chunks = hidden >> 3;
   float* residual_row = residual + static_cast<size_t>(row) * hidden;
-  const T* delta_row = delta + static_cast<size_t>(row) * hidden;
+  const T* delta_row = kDelta ? delta + static_cast<size_t>(row) * hidden : nullptr;
   float values[VPT][8];
   float squares = 0.0f;
 #pragma unroll
@@ -137,8 +139,8 @@ __global__ void __launch_bounds__(kRowThreadsCap) rms_norm_residual_kernel(
     if (chunk < chunks) {
       const float4 r0 = load_stream_f4(residual_row + chunk * 8);
       const float4 r1 = load_stream_f4(residual_row + chunk * 8 + 4);
-      float d[8];
-      unpack8<T>(load_stream(delta_row + chunk * 8), d);
+      float d[8] = {};
+      if (kDelta) unpack8<T>(load_stream(delta_row + chunk * 8), d);
       values[k][0] = r0.x + d[0];
       values[k][1] = r0.y + d[1];
       values[k][2] = r0.z + d[2];
@@ -156,13 +158,15 @@ __global__ void __launch_bounds__(kRowThreadsCap) rms_norm_residual_kernel(
   }
   const float total = block_sum(squares, scratch);
   const float scale = rsqrtf(total / static_cast<float>(hidden) + eps);
+  if (kDelta) {
 #pragma unroll
-  for (int k = 0; k < VPT; ++k) {
-    const int chunk = threadIdx.x + k * blockDim.x;
-    if (chunk >= chunks) continue;
-    float4* out = reinterpret_cast<float4*>(residual_row + chunk * 8);
-    __stcs(out, make_float4(values[k][0], values[k][1], values[k][2], values[k][3]));
-    __stcs(out + 1, make_float4(values[k][4], values[k][5], values[k][6], values[k][7]));
+    for (int k = 0; k < VPT; ++k) {
+      const int chunk = threadIdx.x + k * blockDim.x;
+      if (chunk >= chunks) continue;
+      float4* out = reinterpret_cast<float4*>(residual_row + chunk * 8);
+      __stcs(out, make_float4(values[k][0], values[k][1], values[k][2], values[k][3]));
+      __stcs(out + 1, make_float4(values[k][4], values[k][5], values[k][6], values[k][7]));
+    }
   }
   store_normed_row<T, VPT>(values, scale, gamma, normed + static_cast<size_t>(row) * hidden, chunks);
 }
@@ -428,11 +432,12 @@ cudaError_t norm_typed(float* residual, const void* delta, const float* gamma, i
   auto launch = [&](auto kernel) {  // one CTA per row
     kernel<<<tokens, threads, 0, stream>>>(residual, d, gamma, tokens, hidden, eps, n);
   };
+  const bool add = delta != nullptr;
   switch (vpt) {
-    case 1: launch(rms_norm_residual_kernel<T, 1>); break;
-    case 2: launch(rms_norm_residual_kernel<T, 2>); break;
-    case 3: launch(rms_norm_residual_kernel<T, 3>); break;
-    case 4: launch(rms_norm_residual_kernel<T, 4>); break;
+    case 1: add ? launch(rms_norm_residual_kernel<T, 1, true>) : launch(rms_norm_residual_kernel<T, 1, false>); break;
+    case 2: add ? launch(rms_norm_residual_kernel<T, 2, true>) : launch(rms_norm_residual_kernel<T, 2, false>); break;
+    case 3: add ? launch(rms_norm_residual_kernel<T, 3, true>) : launch(rms_norm_residual_kernel<T, 3, false>); break;
+    case 4: add ? launch(rms_norm_residual_kernel<T, 4, true>) : launch(rms_norm_residual_kernel<T, 4, false>); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();

@@ -16,6 +16,8 @@ cudaError_t launch_embed_rms_norm(const int32_t* token_ids, int tokens, const vo
                                   int hidden, const float* gamma, float eps, float* residual,
                                   void* normed, int* status, int dtype, cudaStream_t stream);
 
+// residual += delta; normed = 16-bit(rms(residual) * gamma). With delta == nullptr the residual
+// is only read (it already holds the sum) and is not written.
 cudaError_t launch_rms_norm_residual(float* residual, const void* delta, const float* gamma, int tokens,
                                      int hidden, float eps, void* normed, int dtype, cudaStream_t stream);
 

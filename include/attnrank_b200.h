@@ -49,7 +49,9 @@ int ar_embedding_rms_norm(const int32_t* token_ids, int token_count, const void*
                           int* device_status, int dtype, void* stream);
 
 /* Replaces kernels::add_in_place + kernels::rms_norm (cuda_runtime.hpp:126-127, :135;
- * model.cu:398 then :408-409): residual += delta; normed = 16-bit(rms(residual) * gamma). */
+ * model.cu:398 then :408-409): residual += delta; normed = 16-bit(rms(residual) * gamma).
+ * delta may be NULL (kernels::rms_norm alone, cuda_runtime.hpp:126-127): the residual is then
+ * only read, and left unchanged. */
 int ar_rms_norm_residual(float* residual, const void* delta, const float* gamma, int token_count,
                          int hidden_size, float eps, void* normed, int dtype, void* stream);
 

@@ -158,6 +158,29 @@ def test_rms_norm_residual(cuda, tokens, hidden, dtype):
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("tokens,hidden", [(64, 3584), (33, 8192), (1, 4096)])
+def test_rms_norm_without_delta(cuda, tokens, hidden, dtype):
+    """delta = NULL: the engine's form after a projection GEMM has accumulated into the residual.
+    The residual is read, not written (bit-identical afterwards), and the normed row is the
+    oracle's rms_norm of it (kernels.cu:60-83)."""
+    import torch
+    from oracle import forward as F
+    native = _lib()
+    rng = np.random.default_rng(tokens + hidden)
+    residual = rng.standard_normal((tokens, hidden)).astype(np.float32)
+    gamma = (1.0 + 0.1 * rng.standard_normal(hidden)).astype(np.float32)
+    residual_d = torch.from_numpy(residual).to(cuda)
+    gamma_d = torch.from_numpy(gamma).to(cuda)
+    normed = torch.empty((tokens, hidden), dtype=_torch_dtype(dtype), device=cuda)
+    native.check(native.lib.ar_rms_norm_residual(_ptr(residual_d), None, _ptr(gamma_d), tokens, hidden, 1e-6,
+                                                 _ptr(normed), _code(dtype), _stream()))
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(_to_np(residual_d), residual)
+    _, want_normed = F.op_rms_norm_residual(residual, np.zeros_like(residual), gamma, 1e-6)
+    assert_half_close(_to_np(normed), want_normed, dtype)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("heads,kv_heads,bias", [(28, 4, True), (32, 8, False), (3, 1, True)])
 def test_rotary_bias(cuda, heads, kv_heads, bias, dtype):
     import torch
