@@ -110,8 +110,7 @@ __device__ __forceinline__ void item_rows(const DecodeGemvArgs& a, int item, int
 }
 
 // x into shared memory: copied, or built by the RMSNorm prologue (the formula of the engine's
-// rms_norm_residual_kernel: v = residual + delta, y = v * rsqrt(sum(v^2) / k + eps) * gamma; the
-// generation step passes its projections' fp32 outputs as delta, as the prefill adds them), where
+// rms_norm_residual_kernel: v = residual + delta, y = v * rsqrt(sum(v^2) / k + eps) * gamma), where
 // v may also be the embedding row of the step's token (embed_rms_norm_kernel's formula; an id out
 // of range gives a zero row and a status, as there). Block 0 keeps v in residual_out.
 template <typename T>
@@ -151,14 +150,7 @@ __device__ __forceinline__ void stage_x(const DecodeGemvArgs& a, uint4* xs, floa
       const float4 r0 = __ldcg(reinterpret_cast<const float4*>(a.residual_in + 8 * chunk));
       const float4 r1 = __ldcg(reinterpret_cast<const float4*>(a.residual_in + 8 * chunk + 4));
       float d[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
-      if (delta != nullptr && a.delta_f32) {
-        const float* delta32 = static_cast<const float*>(a.delta) + 8 * chunk;
-        const float4 d0 = __ldcg(reinterpret_cast<const float4*>(delta32));
-        const float4 d1 = __ldcg(reinterpret_cast<const float4*>(delta32 + 4));
-        d[0] = d0.x, d[1] = d0.y, d[2] = d0.z, d[3] = d0.w, d[4] = d1.x, d[5] = d1.y, d[6] = d1.z, d[7] = d1.w;
-      } else if (delta != nullptr) {
-        unpack8<T>(__ldcg(reinterpret_cast<const uint4*>(delta + 8 * chunk)), d);
-      }
+      if (delta != nullptr) unpack8<T>(__ldcg(reinterpret_cast<const uint4*>(delta + 8 * chunk)), d);
       values[v][0] = r0.x + d[0];
       values[v][1] = r0.y + d[1];
       values[v][2] = r0.z + d[2];
@@ -261,10 +253,6 @@ __device__ __forceinline__ void finish_item(const DecodeGemvArgs& a, int item, c
         best = sum[1];
         best_at = r0 + 1;
       }
-    } else if (a.f32_out) {
-      float* out = static_cast<float*>(a.y);
-      out[r0] = sum[0];
-      if (pair) out[r0 + 1] = sum[1];
     } else {
       T* out = static_cast<T*>(a.y);
       if (pair) {

@@ -55,12 +55,10 @@ struct DecodeGemvArgs {
   const void* embed_table = nullptr;
   int vocab = 0;
   const void* delta = nullptr;
-  bool delta_f32 = false;  // delta is fp32 [k] (a projection's accumulator), else 16-bit
   const float* gamma = nullptr;
   float eps = 0.0f;
   float* residual_out = nullptr;
   void* y = nullptr;  // plain / logits / gate|up output
-  bool f32_out = false;  // kDecodePlain: y is fp32 (added to the fp32 residual by the next prologue)
   // kDecodeQkv
   const void* bias_half = nullptr;  // 16-bit bias added before rounding (the fp16 GEMM epilogue), or null
   const float* bias = nullptr;      // fp32 bias added after rounding (the bf16 path), or null

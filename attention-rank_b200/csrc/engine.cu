@@ -347,7 +347,7 @@ void Engine::allocate() {
   normed_ = device_alloc(T * H * 2);
   qkv_ = device_alloc(T * Wqkv * 2);
   attn_ = device_alloc(T * Hq * D * 2);
-  delta_ = device_alloc(2 * H * sizeof(float));  // the generation step's two fp32 projection rows
+  delta_ = device_alloc(2 * H * 2);  // the generation step's two 16-bit projection rows
   gate_up_bytes_ = T * 2 * I * 2;
   gate_up_ = device_alloc(gate_up_bytes_);
   act_ = device_alloc(T * I * 2);

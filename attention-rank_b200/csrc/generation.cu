@@ -221,25 +221,20 @@ bool Engine::launch_persistent_step(bool greedy) {
   s.qkv.context = g.context;
   s.qkv.status = status_;
   s.qkv.dtype = dtype;
-  // o_proj and down_proj write fp32 rows that the next fused norm adds to the fp32 residual, as
-  // the prefill's GEMMs add theirs (the reference adds its fp32 GEMM outputs, model.cu:397, :418)
-  float* delta_attention = static_cast<float*>(delta_);
-  float* delta_mlp = delta_attention + H;
+  void* delta_attention = delta_;
+  void* delta_mlp = static_cast<uint16_t*>(delta_) + H;
   s.qkv.delta = delta_mlp;
-  s.qkv.delta_f32 = true;
   s.out_proj.kind = kDecodePlain;
   s.out_proj.rows = H;
   s.out_proj.k = Hq * D;
   s.out_proj.x = attn_;
   s.out_proj.y = delta_attention;
-  s.out_proj.f32_out = true;
   s.out_proj.dtype = dtype;
   s.gate_up.kind = kDecodeGateUp;
   s.gate_up.rows = I;
   s.gate_up.k = H;
   s.gate_up.eps = c.rms_norm_eps;
   s.gate_up.delta = delta_attention;
-  s.gate_up.delta_f32 = true;
   s.gate_up.y = act_;
   s.gate_up.dtype = dtype;
   s.down.kind = kDecodePlain;
@@ -247,14 +242,12 @@ bool Engine::launch_persistent_step(bool greedy) {
   s.down.k = I;
   s.down.x = act_;
   s.down.y = delta_mlp;
-  s.down.f32_out = true;
   s.down.dtype = dtype;
   s.head.kind = kDecodeLogits;
   s.head.w = output_head();
   s.head.rows = c.vocab_size;
   s.head.k = H;
   s.head.delta = delta_mlp;
-  s.head.delta_f32 = true;
   s.head.gamma = final_norm_;
   s.head.eps = c.rms_norm_eps;
   s.head.y = g.logits;
@@ -303,8 +296,8 @@ void Engine::launch_decode_step(bool greedy) {
   // sum into the other); the two deltas are the o_proj and down_proj outputs
   float* residual[2] = {residual_, residual_ + H};
   int current = 0;
-  float* delta_attention = static_cast<float*>(delta_);  // fp32 projection rows (see above)
-  float* delta_mlp = delta_attention + H;
+  void* delta_attention = delta_;
+  void* delta_mlp = static_cast<uint16_t*>(delta_) + H;
   check_cuda(launch_embed_rms_norm(g.state, 1, embedding_, c.vocab_size, H, layers_[0].input_norm, c.rms_norm_eps,
                                    residual[0], normed_, status_, dtype, stream_),
              "decode embedding");
@@ -324,7 +317,6 @@ void Engine::launch_decode_step(bool greedy) {
   qkv.context = g.context;
   qkv.status = status_;
   qkv.dtype = dtype;
-  qkv.delta_f32 = true;
   DecodeAttentionArgs attention;
   attention.q = g.q;
   attention.context = g.context;
@@ -344,7 +336,6 @@ void Engine::launch_decode_step(bool greedy) {
   out_proj.k = Hq * D;
   out_proj.x = attn_;
   out_proj.y = delta_attention;
-  out_proj.f32_out = true;
   out_proj.dtype = dtype;
   DecodeGemvArgs gate_up;
   gate_up.kind = kDecodeGateUp;
@@ -352,7 +343,6 @@ void Engine::launch_decode_step(bool greedy) {
   gate_up.k = H;
   gate_up.eps = c.rms_norm_eps;
   gate_up.delta = delta_attention;
-  gate_up.delta_f32 = true;
   gate_up.y = act_;
   gate_up.dtype = dtype;
   DecodeGemvArgs down;
@@ -361,7 +351,6 @@ void Engine::launch_decode_step(bool greedy) {
   down.k = I;
   down.x = act_;
   down.y = delta_mlp;
-  down.f32_out = true;
   down.dtype = dtype;
   for (int l = 0; l < c.num_hidden_layers; ++l) {
     const LayerWeights& w = layers_[l];
@@ -405,7 +394,6 @@ void Engine::launch_decode_step(bool greedy) {
   head.k = H;
   head.residual_in = residual[current];
   head.delta = delta_mlp;
-  head.delta_f32 = true;
   head.gamma = final_norm_;
   head.eps = c.rms_norm_eps;
   head.y = g.logits;
