@@ -5,7 +5,6 @@ library with a prompt struct laid out like `ar_prompt`. No GPU: nothing is run o
 from __future__ import annotations
 
 import ctypes
-import os
 import re
 import shutil
 import subprocess
@@ -15,7 +14,7 @@ import pytest
 
 ROOT = Path(__file__).resolve().parents[1]
 DOC = (ROOT / "INTEGRATION.md").read_text()
-REFERENCE = Path(os.environ.get("ATTNRANK_REFERENCE", "/root/reference"))
+from oracle import REFERENCE_ROOT as REFERENCE  # noqa: E402
 REFERENCE_LIBRARY = ROOT / "oracle" / "_ref" / "libattnrank_ref.so"
 LIBRARY_DIR = ROOT / "attention-rank_b200" / "attnrank"
 

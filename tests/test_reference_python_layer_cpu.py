@@ -12,14 +12,13 @@ selection steps all run on this build's types.
 from __future__ import annotations
 
 import importlib.util
-import os
 import sys
 from pathlib import Path
 
 import numpy as np
 import pytest
 
-REFERENCE = Path(os.environ.get("ATTNRANK_REFERENCE", "/root/reference"))
+from oracle import REFERENCE_ROOT as REFERENCE  # noqa: E402
 
 
 @pytest.fixture(scope="module")
