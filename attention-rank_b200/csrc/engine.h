@@ -309,8 +309,8 @@ class Engine {
   void* normed_ = nullptr;
   void* qkv_ = nullptr;
   void* attn_ = nullptr;
-  void* delta_ = nullptr;
-  size_t gate_up_bytes_ = 0;
+  void* delta_ = nullptr;       // 16-bit [2, H]: the decode step's o_proj and down_proj rows
+  size_t gate_up_bytes_ = 0;    // also the scratch on which accumulating GEMMs are autotuned
   void* gate_up_ = nullptr;
   void* act_ = nullptr;
   float* lse_ = nullptr;
