@@ -54,13 +54,17 @@ struct __align__(8) MassShared {
 // dynamic shared memory layout (1024-byte aligned base):
 //   [0, 32K)      Q tile: two 128B-swizzled halves of 128 rows x 64 columns
 //   [32K, 96K)    K tiles: two stages x two halves
-//   [96K, 112K)   per-(span, row) running sums, fp32 [kMassMaxSpans][128]
-//   [112K, ...)   MassShared
+//   [96K, ...)    MassShared
+//   then          per-(span, row) running sums, fp32 [span_count][128]
+// Sized by the call's span count: up to 24 spans two CTAs share an SM (one CTA's exponentials
+// and span sums overlap the other's loads and MMAs).
 constexpr uint32_t kQOffset = 0;
 constexpr uint32_t kKOffset = kTileBytes;
-constexpr uint32_t kSigmaOffset = 3 * kTileBytes;
-constexpr uint32_t kControlOffset = kSigmaOffset + kMassMaxSpans * kMassRowTile * 4;
-constexpr size_t kSmemBytes = kControlOffset + sizeof(MassShared) + 1024;  // + alignment slack
+constexpr uint32_t kControlOffset = 3 * kTileBytes;
+constexpr uint32_t kSigmaOffset = kControlOffset + ((sizeof(MassShared) + 15) & ~static_cast<uint32_t>(15));
+constexpr size_t smem_bytes(int span_count) {
+  return kSigmaOffset + static_cast<size_t>(span_count) * kMassRowTile * 4 + 1024;  // + alignment slack
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* pointer) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(pointer));
@@ -167,7 +171,7 @@ struct KernelArgs {
   uint32_t instr_desc;
 };
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     document_mass_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
                          const KernelArgs args) {
   extern __shared__ uint8_t smem_raw[];
@@ -435,6 +439,36 @@ __global__ void finalize_mass_kernel(const float* __restrict__ partials, const i
   if (active && accumulator != nullptr) accumulator[layer * span_count + s] += static_cast<float>(total);
 }
 
+// The same per-(prompt, layer) rows without the cross-prompt accumulator (the kernel-level C ABI):
+// one warp per (prompt, layer), so the prompts no longer queue behind one another. Every value is
+// computed exactly as in finalize_mass_kernel (same order of each sum).
+__global__ void finalize_rows_kernel(const float* __restrict__ partials, const int32_t* __restrict__ item_offsets,
+                                     const int32_t* __restrict__ query_spans, const int32_t* __restrict__ prompt_offsets,
+                                     int span_count, int item_count, int layers, int query_heads,
+                                     double* __restrict__ rows_out, double* __restrict__ raw_rows_out) {
+  const int p = blockIdx.x;
+  const int layer = blockIdx.y;
+  const int s = threadIdx.x;
+  const bool active = s < span_count;
+  const float* layer_partials = partials + static_cast<size_t>(layer) * item_count * span_count;
+  const int length = prompt_offsets[p + 1] - prompt_offsets[p];
+  const ProbeRows rows = probe_rows(query_spans + 2 * p, length);
+  const double observations = static_cast<double>(rows.query_end - rows.query_begin) * query_heads;
+  double raw = 0.0;
+  if (active) {
+    for (int item = item_offsets[p]; item < item_offsets[p + 1]; ++item) {
+      raw += static_cast<double>(layer_partials[static_cast<size_t>(item) * span_count + s]);
+    }
+  }
+  double row = observations > 0.0 ? raw / observations : 0.0;
+  if (active && raw_rows_out != nullptr) raw_rows_out[(static_cast<size_t>(p) * layers + layer) * span_count + s] = row;
+  double sum = row;  // inactive lanes hold 0
+#pragma unroll
+  for (int offset = 16; offset > 0; offset >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, offset);
+  if (sum > 0.0) row /= sum;
+  if (active && rows_out != nullptr) rows_out[(static_cast<size_t>(p) * layers + layer) * span_count + s] = row;
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -486,7 +520,7 @@ cudaError_t launch_document_mass(const MassArgs& args, cudaStream_t stream) {
   static uint64_t configured_devices = 0;
   if (device < 64 && !(configured_devices & (1ull << device))) {
     const cudaError_t status = cudaFuncSetAttribute(document_mass_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                    static_cast<int>(kSmemBytes));
+                                                    static_cast<int>(smem_bytes(kMassMaxSpans)));
     if (status != cudaSuccess) return status;
     configured_devices |= 1ull << device;
   }
@@ -506,13 +540,20 @@ cudaError_t launch_document_mass(const MassArgs& args, cudaStream_t stream) {
   kernel_args.partials = args.partials;
   kernel_args.status = args.status;
   kernel_args.instr_desc = instr_desc(args.dtype == kActFp16 ? 0u : 1u);
-  document_mass_kernel<<<args.item_count, kThreads, kSmemBytes, stream>>>(q_map, k_map, kernel_args);
+  document_mass_kernel<<<args.item_count, kThreads, smem_bytes(args.span_count), stream>>>(q_map, k_map, kernel_args);
   return cudaGetLastError();
 }
 
 cudaError_t launch_finalize_mass(const FinalizeArgs& args, cudaStream_t stream) {
   if (args.prompt_count <= 0 || args.layers <= 0) return cudaSuccess;
   if (args.span_count <= 0 || args.span_count > kMassMaxSpans) return cudaErrorInvalidValue;
+  if (args.accumulator == nullptr) {
+    if (args.layers > 65535) return cudaErrorInvalidValue;  // grid y
+    finalize_rows_kernel<<<dim3(args.prompt_count, args.layers), 32, 0, stream>>>(
+        args.partials, args.item_offsets, args.query_spans, args.prompt_offsets, args.span_count, args.item_count,
+        args.layers, args.query_heads, args.rows, args.raw_rows);
+    return cudaGetLastError();
+  }
   finalize_mass_kernel<<<args.layers, 32, 0, stream>>>(args.partials, args.item_offsets, args.query_spans, args.prompt_offsets,
                                              args.prompt_count, args.span_count, args.item_count, args.layers,
                                              args.query_heads, args.rows, args.raw_rows, args.accumulator);
